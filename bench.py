@@ -1,0 +1,492 @@
+#!/usr/bin/env python
+"""Benchmark of the KV-cache append + attention path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+
+Metric: decode KV-append+attention us/token and HBM GB/s (% of
+roofline) at 1/2/4/8 B200.  A step is one decode step of the path across every
+layer of the model -- per layer one kv_append (QK-Norm/RoPE/F16 append) and
+one kv_attend (attention over the whole cache, plus the per-layer all-gather
+of head outputs when the cache is sharded by KV head over N GPUs) -- at
+positions n_past, n_past+1, ... (cycling over the configuration's step count).
+`value` is the whole-job algorithmic HBM traffic per second (GB/s): per layer
+n_kv*Hkv*d*2*2 (read K and V) + Hkv*d*2*2 (append) + Hkv*d*4*2 (read k, v) +
+Hq*d*4*2 (read q, write o), summed over layers and steps, divided by the max
+over ranks of the device-timed region.  Inputs are synthetic (seeded
+generator) with the configuration's shapes; the cache (GiBs) exceeds L2 every
+step, so no flush is needed.
+
+Default workload: llama-3.2-3B shape, 32k context (the single-GPU decode
+configuration); `--config llama3.1-8b-128k` runs the 128k configuration.
+`--impl reference` times the CPU restatement of the reference's path (the
+oracle; the reference's own ggml backend is not vendored) on the host cores.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ggml-loader_b200"))
+
+METRIC = "decode KV-append+attention µs/token and HBM GB/s (% of roofline) at 1/2/4/8 B200"
+DEFAULT_CONFIG = "llama3.2-3b"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ---------------------------------------------------------------------------
+# algorithmic bytes
+# ---------------------------------------------------------------------------
+
+def layer_bytes(sp, n_kv, n_new=1, shards=1):
+    hq, hkv, d = sp["n_head"] // shards, sp["n_head_kv"] // shards, sp["head_dim"]
+    return (n_kv * hkv * d * 2 * 2 + n_new * hkv * d * 2 * 2 + n_new * hkv * d * 4 * 2 + n_new * hq * d * 4 * 2)
+
+
+def step_bytes(sp, n_past, n_new=1):
+    return sp["n_layer"] * layer_bytes(sp, n_past + n_new, n_new)
+
+
+def positions(sp, first_step, count):
+    cyc = max(1, sp["steps"])
+    return [sp["n_past"] + ((first_step + i) % cyc) for i in range(count)]
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def committed_traffic(config, kernel):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, or None."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return j.get(config, {}).get(kernel)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits", "-lms", "50",
+                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.time(), line.strip()))
+
+    def mark(self, which):
+        if which == "start":
+            self.t0 = time.time()
+        else:
+            self.t1 = time.time()
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.reader.join(timeout=2)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        parsed = []
+        for t, line in self.rows:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 10:
+                continue
+            try:
+                parsed.append((t, float(f[2]), float(f[3]), f[4], f[5:]))
+            except ValueError:
+                continue
+        inside = [p for p in parsed if self.t0 and self.t1 and self.t0 - 0.06 <= p[0] <= self.t1 + 0.06]
+        use = inside or parsed[-3:]
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for p in use:
+            for n, v in zip(names[1:], p[4][1:]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(p[1] for p in use), "sm_max_mhz": max(p[2] for p in use),
+                "reasons": sorted(reasons), "samples": len(use), "in_region": bool(inside)}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (the oracle: test infrastructure, used here only as the baseline)
+# ---------------------------------------------------------------------------
+
+class CpuPath:
+    """The CPU restatement of the reference path (the oracle) on a sample of the
+    workload: the first few layers of the model with their cache rows
+    generated on the host, decode steps at the configuration's positions."""
+
+    def __init__(self, sp, max_steps, n_threads=0):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import numpy as np
+        import kv_oracle as O
+        from kv_b200 import synth
+        self.sp, self.O, self.synth = sp, O, synth
+        hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+        self.max_steps = max(1, min(max_steps, sp["steps"]))
+        n_ctx = sp["n_past"] + self.max_steps
+        per_layer_cache = 2 * n_ctx * hkv * d * 2
+        self.n_lay = max(1, min(sp["n_layer"], 4, int(2e9 // per_layer_cache)))
+        self.caches = []
+        for l in range(self.n_lay):
+            kc = np.zeros((n_ctx, hkv, d), np.uint16)
+            vc = np.zeros((n_ctx, hkv, d), np.uint16)
+            kc[:sp["n_past"]] = O.gen_cache_rows(sp["seed"], synth.STREAM_CACHE + 2 * l, 0, sp["n_past"], hkv, d)
+            vc[:sp["n_past"]] = O.gen_cache_rows(sp["seed"], synth.STREAM_CACHE + 2 * l + 1, 0, sp["n_past"],
+                                                 hkv, d)
+            self.caches.append((kc, vc))
+        self.orc = O.Oracle(sp)
+        self.threads = n_threads if n_threads > 0 else O.online_cores()
+        self.norms = [synth.norm_weights(sp, l) if sp["qk_norm"] else (None, None) for l in range(self.n_lay)]
+        self.inputs = [[synth.qkv_rows(sp, s, l, 1) for l in range(self.n_lay)] for s in range(self.max_steps)]
+
+    def step(self, s):
+        """One decode step over the sample layers; returns (seconds, bytes, layer-steps)."""
+        sp = self.sp
+        hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+        s %= self.max_steps
+        n_past = sp["n_past"] + s
+        t = 0.0
+        for l in range(self.n_lay):
+            rows = self.inputs[s][l]
+            q, k, v = rows[:, :hq * d], rows[:, hq * d:(hq + hkv) * d], rows[:, (hq + hkv) * d:]
+            kc, vc = self.caches[l]
+            t0 = time.perf_counter()
+            qr = self.orc.append(kc, vc, n_past, q, k, v, self.norms[l][0], self.norms[l][1])
+            self.orc.attend(kc, vc, n_past, qr, n_threads=self.threads)
+            t += time.perf_counter() - t0
+        return t, self.n_lay * layer_bytes(sp, n_past + 1), self.n_lay
+
+    def describe(self, steps):
+        sp = self.sp
+        return ("%d decode step(s) x first %d of %d layers at n_kv from %d, %d threads; per-token time "
+                "extrapolated linearly to all layers" % (steps, self.n_lay, sp["n_layer"], sp["n_past"] + 1,
+                                                       self.threads))
+
+
+def cpu_sample(sp, seconds, max_steps):
+    """(GB/s, us per token, description, threads) of the CPU path over about `seconds`."""
+    cp = CpuPath(sp, max_steps)
+    t_total, nbytes, nls, s = 0.0, 0, 0, 0
+    while s < cp.max_steps and (t_total < seconds or s == 0):
+        t, b, n = cp.step(s)
+        t_total += t
+        nbytes += b
+        nls += n
+        s += 1
+    return nbytes / t_total / 1e9, t_total / nls * sp["n_layer"] * 1e6, cp.describe(s), cp.threads
+
+
+def run_reference(args, sp):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cp = CpuPath(sp, args.warmup + args.steps)
+    t_total, nbytes, nls = 0.0, 0, 0
+    for i in range(args.warmup + args.steps):
+        t, b, n = cp.step(i)
+        if i >= args.warmup:
+            t_total += t
+            nbytes += b
+            nls += n
+    gbs = nbytes / t_total / 1e9
+    us = t_total / nls * sp["n_layer"] * 1e6
+    desc = cp.describe(1)
+    threads = cp.threads
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1000.0, 4),
+        "us_per_token": round(us, 1), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f16 cache, f32 math", "data": "synthetic (seeded generator, configuration shapes)",
+        "config": {"workload": sp["name"], "n_layer": sp["n_layer"], "n_head": sp["n_head"],
+                   "n_head_kv": sp["n_head_kv"], "head_dim": sp["head_dim"], "n_ctx": sp["n_ctx"],
+                   "n_past": sp["n_past"], "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": "each step: " + desc},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "CPU restatement of model.cpp:1382-1445 (ggml not vendored, reference backend unbuildable)",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# the GPU arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, sp):
+    import numpy as np
+    import torch
+    import kv_b200 as K
+    from kv_b200 import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        log("note: --gpus %d but WORLD_SIZE %d; using WORLD_SIZE" % (args.gpus, world))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    if sp["n_head_kv"] % world:
+        raise SystemExit("n_head_kv %d does not shard over %d GPUs" % (sp["n_head_kv"], world))
+
+    comm_id = None
+    if world > 1:
+        buf = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            buf.copy_(torch.tensor(list(K.comm_unique_id()), dtype=torch.uint8))
+        dist.broadcast(buf, 0)
+        comm_id = bytes(buf.cpu().tolist())
+
+    n_new = sp["n_new"]
+    L, hq, hkv, d = sp["n_layer"], sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+    W = (hq + 2 * hkv) * d
+    cfg = K.make_config(sp, n_ctx=sp["n_ctx"], n_batch_max=max(16, n_new), device=local, n_shards=world,
+                        shard=rank, comm_id=comm_id)
+    ctx = K.Context(cfg)
+    stream = torch.cuda.current_stream()
+    t0 = time.time()
+    ctx.fill_synthetic(sp["seed"], 0, sp["n_past"], stream=stream)
+    cyc = max(1, sp["steps"])
+    inputs = torch.empty((cyc, L, n_new, W), dtype=torch.float32, device=dev)
+    for s in range(cyc):
+        for l in range(L):
+            K.gen_normal_device(inputs[s, l], sp["seed"], synth.STREAM_QKV + s * 1024 + l, n_new * W, stream=stream)
+    qn = kn = None
+    if sp["qk_norm"]:
+        ws = [synth.norm_weights(sp, l) for l in range(L)]
+        qn = torch.from_numpy(np.stack([w[0] for w in ws])).to(dev)
+        kn = torch.from_numpy(np.stack([w[1] for w in ws])).to(dev)
+    out = torch.empty((L, n_new, hq * d), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+    log("rank %d: cache %.2f GiB filled, inputs ready in %.1f s" % (
+        rank, K.cache_bytes(cfg, sp["n_ctx"]) / world / 2 ** 30, time.time() - t0))
+
+    def step(s, src=None):
+        base = (src if src is not None else inputs[s % cyc]).data_ptr()
+        n_past = sp["n_past"] + (s % cyc)
+        ctx.forward(n_past, n_new, base, W, base + 4 * hq * d, W, base + 4 * (hq + hkv) * d, W, n_new * W,
+                    qn, kn, d, out, n_new * hq * d, stream=stream)
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # warm-up
+    for s in range(args.warmup):
+        step(s)
+    barrier()
+
+    # timed region (the clock sampler runs on rank 0 for its own GPU)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    smi_index = vis.split(",")[local].strip() if vis else str(local)
+    sampler = ClockSampler(smi_index)
+    if rank == 0:
+        sampler.start()
+    lead = 100   # untimed steps on every rank while the sampler starts
+    for s in range(args.warmup, args.warmup + lead):
+        step(s)
+    barrier()
+    first = args.warmup + lead
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ctx.launch_count()
+    barrier()
+    sampler.mark("start")
+    e0.record(stream)
+    for i in range(args.steps):
+        step(first + i)
+    e1.record(stream)
+    e1.synchronize()
+    sampler.mark("end")
+    launches = ctx.launch_count() - launches0
+    ms = e0.elapsed_time(e1)
+    barrier()
+    if rank == 0:
+        sampler.stop()
+    ms = max_over_ranks(ms)
+    pos = positions(sp, first, args.steps)
+    total_bytes = sum(step_bytes(sp, p, n_new) for p in pos)
+    value = total_bytes / (ms / 1e3) / 1e9
+    ms_step = ms / args.steps
+
+    # per-kernel durations (separate pass, CUDA events around each launch)
+    prof_steps = min(args.steps, 32)
+    ctx.profile(True)
+    ctx.profile_reset()
+    pfirst = first + args.steps
+    for i in range(prof_steps):
+        step(pfirst + i)
+    torch.cuda.synchronize()
+    kern = {}
+    for name in ("append", "scores", "pv", "gather"):
+        n, tms = ctx.profile_read(name)
+        kern[name] = (n, tms)
+    ctx.profile(False)
+    ppos = positions(sp, pfirst, prof_steps)
+    mean_nkv = statistics.mean(p + n_new for p in ppos)
+    hkv_l, hq_l = hkv // world, hq // world
+    algo = {
+        "scores": mean_nkv * hkv_l * d * 2,
+        "pv": mean_nkv * hkv_l * d * 2 + n_new * hq_l * d * 4,
+        "append": n_new * (hkv_l * d * (4 * 2 + 2 * 2) + hq_l * d * 4),
+    }
+    dom = max(("scores", "pv"), key=lambda k: kern[k][1])
+    n_dom, t_dom = kern[dom]
+    peak, peak_kind = measured_peak()
+    achieved = algo[dom] / (t_dom / n_dom / 1e3) / 1e9 if n_dom else None
+    kernel_table = {k: {"launches": v[0], "total_ms": round(v[1], 4),
+                        "avg_us": round(v[1] / v[0] * 1e3, 3) if v[0] else None} for k, v in kern.items()}
+
+    # end to end through the C ABI with host buffers: H2D inputs, D2H outputs, every step
+    host_in = torch.empty((cyc, L, n_new, W), dtype=torch.float32, pin_memory=True)
+    host_in.copy_(inputs.cpu())
+    host_out = torch.empty((L, n_new, hq * d), dtype=torch.float32, pin_memory=True)
+    staging = torch.empty((L, n_new, W), dtype=torch.float32, device=dev)
+    e2e_steps = args.steps
+    efirst = pfirst + prof_steps
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for i in range(e2e_steps):
+        s = efirst + i
+        staging.copy_(host_in[s % cyc], non_blocking=True)
+        step(s, src=staging)
+        host_out.copy_(out, non_blocking=True)
+        stream.synchronize()
+    f1.record(stream)
+    f1.synchronize()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+    epos = positions(sp, efirst, e2e_steps)
+    e2e_value = sum(step_bytes(sp, p, n_new) for p in epos) / (e2e_ms / 1e3) / 1e9
+    h2d = L * n_new * W * 4
+    d2h = L * n_new * hq * d * 4
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        gbs, us, desc, threads = cpu_sample(sp, args.cpu_seconds, 64)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc,
+               "us_per_token": round(us, 1)}
+
+    clocks = sampler.summary() if rank == 0 else None
+    barrier()
+    if rank == 0:
+        us_tok = ms_step * 1e3
+        ideal_us = statistics.mean(step_bytes(sp, p, n_new) for p in pos) / (peak * world * 1e9) * 1e6
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "us_per_token": round(us_tok, 2),
+            "pct_of_roofline": round(100.0 * value / (peak * world), 2),
+            "pct_of_nominal_8tbs": round(100.0 * value / (NOMINAL_HBM_GBS * world), 2),
+            "ideal_us_per_token": round(ideal_us, 2),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16 cache, f32 math",
+            "data": "synthetic (seeded splitmix64/Irwin-Hall generator, configuration shapes; no weights)",
+            "config": {"workload": sp["name"], "n_layer": L, "n_head": hq, "n_head_kv": hkv, "head_dim": d,
+                       "n_ctx": sp["n_ctx"], "n_past": sp["n_past"], "n_new": n_new,
+                       "positions": "n_past + (step mod %d)" % cyc, "global_batch": 1,
+                       "parallelism": ("kv-head shards x%d + per-layer all-gather" % world) if world > 1
+                       else "single GPU",
+                       "l2": "no flush: each step reads %.2f GB of cache (> 126 MB L2)" % (
+                           statistics.mean(step_bytes(sp, p, n_new) for p in pos) / 1e9)},
+            "roofline": {"bound": "hbm", "kernel": "kv_" + dom, "achieved": round(achieved, 1) if achieved else None,
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
+                         "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": int(algo[dom]),
+                         "traffic": committed_traffic(sp["name"], "kv_" + dom),
+                         "kernels": kernel_table},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "us_per_token": round(e2e_ms / e2e_steps * 1e3, 2),
+                    "note": "pinned host inputs copied in and outputs copied out every step, host sync per step"},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[1])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default=DEFAULT_CONFIG)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    from kv_b200 import specs
+    sp = specs.get(args.config)
+    if args.steps is None:
+        args.steps = sp["steps"]
+    if args.warmup < 3:
+        log("note: raising --warmup to 3")
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args, sp)
+    return run_ours(args, sp)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

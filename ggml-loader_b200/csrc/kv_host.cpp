@@ -1,0 +1,811 @@
+// kv_host.cpp -- host side of the KV path library: the C ABI of include/kv_api.h
+// and include/kv_bench.h.
+//
+// Owns the per-context device memory (cache, RoPE table, scratch), the context
+// sizing rule, argument checking and the kernel launch sequence of one layer:
+//   kv_append -> append kernel
+//   kv_attend -> scores kernel + P.V kernel (per group of query rows)
+//                [+ NCCL all-gather of the head outputs when sharded]
+// Compiled with -ffp-contract=off: the RoPE table is compared bit-for-bit with
+// the CPU path, whose products and sums are separately rounded.
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "kv_api.h"
+#include "kv_bench.h"
+#include "kv_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what)
+{
+    return fail(KV_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define KV_CUDA(call)                                     \
+    do {                                                  \
+        cudaError_t e_ = (call);                          \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+    } while (0)
+
+// ---------------------------------------------------------------------------
+// NCCL, loaded at run time so single-GPU use needs no NCCL at all
+// ---------------------------------------------------------------------------
+struct NcclId {
+    char internal[128];
+};
+typedef struct ncclComm *ncclComm_t;
+constexpr int kNcclFloat32 = 7;
+
+struct NcclApi {
+    bool tried = false;
+    void *h = nullptr;
+    int (*GetUniqueId)(NcclId *) = nullptr;
+    int (*CommInitRank)(ncclComm_t *, int, NcclId, int) = nullptr;
+    int (*AllGather)(const void *, void *, size_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    int (*CommDestroy)(ncclComm_t) = nullptr;
+    const char *(*GetErrorString)(int) = nullptr;
+};
+
+NcclApi &nccl()
+{
+    static NcclApi api;
+    if (!api.tried) {
+        api.tried = true;
+        api.h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!api.h) api.h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (api.h) {
+            api.GetUniqueId = (int (*)(NcclId *))dlsym(api.h, "ncclGetUniqueId");
+            api.CommInitRank = (int (*)(ncclComm_t *, int, NcclId, int))dlsym(api.h, "ncclCommInitRank");
+            api.AllGather = (int (*)(const void *, void *, size_t, int, ncclComm_t, cudaStream_t))dlsym(
+                api.h, "ncclAllGather");
+            api.CommDestroy = (int (*)(ncclComm_t))dlsym(api.h, "ncclCommDestroy");
+            api.GetErrorString = (const char *(*)(int))dlsym(api.h, "ncclGetErrorString");
+            if (!api.GetUniqueId || !api.CommInitRank || !api.AllGather || !api.CommDestroy) {
+                api.GetUniqueId = nullptr;
+            }
+        }
+    }
+    return api;
+}
+
+// ---------------------------------------------------------------------------
+// RoPE table: (cos, sin) per (position, pair), the ggml_rope_ext angle schedule
+// (model.cpp:1396-1403 with the parameters of model.cpp:1312-1316)
+// ---------------------------------------------------------------------------
+float yarn_dim(int n_dims, int n_ctx_orig, float n_turns, float base)
+{
+    const float two_pi = 2.0f * (float)M_PI;
+    return (float)n_dims * logf((float)n_ctx_orig / (n_turns * two_pi)) / (2.0f * logf(base));
+}
+
+struct RopeSpec {
+    int n_rot;
+    float base, freq_scale, attn_factor, ext_factor, beta_fast, beta_slow;
+    int n_ctx_orig;
+    const float *ff;  // [n_rot/2] or null
+};
+
+void rope_rows(const RopeSpec &r, int64_t p0, int64_t p1, float *out)
+{
+    const int half = r.n_rot / 2;
+    const float step = powf(r.base, -2.0f / (float)r.n_rot);
+    float lo = 0.0f, hi = 0.0f;
+    if (r.ext_factor != 0.0f) {
+        const float a = floorf(yarn_dim(r.n_rot, r.n_ctx_orig, r.beta_fast, r.base));
+        const float b = ceilf(yarn_dim(r.n_rot, r.n_ctx_orig, r.beta_slow, r.base));
+        lo = a > 0.0f ? a : 0.0f;
+        hi = b < (float)(r.n_rot - 1) ? b : (float)(r.n_rot - 1);
+    }
+    for (int64_t p = p0; p < p1; p++) {
+        float theta = (float)p;
+        float *row = out + (size_t)(p - p0) * (size_t)half * 2u;
+        for (int i = 0; i < half; i++) {
+            const float f = r.ff ? r.ff[i] : 1.0f;
+            const float t_ext = theta / f;
+            const float t_int = r.freq_scale * t_ext;
+            float t = t_int;
+            float ms = r.attn_factor;
+            if (r.ext_factor != 0.0f) {
+                const float den = (hi - lo) > 0.001f ? (hi - lo) : 0.001f;
+                float y = ((float)i - lo) / den;  // pair index == i0/2
+                y = y < 0.0f ? 0.0f : (y > 1.0f ? 1.0f : y);
+                const float mix = (1.0f - y) * r.ext_factor;
+                t = t_int * (1.0f - mix) + t_ext * mix;
+                ms *= 1.0f + 0.1f * logf(1.0f / r.freq_scale);
+            }
+            row[2 * i + 0] = cosf(t) * ms;
+            row[2 * i + 1] = sinf(t) * ms;
+            theta *= step;
+        }
+    }
+}
+
+void build_rope_table(const RopeSpec &r, int64_t n_pos, float *out)
+{
+    const int64_t half = r.n_rot / 2;
+    unsigned nt = std::thread::hardware_concurrency();
+    if (nt == 0) nt = 1;
+    if (nt > 32) nt = 32;
+    if (n_pos < 4096) nt = 1;
+    const int64_t chunk = (n_pos + nt - 1) / nt;
+    std::vector<std::thread> th;
+    for (unsigned w = 0; w < nt; w++) {
+        const int64_t a = (int64_t)w * chunk, b = std::min(n_pos, a + chunk);
+        if (a >= b) break;
+        th.emplace_back([&r, a, b, out, half] { rope_rows(r, a, b, out + (size_t)a * (size_t)half * 2u); });
+    }
+    for (auto &t : th) t.join();
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// the context
+// ---------------------------------------------------------------------------
+struct kv_ctx {
+    kv_config cfg{};
+    std::vector<float> freq_factors;
+    int device = 0;
+    int sm_count = 148;
+    int64_t n_ctx = 0;
+    int D = 0, hq_loc = 0, hkv_loc = 0, r = 1, hq0 = 0, hkv0 = 0;
+    int rmax = 0, split_max = 0, max_splits = 0;
+    float scale = 1.0f;
+
+    __half *cache = nullptr;  // [n_layer][2][n_ctx][hkv_loc][D]
+    int64_t layer_elems = 0;  // n_ctx * hkv_loc * D
+    float2 *rope = nullptr;   // [n_ctx][n_rot/2]
+    __half *qbuf = nullptr;   // [n_batch_max][hq_loc][D]
+    float *S = nullptr;
+    int64_t S_stride = 0;
+    float *part_m = nullptr;
+    double *part_z = nullptr;
+    float *part_o = nullptr;
+    unsigned *counters = nullptr;
+    float *local_out = nullptr;   // sharded prefill: [n_batch_max][hq_loc*D]
+    float *gathered = nullptr;    // [n_shards][n_batch_max][hq_loc*D]
+
+    // state of the last kv_append (kv_attend must follow it)
+    int last_layer = -1;
+    int64_t last_n_past = -1;
+    int last_n_new = 0;
+
+    ncclComm_t comm = nullptr;
+
+    std::atomic<int64_t> launches{0};
+    bool prof_on = false;
+    struct Rec {
+        int k;
+        cudaEvent_t a, b;
+    };
+    std::vector<Rec> recs;
+    std::vector<cudaEvent_t> ev_pool;
+
+    __half *k_layer(int l) const { return cache + (int64_t)l * 2 * layer_elems; }
+    __half *v_layer(int l) const { return cache + ((int64_t)l * 2 + 1) * layer_elems; }
+};
+
+namespace {
+
+bool shape_ok(const kv_config *c, std::string &why)
+{
+    char buf[256];
+    if (c->n_layer <= 0 || c->n_head <= 0 || c->n_head_kv <= 0) { why = "n_layer, n_head and n_head_kv must be > 0"; return false; }
+    if (c->head_dim != 64 && c->head_dim != 96 && c->head_dim != 128) {
+        snprintf(buf, sizeof(buf), "head_dim %d unsupported (64, 96, 128)", c->head_dim);
+        why = buf;
+        return false;
+    }
+    if (c->n_head % c->n_head_kv != 0) { why = "n_head must be a multiple of n_head_kv"; return false; }
+    if (c->n_rot < 0 || c->n_rot > c->head_dim || (c->n_rot & 1)) { why = "n_rot must be even and <= head_dim"; return false; }
+    if (c->rope_mode != KV_ROPE_NORMAL && c->rope_mode != KV_ROPE_NEOX) { why = "rope_mode must be 0 (NORMAL) or 2 (NEOX)"; return false; }
+    if (c->n_rot > 0 && !(c->rope_base > 0.0f)) { why = "rope_base must be > 0"; return false; }
+    if (c->rope_ext_factor != 0.0f && c->n_ctx_orig <= 0) { why = "YaRN (ext_factor != 0) needs n_ctx_orig > 0"; return false; }
+    const int ns = c->n_shards <= 1 ? 1 : c->n_shards;
+    if (c->n_head_kv % ns != 0) { why = "n_head_kv must be a multiple of n_shards"; return false; }
+    if (ns > 1 && (c->shard < 0 || c->shard >= ns)) { why = "shard out of range"; return false; }
+    if (c->n_batch_max < 0) { why = "n_batch_max must be >= 0"; return false; }
+    return true;
+}
+
+uint64_t per_position_bytes(const kv_config *c)
+{
+    const int ns = c->n_shards <= 1 ? 1 : c->n_shards;
+    const uint64_t cache = (uint64_t)c->n_layer * (uint64_t)(c->n_head_kv / ns) * (uint64_t)c->head_dim * 2u * 2u;
+    const uint64_t rope = (uint64_t)(c->n_rot / 2) * sizeof(float2);
+    return cache + rope;
+}
+
+cudaStream_t to_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int ensure_device(const kv_ctx *ctx)
+{
+    int cur = -1;
+    KV_CUDA(cudaGetDevice(&cur));
+    if (cur != ctx->device) KV_CUDA(cudaSetDevice(ctx->device));
+    return KV_OK;
+}
+
+cudaEvent_t pool_event(kv_ctx *ctx)
+{
+    if (!ctx->ev_pool.empty()) {
+        cudaEvent_t e = ctx->ev_pool.back();
+        ctx->ev_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+// Wraps one kernel launch: counts it and, when profiling, brackets it with events.
+template <class F>
+int launch(kv_ctx *ctx, int kernel_id, cudaStream_t st, const char *what, F &&fn)
+{
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (ctx->prof_on) {
+        a = pool_event(ctx);
+        b = pool_event(ctx);
+        cudaEventRecord(a, st);
+    }
+    cudaError_t e = fn();
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    ctx->launches.fetch_add(1, std::memory_order_relaxed);
+    if (ctx->prof_on) {
+        cudaEventRecord(b, st);
+        ctx->recs.push_back({kernel_id, a, b});
+    }
+    return KV_OK;
+}
+
+void choose_splits(const kv_ctx *ctx, int64_t n_kv, int *split_len, int *n_splits)
+{
+    const int target = std::max(1, (2 * ctx->sm_count + ctx->hkv_loc - 1) / ctx->hkv_loc);
+    int64_t len = (n_kv + target - 1) / target;
+    len = ((len + 63) / 64) * 64;
+    if (len < 64) len = 64;
+    if (len > ctx->split_max) len = ctx->split_max;
+    *split_len = (int)len;
+    *n_splits = (int)((n_kv + len - 1) / len);
+}
+
+void free_all(kv_ctx *ctx)
+{
+    for (auto &r : ctx->recs) {
+        cudaEventDestroy(r.a);
+        cudaEventDestroy(r.b);
+    }
+    for (auto e : ctx->ev_pool) cudaEventDestroy(e);
+    ctx->recs.clear();
+    ctx->ev_pool.clear();
+    if (ctx->comm && nccl().CommDestroy) nccl().CommDestroy(ctx->comm);
+    ctx->comm = nullptr;
+    void *ptrs[] = {ctx->cache, ctx->rope, ctx->qbuf, ctx->S, ctx->part_m, ctx->part_z,
+                    ctx->part_o, ctx->counters, ctx->local_out, ctx->gathered};
+    for (void *p : ptrs)
+        if (p) cudaFree(p);
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int kv_config_init(kv_config *cfg)
+{
+    if (!cfg) return fail(KV_E_ARG, "cfg is NULL");
+    std::memset(cfg, 0, sizeof(*cfg));
+    cfg->rope_mode = KV_ROPE_NEOX;
+    cfg->rope_base = 10000.0f;
+    cfg->rope_freq_scale = 1.0f;
+    cfg->rope_attn_factor = 1.0f;
+    cfg->rms_eps = 1e-6f;
+    cfg->n_batch_max = 512;
+    cfg->device = -1;
+    cfg->n_shards = 1;
+    return KV_OK;
+}
+
+uint64_t kv_cache_bytes(const kv_config *cfg, int64_t n_ctx)
+{
+    if (!cfg || n_ctx < 0) return 0;
+    const uint64_t per_token = (uint64_t)cfg->n_layer * (uint64_t)cfg->head_dim * (uint64_t)cfg->n_head_kv * 2u * 2u;
+    return per_token * (uint64_t)n_ctx;
+}
+
+int64_t kv_auto_n_ctx(const kv_config *cfg, int64_t free_bytes)
+{
+    if (!cfg) return 0;
+    if (free_bytes <= 0) return 4096;  // N_CTX_DEFAULT (model.h:43)
+    const uint64_t reserve = (uint64_t)384 << 20;
+    uint64_t budget = (uint64_t)free_bytes;
+    budget -= std::min(budget, reserve);
+    budget = (uint64_t)((double)budget * 0.8);
+    const uint64_t per_tok = per_position_bytes(cfg);
+    const int64_t raw = per_tok > 0 ? (int64_t)(budget / per_tok) : 4096;
+    int64_t n_ctx = (raw / 64) * 64;
+    int64_t limit = cfg->n_ctx_train > 0 ? cfg->n_ctx_train : 262144;
+    if (cfg->longrope_clamp && cfg->n_ctx_orig > 0) limit = std::min<int64_t>(limit, cfg->n_ctx_orig);
+    if (n_ctx > limit) n_ctx = limit;
+    if (n_ctx < 512) n_ctx = std::min<int64_t>(512, limit);
+    return n_ctx;
+}
+
+int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
+{
+    if (!cfg_in || !out) return fail(KV_E_ARG, "NULL argument");
+    *out = nullptr;
+    std::string why;
+    if (!shape_ok(cfg_in, why)) return fail(KV_E_ARG, "kv_alloc: %s", why.c_str());
+
+    kv_ctx *ctx = new kv_ctx();
+    ctx->cfg = *cfg_in;
+    kv_config &c = ctx->cfg;
+    if (c.n_shards <= 1) { c.n_shards = 1; c.shard = 0; }
+    if (c.n_batch_max == 0) c.n_batch_max = 512;
+    if (c.rope_freq_factors && c.n_rot > 0) {
+        ctx->freq_factors.assign(c.rope_freq_factors, c.rope_freq_factors + c.n_rot / 2);
+        c.rope_freq_factors = ctx->freq_factors.data();
+    } else {
+        c.rope_freq_factors = nullptr;
+    }
+    c.comm_id = nullptr;
+
+    auto bail = [&](int code) {
+        free_all(ctx);
+        delete ctx;
+        return code;
+    };
+    cudaError_t e;
+    if (c.device >= 0) {
+        e = cudaSetDevice(c.device);
+        if (e != cudaSuccess) return bail(cuda_fail(e, "cudaSetDevice"));
+    }
+    e = cudaGetDevice(&ctx->device);
+    if (e != cudaSuccess) return bail(cuda_fail(e, "cudaGetDevice"));
+    e = cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, ctx->device);
+    if (e != cudaSuccess) return bail(cuda_fail(e, "cudaDeviceGetAttribute"));
+
+    ctx->D = c.head_dim;
+    ctx->hkv_loc = c.n_head_kv / c.n_shards;
+    ctx->r = c.n_head / c.n_head_kv;
+    ctx->hq_loc = ctx->hkv_loc * ctx->r;
+    ctx->hkv0 = c.shard * ctx->hkv_loc;
+    ctx->hq0 = c.shard * ctx->hq_loc;
+    ctx->rmax = kvb::decode_rmax(ctx->D);
+    ctx->split_max = kvb::decode_split_max(ctx->D);
+    ctx->scale = 1.0f / sqrtf((float)ctx->D);
+
+    if (c.n_ctx <= 0) {
+        size_t fr = 0, tot = 0;
+        e = cudaMemGetInfo(&fr, &tot);
+        ctx->n_ctx = kv_auto_n_ctx(&c, e == cudaSuccess ? (int64_t)fr : -1);
+        fprintf(stderr,
+                "n_ctx=auto: free HBM %.0f MiB, reserve 384 MiB, %.1f KiB per position -> n_ctx=%lld\n",
+                (double)fr / (1024.0 * 1024.0), (double)per_position_bytes(&c) / 1024.0, (long long)ctx->n_ctx);
+    } else {
+        ctx->n_ctx = c.n_ctx;
+    }
+    c.n_ctx = ctx->n_ctx;
+    if (c.n_batch_max > ctx->n_ctx) c.n_batch_max = (int32_t)ctx->n_ctx;
+
+    const int64_t D = ctx->D;
+    ctx->layer_elems = ctx->n_ctx * ctx->hkv_loc * D;
+    const size_t cache_bytes = (size_t)c.n_layer * 2u * (size_t)ctx->layer_elems * sizeof(__half);
+    e = cudaMalloc(&ctx->cache, cache_bytes);
+    if (e != cudaSuccess) {
+        return bail(fail(KV_E_OOM, "failed to allocate KV cache (%lld positions x %d layers, %.0f MiB requested): %s",
+                         (long long)ctx->n_ctx, c.n_layer, (double)cache_bytes / (1024.0 * 1024.0),
+                         cudaGetErrorString(e)));
+    }
+    cudaGetLastError();
+
+    const int half = c.n_rot / 2;
+    if (half > 0) {
+        std::vector<float> table((size_t)ctx->n_ctx * (size_t)half * 2u);
+        RopeSpec rs{c.n_rot, c.rope_base, c.rope_freq_scale, c.rope_attn_factor, c.rope_ext_factor,
+                    c.rope_beta_fast, c.rope_beta_slow, c.n_ctx_orig, c.rope_freq_factors};
+        build_rope_table(rs, ctx->n_ctx, table.data());
+        e = cudaMalloc(&ctx->rope, table.size() * sizeof(float));
+        if (e != cudaSuccess) return bail(fail(KV_E_OOM, "RoPE table allocation: %s", cudaGetErrorString(e)));
+        e = cudaMemcpy(ctx->rope, table.data(), table.size() * sizeof(float), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return bail(cuda_fail(e, "RoPE table upload"));
+    }
+
+    ctx->S_stride = ((ctx->n_ctx + 3) / 4) * 4;
+    const int target = std::max(1, (2 * ctx->sm_count + ctx->hkv_loc - 1) / ctx->hkv_loc);
+    ctx->max_splits = (int)std::max<int64_t>(target, (ctx->n_ctx + ctx->split_max - 1) / ctx->split_max);
+    const size_t n_part = (size_t)ctx->hkv_loc * (size_t)ctx->max_splits * (size_t)ctx->rmax;
+    struct { void **p; size_t bytes; } allocs[] = {
+        {(void **)&ctx->qbuf, (size_t)c.n_batch_max * ctx->hq_loc * D * sizeof(__half)},
+        {(void **)&ctx->S, (size_t)ctx->hkv_loc * ctx->rmax * (size_t)ctx->S_stride * sizeof(float)},
+        {(void **)&ctx->part_m, n_part * sizeof(float)},
+        {(void **)&ctx->part_z, n_part * sizeof(double)},
+        {(void **)&ctx->part_o, n_part * (size_t)D * sizeof(float)},
+        {(void **)&ctx->counters, (size_t)ctx->hkv_loc * sizeof(unsigned)},
+    };
+    for (auto &a : allocs) {
+        e = cudaMalloc(a.p, a.bytes);
+        if (e != cudaSuccess) return bail(fail(KV_E_OOM, "scratch allocation (%zu bytes): %s", a.bytes, cudaGetErrorString(e)));
+    }
+    e = cudaMemset(ctx->counters, 0, (size_t)ctx->hkv_loc * sizeof(unsigned));
+    if (e != cudaSuccess) return bail(cuda_fail(e, "cudaMemset"));
+    e = kvb::decode_prepare(ctx->D);
+    if (e != cudaSuccess) return bail(cuda_fail(e, "decode_prepare"));
+
+    if (c.n_shards > 1) {
+        if (!cfg_in->comm_id) return bail(fail(KV_E_ARG, "n_shards > 1 needs comm_id"));
+        NcclApi &api = nccl();
+        if (!api.GetUniqueId) return bail(fail(KV_E_UNSUPPORTED, "libnccl.so.2 could not be loaded"));
+        const size_t cols = (size_t)ctx->hq_loc * D;
+        e = cudaMalloc(&ctx->local_out, (size_t)c.n_batch_max * cols * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&ctx->gathered, (size_t)c.n_shards * c.n_batch_max * cols * sizeof(float));
+        if (e != cudaSuccess) return bail(fail(KV_E_OOM, "gather buffers: %s", cudaGetErrorString(e)));
+        NcclId id;
+        std::memcpy(id.internal, cfg_in->comm_id, sizeof(id.internal));
+        const int rc = api.CommInitRank(&ctx->comm, c.n_shards, id, c.shard);
+        if (rc != 0) {
+            ctx->comm = nullptr;
+            return bail(fail(KV_E_COMM, "ncclCommInitRank: %s", api.GetErrorString ? api.GetErrorString(rc) : "error"));
+        }
+    }
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return bail(cuda_fail(e, "kv_alloc sync"));
+    *out = ctx;
+    return KV_OK;
+}
+
+int kv_free(kv_ctx *ctx)
+{
+    if (!ctx) return KV_OK;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != ctx->device) cudaSetDevice(ctx->device);
+    cudaDeviceSynchronize();
+    const int dev = ctx->device;
+    free_all(ctx);
+    delete ctx;
+    if (cur >= 0 && cur != dev) cudaSetDevice(cur);
+    return KV_OK;
+}
+
+int kv_n_ctx(const kv_ctx *ctx, int64_t *n_ctx)
+{
+    if (!ctx || !n_ctx) return fail(KV_E_ARG, "NULL argument");
+    *n_ctx = ctx->n_ctx;
+    return KV_OK;
+}
+
+int kv_shard_info(const kv_ctx *ctx, int32_t *q_head0, int32_t *n_q_heads, int32_t *kv_head0, int32_t *n_kv_heads)
+{
+    if (!ctx) return fail(KV_E_ARG, "NULL context");
+    if (q_head0) *q_head0 = ctx->hq0;
+    if (n_q_heads) *n_q_heads = ctx->hq_loc;
+    if (kv_head0) *kv_head0 = ctx->hkv0;
+    if (n_kv_heads) *n_kv_heads = ctx->hkv_loc;
+    return KV_OK;
+}
+
+int kv_append(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
+              const float *q, int64_t q_stride, const float *k, int64_t k_stride,
+              const float *v, int64_t v_stride, const float *q_norm_w, const float *k_norm_w,
+              void *stream)
+{
+    if (!ctx) return fail(KV_E_ARG, "NULL context");
+    const kv_config &c = ctx->cfg;
+    if (layer < 0 || layer >= c.n_layer) return fail(KV_E_ARG, "layer %d out of range", layer);
+    if (n_new <= 0 || n_past < 0) return fail(KV_E_ARG, "n_new must be > 0 and n_past >= 0");
+    if (n_new > c.n_batch_max) return fail(KV_E_RANGE, "n_new %d exceeds n_batch_max %d", n_new, c.n_batch_max);
+    if (n_past + n_new > ctx->n_ctx)
+        return fail(KV_E_RANGE, "rows [%lld, %lld) exceed n_ctx %lld", (long long)n_past,
+                    (long long)(n_past + n_new), (long long)ctx->n_ctx);
+    if (!q || !k || !v) return fail(KV_E_ARG, "q, k and v are required");
+    const int64_t D = ctx->D;
+    if (n_new > 1 && (q_stride < c.n_head * D || k_stride < c.n_head_kv * D || v_stride < c.n_head_kv * D))
+        return fail(KV_E_ARG, "row strides shorter than a token's heads");
+    if (c.qk_norm && (!q_norm_w || !k_norm_w)) return fail(KV_E_ARG, "qk_norm needs q_norm_w and k_norm_w");
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+
+    kvb::AppendParams p;
+    p.q = q; p.k = k; p.v = v;
+    p.q_stride = q_stride; p.k_stride = k_stride; p.v_stride = v_stride;
+    p.q_norm_w = q_norm_w; p.k_norm_w = k_norm_w;
+    p.n_new = n_new; p.n_past = n_past;
+    p.hq_loc = ctx->hq_loc; p.hkv_loc = ctx->hkv_loc; p.hq0 = ctx->hq0; p.hkv0 = ctx->hkv0;
+    p.n_rot = c.n_rot; p.rope_mode = c.rope_mode; p.qk_norm = c.qk_norm; p.eps = c.rms_eps;
+    p.rope = ctx->rope;
+    p.kc = ctx->k_layer(layer); p.vc = ctx->v_layer(layer);
+    p.qbuf = ctx->qbuf;
+    auto al16 = [](const void *x) { return ((uintptr_t)x & 15u) == 0; };
+    const bool vec = al16(q) && al16(k) && al16(v) && (n_new == 1 || ((q_stride | k_stride | v_stride) & 3) == 0);
+    rc = launch(ctx, KV_K_APPEND, to_stream(stream), "append kernel",
+                [&] { return kvb::launch_append(ctx->D, vec, p, to_stream(stream)); });
+    if (rc) return rc;
+    ctx->last_layer = layer;
+    ctx->last_n_past = n_past;
+    ctx->last_n_new = n_new;
+    return KV_OK;
+}
+
+int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *out, void *stream)
+{
+    if (!ctx) return fail(KV_E_ARG, "NULL context");
+    if (!out) return fail(KV_E_ARG, "out is NULL");
+    if (layer != ctx->last_layer || n_past != ctx->last_n_past || n_new != ctx->last_n_new)
+        return fail(KV_E_STATE, "kv_attend(layer %d, n_past %lld, n_new %d) does not follow kv_append of the same rows",
+                    layer, (long long)n_past, n_new);
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+    const kv_config &c = ctx->cfg;
+    const cudaStream_t st = to_stream(stream);
+    const int64_t D = ctx->D;
+    const int64_t n_kv = n_past + n_new;
+    const bool sharded = c.n_shards > 1;
+    const bool direct = !sharded || n_new == 1;
+    float *dst = direct ? out : ctx->local_out;
+    const int64_t dst_stride = direct ? (int64_t)c.n_head * D : (int64_t)ctx->hq_loc * D;
+    const int dst_head0 = direct ? ctx->hq0 : 0;
+
+    int split_len = 0, n_splits = 0;
+    choose_splits(ctx, n_kv, &split_len, &n_splits);
+    if (n_splits > ctx->max_splits) return fail(KV_E_RANGE, "internal: %d splits > %d", n_splits, ctx->max_splits);
+
+    const int rows = n_new * ctx->r;
+    for (int row0 = 0; row0 < rows; row0 += ctx->rmax) {
+        const int nrows = std::min(ctx->rmax, rows - row0);
+        kvb::ScoresParams sp;
+        sp.kc = ctx->k_layer(layer);
+        sp.row_elems = (int32_t)(ctx->hkv_loc * D);
+        sp.qbuf = ctx->qbuf;
+        sp.hq_loc = ctx->hq_loc; sp.r = ctx->r;
+        sp.row0 = row0; sp.nrows = nrows;
+        sp.n_past = n_past; sp.n_kv = n_kv;
+        sp.split_len = split_len; sp.n_splits = n_splits;
+        sp.scale = ctx->scale;
+        sp.S = ctx->S; sp.S_stride = ctx->S_stride;
+        sp.part_m = ctx->part_m; sp.part_z = ctx->part_z;
+        rc = launch(ctx, KV_K_SCORES, st, "scores kernel",
+                    [&] { return kvb::launch_scores(ctx->D, sp, ctx->hkv_loc, st); });
+        if (rc) return rc;
+        kvb::PVParams pp;
+        pp.vc = ctx->v_layer(layer);
+        pp.row_elems = sp.row_elems;
+        pp.S = ctx->S; pp.S_stride = ctx->S_stride;
+        pp.part_m = ctx->part_m; pp.part_z = ctx->part_z; pp.part_o = ctx->part_o;
+        pp.counters = ctx->counters;
+        pp.r = ctx->r; pp.row0 = row0; pp.nrows = nrows;
+        pp.n_past = n_past; pp.n_kv = n_kv;
+        pp.split_len = split_len; pp.n_splits = n_splits;
+        pp.out = dst; pp.out_stride = dst_stride; pp.out_head0 = dst_head0;
+        rc = launch(ctx, KV_K_PV, st, "P.V kernel", [&] { return kvb::launch_pv(ctx->D, pp, ctx->hkv_loc, st); });
+        if (rc) return rc;
+    }
+
+    if (sharded) {
+        NcclApi &api = nccl();
+        const size_t cols = (size_t)ctx->hq_loc * D;
+        int nr;
+        if (direct) {
+            // in place: this shard's heads already sit at out + shard*cols
+            nr = api.AllGather(out + (size_t)c.shard * cols, out, cols, kNcclFloat32, ctx->comm, st);
+        } else {
+            nr = api.AllGather(ctx->local_out, ctx->gathered, (size_t)n_new * cols, kNcclFloat32, ctx->comm, st);
+        }
+        if (nr != 0) return fail(KV_E_COMM, "ncclAllGather: %s", api.GetErrorString ? api.GetErrorString(nr) : "error");
+        if (!direct) {
+            rc = launch(ctx, KV_K_GATHER, st, "unshard kernel", [&] {
+                return kvb::launch_unshard(out, (int64_t)c.n_head * D, ctx->gathered, c.n_shards, n_new, (int)cols, st);
+            });
+            if (rc) return rc;
+        }
+    }
+    return KV_OK;
+}
+
+int kv_forward(kv_ctx *ctx, int64_t n_past, int32_t n_new,
+               const float *q, int64_t q_stride, const float *k, int64_t k_stride,
+               const float *v, int64_t v_stride, int64_t in_layer_stride,
+               const float *q_norm_w, const float *k_norm_w, int64_t norm_layer_stride,
+               float *out, int64_t out_layer_stride, void *stream)
+{
+    if (!ctx) return fail(KV_E_ARG, "NULL context");
+    for (int l = 0; l < ctx->cfg.n_layer; l++) {
+        const int64_t io = (int64_t)l * in_layer_stride;
+        const int64_t no = (int64_t)l * norm_layer_stride;
+        int rc = kv_append(ctx, l, n_past, n_new, q + io, q_stride, k + io, k_stride, v + io, v_stride,
+                           q_norm_w ? q_norm_w + no : nullptr, k_norm_w ? k_norm_w + no : nullptr, stream);
+        if (rc) return rc;
+        rc = kv_attend(ctx, l, n_past, n_new, out + (int64_t)l * out_layer_stride, stream);
+        if (rc) return rc;
+    }
+    return KV_OK;
+}
+
+static int rows_io(kv_ctx *ctx, int32_t layer, int32_t which, int64_t row0, int64_t nrows, void *host, bool to_host)
+{
+    if (!ctx || !host) return fail(KV_E_ARG, "NULL argument");
+    if (layer < 0 || layer >= ctx->cfg.n_layer || (which != 0 && which != 1))
+        return fail(KV_E_ARG, "bad layer or which");
+    if (row0 < 0 || nrows < 0 || row0 + nrows > ctx->n_ctx) return fail(KV_E_RANGE, "rows outside the cache");
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+    __half *base = (which == 0 ? ctx->k_layer(layer) : ctx->v_layer(layer)) + row0 * (int64_t)ctx->hkv_loc * ctx->D;
+    const size_t bytes = (size_t)nrows * ctx->hkv_loc * ctx->D * sizeof(__half);
+    if (bytes == 0) return KV_OK;
+    KV_CUDA(cudaDeviceSynchronize());
+    if (to_host) KV_CUDA(cudaMemcpy(host, base, bytes, cudaMemcpyDeviceToHost));
+    else KV_CUDA(cudaMemcpy(base, host, bytes, cudaMemcpyHostToDevice));
+    return KV_OK;
+}
+
+int kv_export_rows(kv_ctx *ctx, int32_t layer, int32_t which, int64_t row0, int64_t nrows, uint16_t *host_dst)
+{
+    return rows_io(ctx, layer, which, row0, nrows, host_dst, true);
+}
+
+int kv_import_rows(kv_ctx *ctx, int32_t layer, int32_t which, int64_t row0, int64_t nrows, const uint16_t *host_src)
+{
+    return rows_io(ctx, layer, which, row0, nrows, const_cast<uint16_t *>(host_src), false);
+}
+
+int kv_comm_unique_id(void *id_out)
+{
+    if (!id_out) return fail(KV_E_ARG, "id_out is NULL");
+    NcclApi &api = nccl();
+    if (!api.GetUniqueId) return fail(KV_E_UNSUPPORTED, "libnccl.so.2 could not be loaded");
+    NcclId id;
+    const int rc = api.GetUniqueId(&id);
+    if (rc != 0) return fail(KV_E_COMM, "ncclGetUniqueId failed (%d)", rc);
+    std::memcpy(id_out, id.internal, sizeof(id.internal));
+    return KV_OK;
+}
+
+const char *kv_strerror(int code)
+{
+    switch (code) {
+    case KV_OK: return "ok";
+    case KV_E_ARG: return "invalid argument";
+    case KV_E_OOM: return "device out of memory";
+    case KV_E_RANGE: return "row range out of bounds";
+    case KV_E_CUDA: return "CUDA error";
+    case KV_E_COMM: return "collective error";
+    case KV_E_TIMEOUT: return "device wait timed out";
+    case KV_E_STATE: return "call order violated";
+    case KV_E_UNSUPPORTED: return "unsupported";
+    default: return "unknown error";
+    }
+}
+
+const char *kv_last_error(void) { return g_last_error.c_str(); }
+
+// ---- kv_bench.h -------------------------------------------------------------
+
+int kv_fill_synthetic(kv_ctx *ctx, uint64_t seed, uint64_t stream_base, int64_t row0, int64_t nrows, void *stream)
+{
+    if (!ctx) return fail(KV_E_ARG, "NULL context");
+    if (row0 < 0 || nrows < 0 || row0 + nrows > ctx->n_ctx) return fail(KV_E_RANGE, "rows outside the cache");
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+    kvb::FillParams p;
+    p.cache = ctx->cache;
+    p.n_layer = ctx->cfg.n_layer;
+    p.D = ctx->D;
+    p.hkv_loc = ctx->hkv_loc;
+    p.hkv_total = ctx->cfg.n_head_kv;
+    p.hkv0 = ctx->hkv0;
+    p.n_ctx = ctx->n_ctx;
+    p.row0 = row0;
+    p.nrows = nrows;
+    p.seed = seed;
+    p.stream_base = stream_base;
+    KV_CUDA(kvb::launch_fill(p, to_stream(stream)));
+    return KV_OK;
+}
+
+int kv_gen_normal_device(float *dst, uint64_t seed, uint64_t stream, uint64_t idx0, int64_t n, void *cuda_stream)
+{
+    if (!dst || n < 0) return fail(KV_E_ARG, "bad argument");
+    KV_CUDA(kvb::launch_gen_normal(dst, seed, stream, idx0, n, to_stream(cuda_stream)));
+    return KV_OK;
+}
+
+int kv_profile_enable(kv_ctx *ctx, int on)
+{
+    if (!ctx) return fail(KV_E_ARG, "NULL context");
+    ctx->prof_on = on != 0;
+    return KV_OK;
+}
+
+int kv_profile_reset(kv_ctx *ctx)
+{
+    if (!ctx) return fail(KV_E_ARG, "NULL context");
+    for (auto &r : ctx->recs) {
+        cudaEventSynchronize(r.b);
+        ctx->ev_pool.push_back(r.a);
+        ctx->ev_pool.push_back(r.b);
+    }
+    ctx->recs.clear();
+    return KV_OK;
+}
+
+int kv_profile_read(kv_ctx *ctx, int32_t kernel, int64_t *launches, double *total_ms)
+{
+    if (!ctx || kernel < 0 || kernel >= KV_K_COUNT) return fail(KV_E_ARG, "bad argument");
+    int64_t n = 0;
+    double ms = 0.0;
+    for (auto &r : ctx->recs) {
+        if (r.k != kernel) continue;
+        KV_CUDA(cudaEventSynchronize(r.b));
+        float t = 0.0f;
+        KV_CUDA(cudaEventElapsedTime(&t, r.a, r.b));
+        n++;
+        ms += t;
+    }
+    if (launches) *launches = n;
+    if (total_ms) *total_ms = ms;
+    return KV_OK;
+}
+
+const char *kv_kernel_name(int32_t kernel)
+{
+    static const char *names[KV_K_COUNT] = {"kv_append", "kv_scores", "kv_pv", "kv_prefill", "kv_unshard"};
+    return (kernel >= 0 && kernel < KV_K_COUNT) ? names[kernel] : "?";
+}
+
+int64_t kv_launch_count(const kv_ctx *ctx) { return ctx ? ctx->launches.load() : 0; }
+
+int kv_rope_table_host(const kv_config *cfg, int64_t pos0, int64_t npos, float *out)
+{
+    if (!cfg || !out || pos0 < 0 || npos < 0) return fail(KV_E_ARG, "bad argument");
+    std::string why;
+    if (!shape_ok(cfg, why)) return fail(KV_E_ARG, "%s", why.c_str());
+    if (cfg->n_rot == 0 || npos == 0) return KV_OK;
+    RopeSpec rs{cfg->n_rot, cfg->rope_base, cfg->rope_freq_scale, cfg->rope_attn_factor, cfg->rope_ext_factor,
+                cfg->rope_beta_fast, cfg->rope_beta_slow, cfg->n_ctx_orig, cfg->rope_freq_factors};
+    rope_rows(rs, pos0, pos0 + npos, out);
+    return KV_OK;
+}
+
+int kv_shard_geometry(const kv_config *cfg, int32_t shard, int32_t *q_head0, int32_t *n_q_heads,
+                      int32_t *kv_head0, int32_t *n_kv_heads)
+{
+    if (!cfg) return fail(KV_E_ARG, "NULL cfg");
+    std::string why;
+    if (!shape_ok(cfg, why)) return fail(KV_E_ARG, "%s", why.c_str());
+    const int ns = cfg->n_shards <= 1 ? 1 : cfg->n_shards;
+    if (shard < 0 || shard >= ns) return fail(KV_E_ARG, "shard out of range");
+    const int hkv = cfg->n_head_kv / ns, r = cfg->n_head / cfg->n_head_kv;
+    if (q_head0) *q_head0 = shard * hkv * r;
+    if (n_q_heads) *n_q_heads = hkv * r;
+    if (kv_head0) *kv_head0 = shard * hkv;
+    if (n_kv_heads) *n_kv_heads = hkv;
+    return KV_OK;
+}
+
+}  // extern "C"

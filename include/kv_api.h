@@ -1,0 +1,196 @@
+/*
+ * kv_api.h -- C ABI of the B200 KV-cache append + attention path.
+ *
+ * This is the drop-in boundary for GGML-Loader's per-layer KV-cache hot path
+ * (src/model.cpp in the reference).  A caller that today builds the ggml op
+ * sequence in build_graph() for the phi3 / qwen2 / qwen3 / llama architectures
+ * calls, per layer:
+ *
+ *     kv_append(ctx, layer, n_past, n_new, q, k, v, ...)   -- replaces the
+ *         QK-Norm (model.cpp:1382-1387), ggml_rope_ext (1389-1404) and the
+ *         ggml_cpy of K/V into the cache view (1406-1414);
+ *     kv_attend(ctx, layer, n_past, n_new, out, ...)        -- replaces the
+ *         attention over cache rows [0, n_past+n_new): ggml_mul_mat(K,Q),
+ *         ggml_soft_max_ext with the causal mask, ggml_mul_mat(V^T, KQ) and the
+ *         output permute (1416-1445), or the flash-attn branch (1426-1434).
+ *
+ * and at start-up kv_alloc() in place of init_kv_cache() (model.cpp:821-867),
+ * with the context auto-sizing of auto_n_ctx() (model.cpp:1002-1059) computed
+ * from free HBM instead of /proc/meminfo.
+ *
+ * Conventions
+ *  - All tensors passed to kv_append / kv_attend are DEVICE pointers, F32.
+ *  - Calls are ordered on the given CUDA stream (a cudaStream_t passed as
+ *    void*; NULL = the legacy default stream).  No call blocks the host except
+ *    kv_alloc, kv_free and the row import/export helpers.
+ *  - Errors are negative return codes; the library never exits the process
+ *    (the reference prints and calls exit(1), model.cpp:859-865).
+ *  - One host thread drives one kv_ctx; the context's scratch is shared by
+ *    its calls, so calls on one context must not overlap on the device.
+ */
+#ifndef KV_API_H
+#define KV_API_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes -------------------------------------------------------- */
+#define KV_OK              0
+#define KV_E_ARG          -1  /* bad argument or unsupported shape          */
+#define KV_E_OOM          -2  /* device allocation failed                   */
+#define KV_E_RANGE        -3  /* row range outside [0, n_ctx) / batch limit */
+#define KV_E_CUDA         -4  /* CUDA runtime error                         */
+#define KV_E_COMM         -5  /* collective (NCCL) error                    */
+#define KV_E_TIMEOUT      -6  /* a bounded device-side wait gave up         */
+#define KV_E_STATE        -7  /* call order violated (attend w/o append)    */
+#define KV_E_UNSUPPORTED  -8  /* feature not built / not available          */
+
+/* ---- RoPE modes (ggml values, model.cpp:1395) ---------------------------- */
+#define KV_ROPE_NORMAL 0      /* adjacent pairs (llama)                   */
+#define KV_ROPE_NEOX   2      /* split halves (phi3 / qwen2 / qwen3)      */
+
+typedef struct kv_ctx kv_ctx;
+
+/*
+ * Model attention parameters, the subset of `struct hparams` (model.h:63-95)
+ * that the path reads, plus allocation and sharding options.
+ */
+typedef struct kv_config {
+    int32_t n_layer;            /* hparams::n_layer                               */
+    int32_t n_head;             /* hparams::n_head (query heads, whole model)     */
+    int32_t n_head_kv;          /* hparams::n_head_kv                             */
+    int32_t head_dim;           /* hparams::n_embd_head; 64, 96 or 128            */
+    int32_t n_rot;              /* hparams::n_rot (even, <= head_dim)             */
+    int32_t rope_mode;          /* KV_ROPE_NORMAL (llama) / KV_ROPE_NEOX (others) */
+    float   rope_base;          /* hparams::rope_freq_base                        */
+    float   rope_freq_scale;    /* 1.0 for every reference architecture           */
+    float   rope_attn_factor;   /* hparams::rope_attn_factor (mscale)             */
+    float   rope_ext_factor;    /* 1.0 with phi3 LongRoPE, else 0 (model.cpp:1312)*/
+    float   rope_beta_fast;     /* 32 with LongRoPE, else 0                       */
+    float   rope_beta_slow;     /* 1 with LongRoPE, else 0                        */
+    int32_t n_ctx_orig;         /* hparams::n_ctx_orig                            */
+    const float *rope_freq_factors; /* HOST [n_rot/2] or NULL; copied by kv_alloc.
+                                   phi3 rope_factors_short (model.cpp:555-557) or
+                                   llama3 rope_freqs                             */
+    int32_t qk_norm;            /* hparams::has_qk_norm (qwen3)                   */
+    float   rms_eps;            /* hparams::rms_eps                               */
+    int64_t n_ctx;              /* cache positions; 0 = auto from free HBM         */
+    int64_t n_ctx_train;        /* auto-sizing clamp; 0 = 262144 cap              */
+    int32_t longrope_clamp;     /* 1: auto-sizing also clamps to n_ctx_orig
+                                   (phi3 with LongRoPE, model.cpp:1037-1039)     */
+    int32_t n_batch_max;        /* max n_new per call; 0 = 512                    */
+    int32_t device;             /* CUDA device ordinal; -1 = current device       */
+    int32_t n_shards;           /* GPUs sharing the cache by KV head; 0/1 = one   */
+    int32_t shard;              /* this context's shard index in [0, n_shards)    */
+    const void *comm_id;        /* 128-byte id from kv_comm_unique_id() on shard 0,
+                                   the same bytes on every shard; n_shards > 1    */
+} kv_config;
+
+/* Defaults: NEOX RoPE, base 10000, scale 1, attn factor 1, no YaRN, eps 1e-6,
+ * n_ctx 0 (auto), n_batch_max 512, device -1, one shard.  Shape fields 0. */
+int kv_config_init(kv_config *cfg);
+
+/* Bytes of the whole K+V cache at n_ctx positions, all layers and all shards:
+ * exactly kv_cache_bytes() of the reference (model.cpp:869-885). */
+uint64_t kv_cache_bytes(const kv_config *cfg, int64_t n_ctx);
+
+/* Context auto-sizing rule of auto_n_ctx() (model.cpp:1002-1059) applied to
+ * `free_bytes` of one GPU: (free - 384 MiB) * 0.8 / per-position bytes of this
+ * shard (cache rows + RoPE table row), rounded down to a multiple of 64,
+ * clamped to n_ctx_train (262144 if 0) and n_ctx_orig with longrope_clamp,
+ * floor 512.  free_bytes <= 0 gives the reference's fallback, 4096. */
+int64_t kv_auto_n_ctx(const kv_config *cfg, int64_t free_bytes);
+
+/* Allocate the cache (+ RoPE table + scratch) on the configured device;
+ * replaces init_kv_cache (model.cpp:821-867).  With cfg->n_ctx == 0 the size
+ * comes from kv_auto_n_ctx(cudaMemGetInfo free).  With n_shards > 1 this
+ * context owns KV heads [shard*n_head_kv/n_shards, (shard+1)*...) and the
+ * matching query heads, and joins the collective identified by comm_id (every
+ * shard must call kv_alloc concurrently, one process or thread per GPU).
+ * Returns KV_OK, KV_E_ARG, KV_E_OOM, KV_E_CUDA or KV_E_COMM. */
+int kv_alloc(const kv_config *cfg, kv_ctx **out);
+
+/* Release everything kv_alloc acquired.  NULL is a no-op. */
+int kv_free(kv_ctx *ctx);
+
+/* Positions the cache holds (the n_ctx actually allocated). */
+int kv_n_ctx(const kv_ctx *ctx, int64_t *n_ctx);
+
+/*
+ * Append n_new tokens' K and V rows at cache rows [n_past, n_past+n_new) of
+ * `layer`, after QK-Norm (if cfg->qk_norm) and RoPE of K; also rotates Q into
+ * the context for the following kv_attend.  Replaces model.cpp:1382-1414.
+ *
+ * q: token t's Q block (n_head*head_dim floats, heads outer) at q + t*q_stride;
+ * k, v likewise with n_head_kv*head_dim floats.  For phi3's fused QKV output
+ * (model.cpp:1088-1094) pass q = row, k = row + n_head*head_dim,
+ * v = row + (n_head+n_head_kv)*head_dim and all three strides equal to the
+ * fused row width.  q_norm_w / k_norm_w: [head_dim] gamma of this layer, or
+ * NULL without QK-Norm.  Sharded contexts read only their own heads.
+ * The F32 -> F16 cast rounds to nearest even; cache bytes equal the reference
+ * CPU path's bit for bit.
+ */
+int kv_append(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
+              const float *q, int64_t q_stride,
+              const float *k, int64_t k_stride,
+              const float *v, int64_t v_stride,
+              const float *q_norm_w, const float *k_norm_w,
+              void *stream);
+
+/*
+ * Attention of the n_new tokens last appended to `layer` (same layer, n_past
+ * and n_new as that kv_append) over cache rows [0, n_past+n_new) with the
+ * causal mask k <= n_past+t (model.cpp:1579-1586) and scale 1/sqrt(head_dim).
+ * out: [n_new][n_head*head_dim] F32, heads outer -- the layout of
+ * `cur` after ggml_cont_2d at model.cpp:1444.  With n_shards > 1 every shard
+ * receives the whole gathered output.  Only rows < n_past+n_new are read, so
+ * rewinding n_past and overwriting rows is allowed (cmd_chat.cpp:749-764).
+ */
+int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
+              float *out, void *stream);
+
+/*
+ * One step of the path over every layer: for layer l in [0, n_layer),
+ * kv_append then kv_attend with inputs at q + l*in_layer_stride (likewise k,
+ * v), gammas at q_norm_w + l*norm_layer_stride, output at
+ * out + l*out_layer_stride.  The per-layer loop of forward_step
+ * (model.cpp:1318, 1496-1597) restricted to this path, driven from C++.
+ */
+int kv_forward(kv_ctx *ctx, int64_t n_past, int32_t n_new,
+               const float *q, int64_t q_stride,
+               const float *k, int64_t k_stride,
+               const float *v, int64_t v_stride, int64_t in_layer_stride,
+               const float *q_norm_w, const float *k_norm_w, int64_t norm_layer_stride,
+               float *out, int64_t out_layer_stride, void *stream);
+
+/* Copy cache rows [row0, row0+nrows) of K (which = 0) or V (which = 1) of
+ * `layer` to / from host memory in the reference layout [row][head][dim] F16
+ * (this context's heads only).  Synchronous.  Used for checking, for the
+ * reference's /save-/load style rebuilds and for tests. */
+int kv_export_rows(kv_ctx *ctx, int32_t layer, int32_t which, int64_t row0,
+                   int64_t nrows, uint16_t *host_dst);
+int kv_import_rows(kv_ctx *ctx, int32_t layer, int32_t which, int64_t row0,
+                   int64_t nrows, const uint16_t *host_src);
+
+/* Shard geometry of a context: first global query head, query heads, first
+ * global KV head, KV heads. */
+int kv_shard_info(const kv_ctx *ctx, int32_t *q_head0, int32_t *n_q_heads,
+                  int32_t *kv_head0, int32_t *n_kv_heads);
+
+/* 128-byte identifier for a new collective; call on shard 0 and hand the
+ * bytes to every shard's kv_config.comm_id.  KV_E_UNSUPPORTED when NCCL
+ * (libnccl.so.2) cannot be loaded. */
+int kv_comm_unique_id(void *id_out);
+
+const char *kv_strerror(int code);
+/* Detail of the last failing call on this host thread ("" if none). */
+const char *kv_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KV_API_H */

@@ -1,0 +1,59 @@
+/*
+ * kv_bench.h -- measurement and synthetic-data helpers of the KV path library.
+ *
+ * Not part of the reference-facing boundary (kv_api.h): the reference has no
+ * counterpart for these.  They exist so the benchmark and the tests can fill a
+ * multi-GiB cache with seeded data on the device and time individual kernels.
+ */
+#ifndef KV_BENCH_H
+#define KV_BENCH_H
+
+#include "kv_api.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Fill cache rows [row0, row0+nrows) of K and V of every layer with the seeded
+ * generator: element (row, global head h, dim d) of layer l's K gets
+ * normal(seed, stream_base + 2l, row*n_head_kv*head_dim + h*head_dim + d), V
+ * uses stream_base + 2l + 1, rounded to F16 (nearest even).  normal() is the
+ * Irwin-Hall sum of twelve 16-bit uniforms from splitmix64, exact in F32, so
+ * the CPU oracle regenerates identical bits. */
+int kv_fill_synthetic(kv_ctx *ctx, uint64_t seed, uint64_t stream_base,
+                      int64_t row0, int64_t nrows, void *stream);
+
+/* dst[i] = normal(seed, stream, idx0 + i) for i < n, on the device. */
+int kv_gen_normal_device(float *dst, uint64_t seed, uint64_t stream,
+                         uint64_t idx0, int64_t n, void *cuda_stream);
+
+/* Per-kernel timing with CUDA events recorded around each launch on the
+ * launching stream.  Kernel ids below.  Enabling adds one event pair per
+ * launch; totals accumulate until kv_profile_reset. */
+#define KV_K_APPEND   0
+#define KV_K_SCORES   1
+#define KV_K_PV       2
+#define KV_K_PREFILL  3
+#define KV_K_GATHER   4
+#define KV_K_COUNT    5
+int kv_profile_enable(kv_ctx *ctx, int on);
+int kv_profile_reset(kv_ctx *ctx);
+/* Synchronizes the recorded events; returns launches and summed milliseconds. */
+int kv_profile_read(kv_ctx *ctx, int32_t kernel, int64_t *launches, double *total_ms);
+const char *kv_kernel_name(int32_t kernel);
+
+/* Number of kernels this library launched since kv_alloc (host-side count). */
+int64_t kv_launch_count(const kv_ctx *ctx);
+
+/* Host-only pieces of kv_alloc, callable without a GPU (for checking):
+ * the (cos, sin) RoPE table kv_alloc uploads, rows pos0 .. pos0+npos-1,
+ * out[(p*(n_rot/2) + i)*2 + {0,1}]; and the heads shard `shard` of
+ * cfg->n_shards owns. */
+int kv_rope_table_host(const kv_config *cfg, int64_t pos0, int64_t npos, float *out);
+int kv_shard_geometry(const kv_config *cfg, int32_t shard, int32_t *q_head0, int32_t *n_q_heads,
+                      int32_t *kv_head0, int32_t *n_kv_heads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KV_BENCH_H */

@@ -1,0 +1,239 @@
+"""ctypes wrapper over the CPU oracle (oracle/kv_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+CPU legs of bench.py, never by the product package.  See kv_oracle.h for what
+is restated from the reference (src/model.cpp:1382-1445, 821-885, 1002-1059)
+and for the assumptions A1-A5 (parity unpinned: ggml is not vendored).
+"""
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(HERE, "lib", "libkv_oracle.so")
+_REF_PATH = os.path.join(HERE, "_ref", "libmoe_scalar.so")
+_lib = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+
+
+class KvoCfg(ctypes.Structure):
+    _fields_ = [
+        ("n_head", ctypes.c_int32),
+        ("n_head_kv", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("n_rot", ctypes.c_int32),
+        ("rope_mode", ctypes.c_int32),
+        ("n_ctx_orig", ctypes.c_int32),
+        ("rope_base", ctypes.c_float),
+        ("rope_freq_scale", ctypes.c_float),
+        ("rope_attn_factor", ctypes.c_float),
+        ("rope_ext_factor", ctypes.c_float),
+        ("rope_beta_fast", ctypes.c_float),
+        ("rope_beta_slow", ctypes.c_float),
+        ("rope_freq_factors", _f32p),
+        ("qk_norm", ctypes.c_int32),
+        ("rms_eps", ctypes.c_float),
+    ]
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            import importlib.util
+            spec = importlib.util.spec_from_file_location("_oracle_build", os.path.join(HERE, "build.py"))
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            mod.build_oracle()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.kvo_f32_to_f16.restype = ctypes.c_uint16
+        L.kvo_f32_to_f16.argtypes = [ctypes.c_float]
+        L.kvo_f16_to_f32.restype = ctypes.c_float
+        L.kvo_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.kvo_f32_to_f16_n.argtypes = [_f32p, _u16p, ctypes.c_int64]
+        L.kvo_rope_corr_dims.argtypes = [ctypes.POINTER(KvoCfg), _f32p]
+        L.kvo_rope_table.argtypes = [ctypes.POINTER(KvoCfg), ctypes.c_int64, ctypes.c_int64, _f32p]
+        L.kvo_rms_norm_mul.argtypes = [_f32p, _f32p, ctypes.c_int32, ctypes.c_float, _f32p]
+        L.kvo_rope_row.argtypes = [ctypes.POINTER(KvoCfg), _f32p, _f32p, _f32p]
+        L.kvo_append.restype = ctypes.c_int
+        L.kvo_append.argtypes = [ctypes.POINTER(KvoCfg), ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                 _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, _f32p, ctypes.c_int64,
+                                 _f32p, _f32p, _u16p, _u16p, _f32p]
+        L.kvo_attend.restype = ctypes.c_int
+        L.kvo_attend.argtypes = [ctypes.POINTER(KvoCfg), ctypes.c_int64, ctypes.c_int32,
+                                 _f32p, _u16p, _u16p, _f32p, ctypes.c_int32]
+        L.kvo_kv_cache_bytes.restype = ctypes.c_uint64
+        L.kvo_kv_cache_bytes.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64]
+        L.kvo_auto_n_ctx.restype = ctypes.c_int64
+        L.kvo_auto_n_ctx.argtypes = [ctypes.c_int64, ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64]
+        L.kvo_bits.restype = ctypes.c_uint64
+        L.kvo_bits.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64]
+        L.kvo_normal.restype = ctypes.c_float
+        L.kvo_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64]
+        L.kvo_gen_normal_f32.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64, _f32p]
+        L.kvo_gen_normal_f16.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64, _u16p]
+        L.kvo_gen_uniform_f32.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64,
+                                          ctypes.c_float, ctypes.c_float, _f32p]
+        L.kvo_gen_cache_rows.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _u16p]
+        L.kvo_online_cores.restype = ctypes.c_int32
+        _lib = L
+    return _lib
+
+
+def _p(a, t=_f32p):
+    return None if a is None else a.ctypes.data_as(t)
+
+
+class Oracle:
+    """One layer's attention parameters plus the oracle entry points.
+
+    `spec` is a kv_b200 model spec dict (n_head, n_head_kv, head_dim, n_rot,
+    rope_mode, rope_base, ...).  The freq-factor array is kept alive here.
+    """
+
+    def __init__(self, spec):
+        self.spec = dict(spec)
+        ff = spec.get("rope_freq_factors")
+        self._ff = None if ff is None else np.ascontiguousarray(ff, dtype=np.float32)
+        c = KvoCfg()
+        c.n_head = spec["n_head"]
+        c.n_head_kv = spec["n_head_kv"]
+        c.head_dim = spec["head_dim"]
+        c.n_rot = spec.get("n_rot", spec["head_dim"])
+        c.rope_mode = spec.get("rope_mode", 2)
+        c.n_ctx_orig = spec.get("n_ctx_orig", 0)
+        c.rope_base = spec.get("rope_base", 10000.0)
+        c.rope_freq_scale = spec.get("rope_freq_scale", 1.0)
+        c.rope_attn_factor = spec.get("rope_attn_factor", 1.0)
+        c.rope_ext_factor = spec.get("rope_ext_factor", 0.0)
+        c.rope_beta_fast = spec.get("rope_beta_fast", 0.0)
+        c.rope_beta_slow = spec.get("rope_beta_slow", 0.0)
+        c.rope_freq_factors = _p(self._ff)
+        c.qk_norm = 1 if spec.get("qk_norm") else 0
+        c.rms_eps = spec.get("rms_eps", 1e-6)
+        self.cfg = c
+
+    # -- pieces ---------------------------------------------------------
+    def rope_table(self, pos0, npos):
+        half = self.cfg.n_rot // 2
+        out = np.zeros((npos, half, 2), np.float32)
+        lib().kvo_rope_table(ctypes.byref(self.cfg), pos0, npos, _p(out))
+        return out
+
+    def corr_dims(self):
+        out = np.zeros(2, np.float32)
+        lib().kvo_rope_corr_dims(ctypes.byref(self.cfg), _p(out))
+        return out
+
+    def rope_row(self, cs_row, x):
+        x = np.ascontiguousarray(x, np.float32)
+        cs_row = np.ascontiguousarray(cs_row, np.float32)
+        y = np.empty_like(x)
+        lib().kvo_rope_row(ctypes.byref(self.cfg), _p(cs_row), _p(x), _p(y))
+        return y
+
+    # -- the path ------------------------------------------------------
+    def append(self, kcache, vcache, n_past, q, k, v, q_norm_w=None, k_norm_w=None):
+        """q: [n_new, >=n_head*d] rows; k, v: [n_new, >=n_head_kv*d] rows (row
+        strides taken from the arrays).  kcache/vcache: uint16 [n_ctx, hkv, d],
+        modified in place.  Returns the rotated Q as [n_new, n_head, d] F32."""
+        n_new = q.shape[0]
+        for a in (q, k, v):
+            assert a.dtype == np.float32 and a.strides[1] == 4
+        assert kcache.flags.c_contiguous and vcache.flags.c_contiguous
+        d, hq = self.cfg.head_dim, self.cfg.n_head
+        q_out = np.zeros((n_new, hq, d), np.float32)
+        qn = None if q_norm_w is None else np.ascontiguousarray(q_norm_w, np.float32)
+        kn = None if k_norm_w is None else np.ascontiguousarray(k_norm_w, np.float32)
+        rc = lib().kvo_append(ctypes.byref(self.cfg), kcache.shape[0], n_past, n_new,
+                              _p(q), q.strides[0] // 4, _p(k), k.strides[0] // 4, _p(v), v.strides[0] // 4,
+                              _p(qn), _p(kn), _p(kcache, _u16p), _p(vcache, _u16p), _p(q_out))
+        assert rc == 0, rc
+        return q_out
+
+    def attend(self, kcache, vcache, n_past, q_roped, n_threads=0):
+        q_roped = np.ascontiguousarray(q_roped, np.float32)
+        n_new = q_roped.shape[0]
+        out = np.zeros((n_new, self.cfg.n_head * self.cfg.head_dim), np.float32)
+        rc = lib().kvo_attend(ctypes.byref(self.cfg), n_past, n_new, _p(q_roped),
+                              _p(kcache, _u16p), _p(vcache, _u16p), _p(out), n_threads)
+        assert rc == 0, rc
+        return out
+
+
+# -- generators and helpers --------------------------------------------------
+
+def f32_to_f16_bits(x):
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(x.shape, np.uint16)
+    lib().kvo_f32_to_f16_n(_p(x), _p(out, _u16p), x.size)
+    return out
+
+
+def gen_normal_f32(seed, stream, n, idx0=0):
+    out = np.empty(n, np.float32)
+    lib().kvo_gen_normal_f32(seed, stream, idx0, n, _p(out))
+    return out
+
+
+def gen_normal_f16(seed, stream, n, idx0=0):
+    out = np.empty(n, np.uint16)
+    lib().kvo_gen_normal_f16(seed, stream, idx0, n, _p(out, _u16p))
+    return out
+
+
+def gen_uniform_f32(seed, stream, n, lo, hi, idx0=0):
+    out = np.empty(n, np.float32)
+    lib().kvo_gen_uniform_f32(seed, stream, idx0, n, lo, hi, _p(out))
+    return out
+
+
+def gen_cache_rows(seed, stream, row0, nrows, n_head_kv, head_dim, h0=0, nh=None):
+    nh = n_head_kv if nh is None else nh
+    out = np.empty((nrows, nh, head_dim), np.uint16)
+    lib().kvo_gen_cache_rows(seed, stream, row0, nrows, n_head_kv, head_dim, h0, nh, _p(out, _u16p))
+    return out
+
+
+def kv_cache_bytes(n_layer, n_head_kv, head_dim, n_ctx):
+    return int(lib().kvo_kv_cache_bytes(n_layer, n_head_kv, head_dim, n_ctx))
+
+
+def auto_n_ctx(avail, per_tok, n_ctx_train=0, longrope_orig=0):
+    return int(lib().kvo_auto_n_ctx(avail, per_tok, n_ctx_train, longrope_orig))
+
+
+def online_cores():
+    return int(lib().kvo_online_cores())
+
+
+# -- the reference's own scalar backend (oracle/_ref, built from its sources) -
+
+class _RefBackend(ctypes.Structure):
+    _fields_ = [
+        ("name", ctypes.c_char_p),
+        ("self", ctypes.c_void_p),
+        ("matmul", ctypes.c_void_p),
+        ("matmul_batch", ctypes.c_void_p),
+        ("rmsnorm", ctypes.CFUNCTYPE(None, ctypes.c_void_p, _f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_float)),
+        ("rope", ctypes.CFUNCTYPE(None, ctypes.c_void_p, _f32p, ctypes.c_int, _f32p, _f32p)),
+        ("softmax", ctypes.CFUNCTYPE(None, ctypes.c_void_p, _f32p, ctypes.c_int)),
+        ("swiglu", ctypes.c_void_p),
+        ("begin_batch", ctypes.c_void_p),
+        ("end_batch", ctypes.c_void_p),
+        ("sync", ctypes.c_void_p),
+    ]
+
+
+def reference_scalar_backend():
+    """The reference's compute_backend_scalar() vtable (compute_backend.c:101-117),
+    or None when oracle/_ref was not built (no reference checkout)."""
+    if not os.path.exists(_REF_PATH):
+        return None
+    L = ctypes.CDLL(_REF_PATH)
+    L.compute_backend_scalar.restype = ctypes.POINTER(_RefBackend)
+    return L.compute_backend_scalar().contents

@@ -1,0 +1,140 @@
+"""CPU tests of the library's host side (no GPU needed): the C ABI loads and
+exports every function its headers declare, the sizing rules equal the
+reference's (model.cpp:869-885, 1002-1059), the RoPE table that kv_alloc
+uploads equals the oracle's bit for bit, the shard geometry, and clean
+failure (an error code, no crash) of kv_alloc where there is no GPU.
+"""
+import ctypes
+import os
+import re
+import sys
+
+import numpy as np
+import pytest
+
+import kv_b200 as K
+import kv_oracle as O
+from kv_b200 import specs
+
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+import make_golden as G  # noqa: E402
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_functions():
+    names = []
+    for h in ("kv_api.h", "kv_bench.h"):
+        src = open(os.path.join(ROOT, "include", h)).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        names += re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\*?\s*(kv_[a-z_0-9]+)\s*\(", src, flags=re.M)
+    return sorted(set(names))
+
+
+def test_library_loads_and_exports_every_declared_function():
+    L = K.lib()
+    names = _declared_functions()
+    assert len(names) >= 20, names
+    for n in names:
+        assert hasattr(L, n), "missing export %s" % n
+
+
+def test_config_defaults():
+    c = K.KvConfig()
+    assert K.lib().kv_config_init(ctypes.byref(c)) == 0
+    assert c.rope_mode == 2 and c.rope_base == 10000.0 and c.rope_freq_scale == 1.0
+    assert c.rope_attn_factor == 1.0 and c.n_batch_max == 512 and c.device == -1 and c.n_shards == 1
+    assert abs(c.rms_eps - 1e-6) < 1e-12
+
+
+@pytest.mark.parametrize("name", list(specs.specs()))
+def test_cache_bytes_equals_reference_rule(name):
+    sp = specs.get(name)
+    cfg = K.make_config(sp)
+    for n_ctx in (1, 64, sp["n_ctx"]):
+        assert K.cache_bytes(cfg, n_ctx) == O.kv_cache_bytes(sp["n_layer"], sp["n_head_kv"], sp["head_dim"], n_ctx)
+
+
+@pytest.mark.parametrize("name", list(specs.specs()))
+@pytest.mark.parametrize("shards", [1, 2])
+def test_auto_n_ctx_equals_reference_rule(name, shards):
+    sp = specs.get(name)
+    if sp["n_head_kv"] % shards:
+        pytest.skip("heads do not shard")
+    cfg = K.make_config(sp, n_shards=shards)
+    # per-position bytes of one shard: its cache rows plus one RoPE table row
+    per_tok = sp["n_layer"] * (sp["n_head_kv"] // shards) * sp["head_dim"] * 4 + (sp["n_rot"] // 2) * 8
+    for free in (-1, 0, 300 << 20, 1 << 30, 24 << 30, 180 << 30):
+        for train in (0, 4096, 131072):
+            cfg.n_ctx_train = train
+            assert K.auto_n_ctx(cfg, free) == O.auto_n_ctx(free, per_tok, train), (free, train)
+
+
+def test_auto_n_ctx_longrope_clamp():
+    sp = specs.get("phi3-mini")
+    sp.update({k: v for k, v in G.LONGROPE.items()})
+    cfg = K.make_config(sp)
+    assert K.auto_n_ctx(cfg, 180 << 30) == 4096
+    cfg.longrope_clamp = 0
+    assert K.auto_n_ctx(cfg, 180 << 30) > 4096
+
+
+ROPE_CASES = ["qwen2-0.5b", "llama3.2-3b", "phi3-mini", "qwen3-8b-prefill", "llama3.1-8b-128k", "longrope",
+              "partial"]
+
+
+@pytest.mark.parametrize("name", ROPE_CASES)
+def test_rope_table_bitexact_vs_oracle(name):
+    if name == "longrope":
+        sp = specs.get("phi3-mini")
+        sp.update({k: v for k, v in G.LONGROPE.items()})
+    elif name == "partial":
+        sp = specs.get("phi3-mini")
+        sp["n_rot"] = 64
+    else:
+        sp = specs.get(name)
+    cfg = K.make_config(sp)
+    orc = O.Oracle(sp)
+    for pos0, npos in ((0, 300), (4000, 200), (131000, 72), (262000, 8)):
+        got = K.rope_table_host(cfg, pos0, npos)
+        want = orc.rope_table(pos0, npos)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (name, pos0)
+
+
+def test_shard_geometry():
+    sp = specs.get("llama3.1-8b-128k")
+    for G_ in (1, 2, 4, 8):
+        cfg = K.make_config(sp, n_shards=G_)
+        seen_q, seen_kv = [], []
+        for g in range(G_):
+            q0, nq, kv0, nkv = K.shard_geometry(cfg, g)
+            assert nkv == 8 // G_ and nq == 4 * nkv
+            assert q0 == kv0 * 4          # a KV head's GQA group stays on its shard
+            seen_q += list(range(q0, q0 + nq))
+            seen_kv += list(range(kv0, kv0 + nkv))
+        assert seen_q == list(range(32)) and seen_kv == list(range(8))
+    bad = K.make_config(specs.get("qwen2-0.5b"), n_shards=4)   # 2 KV heads do not split 4 ways
+    with pytest.raises(K.KvError) as e:
+        K.shard_geometry(bad, 0)
+    assert e.value.code == K.KV_E_ARG
+
+
+def test_bad_shapes_rejected():
+    sp = specs.get("llama3.2-3b")
+    for field, val in (("head_dim", 80), ("n_rot", 7), ("rope_mode", 1), ("n_head", 25)):
+        cfg = K.make_config(sp)
+        setattr(cfg, field, val)
+        with pytest.raises(K.KvError) as e:
+            K.rope_table_host(cfg, 0, 1)
+        assert e.value.code == K.KV_E_ARG
+
+
+def test_alloc_without_gpu_returns_error():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    cfg = K.make_config(specs.get("qwen2-0.5b"), n_ctx=256)
+    h = ctypes.c_void_p()
+    rc = K.lib().kv_alloc(ctypes.byref(cfg), ctypes.byref(h))
+    assert rc == K.KV_E_CUDA and not h.value
+    assert "cuda" in K.last_error().lower()

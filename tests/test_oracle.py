@@ -1,0 +1,348 @@
+"""CPU tests of the oracle (oracle/kv_oracle.c) -- the checker the GPU path is
+compared against.  The reference ships no fixtures for this path (ggml is not
+vendored), so the oracle is pinned by: (1) exhaustive/numpy checks of its F16
+rounding, (2) the reference's own scalar math backend
+(src/moe_stream/compute_backend.c, built by oracle/build.py into oracle/_ref)
+for the NEOX rotation, RMSNorm and softmax formulas, (3) an independent
+float64 numpy restatement of the attention, and (4) the committed golden
+fixtures (regression pin).
+"""
+import ctypes
+import math
+import os
+import sys
+
+import numpy as np
+import pytest
+
+import kv_oracle as O
+from kv_b200 import specs, synth
+
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+import make_golden as G  # noqa: E402
+
+f32p = ctypes.POINTER(ctypes.c_float)
+
+
+def _fp(a):
+    return a.ctypes.data_as(f32p)
+
+
+# ---------------------------------------------------------------------------
+# F16 conversion (A3)
+# ---------------------------------------------------------------------------
+
+def test_f16_to_f32_all_halves():
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    want = bits.view(np.float16).astype(np.float32)
+    got = np.array([O.lib().kvo_f16_to_f32(int(b)) for b in bits], np.float32)
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32))
+
+
+def test_f32_to_f16_round_to_nearest_even():
+    rng = np.random.default_rng(1)
+    halves = np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.float16)
+    finite = halves[np.isfinite(halves)].astype(np.float32)
+    # exact halves, exact ties between neighbours, and random floats over the whole range
+    with np.errstate(over="ignore"):
+        nxt = np.nextafter(finite.astype(np.float16), np.float16(np.inf)).astype(np.float32)
+    ties = ((finite.astype(np.float64) + nxt.astype(np.float64)) / 2).astype(np.float32)
+    rnd = np.concatenate([
+        rng.standard_normal(200000).astype(np.float32),
+        (rng.standard_normal(100000) * 1e-5).astype(np.float32),      # subnormal halves
+        (rng.standard_normal(100000) * 3e4).astype(np.float32),       # near overflow
+        np.array([65504, 65519.99, 65520, 65536, 1e-8, 2.0 ** -25, 2.0 ** -24, -0.0, np.inf, -np.inf],
+                 np.float32),
+    ])
+    x = np.concatenate([finite, ties[np.isfinite(ties)], rnd]).astype(np.float32)
+    got = O.f32_to_f16_bits(x)
+    with np.errstate(over="ignore"):
+        want = x.astype(np.float16).view(np.uint16)
+    assert np.array_equal(got, want)
+
+
+# ---------------------------------------------------------------------------
+# seeded generator: C oracle == numpy (and the device generator, in GPU tests)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("seed,stream,idx0", [(0x6B760001, synth.STREAM_CACHE, 0), (7, 12345, 10 ** 9)])
+def test_generator_c_matches_numpy(seed, stream, idx0):
+    n = 20000
+    a = O.gen_normal_f32(seed, stream, n, idx0)
+    b = synth.normal(seed, stream, n, idx0)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    ua = O.gen_uniform_f32(seed, stream, n, 0.5, 1.5, idx0)
+    ub = synth.uniform(seed, stream, n, 0.5, 1.5, idx0)
+    assert np.array_equal(ua.view(np.uint32), ub.view(np.uint32))
+    assert abs(float(a.mean())) < 0.03 and abs(float(a.var()) - 1.0) < 0.05
+    assert ua.min() >= 0.5 and ua.max() < 1.5
+
+
+def test_cache_rows_use_global_head_index():
+    hkv, d = 8, 128
+    full = O.gen_cache_rows(5, synth.STREAM_CACHE, 10, 3, hkv, d)
+    part = O.gen_cache_rows(5, synth.STREAM_CACHE, 10, 3, hkv, d, h0=2, nh=3)
+    assert np.array_equal(full[:, 2:5], part)
+    idx0 = 10 * hkv * d
+    ref = synth.normal(5, synth.STREAM_CACHE, 3 * hkv * d, idx0).astype(np.float16).view(np.uint16)
+    assert np.array_equal(full.reshape(-1), ref)
+
+
+# ---------------------------------------------------------------------------
+# RoPE (A2)
+# ---------------------------------------------------------------------------
+
+def _cfg(name, **kw):
+    sp = specs.get(name)
+    sp.update(kw)
+    return sp
+
+
+@pytest.mark.parametrize("name", ["qwen2-0.5b", "llama3.2-3b", "phi3-mini", "llama3.1-8b-128k"])
+def test_rope_table_is_iterated_float_schedule(name):
+    sp = _cfg(name)
+    orc = O.Oracle(sp)
+    pos = [0, 1, 17, 4095, 32000, 131063]
+    n_rot = sp["n_rot"]
+    step = np.float32(np.float32(sp["rope_base"]) ** np.float32(-2.0 / n_rot))
+    ff = sp["rope_freq_factors"]
+    for p in pos:
+        t = orc.rope_table(p, 1)[0]
+        theta = np.float32(p)
+        for i in range(n_rot // 2):
+            f = np.float32(1.0) if ff is None else ff[i]
+            ang = np.float32(theta / f)
+            # libm float cos/sin of the float angle; compare loosely to numpy's
+            assert abs(float(t[i, 0]) - math.cos(float(ang))) < 2e-6 * max(1.0, abs(float(ang))) + 1e-6
+            assert abs(float(t[i, 1]) - math.sin(float(ang))) < 2e-6 * max(1.0, abs(float(ang))) + 1e-6
+            theta = np.float32(theta * step)
+
+
+def test_rope_yarn_corr_dims_and_mscale():
+    sp = _cfg("phi3-mini", **{k: v for k, v in G.LONGROPE.items()})
+    orc = O.Oracle(sp)
+    dims = orc.corr_dims()
+    # corr_dim(n_turns) = n_dims * ln(n_ctx_orig / (2 pi n_turns)) / (2 ln base)
+    def cd(b):
+        return 96 * math.log(4096 / (2 * math.pi * b)) / (2 * math.log(1e4))
+    assert dims[0] == max(0.0, math.floor(cd(32.0)))
+    assert dims[1] == min(95.0, math.ceil(cd(1.0)))
+    t0 = orc.rope_table(0, 1)[0]
+    # at position 0 every angle is 0: cos = mscale = attn_factor (freq_scale 1 -> no extra term)
+    assert np.all(t0[:, 0] == np.float32(sp["rope_attn_factor"]))
+    assert np.all(t0[:, 1] == 0.0)
+
+
+def test_rope_neox_matches_reference_scalar_backend():
+    ref = O.reference_scalar_backend()
+    if ref is None:
+        pytest.skip("oracle/_ref not built (no reference checkout on this host)")
+    sp = _cfg("qwen3-8b-prefill")
+    orc = O.Oracle(sp)
+    rng = np.random.default_rng(3)
+    d = sp["head_dim"]
+    for p in (0, 5, 16384, 40000):
+        cs = orc.rope_table(p, 1)[0]
+        x = rng.standard_normal(d).astype(np.float32)
+        ours = orc.rope_row(cs, x)
+        v = x.copy()
+        c = np.ascontiguousarray(cs[:, 0])
+        s = np.ascontiguousarray(cs[:, 1])
+        ref.rope(None, _fp(v), d, _fp(c), _fp(s))  # compute_backend.c:56-66 (NEOX halves)
+        assert np.array_equal(ours.view(np.uint32), v.view(np.uint32))
+
+
+def test_rope_normal_pairs_adjacent():
+    sp = _cfg("llama3.2-3b")
+    orc = O.Oracle(sp)
+    cs = orc.rope_table(1234, 1)[0]
+    x = np.arange(128, dtype=np.float32) / 7.0
+    y = orc.rope_row(cs, x)
+    for i in range(64):
+        c, s = cs[i]
+        a, b = x[2 * i], x[2 * i + 1]
+        assert y[2 * i] == np.float32(np.float32(a * c) - np.float32(b * s))
+        assert y[2 * i + 1] == np.float32(np.float32(a * s) + np.float32(b * c))
+
+
+def test_rope_partial_rotation_passes_tail_through():
+    sp = _cfg("phi3-mini", n_rot=64)
+    orc = O.Oracle(sp)
+    cs = orc.rope_table(99, 1)[0]
+    x = np.random.default_rng(0).standard_normal(96).astype(np.float32)
+    y = orc.rope_row(cs, x)
+    assert np.array_equal(y[64:], x[64:])
+    assert not np.array_equal(y[:64], x[:64])
+
+
+# ---------------------------------------------------------------------------
+# RMSNorm (A1) and softmax (A5) against the reference scalar backend
+# ---------------------------------------------------------------------------
+
+def test_rmsnorm_matches_reference_scalar_backend():
+    ref = O.reference_scalar_backend()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    rng = np.random.default_rng(4)
+    for n in (64, 96, 128):
+        x = rng.standard_normal(n).astype(np.float32)
+        w = rng.uniform(0.5, 1.5, n).astype(np.float32)
+        ours = np.empty(n, np.float32)
+        O.lib().kvo_rms_norm_mul(_fp(x), _fp(w), n, 1e-6, _fp(ours))
+        theirs = np.empty(n, np.float32)
+        ref.rmsnorm(None, _fp(theirs), _fp(x), _fp(w), n, 1e-6)  # compute_backend.c:42-54
+        # the reference's scalar backend sums squares in float, ggml in double
+        assert np.max(np.abs(ours - theirs) / np.maximum(np.abs(theirs), 1e-3)) < 2e-6
+        # and the double-sum restatement exactly
+        sq = (x * x).astype(np.float64)
+        mean = np.float32(np.cumsum(sq)[-1] / n)
+        sc = np.float32(1.0) / np.sqrt(np.float32(mean + np.float32(1e-6)))
+        want = ((x * sc).astype(np.float32) * w).astype(np.float32)
+        assert np.array_equal(ours.view(np.uint32), want.view(np.uint32))
+
+
+def _np_attention(sp, n_past, q_roped, kc, vc):
+    """Independent float64 restatement of model.cpp:1416-1445 with ggml's F16
+    conversions of Q and of P (A4) and a double softmax sum (A5)."""
+    hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+    r = hq // hkv
+    n_new = q_roped.shape[0]
+    n_kv = n_past + n_new
+    scale = np.float32(1.0) / np.sqrt(np.float32(d))
+    K = kc[:n_kv].view(np.float16).astype(np.float64)
+    V = vc[:n_kv].view(np.float16).astype(np.float64)
+    q16 = q_roped.astype(np.float16).astype(np.float64)
+    out = np.zeros((n_new, hq * d))
+    for t in range(n_new):
+        lim = n_past + t
+        for h in range(hq):
+            kv = h // r  # GQA: contiguous groups (moe_stream/qwen_model.c:499)
+            s = (K[: lim + 1, kv] @ q16[t, h]).astype(np.float32) * scale
+            e = np.exp((s - s.max()).astype(np.float64)).astype(np.float32)
+            p = (e * np.float32(1.0 / e.astype(np.float64).sum())).astype(np.float16).astype(np.float64)
+            out[t, h * d:(h + 1) * d] = p @ V[: lim + 1, kv]
+    return out
+
+
+@pytest.mark.parametrize("case", G.CASES, ids=[c["name"] for c in G.CASES])
+def test_attention_matches_float64_restatement(case):
+    sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
+    orc = O.Oracle(sp)
+    q_roped = orc.append(kc, vc, case["n_past"], q, k, v, qn, kn)
+    got = orc.attend(kc, vc, case["n_past"], q_roped)
+    want = _np_attention(sp, case["n_past"], q_roped, kc, vc)
+    err = np.abs(got - want)
+    # the two restatements accumulate scores in different orders, so an
+    # occasional p lands on the neighbouring F16 value: one F16 ulp of p
+    # (<= 2^-11 p) times |v| (<= 6) bounds the per-element difference
+    assert err.max() < 1e-4
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) < 3e-5
+
+
+def test_softmax_semantics_against_reference_scalar_backend():
+    ref = O.reference_scalar_backend()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    case = G.CASES[2]
+    sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
+    orc = O.Oracle(sp)
+    q_roped = orc.append(kc, vc, case["n_past"], q, k, v, qn, kn)
+    got = orc.attend(kc, vc, case["n_past"], q_roped)
+    d, r = sp["head_dim"], sp["n_head"] // sp["n_head_kv"]
+    n_kv = case["n_past"] + 1
+    K = kc[:n_kv].view(np.float16).astype(np.float32)
+    V = vc[:n_kv].view(np.float16).astype(np.float32)
+    for h in range(sp["n_head"]):
+        kvh = h // r
+        s = (K[:, kvh] @ q_roped[0, h].astype(np.float16).astype(np.float32)) * np.float32(1 / math.sqrt(d))
+        s = np.ascontiguousarray(s, np.float32)
+        ref.softmax(None, _fp(s), n_kv)   # compute_backend.c:68-86
+        o = s.astype(np.float16).astype(np.float32) @ V[:, kvh]
+        assert np.allclose(o, got[0, h * d:(h + 1) * d], rtol=0, atol=2e-5)
+
+
+def test_attention_thread_count_invariant():
+    case = G.CASES[6]
+    sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
+    orc = O.Oracle(sp)
+    q_roped = orc.append(kc, vc, case["n_past"], q, k, v, qn, kn)
+    a = orc.attend(kc, vc, case["n_past"], q_roped, n_threads=1)
+    b = orc.attend(kc, vc, case["n_past"], q_roped, n_threads=8)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_append_matches_numpy_restatement():
+    """kvo_append == numpy float32 ops (no FMA) with the oracle's RoPE table."""
+    case = G.CASES[6]   # qwen3: QK-Norm + NEOX
+    sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
+    orc = O.Oracle(sp)
+    n_past, n_new, d = case["n_past"], case["n_new"], sp["head_dim"]
+    q_roped = orc.append(kc, vc, n_past, q, k, v, qn, kn)
+    cs = orc.rope_table(n_past, n_new)
+    half = d // 2
+
+    def norm(x, w):
+        sq = (x * x).astype(np.float32).astype(np.float64)
+        mean = np.float32(np.cumsum(sq)[-1] / d)
+        sc = np.float32(1.0) / np.sqrt(np.float32(mean + np.float32(sp["rms_eps"])))
+        return ((x * sc).astype(np.float32) * w).astype(np.float32)
+
+    def rope(x, c):
+        y = x.copy()
+        a, b = x[:half], x[half:]
+        y[:half] = (a * c[:, 0]).astype(np.float32) - (b * c[:, 1]).astype(np.float32)
+        y[half:] = (a * c[:, 1]).astype(np.float32) + (b * c[:, 0]).astype(np.float32)
+        return y
+
+    hkv = sp["n_head_kv"]
+    for t in range(n_new):
+        for h in range(hkv):
+            x = k[t, h * d:(h + 1) * d]
+            want = rope(norm(x, kn), cs[t]).astype(np.float16).view(np.uint16)
+            assert np.array_equal(kc[n_past + t, h], want)
+            assert np.array_equal(vc[n_past + t, h], v[t, h * d:(h + 1) * d].astype(np.float16).view(np.uint16))
+        for h in range(sp["n_head"]):
+            want = rope(norm(q[t, h * d:(h + 1) * d], qn), cs[t])
+            assert np.array_equal(q_roped[t, h].view(np.uint32), want.view(np.uint32))
+
+
+# ---------------------------------------------------------------------------
+# sizing (model.cpp:869-885, 1002-1059)
+# ---------------------------------------------------------------------------
+
+def test_kv_cache_bytes_reference_rule():
+    for sp in specs.specs().values():
+        want = sp["n_layer"] * sp["head_dim"] * sp["n_head_kv"] * 2 * 2 * sp["n_ctx"]
+        assert O.kv_cache_bytes(sp["n_layer"], sp["n_head_kv"], sp["head_dim"], sp["n_ctx"]) == want
+    # 128k llama-3.1-8B cache: 16 GiB
+    assert O.kv_cache_bytes(32, 8, 128, 131072) == 16 * 2 ** 30
+
+
+def test_auto_n_ctx_reference_rule():
+    MiB = 2 ** 20
+    assert O.auto_n_ctx(-1, 1000) == 4096                          # unreadable -> N_CTX_DEFAULT
+    per = 131072                                                   # 128 KiB / position
+    avail = 4096 * MiB
+    raw = int((avail - 384 * MiB) * 0.8) // per
+    assert O.auto_n_ctx(avail, per) == (raw // 64) * 64
+    assert O.auto_n_ctx(avail, per, n_ctx_train=2048) == 2048      # clamp to trained ctx
+    assert O.auto_n_ctx(400 * MiB, per) == 512                     # floor
+    assert O.auto_n_ctx(400 * MiB, per, n_ctx_train=256) == 256    # floor never above the limit
+    assert O.auto_n_ctx(10 ** 15, per) == 262144                   # default cap
+    assert O.auto_n_ctx(10 ** 15, per, 131072, longrope_orig=4096) == 4096
+
+
+# ---------------------------------------------------------------------------
+# golden fixtures (regression pin of the oracle)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("case", G.CASES, ids=[c["name"] for c in G.CASES])
+def test_golden_fixture(case):
+    want = G.load(case)
+    got = G.run_oracle(case)
+    for key in ("k_new", "v_new"):
+        assert np.array_equal(got[key], want[key]), key
+    for key in ("q_roped", "out"):
+        assert np.array_equal(got[key].view(np.uint32), want[key].view(np.uint32)), key
