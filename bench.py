@@ -298,9 +298,7 @@ def run_ours(args, sp):
     ctx.fill_synthetic(sp["seed"], 0, sp["n_past"], stream=stream)
     cyc = max(1, sp["steps"])
     inputs = torch.empty((cyc, L, n_new, W), dtype=torch.float32, device=dev)
-    for s in range(cyc):
-        for l in range(L):
-            K.gen_normal_device(inputs[s, l], sp["seed"], synth.STREAM_QKV + s * 1024 + l, n_new * W, stream=stream)
+    K.gen_normal_device(inputs, sp["seed"], synth.STREAM_QKV, inputs.numel(), stream=stream)
     qn = kn = None
     if sp["qk_norm"]:
         ws = [synth.norm_weights(sp, l) for l in range(L)]
@@ -395,28 +393,33 @@ def run_ours(args, sp):
                         "avg_us": round(v[1] / v[0] * 1e3, 3) if v[0] else None} for k, v in kern.items()}
 
     # end to end through the C ABI with host buffers: H2D inputs, D2H outputs, every step
-    host_in = torch.empty((cyc, L, n_new, W), dtype=torch.float32, pin_memory=True)
-    host_in.copy_(inputs.cpu())
-    host_out = torch.empty((L, n_new, hq * d), dtype=torch.float32, pin_memory=True)
-    staging = torch.empty((L, n_new, W), dtype=torch.float32, device=dev)
-    e2e_steps = args.steps
-    efirst = pfirst + prof_steps
-    barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    for i in range(e2e_steps):
-        s = efirst + i
-        staging.copy_(host_in[s % cyc], non_blocking=True)
-        step(s, src=staging)
-        host_out.copy_(out, non_blocking=True)
-        stream.synchronize()
-    f1.record(stream)
-    f1.synchronize()
-    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
-    epos = positions(sp, efirst, e2e_steps)
-    e2e_value = sum(step_bytes(sp, p, n_new) for p in epos) / (e2e_ms / 1e3) / 1e9
     h2d = L * n_new * W * 4
     d2h = L * n_new * hq * d * 4
+    e2e = None
+    if not args.no_e2e:
+        host_in = torch.empty((cyc, L, n_new, W), dtype=torch.float32, pin_memory=True)
+        host_in.copy_(inputs.cpu())
+        host_out = torch.empty((L, n_new, hq * d), dtype=torch.float32, pin_memory=True)
+        staging = torch.empty((L, n_new, W), dtype=torch.float32, device=dev)
+        e2e_steps = args.steps
+        efirst = pfirst + prof_steps
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for i in range(e2e_steps):
+            s = efirst + i
+            staging.copy_(host_in[s % cyc], non_blocking=True)
+            step(s, src=staging)
+            host_out.copy_(out, non_blocking=True)
+            stream.synchronize()
+        f1.record(stream)
+        f1.synchronize()
+        e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+        epos = positions(sp, efirst, e2e_steps)
+        e2e_value = sum(step_bytes(sp, p, n_new) for p in epos) / (e2e_ms / 1e3) / 1e9
+        e2e = {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "us_per_token": round(e2e_ms / e2e_steps * 1e3, 2),
+               "note": "pinned host inputs copied in and outputs copied out every step, host sync per step"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -451,9 +454,7 @@ def run_ours(args, sp):
                          "algorithmic_bytes_per_launch": int(algo[dom]),
                          "traffic": committed_traffic(sp["name"], "kv_" + dom),
                          "kernels": kernel_table},
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "us_per_token": round(e2e_ms / e2e_steps * 1e3, 2),
-                    "note": "pinned host inputs copied in and outputs copied out every step, host sync per step"},
+            "e2e": e2e,
             "gpu_launches": int(launches),
             "clocks": clocks,
             "cpu_baseline": cpu,
@@ -475,9 +476,15 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) pass")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="override the layer count (small profiling cases only; the bench line is invalid)")
     args = ap.parse_args()
     from kv_b200 import specs
     sp = specs.get(args.config)
+    if args.layers:
+        sp["n_layer"] = args.layers
+        sp["name"] += "-%dlayers" % args.layers
     if args.steps is None:
         args.steps = sp["steps"]
     if args.warmup < 3:
