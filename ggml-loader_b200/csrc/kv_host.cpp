@@ -162,6 +162,12 @@ void build_rope_table(const RopeSpec &r, int64_t n_pos, float *out)
 
 }  // namespace
 
+int kvb::set_last_error(int code, const char *msg)
+{
+    g_last_error = msg ? msg : "";
+    return code;
+}
+
 // ---------------------------------------------------------------------------
 // the context
 // ---------------------------------------------------------------------------

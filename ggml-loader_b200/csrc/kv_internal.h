@@ -93,4 +93,7 @@ cudaError_t launch_fill(const FillParams &p, cudaStream_t st);
 cudaError_t launch_gen_normal(float *dst, uint64_t seed, uint64_t stream, uint64_t idx0, int64_t n,
                               cudaStream_t st);
 
+// Records the detail string kv_last_error() returns on this host thread.
+int set_last_error(int code, const char *msg);
+
 }  // namespace kvb

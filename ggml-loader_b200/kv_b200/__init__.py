@@ -93,6 +93,7 @@ def lib():
         "kv_profile_read": (ctypes.c_int, [_vp, _i32, ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_double)]),
         "kv_kernel_name": (ctypes.c_char_p, [_i32]),
         "kv_launch_count": (_i64, [_vp]),
+        "kv_attend_decode_noalloc": (ctypes.c_int, [_vp, _vp, _i32, _i32, _i32, _i64, _vp, _vp, _vp]),
         "kv_rope_table_host": (ctypes.c_int, [cfgp, _i64, _i64, _vp]),
         "kv_shard_geometry": (ctypes.c_int, [cfgp, _i32] + [ctypes.POINTER(_i32)] * 4),
     }
@@ -297,6 +298,14 @@ class Context:
 
     def launch_count(self):
         return int(lib().kv_launch_count(self.h))
+
+
+def attend_decode_noalloc(k_cache, v_cache, n_head, n_head_kv, head_dim, n_kv, q, out, stream=None):
+    """kv_attend_decode_noalloc: one token's decode attention over caller-owned
+    buffers, with the library's fixed built-in scratch (no device allocation)."""
+    return _check(lib().kv_attend_decode_noalloc(_ptr(k_cache), _ptr(v_cache), n_head, n_head_kv, head_dim, n_kv,
+                                                 _ptr(q), _ptr(out), _stream(stream)),
+                  "kv_attend_decode_noalloc")
 
 
 def gen_normal_device(dst, seed, stream_id, n, idx0=0, stream=None):

@@ -167,6 +167,33 @@ int kv_forward(kv_ctx *ctx, int64_t n_past, int32_t n_new,
                const float *q_norm_w, const float *k_norm_w, int64_t norm_layer_stride,
                float *out, int64_t out_layer_stride, void *stream);
 
+/*
+ * Decode attention that allocates nothing.  No counterpart in the reference:
+ * it exists for callers that cannot call cudaMalloc -- a host framework that
+ * owns and plans all device memory up front (ggml's graph allocator, a serving
+ * engine that reserves HBM for its own pool) and runs this op as a callback in
+ * the middle of its compute, where an allocation would fail for lack of free
+ * memory or stall the device.  Such a caller cannot hold a kv_ctx (kv_alloc
+ * allocates), so it passes its own cache and buffers:
+ *   k_cache, v_cache: one layer's cache, [rows][n_head_kv][head_dim] F16,
+ *                     16-byte aligned; rows [0, n_kv) are attended, the new
+ *                     token's K/V already written at row n_kv-1;
+ *   q:   the new token's rotated query, [n_head][head_dim] F32 (device);
+ *   out: [n_head*head_dim] F32 (device), the layout kv_attend writes.
+ * Same math as kv_attend for one token.  Its scratch is a fixed 8 MiB array
+ * built into the library (held by every GPU that loads it until exit); a call
+ * needs about n_head_kv*rows_per_pass*n_kv*4 bytes of it for scores (rows per
+ * pass: 4 at head_dim 96/128, 8 at 64 -- about 60k keys with 8 KV heads at
+ * head_dim 128, 15k with 32 at 96) and returns KV_E_RANGE, with
+ * kv_last_error() saying so,
+ * when the shape does not fit.  The first call on a device looks up the
+ * array's device address, so make it before any stream capture.  Calls share
+ * the array: calls that overlap on the GPU race and must be serialised.
+ */
+int kv_attend_decode_noalloc(const uint16_t *k_cache, const uint16_t *v_cache,
+                             int32_t n_head, int32_t n_head_kv, int32_t head_dim, int64_t n_kv,
+                             const float *q, float *out, void *stream);
+
 /* Copy cache rows [row0, row0+nrows) of K (which = 0) or V (which = 1) of
  * `layer` to / from host memory in the reference layout [row][head][dim] F16
  * (this context's heads only).  Synchronous.  Used for checking, for the
