@@ -185,14 +185,20 @@ struct kv_ctx {
     int64_t layer_elems = 0;  // n_ctx * hkv_loc * D
     float2 *rope = nullptr;   // [n_ctx][n_rot/2]
     __half *qbuf = nullptr;   // [n_batch_max][hq_loc][D]
-    float *S = nullptr;
+    float *S = nullptr;       // [hkv_loc][8][S_stride]
     int64_t S_stride = 0;
-    float *part_m = nullptr;
+    float *part_m = nullptr;  // [max_cta][2][8]
     double *part_z = nullptr;
-    float *part_o = nullptr;
+    float *part_o = nullptr;  // [max_cta][2][8][D]
     unsigned *counters = nullptr;
+    unsigned *err = nullptr;  // device error word of the bounded waits
     float *local_out = nullptr;   // sharded prefill: [n_batch_max][hq_loc*D]
     float *gathered = nullptr;    // [n_shards][n_batch_max][hq_loc*D]
+    int max_cta = 0;
+    std::vector<CUtensorMap> kmaps, vmaps;  // per layer: [n_ctx][hkv_loc][D] F16, box D x 1 x 64
+    CUtensorMap smap{};                     // scores [hkv_loc*8][S_stride] F32, box 68 x 8
+    uint64_t limit_ns = 1000000000ull;      // bound of every device-side wait (1 s)
+    int inject = 0;                         // test hook, applies to the next decode launch
 
     // state of the last kv_append (kv_attend must follow it)
     int last_layer = -1;
@@ -287,15 +293,49 @@ int launch(kv_ctx *ctx, int kernel_id, cudaStream_t st, const char *what, F &&fn
     return KV_OK;
 }
 
-void choose_splits(const kv_ctx *ctx, int64_t n_kv, int *split_len, int *n_splits)
+// CTAs of the balanced decode split: one per SM, never fewer than the heads
+// (so a CTA's key range spans at most two heads), never more than the rows,
+// and no CTA with less than ~64 keys of work.
+int decode_ctas(const kv_ctx *ctx, int64_t n_kv)
 {
-    const int target = std::max(1, (2 * ctx->sm_count + ctx->hkv_loc - 1) / ctx->hkv_loc);
-    int64_t len = (n_kv + target - 1) / target;
-    len = ((len + 63) / 64) * 64;
-    if (len < 64) len = 64;
-    if (len > ctx->split_max) len = ctx->split_max;
-    *split_len = (int)len;
-    *n_splits = (int)((n_kv + len - 1) / len);
+    const int64_t T = (int64_t)ctx->hkv_loc * n_kv;
+    int64_t c = std::min<int64_t>(ctx->sm_count, (T + 63) / 64);
+    c = std::max<int64_t>(c, ctx->hkv_loc);
+    c = std::min<int64_t>(c, T);
+    return (int)c;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+int encode_map(CUtensorMap *m, CUtensorMapDataType dt, int rank, void *base, const cuuint64_t *dims,
+               const cuuint64_t *strides, const cuuint32_t *box, CUtensorMapSwizzle swizzle)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(KV_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint32_t es[3] = {1, 1, 1};
+    const CUresult r = fn(m, dt, (cuuint32_t)rank, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(KV_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return KV_OK;
 }
 
 void free_all(kv_ctx *ctx)
@@ -310,7 +350,7 @@ void free_all(kv_ctx *ctx)
     if (ctx->comm && nccl().CommDestroy) nccl().CommDestroy(ctx->comm);
     ctx->comm = nullptr;
     void *ptrs[] = {ctx->cache, ctx->rope, ctx->qbuf, ctx->S, ctx->part_m, ctx->part_z,
-                    ctx->part_o, ctx->counters, ctx->local_out, ctx->gathered};
+                    ctx->part_o, ctx->counters, ctx->err, ctx->local_out, ctx->gathered};
     for (void *p : ptrs)
         if (p) cudaFree(p);
 }
@@ -443,26 +483,58 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
         if (e != cudaSuccess) return bail(cuda_fail(e, "RoPE table upload"));
     }
 
-    ctx->S_stride = ((ctx->n_ctx + 3) / 4) * 4;
-    const int target = std::max(1, (2 * ctx->sm_count + ctx->hkv_loc - 1) / ctx->hkv_loc);
-    ctx->max_splits = (int)std::max<int64_t>(target, (ctx->n_ctx + ctx->split_max - 1) / ctx->split_max);
-    const size_t n_part = (size_t)ctx->hkv_loc * (size_t)ctx->max_splits * (size_t)ctx->rmax;
+    // scores rows are padded to 4 floats and one score-tile width past n_ctx,
+    // so a score tile read at a 16-byte-aligned x never leaves the buffer
+    const int stile = kvb::decode3_tile_keys() + 4;
+    ctx->S_stride = ((ctx->n_ctx + 3) / 4) * 4 + stile;
+    ctx->max_cta = std::max(ctx->sm_count, ctx->hkv_loc);
+    const size_t n_part = (size_t)ctx->max_cta * 2u * 8u;
     struct { void **p; size_t bytes; } allocs[] = {
         {(void **)&ctx->qbuf, (size_t)c.n_batch_max * ctx->hq_loc * D * sizeof(__half)},
-        {(void **)&ctx->S, (size_t)ctx->hkv_loc * ctx->rmax * (size_t)ctx->S_stride * sizeof(float)},
+        {(void **)&ctx->S, (size_t)ctx->hkv_loc * 8u * (size_t)ctx->S_stride * sizeof(float)},
         {(void **)&ctx->part_m, n_part * sizeof(float)},
         {(void **)&ctx->part_z, n_part * sizeof(double)},
         {(void **)&ctx->part_o, n_part * (size_t)D * sizeof(float)},
         {(void **)&ctx->counters, (size_t)ctx->hkv_loc * sizeof(unsigned)},
+        {(void **)&ctx->err, sizeof(unsigned)},
     };
     for (auto &a : allocs) {
         e = cudaMalloc(a.p, a.bytes);
         if (e != cudaSuccess) return bail(fail(KV_E_OOM, "scratch allocation (%zu bytes): %s", a.bytes, cudaGetErrorString(e)));
     }
     e = cudaMemset(ctx->counters, 0, (size_t)ctx->hkv_loc * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, sizeof(unsigned));
     if (e != cudaSuccess) return bail(cuda_fail(e, "cudaMemset"));
-    e = kvb::decode_prepare(ctx->D);
-    if (e != cudaSuccess) return bail(cuda_fail(e, "decode_prepare"));
+    e = kvb::decode3_prepare(ctx->D);
+    if (e != cudaSuccess) return bail(cuda_fail(e, "decode3_prepare"));
+
+    // TMA descriptors: each layer's K and V as [n_ctx][hkv_loc][D] F16, box =
+    // one head x 128 keys x a 64-wide column block with 128-byte swizzle (32
+    // wide, 64-byte swizzle at head_dim 96); the scores as [hkv_loc*8][S_stride]
+    // F32, box 132 x 8
+    ctx->kmaps.resize(c.n_layer);
+    ctx->vmaps.resize(c.n_layer);
+    {
+        const int bw = kvb::decode3_box_width(ctx->D);
+        const CUtensorMapSwizzle sw = bw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+        const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)ctx->hkv_loc, (cuuint64_t)ctx->n_ctx};
+        const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)ctx->hkv_loc * D * 2};
+        const cuuint32_t box[3] = {(cuuint32_t)bw, 1, (cuuint32_t)kvb::decode3_tile_keys()};
+        for (int l = 0; l < c.n_layer; l++) {
+            int rc = encode_map(&ctx->kmaps[l], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ctx->k_layer(l), dims, strides,
+                                box, sw);
+            if (rc == KV_OK)
+                rc = encode_map(&ctx->vmaps[l], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ctx->v_layer(l), dims, strides,
+                                box, sw);
+            if (rc != KV_OK) return bail(rc);
+        }
+        const cuuint64_t sdims[2] = {(cuuint64_t)ctx->S_stride, (cuuint64_t)ctx->hkv_loc * 8};
+        const cuuint64_t sstr[1] = {(cuuint64_t)ctx->S_stride * 4};
+        const cuuint32_t sbox[2] = {(cuuint32_t)stile, 8};
+        const int rc = encode_map(&ctx->smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ctx->S, sdims, sstr, sbox,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc != KV_OK) return bail(rc);
+    }
 
     if (c.n_shards > 1) {
         if (!cfg_in->comm_id) return bail(fail(KV_E_ARG, "n_shards > 1 needs comm_id"));
@@ -578,38 +650,41 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     const int64_t dst_stride = direct ? (int64_t)c.n_head * D : (int64_t)ctx->hq_loc * D;
     const int dst_head0 = direct ? ctx->hq0 : 0;
 
-    int split_len = 0, n_splits = 0;
-    choose_splits(ctx, n_kv, &split_len, &n_splits);
-    if (n_splits > ctx->max_splits) return fail(KV_E_RANGE, "internal: %d splits > %d", n_splits, ctx->max_splits);
+    kvb::DecodeParams dp;
+    dp.hkv = ctx->hkv_loc;
+    dp.r = ctx->r;
+    dp.hq_loc = ctx->hq_loc;
+    dp.n_kv = n_kv;
+    dp.n_past = n_past;
+    dp.n_cta = decode_ctas(ctx, n_kv);
+    dp.scale = ctx->scale;
+    dp.qbuf = ctx->qbuf;
+    dp.S = ctx->S;
+    dp.S_stride = ctx->S_stride;
+    dp.part_m = ctx->part_m;
+    dp.part_z = ctx->part_z;
+    dp.part_o = ctx->part_o;
+    dp.counters = ctx->counters;
+    dp.err = ctx->err;
+    dp.limit_ns = ctx->limit_ns;
+    dp.inject = ctx->inject;
+    ctx->inject = 0;
+    dp.out = dst;
+    dp.out_stride = dst_stride;
+    dp.out_head0 = dst_head0;
+    if (dp.n_cta > ctx->max_cta) return fail(KV_E_RANGE, "internal: %d CTAs > %d", dp.n_cta, ctx->max_cta);
 
     const int rows = n_new * ctx->r;
-    for (int row0 = 0; row0 < rows; row0 += ctx->rmax) {
-        const int nrows = std::min(ctx->rmax, rows - row0);
-        kvb::ScoresParams sp;
-        sp.kc = ctx->k_layer(layer);
-        sp.row_elems = (int32_t)(ctx->hkv_loc * D);
-        sp.qbuf = ctx->qbuf;
-        sp.hq_loc = ctx->hq_loc; sp.r = ctx->r;
-        sp.row0 = row0; sp.nrows = nrows;
-        sp.n_past = n_past; sp.n_kv = n_kv;
-        sp.split_len = split_len; sp.n_splits = n_splits;
-        sp.scale = ctx->scale;
-        sp.S = ctx->S; sp.S_stride = ctx->S_stride;
-        sp.part_m = ctx->part_m; sp.part_z = ctx->part_z;
+    const int rows_per = kvb::decode3_rows();
+    const CUtensorMap &km = ctx->kmaps[layer], &vm = ctx->vmaps[layer];
+    for (int row0 = 0; row0 < rows; row0 += rows_per) {
+        dp.row0 = row0;
+        dp.nrows = std::min(rows_per, rows - row0);
         rc = launch(ctx, KV_K_SCORES, st, "scores kernel",
-                    [&] { return kvb::launch_scores(ctx->D, sp, ctx->hkv_loc, st); });
+                    [&] { return kvb::launch_decode3(ctx->D, 0, km, vm, ctx->smap, dp, st); });
         if (rc) return rc;
-        kvb::PVParams pp;
-        pp.vc = ctx->v_layer(layer);
-        pp.row_elems = sp.row_elems;
-        pp.S = ctx->S; pp.S_stride = ctx->S_stride;
-        pp.part_m = ctx->part_m; pp.part_z = ctx->part_z; pp.part_o = ctx->part_o;
-        pp.counters = ctx->counters;
-        pp.r = ctx->r; pp.row0 = row0; pp.nrows = nrows;
-        pp.n_past = n_past; pp.n_kv = n_kv;
-        pp.split_len = split_len; pp.n_splits = n_splits;
-        pp.out = dst; pp.out_stride = dst_stride; pp.out_head0 = dst_head0;
-        rc = launch(ctx, KV_K_PV, st, "P.V kernel", [&] { return kvb::launch_pv(ctx->D, pp, ctx->hkv_loc, st); });
+        rc = launch(ctx, KV_K_PV, st, "P.V kernel",
+                    [&] { return kvb::launch_decode3(ctx->D, 1, km, vm, ctx->smap, dp, st); });
         if (rc) return rc;
     }
 
@@ -709,6 +784,31 @@ const char *kv_strerror(int code)
 }
 
 const char *kv_last_error(void) { return g_last_error.c_str(); }
+
+int kv_status(kv_ctx *ctx, void *stream)
+{
+    if (!ctx) return fail(KV_E_ARG, "NULL context");
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+    KV_CUDA(cudaStreamSynchronize(to_stream(stream)));
+    unsigned word = 0;
+    KV_CUDA(cudaMemcpy(&word, ctx->err, sizeof(word), cudaMemcpyDeviceToHost));
+    if (word == 0) return KV_OK;
+    // a CTA that left early never counted itself in: restart the per-head tickets
+    KV_CUDA(cudaMemset(ctx->counters, 0, (size_t)ctx->hkv_loc * sizeof(unsigned)));
+    KV_CUDA(cudaMemset(ctx->err, 0, sizeof(unsigned)));
+    return fail(KV_E_TIMEOUT, "a device-side wait expired (error word 0x%x); the outputs of that call are invalid",
+                word);
+}
+
+int kv_debug_inject(kv_ctx *ctx, int32_t what, uint64_t limit_ns)
+{
+    if (!ctx) return fail(KV_E_ARG, "NULL context");
+    if (what != 0 && what != 1) return fail(KV_E_ARG, "unknown injection %d", what);
+    ctx->inject = what;
+    if (limit_ns) ctx->limit_ns = limit_ns;
+    return KV_OK;
+}
 
 // ---- kv_bench.h -------------------------------------------------------------
 

@@ -1,6 +1,7 @@
 // kv_internal.h -- shared declarations of the KV path library (host <-> kernels).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -72,6 +73,41 @@ int decode_split_max(int D);
 cudaError_t decode_prepare(int D);   // raises dynamic smem limits once
 cudaError_t launch_scores(int D, const ScoresParams &p, int hkv_loc, cudaStream_t st);
 cudaError_t launch_pv(int D, const PVParams &p, int hkv_loc, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// decode attention (TMA ring, balanced persistent split, mma.sync): kv_decode3.cu
+// ---------------------------------------------------------------------------
+struct DecodeParams {
+    int32_t hkv, r, hq_loc;          // local KV heads, GQA group, local query heads
+    int64_t n_kv, n_past;
+    int32_t row0, nrows;             // query rows of this launch, nrows <= decode3_rows()
+    int32_t n_cta;                   // CTAs; hkv <= n_cta <= hkv*n_kv
+    float scale;
+    const __half *qbuf;              // [n_new][hq_loc][D]
+    float *S;                        // [hkv][8][S_stride]
+    int64_t S_stride;
+    float *part_m;                   // [n_cta][2][8]
+    double *part_z;
+    float *part_o;                   // [n_cta][2][8][D]
+    unsigned *counters;              // [hkv], zero between calls
+    unsigned *err;                   // error word (bit 0: consumer wait expired, bit 1: producer)
+    uint64_t limit_ns;               // bound of every mbarrier wait
+    int32_t inject;                  // test hook: 1 = producer withholds tile 1
+    float *out;
+    int64_t out_stride;
+    int32_t out_head0;
+};
+
+// kv_decode3.cu: query rows per launch (8), keys per tile (128), and the
+// column-box width of the K/V tensor maps (64 halves with 128-byte swizzle,
+// 32 with 64-byte swizzle for head_dim 96).
+int decode3_rows();
+int decode3_tile_keys();
+int decode3_box_width(int D);
+cudaError_t decode3_prepare(int D);
+// which: 0 = scores pass, 1 = P.V pass.
+cudaError_t launch_decode3(int D, int which, const CUtensorMap &kmap, const CUtensorMap &vmap,
+                           const CUtensorMap &smap, const DecodeParams &p, cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // gather / layout helpers

@@ -94,6 +94,8 @@ def lib():
         "kv_kernel_name": (ctypes.c_char_p, [_i32]),
         "kv_launch_count": (_i64, [_vp]),
         "kv_attend_decode_noalloc": (ctypes.c_int, [_vp, _vp, _i32, _i32, _i32, _i64, _vp, _vp, _vp]),
+        "kv_status": (ctypes.c_int, [_vp, _vp]),
+        "kv_debug_inject": (ctypes.c_int, [_vp, _i32, _u64]),
         "kv_rope_table_host": (ctypes.c_int, [cfgp, _i64, _i64, _vp]),
         "kv_shard_geometry": (ctypes.c_int, [cfgp, _i32] + [ctypes.POINTER(_i32)] * 4),
     }
@@ -103,15 +105,6 @@ def lib():
         fn.argtypes = args
     _lib = L
     return L
-
-
-def exported_symbols():
-    """Names this binding expects the library to export."""
-    return ["kv_config_init", "kv_cache_bytes", "kv_auto_n_ctx", "kv_alloc", "kv_free", "kv_n_ctx",
-            "kv_append", "kv_attend", "kv_forward", "kv_export_rows", "kv_import_rows", "kv_shard_info",
-            "kv_comm_unique_id", "kv_strerror", "kv_last_error", "kv_fill_synthetic",
-            "kv_gen_normal_device", "kv_profile_enable", "kv_profile_reset", "kv_profile_read",
-            "kv_kernel_name", "kv_launch_count"]
 
 
 def strerror(code):
@@ -298,6 +291,13 @@ class Context:
 
     def launch_count(self):
         return int(lib().kv_launch_count(self.h))
+
+    def status(self, stream=None):
+        """KV_OK, or KV_E_TIMEOUT if a bounded device-side wait expired (raises)."""
+        return _check(lib().kv_status(self.h, _stream(stream)), "kv_status")
+
+    def debug_inject(self, what, limit_ns=0):
+        _check(lib().kv_debug_inject(self.h, what, limit_ns), "kv_debug_inject")
 
 
 def attend_decode_noalloc(k_cache, v_cache, n_head, n_head_kv, head_dim, n_kv, q, out, stream=None):

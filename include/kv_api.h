@@ -213,6 +213,12 @@ int kv_shard_info(const kv_ctx *ctx, int32_t *q_head0, int32_t *n_q_heads,
  * (libnccl.so.2) cannot be loaded. */
 int kv_comm_unique_id(void *id_out);
 
+/* Deferred device-side errors: waits for `stream`, then returns KV_E_TIMEOUT
+ * (and clears the record) if a bounded wait inside one of this context's
+ * kernels expired since the last check -- the outputs of that call are not
+ * valid -- else KV_OK.  The context stays usable either way. */
+int kv_status(kv_ctx *ctx, void *stream);
+
 const char *kv_strerror(int code);
 /* Detail of the last failing call on this host thread ("" if none). */
 const char *kv_last_error(void);

@@ -45,6 +45,13 @@ const char *kv_kernel_name(int32_t kernel);
 /* Number of kernels this library launched since kv_alloc (host-side count). */
 int64_t kv_launch_count(const kv_ctx *ctx);
 
+/* Failure injection for tests.  what = 1: in the next decode launch the tile
+ * producer withholds one tile, so the consumers' bounded wait expires (the
+ * call's output is invalid and kv_status reports KV_E_TIMEOUT; no fault, no
+ * hang).  limit_ns > 0 also sets the bound of every device-side wait of this
+ * context (default 1 s); 0 keeps it. */
+int kv_debug_inject(kv_ctx *ctx, int32_t what, uint64_t limit_ns);
+
 /* Host-only pieces of kv_alloc, callable without a GPU (for checking):
  * the (cos, sin) RoPE table kv_alloc uploads, rows pos0 .. pos0+npos-1,
  * out[(p*(n_rot/2) + i)*2 + {0,1}]; and the heads shard `shard` of

@@ -309,3 +309,27 @@ def test_auto_n_ctx_allocation(cuda):
     cfg = K.make_config(sp, n_ctx=0)
     with K.Context(cfg) as ctx:
         assert ctx.n_ctx == 8192
+
+
+def test_expired_wait_reports_timeout_and_context_recovers(cuda):
+    """Failure detection without a fault: the test hook makes the tile producer
+    withhold one tile, so the consumers' bounded mbarrier wait (shortened to
+    50 ms here) expires.  The kernel records the error word and returns; the
+    host reads KV_E_TIMEOUT from kv_status, and the next call is correct."""
+    case = dict(name="inject", spec="llama3.2-3b", n_ctx=4096, n_past=3000, n_new=1)
+    run = Run(case, cuda)
+    sp = run.sp
+    rows = synth.qkv_rows(sp, 0, 0, 1)
+    run.ctx.debug_inject(1, limit_ns=50_000_000)
+    run.step(rows, 3000)
+    with pytest.raises(K.KvError) as e:
+        run.ctx.status()
+    assert e.value.code == K.KV_E_TIMEOUT
+    assert run.ctx.status() == K.KV_OK          # the record was cleared
+    out = run.step(rows, 3000)                   # same call again, no injection
+    assert run.ctx.status() == K.KV_OK
+    kc, vc = _oracle_layer(sp, 4096, 3000)
+    orc = O.Oracle(sp)
+    q, k, v = _split(sp, rows)
+    qr = orc.append(kc, vc, 3000, q, k, v)
+    assert_close(out, orc.attend(kc, vc, 3000, qr))
