@@ -171,6 +171,17 @@ int kvb::set_last_error(int code, const char *msg)
 // ---------------------------------------------------------------------------
 // the context
 // ---------------------------------------------------------------------------
+struct Pending {
+    bool on = false;
+    int layer = -1;
+    int64_t n_past = 0;
+    int n_new = 0;
+    const float *q = nullptr, *k = nullptr, *v = nullptr;
+    int64_t q_stride = 0, k_stride = 0, v_stride = 0;
+    const float *qn = nullptr, *kn = nullptr;
+    cudaStream_t st = nullptr;
+};
+
 struct kv_ctx {
     kv_config cfg{};
     std::vector<float> freq_factors;
@@ -195,11 +206,12 @@ struct kv_ctx {
     float *local_out = nullptr;   // sharded prefill: [n_batch_max][hq_loc*D]
     float *gathered = nullptr;    // [n_shards][n_batch_max][hq_loc*D]
     int max_cta = 0;
-    std::vector<CUtensorMap> kmaps, vmaps;  // per layer: [n_ctx][hkv_loc][D] F16, box D x 1 x 64
-    CUtensorMap smap{};                     // scores [hkv_loc*8][S_stride] F32, box 68 x 8
+    std::vector<CUtensorMap> kmaps, vmaps;  // per layer: [n_ctx][hkv_loc][D] F16, swizzled column boxes
+    CUtensorMap smap{};                     // scores [hkv_loc*8][S_stride] F32
     uint64_t limit_ns = 1000000000ull;      // bound of every device-side wait (1 s)
     int inject = 0;                         // test hook, applies to the next decode launch
 
+    Pending pend;  // a deferred single-token kv_append
     // state of the last kv_append (kv_attend must follow it)
     int last_layer = -1;
     int64_t last_n_past = -1;
@@ -238,6 +250,7 @@ bool shape_ok(const kv_config *c, std::string &why)
     if (c->rope_ext_factor != 0.0f && c->n_ctx_orig <= 0) { why = "YaRN (ext_factor != 0) needs n_ctx_orig > 0"; return false; }
     const int ns = c->n_shards <= 1 ? 1 : c->n_shards;
     if (c->n_head_kv % ns != 0) { why = "n_head_kv must be a multiple of n_shards"; return false; }
+    if (c->n_head_kv / ns > kvb::kMaxLocalHeads) { why = "more than 64 KV heads per shard"; return false; }
     if (ns > 1 && (c->shard < 0 || c->shard >= ns)) { why = "shard out of range"; return false; }
     if (c->n_batch_max < 0) { why = "n_batch_max must be >= 0"; return false; }
     return true;
@@ -353,6 +366,34 @@ void free_all(kv_ctx *ctx)
                     ctx->part_o, ctx->counters, ctx->err, ctx->local_out, ctx->gathered};
     for (void *p : ptrs)
         if (p) cudaFree(p);
+}
+
+
+// The single-token append a kv_append deferred to the following kv_attend.
+int run_append(kv_ctx *ctx, const Pending &pd)
+{
+    const kv_config &c = ctx->cfg;
+    kvb::AppendParams p;
+    p.q = pd.q; p.k = pd.k; p.v = pd.v;
+    p.q_stride = pd.q_stride; p.k_stride = pd.k_stride; p.v_stride = pd.v_stride;
+    p.q_norm_w = pd.qn; p.k_norm_w = pd.kn;
+    p.n_new = pd.n_new; p.n_past = pd.n_past;
+    p.hq_loc = ctx->hq_loc; p.hkv_loc = ctx->hkv_loc; p.hq0 = ctx->hq0; p.hkv0 = ctx->hkv0;
+    p.n_rot = c.n_rot; p.rope_mode = c.rope_mode; p.qk_norm = c.qk_norm; p.eps = c.rms_eps;
+    p.rope = ctx->rope;
+    p.kc = ctx->k_layer(pd.layer); p.vc = ctx->v_layer(pd.layer);
+    p.qbuf = ctx->qbuf;
+    auto al16 = [](const void *x) { return ((uintptr_t)x & 15u) == 0; };
+    const bool vec = al16(pd.q) && al16(pd.k) && al16(pd.v) &&
+                     (pd.n_new == 1 || ((pd.q_stride | pd.k_stride | pd.v_stride) & 3) == 0);
+    return launch(ctx, KV_K_APPEND, pd.st, "append kernel", [&] { return kvb::launch_append(ctx->D, vec, p, pd.st); });
+}
+
+int flush_pending(kv_ctx *ctx)
+{
+    if (!ctx->pend.on) return KV_OK;
+    ctx->pend.on = false;
+    return run_append(ctx, ctx->pend);
 }
 
 }  // namespace
@@ -485,7 +526,7 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
 
     // scores rows are padded to 4 floats and one score-tile width past n_ctx,
     // so a score tile read at a 16-byte-aligned x never leaves the buffer
-    const int stile = kvb::decode3_tile_keys() + 4;
+    const int stile = kvb::attn_tile_keys() + 4;
     ctx->S_stride = ((ctx->n_ctx + 3) / 4) * 4 + stile;
     ctx->max_cta = std::max(ctx->sm_count, ctx->hkv_loc);
     const size_t n_part = (size_t)ctx->max_cta * 2u * 8u;
@@ -505,8 +546,8 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
     e = cudaMemset(ctx->counters, 0, (size_t)ctx->hkv_loc * sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, sizeof(unsigned));
     if (e != cudaSuccess) return bail(cuda_fail(e, "cudaMemset"));
-    e = kvb::decode3_prepare(ctx->D);
-    if (e != cudaSuccess) return bail(cuda_fail(e, "decode3_prepare"));
+    e = kvb::attn_prepare(ctx->D);
+    if (e != cudaSuccess) return bail(cuda_fail(e, "attn_prepare"));
 
     // TMA descriptors: each layer's K and V as [n_ctx][hkv_loc][D] F16, box =
     // one head x 128 keys x a 64-wide column block with 128-byte swizzle (32
@@ -515,11 +556,11 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
     ctx->kmaps.resize(c.n_layer);
     ctx->vmaps.resize(c.n_layer);
     {
-        const int bw = kvb::decode3_box_width(ctx->D);
+        const int bw = kvb::attn_box_width(ctx->D);
         const CUtensorMapSwizzle sw = bw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
         const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)ctx->hkv_loc, (cuuint64_t)ctx->n_ctx};
         const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)ctx->hkv_loc * D * 2};
-        const cuuint32_t box[3] = {(cuuint32_t)bw, 1, (cuuint32_t)kvb::decode3_tile_keys()};
+        const cuuint32_t box[3] = {(cuuint32_t)bw, 1, (cuuint32_t)kvb::attn_tile_keys()};
         for (int l = 0; l < c.n_layer; l++) {
             int rc = encode_map(&ctx->kmaps[l], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ctx->k_layer(l), dims, strides,
                                 box, sw);
@@ -609,26 +650,28 @@ int kv_append(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
     if (c.qk_norm && (!q_norm_w || !k_norm_w)) return fail(KV_E_ARG, "qk_norm needs q_norm_w and k_norm_w");
     int rc = ensure_device(ctx);
     if (rc) return rc;
-
-    kvb::AppendParams p;
-    p.q = q; p.k = k; p.v = v;
-    p.q_stride = q_stride; p.k_stride = k_stride; p.v_stride = v_stride;
-    p.q_norm_w = q_norm_w; p.k_norm_w = k_norm_w;
-    p.n_new = n_new; p.n_past = n_past;
-    p.hq_loc = ctx->hq_loc; p.hkv_loc = ctx->hkv_loc; p.hq0 = ctx->hq0; p.hkv0 = ctx->hkv0;
-    p.n_rot = c.n_rot; p.rope_mode = c.rope_mode; p.qk_norm = c.qk_norm; p.eps = c.rms_eps;
-    p.rope = ctx->rope;
-    p.kc = ctx->k_layer(layer); p.vc = ctx->v_layer(layer);
-    p.qbuf = ctx->qbuf;
-    auto al16 = [](const void *x) { return ((uintptr_t)x & 15u) == 0; };
-    const bool vec = al16(q) && al16(k) && al16(v) && (n_new == 1 || ((q_stride | k_stride | v_stride) & 3) == 0);
-    rc = launch(ctx, KV_K_APPEND, to_stream(stream), "append kernel",
-                [&] { return kvb::launch_append(ctx->D, vec, p, to_stream(stream)); });
+    rc = flush_pending(ctx);
     if (rc) return rc;
+
+    Pending pd;
+    pd.on = true;
+    pd.layer = layer;
+    pd.n_past = n_past;
+    pd.n_new = n_new;
+    pd.q = q; pd.k = k; pd.v = v;
+    pd.q_stride = q_stride; pd.k_stride = k_stride; pd.v_stride = v_stride;
+    pd.qn = q_norm_w; pd.kn = k_norm_w;
+    pd.st = to_stream(stream);
     ctx->last_layer = layer;
     ctx->last_n_past = n_past;
     ctx->last_n_new = n_new;
-    return KV_OK;
+    if (n_new == 1 && ctx->r <= kvb::attn_rows()) {
+        // one token: the attention kernels do the append themselves (same bits);
+        // any other call on this context first performs it with the append kernel
+        ctx->pend = pd;
+        return KV_OK;
+    }
+    return run_append(ctx, pd);
 }
 
 int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *out, void *stream)
@@ -642,6 +685,16 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     if (rc) return rc;
     const kv_config &c = ctx->cfg;
     const cudaStream_t st = to_stream(stream);
+    // the deferred single-token append runs inside the attention kernels when it
+    // belongs to this call and stream; otherwise it is performed now
+    const bool fused = ctx->pend.on && ctx->pend.layer == layer && ctx->pend.n_past == n_past &&
+                       ctx->pend.n_new == 1 && n_new == 1 && ctx->pend.st == st;
+    const Pending pd = ctx->pend;
+    if (fused) ctx->pend.on = false;
+    else {
+        rc = flush_pending(ctx);
+        if (rc) return rc;
+    }
     const int64_t D = ctx->D;
     const int64_t n_kv = n_past + n_new;
     const bool sharded = c.n_shards > 1;
@@ -650,41 +703,74 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     const int64_t dst_stride = direct ? (int64_t)c.n_head * D : (int64_t)ctx->hq_loc * D;
     const int dst_head0 = direct ? ctx->hq0 : 0;
 
-    kvb::DecodeParams dp;
-    dp.hkv = ctx->hkv_loc;
-    dp.r = ctx->r;
-    dp.hq_loc = ctx->hq_loc;
-    dp.n_kv = n_kv;
-    dp.n_past = n_past;
-    dp.n_cta = decode_ctas(ctx, n_kv);
-    dp.scale = ctx->scale;
-    dp.qbuf = ctx->qbuf;
-    dp.S = ctx->S;
-    dp.S_stride = ctx->S_stride;
-    dp.part_m = ctx->part_m;
-    dp.part_z = ctx->part_z;
-    dp.part_o = ctx->part_o;
-    dp.counters = ctx->counters;
-    dp.err = ctx->err;
-    dp.limit_ns = ctx->limit_ns;
-    dp.inject = ctx->inject;
+    kvb::AttnParams ap{};
+    ap.hkv = ctx->hkv_loc;
+    ap.r = ctx->r;
+    ap.hq_loc = ctx->hq_loc;
+    ap.hq0 = ctx->hq0;
+    ap.hkv0 = ctx->hkv0;
+    ap.n_kv = n_kv;
+    ap.n_past = n_past;
+    ap.n_cta = decode_ctas(ctx, n_kv);
+    ap.scale = ctx->scale;
+    ap.fused = fused ? 1 : 0;
+    ap.q = pd.q;
+    ap.k = pd.k;
+    ap.v = pd.v;
+    ap.q_stride = pd.q_stride;
+    ap.q_norm_w = pd.qn;
+    ap.k_norm_w = pd.kn;
+    ap.qk_norm = c.qk_norm;
+    ap.n_rot = c.n_rot;
+    ap.rope_mode = c.rope_mode;
+    ap.eps = c.rms_eps;
+    ap.rope = ctx->rope;
+    ap.kc = ctx->k_layer(layer);
+    ap.vc = ctx->v_layer(layer);
+    ap.qbuf = ctx->qbuf;
+    ap.S = ctx->S;
+    ap.S_stride = ctx->S_stride;
+    ap.part_m = ctx->part_m;
+    ap.part_z = ctx->part_z;
+    ap.part_o = ctx->part_o;
+    ap.counters = ctx->counters;
+    ap.err = ctx->err;
+    ap.limit_ns = ctx->limit_ns;
+    ap.inject = ctx->inject;
     ctx->inject = 0;
-    dp.out = dst;
-    dp.out_stride = dst_stride;
-    dp.out_head0 = dst_head0;
-    if (dp.n_cta > ctx->max_cta) return fail(KV_E_RANGE, "internal: %d CTAs > %d", dp.n_cta, ctx->max_cta);
+    ap.out = dst;
+    ap.out_stride = dst_stride;
+    ap.out_head0 = dst_head0;
+    if (ap.n_cta > ctx->max_cta) return fail(KV_E_RANGE, "internal: %d CTAs > %d", ap.n_cta, ctx->max_cta);
+    {
+        // CTA c covers flattened rows [c*T/C, (c+1)*T/C) (the kernels' split)
+        const int64_t T = (int64_t)ctx->hkv_loc * n_kv, C = ap.n_cta;
+        auto lo = [&](int64_t cc) { return cc * T / C; };
+        auto cta_of = [&](int64_t x) {
+            int64_t cc = std::min<int64_t>(C - 1, x * C / T);
+            while (cc + 1 < C && lo(cc + 1) <= x) cc++;
+            while (cc > 0 && lo(cc) > x) cc--;
+            return cc;
+        };
+        for (int h = 0; h < ctx->hkv_loc; h++) {
+            const int64_t a = cta_of((int64_t)h * n_kv), b = cta_of((int64_t)(h + 1) * n_kv - 1);
+            ap.span_a[h] = (int16_t)a;
+            ap.span_b[h] = (int16_t)b;
+            ap.span_slot[h] = (int8_t)(lo(a) < (int64_t)h * n_kv ? 1 : 0);
+        }
+    }
 
     const int rows = n_new * ctx->r;
-    const int rows_per = kvb::decode3_rows();
+    const int rows_per = kvb::attn_rows();
     const CUtensorMap &km = ctx->kmaps[layer], &vm = ctx->vmaps[layer];
     for (int row0 = 0; row0 < rows; row0 += rows_per) {
-        dp.row0 = row0;
-        dp.nrows = std::min(rows_per, rows - row0);
-        rc = launch(ctx, KV_K_SCORES, st, "scores kernel",
-                    [&] { return kvb::launch_decode3(ctx->D, 0, km, vm, ctx->smap, dp, st); });
+        ap.row0 = row0;
+        ap.nrows = std::min(rows_per, rows - row0);
+        rc = launch(ctx, KV_K_SCORES, st, "attention scores kernel",
+                    [&] { return kvb::launch_attn(ctx->D, 0, km, vm, ctx->smap, ap, st, true); });
         if (rc) return rc;
-        rc = launch(ctx, KV_K_PV, st, "P.V kernel",
-                    [&] { return kvb::launch_decode3(ctx->D, 1, km, vm, ctx->smap, dp, st); });
+        rc = launch(ctx, KV_K_PV, st, "attention P.V kernel",
+                    [&] { return kvb::launch_attn(ctx->D, 1, km, vm, ctx->smap, ap, st, true); });
         if (rc) return rc;
     }
 
@@ -735,6 +821,8 @@ static int rows_io(kv_ctx *ctx, int32_t layer, int32_t which, int64_t row0, int6
         return fail(KV_E_ARG, "bad layer or which");
     if (row0 < 0 || nrows < 0 || row0 + nrows > ctx->n_ctx) return fail(KV_E_RANGE, "rows outside the cache");
     int rc = ensure_device(ctx);
+    if (rc) return rc;
+    rc = flush_pending(ctx);
     if (rc) return rc;
     __half *base = (which == 0 ? ctx->k_layer(layer) : ctx->v_layer(layer)) + row0 * (int64_t)ctx->hkv_loc * ctx->D;
     const size_t bytes = (size_t)nrows * ctx->hkv_loc * ctx->D * sizeof(__half);
@@ -790,6 +878,8 @@ int kv_status(kv_ctx *ctx, void *stream)
     if (!ctx) return fail(KV_E_ARG, "NULL context");
     int rc = ensure_device(ctx);
     if (rc) return rc;
+    rc = flush_pending(ctx);
+    if (rc) return rc;
     KV_CUDA(cudaStreamSynchronize(to_stream(stream)));
     unsigned word = 0;
     KV_CUDA(cudaMemcpy(&word, ctx->err, sizeof(word), cudaMemcpyDeviceToHost));
@@ -817,6 +907,8 @@ int kv_fill_synthetic(kv_ctx *ctx, uint64_t seed, uint64_t stream_base, int64_t 
     if (!ctx) return fail(KV_E_ARG, "NULL context");
     if (row0 < 0 || nrows < 0 || row0 + nrows > ctx->n_ctx) return fail(KV_E_RANGE, "rows outside the cache");
     int rc = ensure_device(ctx);
+    if (rc) return rc;
+    rc = flush_pending(ctx);
     if (rc) return rc;
     kvb::FillParams p;
     p.cache = ctx->cache;

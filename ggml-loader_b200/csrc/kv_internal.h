@@ -75,15 +75,30 @@ cudaError_t launch_scores(int D, const ScoresParams &p, int hkv_loc, cudaStream_
 cudaError_t launch_pv(int D, const PVParams &p, int hkv_loc, cudaStream_t st);
 
 // ---------------------------------------------------------------------------
-// decode attention (TMA ring, balanced persistent split, mma.sync): kv_decode3.cu
+// attention of kv_attend (kv_attend.cu): two TMA-fed, tensor-core kernels
+// per layer, chained with programmatic dependent launch
 // ---------------------------------------------------------------------------
-struct DecodeParams {
+constexpr int kMaxLocalHeads = 64;   // KV heads one context may own
+
+struct AttnParams {
     int32_t hkv, r, hq_loc;          // local KV heads, GQA group, local query heads
+    int32_t hq0, hkv0;               // first owned global head (inputs are replicated rows)
     int64_t n_kv, n_past;
-    int32_t row0, nrows;             // query rows of this launch, nrows <= decode3_rows()
+    int32_t row0, nrows;             // query rows of this launch (row = t*r + j), nrows <= attn_rows()
     int32_t n_cta;                   // CTAs; hkv <= n_cta <= hkv*n_kv
     float scale;
+    // single-token append done inside the kernels (decode): fused = 1
+    int32_t fused;
+    const float *q, *k, *v;          // token 0's Q/K/V blocks (global heads)
+    int64_t q_stride;
+    const float *q_norm_w, *k_norm_w;
+    int32_t qk_norm, n_rot, rope_mode;
+    float eps;
+    const float2 *rope;              // [n_ctx][n_rot/2]
+    __half *kc, *vc;                 // this layer's cache [n_ctx][hkv][D] (new rows written here)
+    // multi-token: rotated Q from the append kernel
     const __half *qbuf;              // [n_new][hq_loc][D]
+    // scratch
     float *S;                        // [hkv][8][S_stride]
     int64_t S_stride;
     float *part_m;                   // [n_cta][2][8]
@@ -92,22 +107,26 @@ struct DecodeParams {
     unsigned *counters;              // [hkv], zero between calls
     unsigned *err;                   // error word (bit 0: consumer wait expired, bit 1: producer)
     uint64_t limit_ns;               // bound of every mbarrier wait
-    int32_t inject;                  // test hook: 1 = producer withholds tile 1
+    int32_t inject;                  // test hook: 1 = producers withhold tile 1
+    // output
     float *out;
     int64_t out_stride;
     int32_t out_head0;
+    // CTAs [span_a[h], span_b[h]] cover local head h; span_slot[h] is the
+    // segment index head h has in CTA span_a[h] (1 when that CTA starts in head h-1)
+    int16_t span_a[kMaxLocalHeads], span_b[kMaxLocalHeads];
+    int8_t span_slot[kMaxLocalHeads];
 };
 
-// kv_decode3.cu: query rows per launch (8), keys per tile (128), and the
-// column-box width of the K/V tensor maps (64 halves with 128-byte swizzle,
-// 32 with 64-byte swizzle for head_dim 96).
-int decode3_rows();
-int decode3_tile_keys();
-int decode3_box_width(int D);
-cudaError_t decode3_prepare(int D);
-// which: 0 = scores pass, 1 = P.V pass.
-cudaError_t launch_decode3(int D, int which, const CUtensorMap &kmap, const CUtensorMap &vmap,
-                           const CUtensorMap &smap, const DecodeParams &p, cudaStream_t st);
+// query rows per launch (8), keys per tile (128), and the column-box width of
+// the K/V tensor maps (64 halves, 128-byte swizzle; 32, 64-byte swizzle at 96)
+int attn_rows();
+int attn_tile_keys();
+int attn_box_width(int D);
+cudaError_t attn_prepare(int D);
+// which: 0 = scores pass, 1 = P.V pass; pdl: launch as a programmatic dependent
+cudaError_t launch_attn(int D, int which, const CUtensorMap &kmap, const CUtensorMap &vmap, const CUtensorMap &smap,
+                        const AttnParams &p, cudaStream_t st, bool pdl);
 
 // ---------------------------------------------------------------------------
 // gather / layout helpers
