@@ -373,19 +373,22 @@ def run_ours(args, sp):
         step(pfirst + i)
     torch.cuda.synchronize()
     kern = {}
-    for name in ("append", "scores", "pv", "gather"):
+    for name in ("append", "attn", "gather"):
         n, tms = ctx.profile_read(name)
         kern[name] = (n, tms)
     ctx.profile(False)
     ppos = positions(sp, pfirst, prof_steps)
     mean_nkv = statistics.mean(p + n_new for p in ppos)
     hkv_l, hq_l = hkv // world, hq // world
+    # per launch: a decode launch performs the append itself (no append kernel
+    # runs), so it carries the layer's whole byte count
+    append_bytes = n_new * (hkv_l * d * (4 * 2 + 2 * 2) + hq_l * d * 4)
+    layer_total = layer_bytes(sp, mean_nkv, n_new, world)
     algo = {
-        "scores": mean_nkv * hkv_l * d * 2,
-        "pv": mean_nkv * hkv_l * d * 2 + n_new * hq_l * d * 4,
-        "append": n_new * (hkv_l * d * (4 * 2 + 2 * 2) + hq_l * d * 4),
+        "append": append_bytes,
+        "attn": layer_total - (append_bytes if kern["append"][0] else 0),
     }
-    dom = max(("scores", "pv"), key=lambda k: kern[k][1])
+    dom = "attn"
     n_dom, t_dom = kern[dom]
     peak, peak_kind = measured_peak()
     achieved = algo[dom] / (t_dom / n_dom / 1e3) / 1e9 if n_dom else None

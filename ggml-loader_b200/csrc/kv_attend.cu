@@ -1,38 +1,45 @@
-// kv_attend.cu -- decode attention of kv_attend: two TMA-fed, tensor-core,
-// programmatic-dependent-launch kernels per layer.
+// kv_attend.cu -- attention of kv_attend: one TMA-fed, tensor-core kernel per
+// layer (and per group of <= 8 query rows), chained to its neighbours with
+// programmatic dependent launch.
 //
 // Numerics: the reference's default attention branch (src/model.cpp:1416-1445):
 // scores = F16(q) . K accumulated in F32, softmax with the global max and sum,
-// p = F16(expf(s - max) * (1/sum)), out = p . V accumulated in F32.  The two
-// passes exist because ggml rounds the *normalised* p to F16 (its mul_mat
-// converts the F32 operand), which needs the global max and sum first.
+// p = F16(expf(s - max) * (1/sum)), out = p . V accumulated in F32.  ggml rounds
+// the *normalised* p to F16 (its mul_mat converts the F32 operand), so no p can
+// be formed before the head's global max and sum are known: the kernel runs a K
+// phase, a per-head statistics exchange, then a V phase.
 //
-// Layout of the work: the layer's Hkv*n_kv (head, key) rows, head-major, are cut
-// into C equal contiguous ranges, one CTA each (C <= SMs, C >= heads), so every
-// SM streams the same number of bytes and a CTA spans at most two heads.
+// Work split: the layer's Hkv*n_kv (head, key) rows, head-major, are cut into C
+// equal contiguous ranges, one CTA each (hkv <= C <= SMs, one CTA per SM, so
+// all CTAs are resident together), every SM streams the same number of bytes
+// and a CTA spans at most two heads (two "segments").
 //
-// attn_scores_kernel (pass 1)
-//   * warp 8 streams 128-key tiles of K (64-wide boxes, 128-byte swizzle; 32-wide,
-//     64-byte swizzle at head_dim 96) with cp.async.bulk.tensor into a 4-5 stage
-//     mbarrier ring; warps 0-7 take 16 keys each and compute S = K . Q^T with
-//     mma.m16n8k16 (F16 x F16 -> F32; the GQA group's query rows are N <= 8);
-//   * decode (one new token): the kernel performs the append.  Each CTA rotates
-//     (and RMS-normalises, qwen3) the query rows of both its heads up front, the
-//     CTA that owns a head's new key rotates that K row, writes it to the cache
-//     and patches it into its staged tile -- bit-identical to kv_append; the RoPE
-//     entries are fetched before griddepcontrol.wait (the table is constant);
-//   * writes the scaled scores and per-(CTA, segment, row) max / sum of exp.
-// attn_pv_kernel (pass 2), a programmatic dependent of pass 1:
-//   * its producer streams the V tiles of existing rows before
-//     griddepcontrol.wait (V does not depend on pass 1), then the score tiles;
-//   * folds the partial max/sum of its heads (host-computed CTA spans), forms
-//     p = F16(expf(s-M)/Z) directly as the mma B fragment, O^T += V^T . P^T
-//     (ldmatrix.trans); rows past the valid keys are zeroed first so stale rows
-//     never reach the sum; writes the new V row (decode) and patches its tile;
-//   * per-(CTA, segment) partial outputs; the last CTA of each head adds them in
-//     CTA order (deterministic), all loads in flight, after its own loop.
-// Every mbarrier wait is bounded (limit_ns): an expired wait sets the error word
-// read by kv_status, and the CTA drains its own tile loads before leaving.
+// attn_decode_kernel
+//   * warp 8 streams the range's K tiles (128 keys; 64-wide boxes with 128-byte
+//     swizzle, 32-wide with 64-byte swizzle at head_dim 96) and straight after
+//     them its V tiles through one NS-stage mbarrier ring (cp.async.bulk.tensor),
+//     so HBM never waits for the phase change;
+//   * K phase: warps 0-7 take 16 keys of a tile each and compute S = K . Q^T with
+//     mma.m16n8k16 (F16 x F16 -> F32; the GQA group's query rows are N <= 8).
+//     Scores go to per-CTA scratch in the order the V phase reads them back,
+//     running max / sum of exp stay in registers;
+//   * decode (one new token) performs the append: every CTA rotates (and
+//     RMS-normalises, qwen3) the query rows of its heads, the CTA that owns a
+//     head's new row rotates the K row, writes K and V to the cache and patches
+//     them into its staged tiles -- bit-identical to kv_append;
+//   * statistics: each CTA publishes its (max, sum) per (segment, row) and counts
+//     itself in on a per-head ticket, then waits (bounded) for the other CTAs of
+//     its heads while the producer keeps filling the ring with V;
+//   * V phase: p = F16(expf(s - M) / Z) formed directly as the mma B fragment,
+//     O^T += V^T . P^T (ldmatrix.trans); rows past the valid keys are zeroed so
+//     stale data never reaches the sum; the scores come back through a
+//     per-thread cp.async ring;
+//   * output: each (CTA, segment) partial is added into a per-head fixed-point
+//     accumulator (2^-40) with 64-bit integer atomics -- exact, so the result
+//     does not depend on the order CTAs finish -- and the head's last CTA
+//     converts it to F32, writes the output and clears the accumulator.
+// Every wait is bounded (limit_ns): an expired wait sets the error word read by
+// kv_status, and the CTA drains its own tile loads before leaving.
 #include <math.h>
 
 #include "kv_internal.h"
@@ -46,13 +53,17 @@ using namespace sm100;
 constexpr int kTK = 128;         // keys per tile (8 warps x 16)
 constexpr int kConsumers = 256;  // warps 0-7
 constexpr int kThreads = 288;    // + producer warp 8
-constexpr int kRows = 8;         // query rows per launch (mma N) and scratch row stride
-constexpr int kSPad = kTK + 4;   // score tile: x rounded down to 4 floats
+constexpr int kRows = 8;         // query rows per launch (mma N)
+constexpr int kSD = 4;           // depth of the per-thread score ring of the V phase
+constexpr int kTileScores = 8 * kRows * 16;   // floats of score scratch per tile
+constexpr int kMaxSpan = 160;  // CTAs one head may span (launches have at most this many CTAs)
+constexpr float kFix = 1099511627776.0f;      // 2^40: output accumulator scale
+constexpr float kUnfix = 1.0f / 1099511627776.0f;
 
 template <int D> struct G4;
-template <> struct G4<64>  { static constexpr int BW = 64, NS1 = 8, NS2 = 6; };
-template <> struct G4<96>  { static constexpr int BW = 32, NS1 = 5, NS2 = 4; };
-template <> struct G4<128> { static constexpr int BW = 64, NS1 = 4, NS2 = 4; };
+template <> struct G4<64>  { static constexpr int BW = 64, NS = 11; };
+template <> struct G4<96>  { static constexpr int BW = 32, NS = 7; };
+template <> struct G4<128> { static constexpr int BW = 64, NS = 5; };
 
 template <int BW>
 __device__ __forceinline__ uint32_t swz(int row, int chunk)
@@ -88,36 +99,10 @@ __device__ __forceinline__ void tile_of(const Range &g, int i, int &h, int64_t &
     else { h = g.h0 + 1; k0 = (int64_t)(i - g.nt0) * kTK; kend = g.e1; }
 }
 
-// index of the (CTA, segment) partial of local head h held by CTA cc
+// index of the (CTA, segment) statistics of local head h held by CTA cc
 __device__ __forceinline__ int64_t part_slot(const AttnParams &p, int h, int cc)
 {
     return (int64_t)cc * 2 + (cc == p.span_a[h] ? p.span_slot[h] : 0);
-}
-
-// ---- producer ----------------------------------------------------------------
-template <int NS, class Issue>
-__device__ void produce(int nt, int first, uint64_t *full, uint64_t *empty, volatile int *abort_flag,
-                        const AttnParams &p, int &issued, Issue &&issue)
-{
-    for (int i = first; i < nt; i++) {
-        if (p.inject == 1 && i == 1) break;   // test hook: withhold tile 1
-        const int s = i % NS;
-        if (i >= NS && !mbar_wait(&empty[s], ((i / NS) - 1) & 1, p.limit_ns)) {
-            atomicOr(p.err, 2u);
-            *abort_flag = 1;
-            break;
-        }
-        if (*abort_flag) break;
-        issue(i, s);
-        issued = i + 1;
-    }
-}
-
-template <int NS>
-__device__ void drain(int issued, int nt, uint64_t *full, const AttnParams &p)
-{
-    if (issued < nt)  // leave no tile load in flight
-        for (int j = issued > NS ? issued - NS : 0; j < issued; j++) mbar_wait(&full[j % NS], (j / NS) & 1, p.limit_ns);
 }
 
 // ---- the fused single-token append ---------------------------------------------
@@ -207,32 +192,65 @@ __device__ __forceinline__ void patch_row(unsigned char *stage, int key, const _
     __syncwarp();
 }
 
+// ---- shared memory -------------------------------------------------------------
+template <int D>
+struct Smem {
+    static constexpr int BW = G4<D>::BW, NB = D / BW, NS = G4<D>::NS;
+    static constexpr uint32_t kSub = kTK * BW * 2, kStage = kSub * NB;
+    static constexpr int RED_LD = D + 4;
+    static constexpr size_t ring = (size_t)NS * kStage;
+    // K phase: rotated q [2 heads][8 rows][D] + per-warp scratch [8][D];
+    // V phase: per-warp partial outputs [8 warps][8 rows][RED_LD]
+    static constexpr size_t uni_k = (size_t)(2 * kRows + 8) * D * 4;
+    static constexpr size_t uni_v = (size_t)8 * kRows * RED_LD * 4;
+    static constexpr size_t uni = uni_k > uni_v ? uni_k : uni_v;
+    static constexpr size_t o_uni = ring;
+    static constexpr size_t o_sS = o_uni + uni;                            // [kSD][256][4] floats
+    static constexpr size_t o_bar = o_sS + (size_t)kSD * kConsumers * 16;  // full[NS], empty[NS]
+    static constexpr size_t o_redm = o_bar + (size_t)2 * NS * 8;           // [2][8 warps][8 rows]
+    static constexpr size_t o_redz = o_redm + 2 * 8 * kRows * 4;
+    static constexpr size_t o_row = o_redz + 2 * 8 * kRows * 4;            // rowM[2][8], rowInv[2][8]
+    static constexpr size_t o_kf = o_row + 4 * kRows * 4;                  // [D] f32
+    static constexpr size_t o_knew = o_kf + (size_t)D * 4;                 // [D] f16
+    static constexpr size_t o_vnew = o_knew + (size_t)D * 2;               // [D] f16
+    static constexpr size_t o_flags = o_vnew + (size_t)D * 2;              // abort, last(seg 0), last(seg 1)
+    static constexpr size_t bytes = o_flags + 16;
+    static_assert(bytes <= 227 * 1024, "shared memory of the attention kernel");
+    static_assert(kStage % 1024 == 0, "ring stages stay 1024-byte aligned");
+};
+
 // ---------------------------------------------------------------------------
-// pass 1
+// the kernel
 // ---------------------------------------------------------------------------
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1) attn_scores_kernel(const __grid_constant__ CUtensorMap kmap,
+__global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                                    const __grid_constant__ CUtensorMap vmap,
                                                                     const AttnParams p)
 {
-    constexpr int BW = G4<D>::BW, NB = D / BW, NS = G4<D>::NS1, KC = D / 16;
-    constexpr uint32_t kSub = kTK * BW * 2, kStage = kSub * NB;
+    using L = Smem<D>;
+    constexpr int BW = L::BW, NB = L::NB, NS = L::NS, KC = D / 16, DT = D / 16, RED_LD = L::RED_LD;
+    constexpr uint32_t kSub = L::kSub, kStage = L::kStage;
 
     extern __shared__ __align__(1024) unsigned char smem[];
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + NS * kStage);
+    float *qs = reinterpret_cast<float *>(smem + L::o_uni);                 // K phase
+    float *tmp = qs + 2 * kRows * D;
+    float *red = reinterpret_cast<float *>(smem + L::o_uni);                // V phase
+    float *sS = reinterpret_cast<float *>(smem + L::o_sS);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::o_bar);
     uint64_t *empty = full + NS;
-    float *red_m = reinterpret_cast<float *>(empty + NS);             // [2][8 warps][8 rows]
-    float *red_z = red_m + 2 * 8 * kRows;
-    float *qs = red_z + 2 * 8 * kRows;                                 // [2 heads][8 rows][D] rotated q
-    float *tmp = qs + 2 * kRows * D;                                   // [8 warps][D]
-    float *kf = tmp + 8 * D;                                           // [D] rotated new K row
-    __half *knew = reinterpret_cast<__half *>(kf + D);                // [D] its F16 bits
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(knew + D);
+    float *red_m = reinterpret_cast<float *>(smem + L::o_redm);
+    float *red_z = reinterpret_cast<float *>(smem + L::o_redz);
+    float *rowM = reinterpret_cast<float *>(smem + L::o_row);
+    float *rowInv = rowM + 2 * kRows;
+    float *kf = reinterpret_cast<float *>(smem + L::o_kf);
+    __half *knew = reinterpret_cast<__half *>(smem + L::o_knew);
+    __half *vnew = reinterpret_cast<__half *>(smem + L::o_vnew);
+    volatile int *flags = reinterpret_cast<volatile int *>(smem + L::o_flags);
 
-    pdl_launch_dependents();
     const int c = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const Range g = cta_range(c, p.n_kv, p.hkv, p.n_cta);
     const bool two = g.nt > g.nt0;
-    // decode: this CTA owns head h0's new key when its first segment ends the head
+    // decode: this CTA owns head h0's new row when its first segment ends the head
     const bool owns_new = p.fused && g.e0 == p.n_kv;
     const int it_new = owns_new ? (int)((p.n_past - g.s0) / kTK) : -1;
 
@@ -241,46 +259,72 @@ __global__ void __launch_bounds__(kThreads, 1) attn_scores_kernel(const __grid_c
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 8);
         }
-        *abort_flag = 0;
+        flags[0] = 0;
+        flags[1] = 0;
+        flags[2] = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
+    // ---- producer: K tiles 0..nt-1, then V tiles 0..nt-1, one ring ----
     if (warp == 8) {
+        int issued = 0;
         if (lane == 0) {
             prefetch_tmap(&kmap);
-            int issued = 0;
+            prefetch_tmap(&vmap);
+            const int total = 2 * g.nt;
             bool waited = false;
-            produce<NS>(g.nt, 0, full, empty, abort_flag, p, issued, [&](int i, int s) {
+            for (int j = 0; j < total; j++) {
+                if (p.inject == 1 && j == 1) break;   // test hook: withhold tile 1
+                const int s = j % NS;
+                if (j >= NS && !mbar_wait(&empty[s], ((j / NS) - 1) & 1, p.limit_ns)) {
+                    atomicOr(p.err, 2u);
+                    flags[0] = 1;
+                    break;
+                }
+                if (flags[0]) break;
+                const bool isv = j >= g.nt;
                 int h;
                 int64_t k0, kend;
-                tile_of(g, i, h, k0, kend);
-                // rows >= n_past may come from the kernel before this one (a
-                // multi-token append): only then is the wait needed
-                if (!waited && !p.fused && k0 + kTK > p.n_past) {
+                tile_of(g, isv ? j - g.nt : j, h, k0, kend);
+                // rows the previous kernel may still write (a multi-token
+                // append's rows, or the row a fused launch of this layer adds)
+                // need its completion; every older kernel has completed,
+                // since the previous one let this one start only after its
+                // own griddepcontrol.wait
+                if (!waited && ((!p.fused && k0 + kTK > p.n_past) || (p.hz_row >= k0 && p.hz_row < k0 + kTK))) {
                     pdl_wait();
                     waited = true;
                 }
                 mbar_arrive_expect_tx(&full[s], kStage);
 #pragma unroll
                 for (int b = 0; b < NB; b++)
-                    tma_load_3d(smem + s * kStage + b * kSub, &kmap, &full[s], b * BW, h, (int)k0);
-            });
-            drain<NS>(issued, g.nt, full, p);
+                    tma_load_3d(smem + s * kStage + b * kSub, isv ? &vmap : &kmap, &full[s], b * BW, h, (int)k0);
+                issued = j + 1;
+            }
             if (!waited) pdl_wait();   // complete only after the previous kernel
         }
+        // the CTA leaves together; if the consumers gave up, tiles they never
+        // took may still be landing: wait for the last load of every slot
+        named_sync(2, kThreads);
+        if (lane == 0 && flags[0])
+            for (int j = issued > NS ? issued - NS : 0; j < issued; j++)
+                mbar_wait(&full[j % NS], (j / NS) & 1, p.limit_ns);
         return;
     }
 
+    // ======================= K phase =======================
     const int gq = lane >> 2, cq = lane & 3;
     const int R = p.nrows;
     const int row_a = 2 * cq, row_b = 2 * cq + 1;
     const int64_t lim_a = p.n_past + (p.row0 + min(row_a, R - 1)) / p.r;
     const int64_t lim_b = p.n_past + (p.row0 + min(row_b, R - 1)) / p.r;
+    float *const Scta = p.S + (int64_t)c * p.S_tiles * kTileScores;
 
     float2 csr[(D + 31) / 32];
     if (p.fused) rope_prefetch<D>(p, csr);
     pdl_wait();   // inputs, qbuf and the rows below may come from the previous kernel
+    pdl_launch_dependents();   // only now: the next kernel may rely on every kernel before this one
 
     // decode: rotate the query rows of both heads and the new K row, one item per warp
     if (p.fused) {
@@ -335,93 +379,104 @@ __global__ void __launch_bounds__(kThreads, 1) attn_scores_kernel(const __grid_c
     float za = 0.0f, zb = 0.0f, za0 = 0.0f, zb0 = 0.0f;
     bool aborted = false;
     const uint32_t ring = smem_addr(smem);
-    const int mi = lane >> 3;
-    const int arow = warp * 16 + (lane & 7) + (mi & 1) * 8;
+    {
+        const int mi = lane >> 3;
+        const int arow = warp * 16 + (lane & 7) + (mi & 1) * 8;
+        // where this lane's four scores land in the warp's 128-float block: the
+        // V phase's lane (row, c') reads keys 2c'+{0,1}, 2c'+8+{0,1} as one float4
+        const int so_a = (row_a * 4 + (gq >> 1)) * 4 + (gq & 1);
+        const int so_b = (row_b * 4 + (gq >> 1)) * 4 + (gq & 1);
 
-    auto upd = [&](float &m, float &z, float s0, float s1) {
-        const float mn = fmaxf(m, fmaxf(s0, s1));
-        const float base = mn == -INFINITY ? 0.0f : mn;
-        z = z * __expf(m - base) + __expf(s0 - base) + __expf(s1 - base);
-        m = mn;
-    };
+        auto upd = [&](float &m, float &z, float s0, float s1) {
+            const float mn = fmaxf(m, fmaxf(s0, s1));
+            const float base = mn == -INFINITY ? 0.0f : mn;
+            z = z * __expf(m - base) + __expf(s0 - base) + __expf(s1 - base);
+            m = mn;
+        };
 
-    for (int i = 0; i < g.nt; i++) {
-        if (i == g.nt0) {
-            ma0 = ma; mb0 = mb; za0 = za; zb0 = zb;
-            ma = mb = -INFINITY;
-            za = zb = 0.0f;
-            load_q(1);
-        }
-        const int s = i % NS;
-        const bool ok = mbar_wait(&full[s], (i / NS) & 1, p.limit_ns);
-        if (__any_sync(0xffffffffu, !ok)) {
-            if (lane == 0) {
-                atomicOr(p.err, 1u);
-                *abort_flag = 1;
+        for (int i = 0; i < g.nt; i++) {
+            if (i == g.nt0) {
+                ma0 = ma; mb0 = mb; za0 = za; zb0 = zb;
+                ma = mb = -INFINITY;
+                za = zb = 0.0f;
+                load_q(1);
             }
-            aborted = true;
-            break;
-        }
-        int h;
-        int64_t k0, kend;
-        tile_of(g, i, h, k0, kend);
-        if (i == it_new && (int)((p.n_past - k0) >> 4) == warp)
-            patch_row<D, BW>(smem + s * kStage, (int)(p.n_past - k0), knew);
+            const int s = i % NS;
+            const bool ok = mbar_wait(&full[s], (i / NS) & 1, p.limit_ns);
+            if (__any_sync(0xffffffffu, !ok)) {
+                if (lane == 0) {
+                    atomicOr(p.err, 1u);
+                    flags[0] = 1;
+                }
+                aborted = true;
+                break;
+            }
+            int h;
+            int64_t k0, kend;
+            tile_of(g, i, h, k0, kend);
+            if (i == it_new && (int)((p.n_past - k0) >> 4) == warp)
+                patch_row<D, BW>(smem + s * kStage, (int)(p.n_past - k0), knew);
 
-        float acc0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, acc1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            float acc0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, acc1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int kc = 0; kc < KC; kc++) {
-            const int dim0 = kc * 16 + (mi >> 1) * 8;
-            const uint32_t addr = ring + s * kStage + (dim0 / BW) * kSub + swz<BW>(arow, (dim0 % BW) >> 3);
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4(addr, a0, a1, a2, a3);
-            if (kc & 1) mma_16816(acc1, a0, a1, a2, a3, bq[kc][0], bq[kc][1]);
-            else mma_16816(acc0, a0, a1, a2, a3, bq[kc][0], bq[kc][1]);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+            for (int kc = 0; kc < KC; kc++) {
+                const int dim0 = kc * 16 + (mi >> 1) * 8;
+                const uint32_t addr = ring + s * kStage + (dim0 / BW) * kSub + swz<BW>(arow, (dim0 % BW) >> 3);
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(addr, a0, a1, a2, a3);
+                if (kc & 1) mma_16816(acc1, a0, a1, a2, a3, bq[kc][0], bq[kc][1]);
+                else mma_16816(acc0, a0, a1, a2, a3, bq[kc][0], bq[kc][1]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
 
-        // (key gq, row 2cq), (key gq, row 2cq+1), (key gq+8, row 2cq), (key gq+8, row 2cq+1)
-        const int64_t key0 = k0 + warp * 16 + gq, key1 = key0 + 8;
-        const bool v0 = key0 < kend, v1 = key1 < kend;
-        const float sa0 = v0 && key0 <= lim_a ? __fmul_rn(acc0[0] + acc1[0], p.scale) : -INFINITY;
-        const float sb0 = v0 && key0 <= lim_b ? __fmul_rn(acc0[1] + acc1[1], p.scale) : -INFINITY;
-        const float sa1 = v1 && key1 <= lim_a ? __fmul_rn(acc0[2] + acc1[2], p.scale) : -INFINITY;
-        const float sb1 = v1 && key1 <= lim_b ? __fmul_rn(acc0[3] + acc1[3], p.scale) : -INFINITY;
-        float *Sa = p.S + ((int64_t)h * kRows + row_a) * p.S_stride;
-        float *Sb = Sa + p.S_stride;
-        if (row_a < R) {
-            if (v0) Sa[key0] = sa0;
-            if (v1) Sa[key1] = sa1;
-            upd(ma, za, sa0, sa1);
-        }
-        if (row_b < R) {
-            if (v0) Sb[key0] = sb0;
-            if (v1) Sb[key1] = sb1;
-            upd(mb, zb, sb0, sb1);
+            // (key gq, row 2cq), (key gq, row 2cq+1), (key gq+8, row 2cq), (key gq+8, row 2cq+1)
+            const int64_t key0 = k0 + warp * 16 + gq, key1 = key0 + 8;
+            const bool v0 = key0 < kend, v1 = key1 < kend;
+            const float sa0 = v0 && key0 <= lim_a ? __fmul_rn(acc0[0] + acc1[0], p.scale) : -INFINITY;
+            const float sb0 = v0 && key0 <= lim_b ? __fmul_rn(acc0[1] + acc1[1], p.scale) : -INFINITY;
+            const float sa1 = v1 && key1 <= lim_a ? __fmul_rn(acc0[2] + acc1[2], p.scale) : -INFINITY;
+            const float sb1 = v1 && key1 <= lim_b ? __fmul_rn(acc0[3] + acc1[3], p.scale) : -INFINITY;
+            float *Sw = Scta + (int64_t)i * kTileScores + warp * 128;
+            if (row_a < R) {
+                if (v0) Sw[so_a] = sa0;
+                if (v1) Sw[so_a + 2] = sa1;
+                upd(ma, za, sa0, sa1);
+            }
+            if (row_b < R) {
+                if (v0) Sw[so_b] = sb0;
+                if (v1) Sw[so_b + 2] = sb1;
+                upd(mb, zb, sb0, sb1);
+            }
         }
     }
 
+    // ======================= statistics =======================
     // (max, sum) per (segment, row): the 8 lanes of a row pair, then the 8 warps
-    const float m_s[2][2] = {{two ? ma0 : ma, two ? mb0 : mb}, {ma, mb}};
-    const float z_s[2][2] = {{two ? za0 : za, two ? zb0 : zb}, {za, zb}};
+    {
+        const float m_s[2][2] = {{two ? ma0 : ma, two ? mb0 : mb}, {ma, mb}};
+        const float z_s[2][2] = {{two ? za0 : za, two ? zb0 : zb}, {za, zb}};
 #pragma unroll
-    for (int sl = 0; sl < 2; sl++)
+        for (int sl = 0; sl < 2; sl++)
 #pragma unroll
-        for (int rr = 0; rr < 2; rr++) {
-            const float m = aborted ? -INFINITY : m_s[sl][rr];
-            float M = m;
+            for (int rr = 0; rr < 2; rr++) {
+                const float m = aborted ? -INFINITY : m_s[sl][rr];
+                float M = m;
 #pragma unroll
-            for (int o = 4; o < 32; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-            float z = (m == -INFINITY) ? 0.0f : z_s[sl][rr] * __expf(m - M);
+                for (int o = 4; o < 32; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+                float z = (m == -INFINITY) ? 0.0f : z_s[sl][rr] * __expf(m - M);
 #pragma unroll
-            for (int o = 4; o < 32; o <<= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-            if (gq == 0) {
-                red_m[(sl * 8 + warp) * kRows + 2 * cq + rr] = M;
-                red_z[(sl * 8 + warp) * kRows + 2 * cq + rr] = z;
+                for (int o = 4; o < 32; o <<= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+                if (gq == 0) {
+                    red_m[(sl * 8 + warp) * kRows + 2 * cq + rr] = M;
+                    red_z[(sl * 8 + warp) * kRows + 2 * cq + rr] = z;
+                }
             }
-        }
-    named_sync(1, kConsumers);
+    }
+    aborted = named_sync_or(1, kConsumers, aborted);
+    // publish: one 16-byte slot per (CTA, segment, row) holding (max, sum), each
+    // word tagged with this launch's epoch, so a reader needs no fence or ticket
+    // -- a slot is valid once both tags match
     if (tid < 2 * kRows) {
         const int sl = tid / kRows, row = tid % kRows;
         float M = -INFINITY;
@@ -433,120 +488,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_scores_kernel(const __grid_c
             const float mw = red_m[(sl * 8 + w) * kRows + row];
             if (mw != -INFINITY) Z += (double)red_z[(sl * 8 + w) * kRows + row] * (double)__expf(mw - M);
         }
-        const int64_t pi = ((int64_t)c * 2 + sl) * kRows + row;
-        p.part_m[pi] = M;
-        p.part_z[pi] = Z;
+        // an aborted CTA publishes empty statistics, so no other CTA waits for it
+        const unsigned long long tag = (unsigned long long)p.epoch << 32;
+        st_volatile_v2(p.stats + 2 * (((int64_t)c * 2 + sl) * kRows + row),
+                       tag | __float_as_uint(aborted ? -INFINITY : M),
+                       tag | __float_as_uint(aborted ? 0.0f : (float)Z));
     }
-}
-
-// ---------------------------------------------------------------------------
-// pass 2
-// ---------------------------------------------------------------------------
-template <int D>
-__global__ void __launch_bounds__(kThreads, 1) attn_pv_kernel(const __grid_constant__ CUtensorMap vmap,
-                                                                const __grid_constant__ CUtensorMap smap,
-                                                                const AttnParams p)
-{
-    constexpr int BW = G4<D>::BW, NB = D / BW, NS = G4<D>::NS2, DT = D / 16;
-    constexpr int RED_LD = D + 4;
-    constexpr uint32_t kSub = kTK * BW * 2, kStage = kSub * NB, kSBytes = kSPad * kRows * 4;
-
-    extern __shared__ __align__(1024) unsigned char smem[];
-    float *sring = reinterpret_cast<float *>(smem + NS * kStage);        // [NS][8][kSPad]
-    float *red = sring + NS * kRows * kSPad;                             // [8 warps][8 rows][RED_LD]
-    uint64_t *full = reinterpret_cast<uint64_t *>(red + 8 * kRows * RED_LD);
-    uint64_t *empty = full + NS;
-    float *rowM = reinterpret_cast<float *>(empty + NS);                // [2][8]
-    float *rowInv = rowM + 2 * kRows;
-    __half *vnew = reinterpret_cast<__half *>(rowInv + 2 * kRows);      // [D]
-    volatile int *flags = reinterpret_cast<volatile int *>(vnew + D);   // abort, last(seg 0), last(seg 1)
-
-    pdl_launch_dependents();
-    const int c = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const Range g = cta_range(c, p.n_kv, p.hkv, p.n_cta);
-    const bool two = g.nt > g.nt0;
-    const int R = p.nrows;
-    const bool owns_new = p.fused && g.e0 == p.n_kv;
-    const int it_new = owns_new ? (int)((p.n_past - g.s0) / kTK) : -1;
-
-    if (tid == 0) {
-        for (int s = 0; s < NS; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 8);
-        }
-        flags[0] = 0;
-        flags[1] = 0;
-        flags[2] = 0;
-        fence_mbar_init();
-    }
-    __syncthreads();
-
-    if (warp == 8) {
-        if (lane == 0) {
-            prefetch_tmap(&vmap);
-            prefetch_tmap(&smap);
-            // V tiles of rows that existed before this step do not depend on the
-            // previous kernel: stream them while it finishes
-            int early = 0;
-            while (early < g.nt && early < NS) {
-                int h;
-                int64_t k0, kend;
-                tile_of(g, early, h, k0, kend);
-                if (k0 + kTK > p.n_past || (p.inject == 1 && early == 1)) break;
-                mbar_arrive_expect_tx(&full[early], kStage + kSBytes);
-#pragma unroll
-                for (int b = 0; b < NB; b++)
-                    tma_load_3d(smem + early * kStage + b * kSub, &vmap, &full[early], b * BW, h, (int)k0);
-                early++;
-            }
-            pdl_wait();   // scores and partials of pass 1 are now visible
-            for (int i = 0; i < early; i++) {
-                int h;
-                int64_t k0, kend;
-                tile_of(g, i, h, k0, kend);
-                tma_load_2d(sring + i * kRows * kSPad, &smap, &full[i], (int)(k0 & ~(int64_t)3), h * kRows);
-            }
-            int issued = early;
-            produce<NS>(g.nt, early, full, empty, flags, p, issued, [&](int i, int s) {
-                int h;
-                int64_t k0, kend;
-                tile_of(g, i, h, k0, kend);
-                mbar_arrive_expect_tx(&full[s], kStage + kSBytes);
-#pragma unroll
-                for (int b = 0; b < NB; b++)
-                    tma_load_3d(smem + s * kStage + b * kSub, &vmap, &full[s], b * BW, h, (int)k0);
-                tma_load_2d(sring + s * kRows * kSPad, &smap, &full[s], (int)(k0 & ~(int64_t)3), h * kRows);
-            });
-            drain<NS>(issued, g.nt, full, p);
-        }
-        return;
-    }
-
-    pdl_wait();
-    // ---- global max and 1/sum of each (segment, query row): one warp per pair ----
-    for (int pr = warp; pr < 2 * kRows; pr += 8) {
-        const int sl = pr / kRows, row = pr % kRows;
-        const int h = g.h0 + sl;
-        float M = -INFINITY, Z = 0.0f;
-        if (row < R && (sl == 0 || two)) {
-            const int ca = p.span_a[h], cb = p.span_b[h];
-            for (int cc = ca + lane; cc <= cb; cc += 32) M = fmaxf(M, p.part_m[part_slot(p, h, cc) * kRows + row]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-            for (int cc = ca + lane; cc <= cb; cc += 32) {
-                const int64_t pi = part_slot(p, h, cc) * kRows + row;
-                const float mj = p.part_m[pi];
-                if (mj != -INFINITY) Z += (float)p.part_z[pi] * __expf(mj - M);
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) Z += __shfl_xor_sync(0xffffffffu, Z, o);
-        }
-        if (lane == 0) {
-            rowM[sl * kRows + row] = M;
-            rowInv[sl * kRows + row] = Z > 0.0f ? __fdiv_rn(1.0f, Z) : 0.0f;
-        }
-    }
-    // decode: the new V row of head h0 goes to the cache and into its tile
+    // decode: the new V row of head h0 goes to the cache now, while others finish
     if (owns_new && warp == 7) {
         const float *src = p.v + (int64_t)(p.hkv0 + g.h0) * D;
         __half *dst = p.vc + (p.n_past * (int64_t)p.hkv + g.h0) * D;
@@ -556,18 +504,104 @@ __global__ void __launch_bounds__(kThreads, 1) attn_pv_kernel(const __grid_const
             dst[i] = h16;
         }
     }
-    named_sync(1, kConsumers);
 
-    const int gq = lane >> 2, cq = lane & 3;
+    // global max and 1/sum of each (segment, query row): warp w polls the slots
+    // of row w of every CTA of its heads (all loads in flight at once; spans of
+    // up to kPU*32 CTAs) until every tag shows this launch, bounded by limit_ns
+    bool late = false;
+    if (!aborted) {
+        constexpr int kPU = kMaxSpan / 32;
+        float mm[2][kPU], zz[2][kPU];
+        unsigned pend = 0u;
+        int ca[2], cb[2];
+#pragma unroll
+        for (int sl = 0; sl < 2; sl++) {
+            const int h = g.h0 + sl;
+            const bool act = warp < R && (sl == 0 || two);
+            ca[sl] = act ? p.span_a[h] : 0;
+            cb[sl] = act ? p.span_b[h] : -1;
+#pragma unroll
+            for (int u = 0; u < kPU; u++) {
+                mm[sl][u] = -INFINITY;
+                zz[sl][u] = 0.0f;
+                if (ca[sl] + lane + 32 * u <= cb[sl]) pend |= 1u << (sl * kPU + u);
+            }
+        }
+        const unsigned ep = p.epoch;
+        const uint64_t t_start = globaltimer();
+        for (;;) {
+#pragma unroll
+            for (int sl = 0; sl < 2; sl++)
+#pragma unroll
+                for (int u = 0; u < kPU; u++) {
+                    const unsigned bit = 1u << (sl * kPU + u);
+                    if (pend & bit) {
+                        const int cc = ca[sl] + lane + 32 * u;
+                        unsigned long long w0, w1;
+                        ld_volatile_v2(p.stats + 2 * (part_slot(p, g.h0 + sl, cc) * kRows + warp), w0, w1);
+                        if ((unsigned)(w0 >> 32) == ep && (unsigned)(w1 >> 32) == ep) {
+                            mm[sl][u] = __uint_as_float((unsigned)w0);
+                            zz[sl][u] = __uint_as_float((unsigned)w1);
+                            pend &= ~bit;
+                        }
+                    }
+                }
+            if (!__any_sync(0xffffffffu, pend != 0u)) break;
+            if (globaltimer() - t_start > p.limit_ns) {
+                late = true;
+                break;
+            }
+        }
+        late = __any_sync(0xffffffffu, late);
+        if (!late) {
+#pragma unroll
+            for (int sl = 0; sl < 2; sl++) {
+                float M = -INFINITY;
+#pragma unroll
+                for (int u = 0; u < kPU; u++) M = fmaxf(M, mm[sl][u]);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+                float Z = 0.0f;
+#pragma unroll
+                for (int u = 0; u < kPU; u++)
+                    if (mm[sl][u] != -INFINITY) Z += zz[sl][u] * __expf(mm[sl][u] - M);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) Z += __shfl_xor_sync(0xffffffffu, Z, o);
+                if (lane == 0) {
+                    rowM[sl * kRows + warp] = M;
+                    rowInv[sl * kRows + warp] = Z > 0.0f ? __fdiv_rn(1.0f, Z) : 0.0f;
+                }
+            }
+        } else if (lane == 0) {
+            atomicOr(p.err, 4u);
+            flags[0] = 1;
+        }
+    }
+    aborted = named_sync_or(1, kConsumers, aborted || late);
+
+    // ======================= V phase =======================
     float oacc[DT][4];
 #pragma unroll
     for (int dt = 0; dt < DT; dt++) oacc[dt][0] = oacc[dt][1] = oacc[dt][2] = oacc[dt][3] = 0.0f;
-    bool aborted = false;
-    const uint32_t ring = smem_addr(smem);
 
-    // this CTA's partial of segment sl into part_o; flags[1+sl] = last CTA of the head
-    auto write_partial = [&](int sl) -> bool {
-        if (named_sync_or(1, kConsumers, aborted)) return false;
+    // scores of tile i for this lane: one float4 of the warp's block, through a
+    // kSD-deep per-thread cp.async ring
+    const float *Sl = Scta + warp * 128 + (gq * 4 + cq) * 4;
+    float *stg = sS + tid * 4;
+    auto stage_s = [&](int i) {
+        if (i < g.nt && gq < R) cp_async_16(stg + (i % kSD) * (kConsumers * 4), Sl + (int64_t)i * kTileScores);
+        cp_async_commit();
+    };
+    if (!aborted)
+        for (int i = 0; i < kSD - 1; i++) stage_s(i);
+
+    // this CTA's partial output of segment sl into the head's fixed-point
+    // accumulator; the head's last CTA converts and writes the output
+    auto flush_out = [&](int sl) {
+        if (named_sync_or(1, kConsumers, aborted)) {
+            aborted = true;
+            return;
+        }
         const int h = g.h0 + sl;
 #pragma unroll
         for (int dt = 0; dt < DT; dt++) {
@@ -579,48 +613,49 @@ __global__ void __launch_bounds__(kThreads, 1) attn_pv_kernel(const __grid_const
             oacc[dt][0] = oacc[dt][1] = oacc[dt][2] = oacc[dt][3] = 0.0f;
         }
         named_sync(1, kConsumers);
+        long long *acc = p.acc + (int64_t)h * kRows * D;
+        bool bad = false;
         for (int idx = tid; idx < R * D; idx += kConsumers) {
             const int row = idx / D, dd = idx - row * D;
             float sum = 0.0f;
 #pragma unroll
             for (int w = 0; w < 8; w++) sum += red[(w * kRows + row) * RED_LD + dd];
-            p.part_o[(((int64_t)c * 2 + sl) * kRows + row) * D + dd] = sum;
+            if (isfinite(sum))
+                atomicAdd(reinterpret_cast<unsigned long long *>(acc + idx),
+                          (unsigned long long)__float2ll_rn(__fmul_rn(sum, kFix)));
+            else
+                bad = true;
         }
+        if (bad) atomicOr(&p.nonfin[h], 1u);
         __threadfence();
         named_sync(1, kConsumers);
         if (tid == 0)
             flags[1 + sl] = atomicAdd(&p.counters[h], 1u) == (unsigned)(p.span_b[h] - p.span_a[h]);
         named_sync(1, kConsumers);
-        return true;
-    };
-
-    // the head's last CTA: sum its CTAs' partials in CTA order, every load in flight
-    auto combine = [&](int h) {
-        __threadfence();
-        const int ca = p.span_a[h], n = p.span_b[h] - ca + 1;
-        const int64_t cstride = (int64_t)2 * kRows * D;
-        for (int idx = tid; idx < R * D; idx += kConsumers) {
-            const int row = idx / D, dd = idx - row * D;
-            const float *src = p.part_o + (int64_t)row * D + dd;
-            float sum = __ldcg(src + part_slot(p, h, ca) * kRows * D);
-            for (int base = 1; base < n; base += 16) {
-                float x[16];
-#pragma unroll
-                for (int u = 0; u < 16; u++) x[u] = base + u < n ? __ldcg(src + (int64_t)(ca + base + u) * cstride) : 0.0f;
-#pragma unroll
-                for (int u = 0; u < 16; u++) sum += x[u];
+        if (flags[1 + sl]) {
+            __threadfence();
+            const bool nan_out = __ldcg(&p.nonfin[h]) != 0u;
+            for (int idx = tid; idx < R * D; idx += kConsumers) {
+                const int row = idx / D, dd = idx - row * D;
+                const long long v = __ldcg(acc + idx);
+                acc[idx] = 0;
+                const int qrow = p.row0 + row;
+                p.out[(int64_t)(qrow / p.r) * p.out_stride + (int64_t)(p.out_head0 + h * p.r + qrow % p.r) * D + dd] =
+                    nan_out ? __int_as_float(0x7fc00000) : __fmul_rn(__ll2float_rn(v), kUnfix);
             }
-            const int qrow = p.row0 + row;
-            p.out[(int64_t)(qrow / p.r) * p.out_stride + (int64_t)(p.out_head0 + h * p.r + qrow % p.r) * D + dd] = sum;
+            if (tid == 0) {
+                p.counters[h] = 0u;
+                p.nonfin[h] = 0u;
+            }
         }
-        if (tid == 0) p.counters[h] = 0u;
     };
 
     for (int i = 0; i < g.nt; i++) {
-        if (i == g.nt0 && i > 0) write_partial(0);
+        if (i == g.nt0 && i > 0) flush_out(0);
         if (aborted) continue;   // keep step with the other warps' barriers
-        const int s = i % NS;
-        const bool ok = mbar_wait(&full[s], (i / NS) & 1, p.limit_ns);
+        const int j = g.nt + i, s = j % NS;
+        stage_s(i + kSD - 1);
+        const bool ok = mbar_wait(&full[s], (j / NS) & 1, p.limit_ns);
         if (__any_sync(0xffffffffu, !ok)) {
             if (lane == 0) {
                 atomicOr(p.err, 1u);
@@ -650,14 +685,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_pv_kernel(const __grid_const
         }
         if (i == it_new && (int)((p.n_past - k0) >> 4) == warp) patch_row<D, BW>(stage, (int)(p.n_past - k0), vnew);
 
-        const float *st = sring + s * kRows * kSPad + (k0 & 3) + gq * kSPad;
+        cp_async_wait<kSD - 1>();
+        const float4 sv = *reinterpret_cast<const float4 *>(stg + (i % kSD) * (kConsumers * 4));
+        const float sc[4] = {sv.x, sv.y, sv.z, sv.w};
         const float M = rowM[sl * kRows + gq], inv = rowInv[sl * kRows + gq];
         __half pv[4];
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             const int kk = kw + 2 * cq + (e & 1) + 8 * (e >> 1);
             const bool valid = gq < R && kk < n_valid;
-            const float pe = __fmul_rn(expf(st[kk] - M), inv);
+            const float pe = __fmul_rn(expf(sc[e] - M), inv);
             pv[e] = valid ? __float2half_rn(pe) : __ushort_as_half((unsigned short)0);
         }
         const uint32_t b0 = pack_half2(pv[0], pv[1]), b1 = pack_half2(pv[2], pv[3]);
@@ -675,59 +712,35 @@ __global__ void __launch_bounds__(kThreads, 1) attn_pv_kernel(const __grid_const
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
-    if (g.nt > 0 && write_partial(two ? 1 : 0)) {
-        if (flags[1]) combine(g.h0);
-        if (two && flags[2]) combine(g.h0 + 1);
-    }
+    cp_async_wait<0>();
+    flush_out(two ? 1 : 0);
+    named_sync(2, kThreads);
 }
 
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 template <int D>
-size_t smem1()
-{
-    constexpr int BW = G4<D>::BW, NB = D / BW, NS = G4<D>::NS1;
-    return (size_t)NS * kTK * BW * 2 * NB + 2 * NS * 8 + 2 * 2 * 8 * kRows * 4 + (size_t)(2 * kRows + 8 + 1) * D * 4 +
-           (size_t)D * 2 + 16;
-}
-
-template <int D>
-size_t smem2()
-{
-    constexpr int BW = G4<D>::BW, NB = D / BW, NS = G4<D>::NS2;
-    return (size_t)NS * kTK * BW * 2 * NB + (size_t)NS * kRows * kSPad * 4 + (size_t)8 * kRows * (D + 4) * 4 +
-           2 * NS * 8 + 4 * kRows * 4 + (size_t)D * 2 + 32;
-}
-
-template <int D>
 cudaError_t prep()
 {
-    cudaError_t e =
-        cudaFuncSetAttribute(attn_scores_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1<D>());
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(attn_pv_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2<D>());
+    return cudaFuncSetAttribute(attn_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)Smem<D>::bytes);
 }
 
 template <int D>
-cudaError_t launch(int which, const CUtensorMap &kmap, const CUtensorMap &vmap, const CUtensorMap &smap,
-                   const AttnParams &p, cudaStream_t st, bool pdl)
+cudaError_t launch(const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnParams &p, cudaStream_t st, bool pdl)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)p.n_cta);
     cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Smem<D>::bytes;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (which == 0) {
-        cfg.dynamicSmemBytes = smem1<D>();
-        return cudaLaunchKernelEx(&cfg, attn_scores_kernel<D>, kmap, p);
-    }
-    cfg.dynamicSmemBytes = smem2<D>();
-    return cudaLaunchKernelEx(&cfg, attn_pv_kernel<D>, vmap, smap, p);
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D>, kmap, vmap, p);
 }
 
 }  // namespace
@@ -735,6 +748,8 @@ cudaError_t launch(int which, const CUtensorMap &kmap, const CUtensorMap &vmap, 
 int attn_rows() { return kRows; }
 int attn_tile_keys() { return kTK; }
 int attn_box_width(int D) { return D == 96 ? 32 : 64; }
+int attn_tile_scores() { return kTileScores; }
+int attn_max_ctas() { return kMaxSpan; }
 
 cudaError_t attn_prepare(int D)
 {
@@ -746,14 +761,14 @@ cudaError_t attn_prepare(int D)
     }
 }
 
-cudaError_t launch_attn(int D, int which, const CUtensorMap &kmap, const CUtensorMap &vmap, const CUtensorMap &smap,
-                        const AttnParams &p, cudaStream_t st, bool pdl)
+cudaError_t launch_attn(int D, const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnParams &p,
+                        cudaStream_t st, bool pdl)
 {
     if (p.nrows < 1 || p.nrows > kRows) return cudaErrorInvalidValue;
     switch (D) {
-    case 64: return launch<64>(which, kmap, vmap, smap, p, st, pdl);
-    case 96: return launch<96>(which, kmap, vmap, smap, p, st, pdl);
-    case 128: return launch<128>(which, kmap, vmap, smap, p, st, pdl);
+    case 64: return launch<64>(kmap, vmap, p, st, pdl);
+    case 96: return launch<96>(kmap, vmap, p, st, pdl);
+    case 128: return launch<128>(kmap, vmap, p, st, pdl);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -196,18 +196,17 @@ struct kv_ctx {
     int64_t layer_elems = 0;  // n_ctx * hkv_loc * D
     float2 *rope = nullptr;   // [n_ctx][n_rot/2]
     __half *qbuf = nullptr;   // [n_batch_max][hq_loc][D]
-    float *S = nullptr;       // [hkv_loc][8][S_stride]
-    int64_t S_stride = 0;
-    float *part_m = nullptr;  // [max_cta][2][8]
-    double *part_z = nullptr;
-    float *part_o = nullptr;  // [max_cta][2][8][D]
-    unsigned *counters = nullptr;
+    float *S = nullptr;       // score scratch, attn_tile_scores() floats per (CTA, tile)
+    int64_t S_floats = 0;
+    unsigned long long *stats = nullptr;  // [max_cta][2][8][2] epoch-tagged (max, sum) slots
+    uint32_t epoch = 0;                   // tag of the last attention launch
+    long long *acc = nullptr; // [hkv_loc][8][D] fixed-point output accumulators
+    unsigned *ctl = nullptr;  // [2][hkv_loc]: output tickets, non-finite flags
     unsigned *err = nullptr;  // device error word of the bounded waits
     float *local_out = nullptr;   // sharded prefill: [n_batch_max][hq_loc*D]
     float *gathered = nullptr;    // [n_shards][n_batch_max][hq_loc*D]
     int max_cta = 0;
     std::vector<CUtensorMap> kmaps, vmaps;  // per layer: [n_ctx][hkv_loc][D] F16, swizzled column boxes
-    CUtensorMap smap{};                     // scores [hkv_loc*8][S_stride] F32
     uint64_t limit_ns = 1000000000ull;      // bound of every device-side wait (1 s)
     int inject = 0;                         // test hook, applies to the next decode launch
 
@@ -216,6 +215,11 @@ struct kv_ctx {
     int last_layer = -1;
     int64_t last_n_past = -1;
     int last_n_new = 0;
+    // the cache row the last fused attention launch appended (stream, layer):
+    // the next launch on that stream for that layer must not read it early
+    cudaStream_t hz_stream = nullptr;
+    int hz_layer = -1;
+    int64_t hz_row = -1;
 
     ncclComm_t comm = nullptr;
 
@@ -312,7 +316,7 @@ int launch(kv_ctx *ctx, int kernel_id, cudaStream_t st, const char *what, F &&fn
 int decode_ctas(const kv_ctx *ctx, int64_t n_kv)
 {
     const int64_t T = (int64_t)ctx->hkv_loc * n_kv;
-    int64_t c = std::min<int64_t>(ctx->sm_count, (T + 63) / 64);
+    int64_t c = std::min<int64_t>(std::min(ctx->sm_count, kvb::attn_max_ctas()), (T + 63) / 64);
     c = std::max<int64_t>(c, ctx->hkv_loc);
     c = std::min<int64_t>(c, T);
     return (int)c;
@@ -362,8 +366,8 @@ void free_all(kv_ctx *ctx)
     ctx->ev_pool.clear();
     if (ctx->comm && nccl().CommDestroy) nccl().CommDestroy(ctx->comm);
     ctx->comm = nullptr;
-    void *ptrs[] = {ctx->cache, ctx->rope, ctx->qbuf, ctx->S, ctx->part_m, ctx->part_z,
-                    ctx->part_o, ctx->counters, ctx->err, ctx->local_out, ctx->gathered};
+    void *ptrs[] = {ctx->cache, ctx->rope, ctx->qbuf, ctx->S, ctx->stats,
+                    ctx->acc, ctx->ctl, ctx->err, ctx->local_out, ctx->gathered};
     for (void *p : ptrs)
         if (p) cudaFree(p);
 }
@@ -484,6 +488,9 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
     ctx->hq_loc = ctx->hkv_loc * ctx->r;
     ctx->hkv0 = c.shard * ctx->hkv_loc;
     ctx->hq0 = c.shard * ctx->hq_loc;
+    if (ctx->hkv_loc > ctx->sm_count)   // the attention kernel keeps one CTA per SM, all resident
+        return bail(fail(KV_E_UNSUPPORTED, "%d local KV heads exceed the device's %d SMs", ctx->hkv_loc,
+                         ctx->sm_count));
     ctx->rmax = kvb::decode_rmax(ctx->D);
     ctx->split_max = kvb::decode_split_max(ctx->D);
     ctx->scale = 1.0f / sqrtf((float)ctx->D);
@@ -524,26 +531,27 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
         if (e != cudaSuccess) return bail(cuda_fail(e, "RoPE table upload"));
     }
 
-    // scores rows are padded to 4 floats and one score-tile width past n_ctx,
-    // so a score tile read at a 16-byte-aligned x never leaves the buffer
-    const int stile = kvb::attn_tile_keys() + 4;
-    ctx->S_stride = ((ctx->n_ctx + 3) / 4) * 4 + stile;
-    ctx->max_cta = std::max(ctx->sm_count, ctx->hkv_loc);
+    // score scratch: CTA c of a launch owns S_tiles(n_kv) tiles from
+    // c*S_tiles on; C*S_tiles <= T/128 + 3C for T = hkv_loc*n_kv rows
+    ctx->max_cta = std::max(std::min(ctx->sm_count, kvb::attn_max_ctas()), ctx->hkv_loc);
+    ctx->S_floats = ((int64_t)ctx->hkv_loc * ctx->n_ctx / kvb::attn_tile_keys() + 3 * (int64_t)ctx->max_cta + 1) *
+                    kvb::attn_tile_scores();
     const size_t n_part = (size_t)ctx->max_cta * 2u * 8u;
     struct { void **p; size_t bytes; } allocs[] = {
         {(void **)&ctx->qbuf, (size_t)c.n_batch_max * ctx->hq_loc * D * sizeof(__half)},
-        {(void **)&ctx->S, (size_t)ctx->hkv_loc * 8u * (size_t)ctx->S_stride * sizeof(float)},
-        {(void **)&ctx->part_m, n_part * sizeof(float)},
-        {(void **)&ctx->part_z, n_part * sizeof(double)},
-        {(void **)&ctx->part_o, n_part * (size_t)D * sizeof(float)},
-        {(void **)&ctx->counters, (size_t)ctx->hkv_loc * sizeof(unsigned)},
+        {(void **)&ctx->S, (size_t)ctx->S_floats * sizeof(float)},
+        {(void **)&ctx->stats, n_part * 2u * sizeof(unsigned long long)},
+        {(void **)&ctx->acc, (size_t)ctx->hkv_loc * 8u * (size_t)D * sizeof(long long)},
+        {(void **)&ctx->ctl, 2u * (size_t)ctx->hkv_loc * sizeof(unsigned)},
         {(void **)&ctx->err, sizeof(unsigned)},
     };
     for (auto &a : allocs) {
         e = cudaMalloc(a.p, a.bytes);
         if (e != cudaSuccess) return bail(fail(KV_E_OOM, "scratch allocation (%zu bytes): %s", a.bytes, cudaGetErrorString(e)));
     }
-    e = cudaMemset(ctx->counters, 0, (size_t)ctx->hkv_loc * sizeof(unsigned));
+    e = cudaMemset(ctx->ctl, 0, 2u * (size_t)ctx->hkv_loc * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(ctx->stats, 0, n_part * 2u * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(ctx->acc, 0, (size_t)ctx->hkv_loc * 8u * (size_t)D * sizeof(long long));
     if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, sizeof(unsigned));
     if (e != cudaSuccess) return bail(cuda_fail(e, "cudaMemset"));
     e = kvb::attn_prepare(ctx->D);
@@ -551,8 +559,7 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
 
     // TMA descriptors: each layer's K and V as [n_ctx][hkv_loc][D] F16, box =
     // one head x 128 keys x a 64-wide column block with 128-byte swizzle (32
-    // wide, 64-byte swizzle at head_dim 96); the scores as [hkv_loc*8][S_stride]
-    // F32, box 132 x 8
+    // wide, 64-byte swizzle at head_dim 96)
     ctx->kmaps.resize(c.n_layer);
     ctx->vmaps.resize(c.n_layer);
     {
@@ -569,12 +576,6 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
                                 box, sw);
             if (rc != KV_OK) return bail(rc);
         }
-        const cuuint64_t sdims[2] = {(cuuint64_t)ctx->S_stride, (cuuint64_t)ctx->hkv_loc * 8};
-        const cuuint64_t sstr[1] = {(cuuint64_t)ctx->S_stride * 4};
-        const cuuint32_t sbox[2] = {(cuuint32_t)stile, 8};
-        const int rc = encode_map(&ctx->smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ctx->S, sdims, sstr, sbox,
-                                  CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (rc != KV_OK) return bail(rc);
     }
 
     if (c.n_shards > 1) {
@@ -729,11 +730,11 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     ap.vc = ctx->v_layer(layer);
     ap.qbuf = ctx->qbuf;
     ap.S = ctx->S;
-    ap.S_stride = ctx->S_stride;
-    ap.part_m = ctx->part_m;
-    ap.part_z = ctx->part_z;
-    ap.part_o = ctx->part_o;
-    ap.counters = ctx->counters;
+    ap.stats = ctx->stats;
+    ap.acc = ctx->acc;
+    ap.counters = ctx->ctl;
+    ap.nonfin = ctx->ctl + ctx->hkv_loc;
+    ap.hz_row = (ctx->hz_stream == st && ctx->hz_layer == layer) ? ctx->hz_row : -1;
     ap.err = ctx->err;
     ap.limit_ns = ctx->limit_ns;
     ap.inject = ctx->inject;
@@ -742,6 +743,15 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     ap.out_stride = dst_stride;
     ap.out_head0 = dst_head0;
     if (ap.n_cta > ctx->max_cta) return fail(KV_E_RANGE, "internal: %d CTAs > %d", ap.n_cta, ctx->max_cta);
+    {
+        // score tiles of the longest CTA range: ceil(ceil(T/C)/128) + 1 (a range
+        // that crosses a head boundary starts a second partial tile)
+        const int64_t T = (int64_t)ctx->hkv_loc * n_kv, C = ap.n_cta, tk = kvb::attn_tile_keys();
+        ap.S_tiles = ((T + C - 1) / C + tk - 1) / tk + 1;
+        if (C * ap.S_tiles * kvb::attn_tile_scores() > ctx->S_floats)
+            return fail(KV_E_RANGE, "internal: score scratch too small for %lld CTAs x %lld tiles", (long long)C,
+                        (long long)ap.S_tiles);
+    }
     {
         // CTA c covers flattened rows [c*T/C, (c+1)*T/C) (the kernels' split)
         const int64_t T = (int64_t)ctx->hkv_loc * n_kv, C = ap.n_cta;
@@ -766,13 +776,20 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     for (int row0 = 0; row0 < rows; row0 += rows_per) {
         ap.row0 = row0;
         ap.nrows = std::min(rows_per, rows - row0);
-        rc = launch(ctx, KV_K_SCORES, st, "attention scores kernel",
-                    [&] { return kvb::launch_attn(ctx->D, 0, km, vm, ctx->smap, ap, st, true); });
+        if (++ctx->epoch == 0) {
+            // the tag wrapped: no slot may carry an old launch's tag 1
+            KV_CUDA(cudaMemsetAsync(ctx->stats, 0, (size_t)ctx->max_cta * 2u * 8u * 2u * sizeof(unsigned long long), st));
+            ctx->epoch = 1;
+        }
+        ap.epoch = ctx->epoch;
+        rc = launch(ctx, KV_K_ATTN, st, "attention kernel",
+                    [&] { return kvb::launch_attn(ctx->D, km, vm, ap, st, true); });
         if (rc) return rc;
-        rc = launch(ctx, KV_K_PV, st, "attention P.V kernel",
-                    [&] { return kvb::launch_attn(ctx->D, 1, km, vm, ctx->smap, ap, st, true); });
-        if (rc) return rc;
+        ap.hz_row = -1;   // row groups after the first do not write the cache
     }
+    ctx->hz_stream = st;
+    ctx->hz_layer = fused ? layer : -1;
+    ctx->hz_row = fused ? n_past : -1;
 
     if (sharded) {
         NcclApi &api = nccl();
@@ -884,8 +901,10 @@ int kv_status(kv_ctx *ctx, void *stream)
     unsigned word = 0;
     KV_CUDA(cudaMemcpy(&word, ctx->err, sizeof(word), cudaMemcpyDeviceToHost));
     if (word == 0) return KV_OK;
-    // a CTA that left early never counted itself in: restart the per-head tickets
-    KV_CUDA(cudaMemset(ctx->counters, 0, (size_t)ctx->hkv_loc * sizeof(unsigned)));
+    // a CTA that left early never counted itself in: restart the per-head
+    // tickets and clear the output accumulators
+    KV_CUDA(cudaMemset(ctx->ctl, 0, 2u * (size_t)ctx->hkv_loc * sizeof(unsigned)));
+    KV_CUDA(cudaMemset(ctx->acc, 0, (size_t)ctx->hkv_loc * 8u * (size_t)ctx->D * sizeof(long long)));
     KV_CUDA(cudaMemset(ctx->err, 0, sizeof(unsigned)));
     return fail(KV_E_TIMEOUT, "a device-side wait expired (error word 0x%x); the outputs of that call are invalid",
                 word);
@@ -972,7 +991,7 @@ int kv_profile_read(kv_ctx *ctx, int32_t kernel, int64_t *launches, double *tota
 
 const char *kv_kernel_name(int32_t kernel)
 {
-    static const char *names[KV_K_COUNT] = {"kv_append", "kv_scores", "kv_pv", "kv_prefill", "kv_unshard"};
+    static const char *names[KV_K_COUNT] = {"kv_append", "kv_attn", "kv_prefill", "kv_unshard"};
     return (kernel >= 0 && kernel < KV_K_COUNT) ? names[kernel] : "?";
 }
 

@@ -75,8 +75,8 @@ cudaError_t launch_scores(int D, const ScoresParams &p, int hkv_loc, cudaStream_
 cudaError_t launch_pv(int D, const PVParams &p, int hkv_loc, cudaStream_t st);
 
 // ---------------------------------------------------------------------------
-// attention of kv_attend (kv_attend.cu): two TMA-fed, tensor-core kernels
-// per layer, chained with programmatic dependent launch
+// attention of kv_attend (kv_attend.cu): one TMA-fed, tensor-core kernel per
+// layer and group of <= 8 query rows, chained with programmatic dependent launch
 // ---------------------------------------------------------------------------
 constexpr int kMaxLocalHeads = 64;   // KV heads one context may own
 
@@ -85,9 +85,9 @@ struct AttnParams {
     int32_t hq0, hkv0;               // first owned global head (inputs are replicated rows)
     int64_t n_kv, n_past;
     int32_t row0, nrows;             // query rows of this launch (row = t*r + j), nrows <= attn_rows()
-    int32_t n_cta;                   // CTAs; hkv <= n_cta <= hkv*n_kv
+    int32_t n_cta;                   // CTAs; hkv <= n_cta <= min(SMs, attn_max_ctas(), hkv*n_kv), all resident
     float scale;
-    // single-token append done inside the kernels (decode): fused = 1
+    // single-token append done inside the kernel (decode): fused = 1
     int32_t fused;
     const float *q, *k, *v;          // token 0's Q/K/V blocks (global heads)
     int64_t q_stride;
@@ -96,17 +96,22 @@ struct AttnParams {
     float eps;
     const float2 *rope;              // [n_ctx][n_rot/2]
     __half *kc, *vc;                 // this layer's cache [n_ctx][hkv][D] (new rows written here)
+    // a cache row the previous launch in the stream may still be writing
+    // (the row a fused launch of this layer appended), -1 if none
+    int64_t hz_row;
     // multi-token: rotated Q from the append kernel
     const __half *qbuf;              // [n_new][hq_loc][D]
     // scratch
-    float *S;                        // [hkv][8][S_stride]
-    int64_t S_stride;
-    float *part_m;                   // [n_cta][2][8]
-    double *part_z;
-    float *part_o;                   // [n_cta][2][8][D]
-    unsigned *counters;              // [hkv], zero between calls
-    unsigned *err;                   // error word (bit 0: consumer wait expired, bit 1: producer)
-    uint64_t limit_ns;               // bound of every mbarrier wait
+    float *S;                        // scores: CTA c, tile i, warp w -> S + ((c*S_tiles + i)*8 + w)*128
+    int64_t S_tiles;                 // tiles reserved per CTA
+    unsigned long long *stats;       // [n_cta][2][8][2] (max, sum of exp) per (CTA, segment, row),
+                                     // each word = epoch << 32 | float bits
+    uint32_t epoch;                  // tag of this launch's statistics (never 0)
+    long long *acc;                  // [hkv][8][D] output accumulators, fixed point 2^-40, zero between calls
+    unsigned *counters;              // [hkv] output tickets, zero between calls
+    unsigned *nonfin;                // [hkv] a non-finite partial output was seen, zero between calls
+    unsigned *err;                   // error word (1: consumer tile wait, 2: producer, 4: statistics wait)
+    uint64_t limit_ns;               // bound of every device-side wait
     int32_t inject;                  // test hook: 1 = producers withhold tile 1
     // output
     float *out;
@@ -118,15 +123,18 @@ struct AttnParams {
     int8_t span_slot[kMaxLocalHeads];
 };
 
-// query rows per launch (8), keys per tile (128), and the column-box width of
-// the K/V tensor maps (64 halves, 128-byte swizzle; 32, 64-byte swizzle at 96)
+// query rows per launch (8), keys per tile (128), the column-box width of the
+// K/V tensor maps (64 halves, 128-byte swizzle; 32, 64-byte swizzle at 96), and
+// the floats of score scratch one tile takes
 int attn_rows();
 int attn_tile_keys();
 int attn_box_width(int D);
+int attn_tile_scores();
+int attn_max_ctas();   // CTAs one launch may have (a head's span is read in one sweep)
 cudaError_t attn_prepare(int D);
-// which: 0 = scores pass, 1 = P.V pass; pdl: launch as a programmatic dependent
-cudaError_t launch_attn(int D, int which, const CUtensorMap &kmap, const CUtensorMap &vmap, const CUtensorMap &smap,
-                        const AttnParams &p, cudaStream_t st, bool pdl);
+// pdl: launch as a programmatic dependent of the previous kernel in the stream
+cudaError_t launch_attn(int D, const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnParams &p,
+                        cudaStream_t st, bool pdl);
 
 // ---------------------------------------------------------------------------
 // gather / layout helpers

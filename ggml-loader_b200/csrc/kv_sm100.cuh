@@ -154,6 +154,37 @@ __device__ __forceinline__ bool named_sync_or(uint32_t id, uint32_t nthreads, bo
     return res != 0;
 }
 
+// ---- per-thread asynchronous copies (L2 -> shared, 16 bytes) ---------------------
+__device__ __forceinline__ void cp_async_16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit()
+{
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ---- cross-CTA slots ------------------------------------------------------------
+// 16-byte stores / loads of two 64-bit words for cross-CTA slots; each word is
+// single-copy atomic, the pair is not (readers check both words).
+__device__ __forceinline__ void st_volatile_v2(unsigned long long *p, unsigned long long a, unsigned long long b)
+{
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+
+__device__ __forceinline__ void ld_volatile_v2(const unsigned long long *p, unsigned long long &a,
+                                               unsigned long long &b)
+{
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue, and wait for the previous kernel's results to be visible.
 __device__ __forceinline__ void pdl_launch_dependents()
