@@ -217,6 +217,13 @@ struct kv_ctx {
     int last_n_new = 0;
     // the cache row the last fused attention launch appended (stream, layer):
     // the next launch on that stream for that layer must not read it early
+    // chunked prefill on the tensor cores (head_dim 64/128, chunks of >= 32 query rows)
+    bool pf = false;
+    int pf_tb = 0;                          // tokens per 128-row query tile
+    CUtensorMap qmap{};                     // qbuf [n_batch_max][hq_loc][D], box 64 x r x tb
+    float *pf_stat = nullptr;               // [sm_count][kseg][128][2]
+    float2 *pf_rstat = nullptr;             // [hkv_loc * blocks][128]
+    float *pf_out = nullptr;                // [sm_count][kseg][128][D]
     cudaStream_t hz_stream = nullptr;
     int hz_layer = -1;
     int64_t hz_row = -1;
@@ -366,8 +373,8 @@ void free_all(kv_ctx *ctx)
     ctx->ev_pool.clear();
     if (ctx->comm && nccl().CommDestroy) nccl().CommDestroy(ctx->comm);
     ctx->comm = nullptr;
-    void *ptrs[] = {ctx->cache, ctx->rope, ctx->qbuf, ctx->S, ctx->stats,
-                    ctx->acc, ctx->ctl, ctx->err, ctx->local_out, ctx->gathered};
+    void *ptrs[] = {ctx->cache, ctx->rope, ctx->qbuf, ctx->S, ctx->stats, ctx->acc, ctx->ctl, ctx->err,
+                    ctx->local_out, ctx->gathered, ctx->pf_stat, ctx->pf_rstat, ctx->pf_out};
     for (void *p : ptrs)
         if (p) cudaFree(p);
 }
@@ -578,6 +585,27 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
         }
     }
 
+    // chunked prefill: the tensor-core path, when chunks can hold 32+ query rows
+    if (kvb::prefill_supported(ctx->D) && ctx->r <= 128 && (int64_t)c.n_batch_max * ctx->r >= 32) {
+        ctx->pf_tb = std::min(128 / ctx->r, (int)c.n_batch_max);   // the Q box's tokens
+        const cuuint64_t qdims[3] = {(cuuint64_t)D, (cuuint64_t)ctx->hq_loc, (cuuint64_t)c.n_batch_max};
+        const cuuint64_t qstr[2] = {(cuuint64_t)D * 2, (cuuint64_t)ctx->hq_loc * D * 2};
+        const cuuint32_t qbox[3] = {64, (cuuint32_t)ctx->r, (cuuint32_t)ctx->pf_tb};
+        int rc = encode_map(&ctx->qmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ctx->qbuf, qdims, qstr, qbox,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc != KV_OK) return bail(rc);
+        const int kseg = kvb::prefill_max_segments();
+        const size_t nblk = (size_t)(c.n_batch_max + ctx->pf_tb - 1) / ctx->pf_tb;
+        const size_t slots = (size_t)ctx->sm_count * kseg * 128u;
+        e = cudaMalloc(&ctx->pf_stat, slots * 2u * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_rstat, (size_t)ctx->hkv_loc * nblk * 128u * sizeof(float2));
+        if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_out, slots * (size_t)D * sizeof(float));
+        if (e != cudaSuccess) return bail(fail(KV_E_OOM, "prefill scratch: %s", cudaGetErrorString(e)));
+        e = kvb::prefill_prepare(ctx->D);
+        if (e != cudaSuccess) return bail(cuda_fail(e, "prefill_prepare"));
+        ctx->pf = true;
+    }
+
     if (c.n_shards > 1) {
         if (!cfg_in->comm_id) return bail(fail(KV_E_ARG, "n_shards > 1 needs comm_id"));
         NcclApi &api = nccl();
@@ -674,6 +702,69 @@ int kv_append(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
     }
     return run_append(ctx, pd);
 }
+
+namespace {
+
+// Chunked-prefill attention on the tensor cores: statistics pass, statistics
+// fold, output pass, output fold (kv_prefill.cu).  The pairs' key tiles, laid
+// end to end, are cut into C equal ranges; C is the SM count, lowered until no
+// range holds more than prefill_max_segments() pairs.
+int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n_past, int32_t n_new, float *dst,
+            int64_t dst_stride, int dst_head0, cudaStream_t st)
+{
+    kvb::PrefillParams pp{};
+    pp.hkv = ctx->hkv_loc;
+    pp.r = ctx->r;
+    pp.hq_loc = ctx->hq_loc;
+    pp.D = ctx->D;
+    pp.n_past = n_past;
+    pp.n_new = n_new;
+    pp.tb = ctx->pf_tb;
+    pp.nblk = (n_new + pp.tb - 1) / pp.tb;
+    std::vector<int64_t> nt(pp.nblk);
+    pp.s_all = 0;
+    for (int b = 0; b < pp.nblk; b++) {
+        nt[b] = (n_past + std::min<int64_t>(n_new, (int64_t)(b + 1) * pp.tb) + 127) / 128;
+        pp.s_all += nt[b];
+    }
+    const int64_t W = (int64_t)pp.hkv * pp.s_all;
+    const int kseg = kvb::prefill_max_segments();
+    // the pairs' starts, to count the segments of each range
+    std::vector<int64_t> start((size_t)pp.hkv * pp.nblk + 1, 0);
+    for (int pr = 0; pr < pp.hkv * pp.nblk; pr++) start[pr + 1] = start[pr] + nt[pr % pp.nblk];
+    int C = (int)std::min<int64_t>(ctx->sm_count, W);
+    for (;; C = std::max(1, C * 3 / 4)) {
+        int worst = 0;
+        for (int cc = 0; cc < C; cc++) {
+            const int64_t lo = (int64_t)cc * W / C, hi = (int64_t)(cc + 1) * W / C;
+            const auto a = std::upper_bound(start.begin(), start.end(), lo) - start.begin() - 1;
+            const auto b = std::upper_bound(start.begin(), start.end(), hi - 1) - start.begin() - 1;
+            worst = std::max(worst, (int)(b - a + 1));
+        }
+        if (worst <= kseg || C == 1) break;
+    }
+    pp.n_cta = C;
+    pp.kseg = kseg;
+    pp.scale = ctx->scale;
+    pp.pstat = ctx->pf_stat;
+    pp.rstat = ctx->pf_rstat;
+    pp.pout = ctx->pf_out;
+    pp.out = dst;
+    pp.out_stride = dst_stride;
+    pp.out_head0 = dst_head0;
+    pp.err = ctx->err;
+    pp.limit_ns = ctx->limit_ns;
+    static const char *what[4] = {"prefill statistics kernel", "prefill statistics fold", "prefill output kernel",
+                                  "prefill output fold"};
+    for (int which = 0; which < 4; which++) {
+        const int rc = launch(ctx, KV_K_PREFILL, st, what[which],
+                              [&] { return kvb::launch_prefill(ctx->D, which, ctx->qmap, km, vm, pp, st); });
+        if (rc) return rc;
+    }
+    return KV_OK;
+}
+
+}  // namespace
 
 int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *out, void *stream)
 {
@@ -773,7 +864,11 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     const int rows = n_new * ctx->r;
     const int rows_per = kvb::attn_rows();
     const CUtensorMap &km = ctx->kmaps[layer], &vm = ctx->vmaps[layer];
-    for (int row0 = 0; row0 < rows; row0 += rows_per) {
+    if (!fused && ctx->pf && rows >= 32) {
+        rc = prefill(ctx, km, vm, n_past, n_new, dst, dst_stride, dst_head0, st);
+        if (rc) return rc;
+    }
+    for (int row0 = 0; row0 < rows && !(!fused && ctx->pf && rows >= 32); row0 += rows_per) {
         ap.row0 = row0;
         ap.nrows = std::min(rows_per, rows - row0);
         if (++ctx->epoch == 0) {

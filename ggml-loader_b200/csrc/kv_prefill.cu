@@ -1,0 +1,550 @@
+// kv_prefill.cu -- attention of a multi-token chunk (prefill) on the 5th-
+// generation tensor cores: tcgen05.mma with TMEM accumulators, operands staged
+// in shared memory by TMA.
+//
+// Numerics: the reference's attention branch (src/model.cpp:1416-1445) for
+// n_new query tokens: S = F16(q) . K (F32 accumulation), causal mask (key <=
+// n_past + token), softmax with the global row max M and sum Z, p = F16(exp(s
+// - M) / Z), O = p . V (F32 accumulation).  ggml rounds the normalised p to
+// F16, so every p needs the final M and Z of its row: pass 1 computes S and
+// the row statistics, pass 2 computes S again, forms p and accumulates P . V.
+// exp is 2^(x log2 e) on the SFU (ex2.approx): within a few F32 ulps of expf,
+// far inside the attention tolerance.
+//
+// Work: query rows are packed GQA-group-major: one 128-row tile holds tb =
+// floor(128 / r) tokens x the r query heads of one KV head (row = token*r +
+// head), so a K/V tile staged once serves every head of the group.  A "pair" is
+// (KV head, block of tb tokens); its keys are the tiles of 128 keys up to the
+// block's last visible key.  The pairs' tiles, laid end to end, are cut into C
+// equal ranges (one CTA each, C <= SMs); a range holds one or more "segments"
+// (the part of one pair it covers).
+//
+// prefill_kernel<D, OUT> (192 threads):
+//   warp 0     TMA: the pair's Q tile, then K tiles (and V tiles in pass 2) into
+//              mbarrier rings;
+//   warp 1     TMEM owner and MMA issuer (one thread): S = Q . K^T, M=128, N=128
+//              keys, K = D, into one of two 128-column TMEM buffers; in pass 2
+//              also O += P . V (M=128, N=D, K=128 keys, V read MN-major) into
+//              D more columns, one tile behind;
+//   warps 2-5  one query row per thread, read from TMEM with tcgen05.ld:
+//              pass 1 keeps the running row max / sum of exp; pass 2 writes p
+//              as F16 into a double-buffered, 128-byte-swizzled P tile (the A
+//              operand of the next MMA) and, at a segment's end, copies O out.
+// prefill_stats_fold   (M, 1/Z) of every (pair, row) from the segments' partials
+// prefill_out_fold     sum of the segments' partial outputs, scattered to out
+// Every wait is bounded (limit_ns) and gives up when the CTA's abort flag is
+// set; the CTA drains its TMA loads and MMAs and frees TMEM before leaving.
+#include <math.h>
+
+#include "kv_internal.h"
+#include "kv_sm100.cuh"
+
+namespace kvb {
+namespace {
+
+using namespace sm100;
+
+constexpr int kPThreads = 192;
+constexpr uint32_t kBox = 128 * 128;   // one [128 rows][64 halves] swizzled box
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D, bool OUT>
+struct PL {
+    static constexpr int NB = D / 64;                        // boxes per Q/K/V row
+    static constexpr uint32_t kTile = (uint32_t)NB * kBox;   // 128 rows x D halves
+    static constexpr int KS = OUT ? (D == 128 ? 2 : 4) : (D == 128 ? 5 : 8);
+    static constexpr int VS = OUT ? (D == 128 ? 2 : 4) : 0;
+    static constexpr size_t o_q = 0;
+    static constexpr size_t o_k = o_q + kTile;
+    static constexpr size_t o_v = o_k + (size_t)KS * kTile;
+    static constexpr size_t o_p = o_v + (size_t)VS * kTile;  // 2 buffers x 2 boxes (128 keys)
+    static constexpr size_t o_bar = o_p + (OUT ? 4 * (size_t)kBox : 0);
+    // q_full, q_empty, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
+    // s_full[2], s_free[2], p_full[2], p_empty[2], o_full, o_empty, drain
+    static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 8 + 3;
+    static constexpr size_t o_tm = o_bar + (size_t)NBAR * 8;
+    static constexpr size_t o_flags = o_tm + 16;
+    static constexpr size_t bytes = o_flags + 16;
+    static_assert(bytes <= 227 * 1024, "shared memory of the prefill kernel");
+};
+
+// ---- the work split ------------------------------------------------------------
+__device__ __forceinline__ int nt_of(const PrefillParams &p, int b)
+{
+    const int64_t last = p.n_past + min(p.n_new, (b + 1) * p.tb);   // keys [0, last)
+    return (int)((last + 127) / 128);
+}
+
+__device__ __forceinline__ int64_t pair_start(const PrefillParams &p, int pair)
+{
+    const int kvh = pair / p.nblk, b = pair % p.nblk;
+    int64_t x = (int64_t)kvh * p.s_all;
+    for (int bb = 0; bb < b; bb++) x += nt_of(p, bb);
+    return x;
+}
+
+// pair holding flattened tile x
+__device__ __forceinline__ int pair_of(const PrefillParams &p, int64_t x)
+{
+    const int kvh = (int)(x / p.s_all);
+    int64_t rem = x - (int64_t)kvh * p.s_all;
+    int b = 0;
+    for (; b < p.nblk - 1; b++) {
+        const int n = nt_of(p, b);
+        if (rem < n) break;
+        rem -= n;
+    }
+    return kvh * p.nblk + b;
+}
+
+__device__ __forceinline__ int64_t cta_lo(const PrefillParams &p, int c)
+{
+    return (int64_t)c * ((int64_t)p.hkv * p.s_all) / p.n_cta;
+}
+
+// segment k of CTA c: pair, its tiles [t0, t1)
+struct Seg {
+    int pair, t0, t1;
+};
+
+template <class F>
+__device__ __forceinline__ void for_segments(const PrefillParams &p, int c, F &&f)
+{
+    int64_t x = cta_lo(p, c);
+    const int64_t hi = cta_lo(p, c + 1);
+    int k = 0;
+    while (x < hi && k < p.kseg) {
+        Seg s;
+        s.pair = pair_of(p, x);
+        const int64_t ps = pair_start(p, s.pair);
+        const int64_t pe = ps + nt_of(p, s.pair % p.nblk);
+        const int64_t e = min(hi, pe);
+        s.t0 = (int)(x - ps);
+        s.t1 = (int)(e - ps);
+        if (!f(k, s)) return;
+        x = e;
+        k++;
+    }
+}
+
+__device__ __forceinline__ void give_up(const PrefillParams &p, volatile int *flags, unsigned bit)
+{
+    if (!flags[0]) {
+        atomicOr(p.err, bit);
+        flags[0] = 1;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// pass 1 (OUT = false) and pass 2 (OUT = true)
+// ---------------------------------------------------------------------------
+template <int D, bool OUT>
+__global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                                 const __grid_constant__ CUtensorMap kmap,
+                                                                 const __grid_constant__ CUtensorMap vmap,
+                                                                 const PrefillParams p)
+{
+    using L = PL<D, OUT>;
+    constexpr int NB = L::NB, KS = L::KS, VS = L::VS;
+    constexpr uint32_t kTile = L::kTile;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::o_bar);
+    uint64_t *q_full = bar, *q_empty = bar + 1;
+    uint64_t *k_full = bar + 2, *k_empty = k_full + KS;
+    uint64_t *v_full = k_empty + KS, *v_empty = v_full + VS;
+    uint64_t *s_full = v_empty + VS, *s_free = s_full + 2;
+    uint64_t *p_full = s_free + 2, *p_empty = p_full + 2;
+    uint64_t *o_full = p_empty + 2, *o_empty = o_full + 1, *drain = o_empty + 1;
+    uint32_t *tm_slot = reinterpret_cast<uint32_t *>(smem + L::o_tm);
+    volatile int *flags = reinterpret_cast<volatile int *>(smem + L::o_flags);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, c = blockIdx.x;
+    int issued_q = 0, issued_k = 0, issued_v = 0;   // TMA loads issued (warp 0, lane 0)
+
+    if (tid == 0) {
+        for (int i = 0; i < L::NBAR; i++) {
+            // the four softmax warps arrive on s_free, p_full and o_empty
+            const uint64_t *bi = &bar[i];
+            const bool four = bi == &s_free[0] || bi == &s_free[1] || bi == &p_full[0] || bi == &p_full[1] ||
+                              bi == o_empty;
+            mbar_init(&bar[i], four ? 4 : 1);
+        }
+        flags[0] = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tm_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tm_slot;
+
+    if (warp == 0) {
+        // ================= TMA =================
+        if (lane == 0) {
+            prefetch_tmap(&qmap);
+            prefetch_tmap(&kmap);
+            if (OUT) prefetch_tmap(&vmap);
+            const uint32_t qbytes = (uint32_t)(p.r * p.tb) * 128u * NB;
+            for_segments(p, c, [&](int k, const Seg &sg) {
+                const int kvh = sg.pair / p.nblk, b = sg.pair % p.nblk;
+                if (k > 0 && !mbar_wait_ab(q_empty, (k - 1) & 1, p.limit_ns, flags)) {
+                    give_up(p, flags, 2u);
+                    return false;
+                }
+                mbar_arrive_expect_tx(q_full, qbytes);
+#pragma unroll
+                for (int bx = 0; bx < NB; bx++)
+                    tma_load_3d(smem + L::o_q + bx * kBox, &qmap, q_full, bx * 64, kvh * p.r, b * p.tb);
+                issued_q++;
+                for (int t = sg.t0; t < sg.t1; t++) {
+                    const int s = issued_k % KS;
+                    if (issued_k >= KS && !mbar_wait_ab(&k_empty[s], ((issued_k / KS) - 1) & 1, p.limit_ns, flags)) {
+                        give_up(p, flags, 2u);
+                        return false;
+                    }
+                    mbar_arrive_expect_tx(&k_full[s], kTile);
+#pragma unroll
+                    for (int bx = 0; bx < NB; bx++)
+                        tma_load_3d(smem + L::o_k + s * kTile + bx * kBox, &kmap, &k_full[s], bx * 64, kvh, t * 128);
+                    issued_k++;
+                    if constexpr (OUT) {
+                        const int sv = issued_v % VS;
+                        if (issued_v >= VS &&
+                            !mbar_wait_ab(&v_empty[sv], ((issued_v / VS) - 1) & 1, p.limit_ns, flags)) {
+                            give_up(p, flags, 2u);
+                            return false;
+                        }
+                        mbar_arrive_expect_tx(&v_full[sv], kTile);
+#pragma unroll
+                        for (int bx = 0; bx < NB; bx++)
+                            tma_load_3d(smem + L::o_v + sv * kTile + bx * kBox, &vmap, &v_full[sv], bx * 64, kvh,
+                                        t * 128);
+                        issued_v++;
+                    }
+                }
+                return true;
+            });
+        }
+    } else if (warp == 1) {
+        // ================= MMA issue =================
+        if (lane == 0) {
+            constexpr uint32_t idS = idesc_f16_f32(128, 128, false);
+            constexpr uint32_t idO = idesc_f16_f32(128, D, true);
+            const uint32_t sq = smem_addr(smem + L::o_q), sk = smem_addr(smem + L::o_k);
+            const uint32_t sv = smem_addr(smem + L::o_v), sp = smem_addr(smem + L::o_p);
+            int j = 0;               // tiles issued (S)
+            int pend = -1;           // tile whose P . V is still to issue
+            bool pend_first = false, pend_last = false;
+            int pend_seg = 0;
+            bool ok = true;
+            auto issue_pv = [&]() -> bool {
+                const int jp = pend, pb = jp & 1, vs = jp % (VS > 0 ? VS : 1);
+                if (!mbar_wait_ab(&p_full[pb], (jp >> 1) & 1, p.limit_ns, flags) ||
+                    !mbar_wait_ab(&v_full[vs], (jp / (VS > 0 ? VS : 1)) & 1, p.limit_ns, flags) ||
+                    (pend_first && pend_seg > 0 && !mbar_wait_ab(o_empty, (pend_seg - 1) & 1, p.limit_ns, flags))) {
+                    give_up(p, flags, 1u);
+                    return false;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint64_t a = sdesc_k_sw128(sp + pb * 2 * kBox + (kk >> 2) * kBox + (kk & 3) * 32);
+                    const uint64_t bd = sdesc_mn_sw128(sv + vs * kTile + kk * 2048, kBox);
+                    umma_ss(tmem + 256, a, bd, idO, !(pend_first && kk == 0));
+                }
+                umma_commit(&p_empty[pb]);
+                umma_commit(&v_empty[vs]);
+                if (pend_last) umma_commit(o_full);
+                return true;
+            };
+            for_segments(p, c, [&](int k, const Seg &sg) {
+                if (!mbar_wait_ab(q_full, k & 1, p.limit_ns, flags)) {
+                    give_up(p, flags, 1u);
+                    return ok = false;
+                }
+                for (int t = sg.t0; t < sg.t1; t++) {
+                    const int s = j % KS, sb = j & 1;
+                    if (!mbar_wait_ab(&k_full[s], (j / KS) & 1, p.limit_ns, flags) ||
+                        (j >= 2 && !mbar_wait_ab(&s_free[sb], ((j - 2) >> 1) & 1, p.limit_ns, flags))) {
+                        give_up(p, flags, 1u);
+                        return ok = false;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; kk++) {
+                        const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+                        umma_ss(tmem + sb * 128, sdesc_k_sw128(sq + off), sdesc_k_sw128(sk + s * kTile + off), idS,
+                                kk > 0);
+                    }
+                    umma_commit(&s_full[sb]);
+                    umma_commit(&k_empty[s]);
+                    if (t == sg.t1 - 1) umma_commit(q_empty);
+                    if constexpr (OUT) {
+                        if (pend >= 0 && !issue_pv()) return ok = false;
+                        pend = j;
+                        pend_first = t == sg.t0;
+                        pend_last = t == sg.t1 - 1;
+                        pend_seg = k;
+                    }
+                    j++;
+                }
+                return true;
+            });
+            if (OUT && ok && pend >= 0) issue_pv();
+            // every MMA this thread issued has completed before TMEM is freed
+            umma_commit(drain);
+            mbar_wait(drain, 0, p.limit_ns);
+        }
+    } else {
+        // ================= softmax / epilogue: one query row per thread =================
+        const int q4 = warp & 3;                  // TMEM lane quarter of this warp
+        const int row = q4 * 32 + lane;           // query row of the tile = token*r + head
+        const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+        const int tok_in = row / p.r, hd = row - tok_in * p.r;
+        const bool row_ok = tok_in < p.tb;
+        int j = 0;
+        for_segments(p, c, [&](int k, const Seg &sg) {
+            const int kvh = sg.pair / p.nblk, b = sg.pair % p.nblk;
+            const int tok = b * p.tb + tok_in;
+            const bool valid = row_ok && tok < p.n_new;
+            const int64_t lim = valid ? p.n_past + tok : -1;   // last visible key
+            float M = 0.0f, inv = 0.0f;
+            if constexpr (OUT) {
+                if (valid) {
+                    const float2 st = p.rstat[(int64_t)sg.pair * 128 + row];
+                    M = st.x;
+                    inv = st.y;
+                }
+            }
+            float m = -INFINITY, z = 0.0f;
+            for (int t = sg.t0; t < sg.t1; t++, j++) {
+                const int sb = j & 1, pb = j & 1;
+                if (!mbar_wait_ab(&s_full[sb], (j >> 1) & 1, p.limit_ns, flags)) {
+                    give_up(p, flags, 1u);
+                    return false;
+                }
+                tc_fence_after();
+                if constexpr (OUT) {
+                    if (j >= 2 && !mbar_wait_ab(&p_empty[pb], ((j - 2) >> 1) & 1, p.limit_ns, flags)) {
+                        give_up(p, flags, 1u);
+                        return false;
+                    }
+                }
+                const int64_t key0 = (int64_t)t * 128;
+                unsigned char *prow = smem + L::o_p + pb * 2 * kBox + row * 128;
+#pragma unroll 1
+                for (int ch = 0; ch < 4; ch++) {
+                    uint32_t v[32];
+                    tmem_ld32(trow + sb * 128 + ch * 32, v);
+                    tmem_wait_ld();
+                    if (ch == 3) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&s_free[sb]);
+                    }
+                    const int64_t kc = key0 + ch * 32;
+                    const int nvis = (int)max((int64_t)0, min((int64_t)32, lim - kc + 1));   // keys of the chunk visible
+                    if constexpr (!OUT) {
+                        float cm = -INFINITY;
+#pragma unroll
+                        for (int e = 0; e < 32; e++) {
+                            const float s = __fmul_rn(__uint_as_float(v[e]), p.scale);
+                            v[e] = __float_as_uint(e < nvis ? s : -INFINITY);
+                            cm = fmaxf(cm, __uint_as_float(v[e]));
+                        }
+                        const float mn = fmaxf(m, cm);
+                        if (mn != -INFINITY) {
+                            const float nb = -mn * kLog2e;
+                            float acc = m == -INFINITY ? 0.0f : z * ex2_approx(fmaf(m, kLog2e, nb));
+#pragma unroll
+                            for (int e = 0; e < 32; e++)
+                                acc += ex2_approx(fmaf(__uint_as_float(v[e]), kLog2e, nb));
+                            z = acc;
+                            m = mn;
+                        }
+                    } else {
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int e = 0; e < 16; e++) {
+                            float pe[2];
+#pragma unroll
+                            for (int u = 0; u < 2; u++) {
+                                const int ee = 2 * e + u;
+                                const float s = __fmul_rn(__uint_as_float(v[ee]), p.scale);
+                                pe[u] = ee < nvis ? __fmul_rn(ex2_approx(__fmul_rn(__fsub_rn(s, M), kLog2e)), inv) : 0.0f;
+                            }
+                            pk[e] = pack_half2(__float2half_rn(pe[0]), __float2half_rn(pe[1]));
+                        }
+                        // keys ch*32 .. +31: box ch/2, 16-byte chunks (ch%2)*4 .. +3, swizzled by row
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            const int chunk = (ch & 1) * 4 + q;
+                            *reinterpret_cast<uint4 *>(prow + (ch >> 1) * kBox + ((chunk ^ (row & 7)) << 4)) =
+                                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                        }
+                    }
+                }
+                if constexpr (OUT) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // P feeds tcgen05.mma
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&p_full[pb]);
+                }
+            }
+            if constexpr (!OUT) {
+                float2 *ps = reinterpret_cast<float2 *>(p.pstat) + ((int64_t)c * p.kseg + k) * 128 + row;
+                *ps = make_float2(m, z);
+            } else {
+                if (!mbar_wait_ab(o_full, k & 1, p.limit_ns, flags)) {
+                    give_up(p, flags, 1u);
+                    return false;
+                }
+                tc_fence_after();
+                float *po = p.pout + (((int64_t)c * p.kseg + k) * 128 + row) * D;
+#pragma unroll 1
+                for (int ch = 0; ch < D / 32; ch++) {
+                    uint32_t v[32];
+                    tmem_ld32(trow + 256 + ch * 32, v);
+                    tmem_wait_ld();
+                    if (valid)
+#pragma unroll
+                        for (int q = 0; q < 8; q++)
+                            *reinterpret_cast<uint4 *>(po + ch * 32 + 4 * q) =
+                                make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(o_empty);
+            }
+            (void)kvh;
+            (void)hd;
+            return true;
+        });
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0 && lane == 0 && flags[0]) {
+        // the CTA gave up: loads nobody waited for may still be landing
+        for (int j = issued_k > KS ? issued_k - KS : 0; j < issued_k; j++)
+            mbar_wait(&k_full[j % KS], (j / KS) & 1, p.limit_ns);
+        if constexpr (OUT)
+            for (int j = issued_v > VS ? issued_v - VS : 0; j < issued_v; j++)
+                mbar_wait(&v_full[j % VS], (j / VS) & 1, p.limit_ns);
+        if (issued_q > 0) mbar_wait(q_full, (issued_q - 1) & 1, p.limit_ns);
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// folds
+// ---------------------------------------------------------------------------
+// CTAs [ca, cb] hold pair `pair`; its segment index in CTA cc
+__device__ __forceinline__ void pair_ctas(const PrefillParams &p, int pair, int &ca, int &cb)
+{
+    const int64_t W = (int64_t)p.hkv * p.s_all;
+    const int64_t x0 = pair_start(p, pair), x1 = x0 + nt_of(p, pair % p.nblk) - 1;
+    auto cta_of = [&](int64_t x) {
+        int cc = (int)min((int64_t)p.n_cta - 1, x * p.n_cta / W);
+        while (cc + 1 < p.n_cta && cta_lo(p, cc + 1) <= x) cc++;
+        while (cc > 0 && cta_lo(p, cc) > x) cc--;
+        return cc;
+    };
+    ca = cta_of(x0);
+    cb = cta_of(x1);
+}
+
+__device__ __forceinline__ int seg_index(const PrefillParams &p, int cc, int pair)
+{
+    return pair - pair_of(p, cta_lo(p, cc));
+}
+
+// (M, 1/Z) per (pair, row): one thread per row, CTAs in order
+__global__ void prefill_stats_fold(const PrefillParams p)
+{
+    const int pair = blockIdx.x, row = threadIdx.x;
+    int ca, cb;
+    pair_ctas(p, pair, ca, cb);
+    const float2 *ps = reinterpret_cast<const float2 *>(p.pstat);
+    float M = -INFINITY;
+    for (int cc = ca; cc <= cb; cc++) M = fmaxf(M, ps[((int64_t)cc * p.kseg + seg_index(p, cc, pair)) * 128 + row].x);
+    double Z = 0.0;
+    for (int cc = ca; cc <= cb; cc++) {
+        const float2 v = ps[((int64_t)cc * p.kseg + seg_index(p, cc, pair)) * 128 + row];
+        if (v.x != -INFINITY) Z += (double)v.y * (double)exp2f((v.x - M) * kLog2e);
+    }
+    p.rstat[(int64_t)pair * 128 + row] = make_float2(M, Z > 0.0 ? __fdiv_rn(1.0f, (float)Z) : 0.0f);
+}
+
+// out row = sum of the pair's partial outputs (CTAs in order); one block per
+// (pair, row), one thread per dim
+__global__ void prefill_out_fold(const PrefillParams p)
+{
+    const int pair = blockIdx.x / 128, row = blockIdx.x % 128, dd = threadIdx.x;
+    const int tok_in = row / p.r, hd = row - tok_in * p.r;
+    const int b = pair % p.nblk, kvh = pair / p.nblk;
+    const int tok = b * p.tb + tok_in;
+    if (tok_in >= p.tb || tok >= p.n_new) return;
+    int ca, cb;
+    pair_ctas(p, pair, ca, cb);
+    float sum = 0.0f;
+    for (int cc = ca; cc <= cb; cc++)
+        sum += __ldg(p.pout + (((int64_t)cc * p.kseg + seg_index(p, cc, pair)) * 128 + row) * p.D + dd);
+    p.out[(int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * p.D + dd] = sum;
+}
+
+template <int D>
+cudaError_t prep_pf()
+{
+    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)PL<D, false>::bytes);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(prefill_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)PL<D, true>::bytes);
+}
+
+template <int D>
+cudaError_t launch_pf(int which, const CUtensorMap &qmap, const CUtensorMap &kmap, const CUtensorMap &vmap,
+                      const PrefillParams &p, cudaStream_t st)
+{
+    switch (which) {
+    case 0:
+        prefill_kernel<D, false><<<p.n_cta, kPThreads, PL<D, false>::bytes, st>>>(qmap, kmap, vmap, p);
+        break;
+    case 1: prefill_stats_fold<<<p.hkv * p.nblk, 128, 0, st>>>(p); break;
+    case 2:
+        prefill_kernel<D, true><<<p.n_cta, kPThreads, PL<D, true>::bytes, st>>>(qmap, kmap, vmap, p);
+        break;
+    default: prefill_out_fold<<<p.hkv * p.nblk * 128, D, 0, st>>>(p); break;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool prefill_supported(int D) { return D == 64 || D == 128; }
+int prefill_max_segments() { return 4; }
+
+cudaError_t prefill_prepare(int D)
+{
+    switch (D) {
+    case 64: return prep_pf<64>();
+    case 128: return prep_pf<128>();
+    default: return cudaSuccess;
+    }
+}
+
+cudaError_t launch_prefill(int D, int which, const CUtensorMap &qmap, const CUtensorMap &kmap,
+                           const CUtensorMap &vmap, const PrefillParams &p, cudaStream_t st)
+{
+    switch (D) {
+    case 64: return launch_pf<64>(which, qmap, kmap, vmap, p, st);
+    case 128: return launch_pf<128>(which, qmap, kmap, vmap, p, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace kvb
