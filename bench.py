@@ -34,9 +34,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "ggml-loader_b200"))
 
 METRIC = "decode KV-append+attention µs/token and HBM GB/s (% of roofline) at 1/2/4/8 B200"
+METRIC_PREFILL = "chunked-prefill KV-append+attention TFLOP/s (% of tensor roofline) on B200"
 DEFAULT_CONFIG = "llama3.2-3b"
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 
 
 def log(*a):
@@ -56,19 +58,30 @@ def step_bytes(sp, n_past, n_new=1):
     return sp["n_layer"] * layer_bytes(sp, n_past + n_new, n_new)
 
 
+def layer_flops(sp, n_past, n_new, shards=1):
+    """Algorithmic attention FLOPs of one layer: 4*d*Hq per visible (query, key)
+    pair -- S = QK^T and O = PV, masked keys count 0."""
+    keys = n_new * n_past + n_new * (n_new + 1) // 2
+    return 4 * sp["head_dim"] * (sp["n_head"] // shards) * keys
+
+
+def step_flops(sp, n_past, n_new):
+    return sp["n_layer"] * layer_flops(sp, n_past, n_new)
+
+
 def positions(sp, first_step, count):
     cyc = max(1, sp["steps"])
     return [sp["n_past"] + ((first_step + i) % cyc) for i in range(count)]
 
 
-def measured_peak():
+def measured_peak(key="hbm_gbs"):
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(p) as f:
             j = json.load(f)
-        return float(j["hbm_gbs"]), "measured"
+        return float(j[key]), "measured"
     except Exception:
-        return FALLBACK_HBM_GBS, "fallback"
+        return (FALLBACK_HBM_GBS if key == "hbm_gbs" else FALLBACK_BF16_TFLOPS), "fallback"
 
 
 def committed_traffic(config, kernel):
@@ -168,7 +181,7 @@ class CpuPath:
         self.sp, self.O, self.synth = sp, O, synth
         hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
         self.max_steps = max(1, min(max_steps, sp["steps"]))
-        n_ctx = sp["n_past"] + self.max_steps
+        n_ctx = sp["n_past"] + self.max_steps + sp["n_new"]
         per_layer_cache = 2 * n_ctx * hkv * d * 2
         self.n_lay = max(1, min(sp["n_layer"], 4, int(2e9 // per_layer_cache)))
         self.caches = []
@@ -182,10 +195,12 @@ class CpuPath:
         self.orc = O.Oracle(sp)
         self.threads = n_threads if n_threads > 0 else O.online_cores()
         self.norms = [synth.norm_weights(sp, l) if sp["qk_norm"] else (None, None) for l in range(self.n_lay)]
-        self.inputs = [[synth.qkv_rows(sp, s, l, 1) for l in range(self.n_lay)] for s in range(self.max_steps)]
+        self.n_new = sp["n_new"]
+        self.inputs = [[synth.qkv_rows(sp, s, l, self.n_new) for l in range(self.n_lay)]
+                       for s in range(self.max_steps)]
 
     def step(self, s):
-        """One decode step over the sample layers; returns (seconds, bytes, layer-steps)."""
+        """One step over the sample layers; returns (seconds, bytes, layer-steps, FLOPs)."""
         sp = self.sp
         hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
         s %= self.max_steps
@@ -199,26 +214,30 @@ class CpuPath:
             qr = self.orc.append(kc, vc, n_past, q, k, v, self.norms[l][0], self.norms[l][1])
             self.orc.attend(kc, vc, n_past, qr, n_threads=self.threads)
             t += time.perf_counter() - t0
-        return t, self.n_lay * layer_bytes(sp, n_past + 1), self.n_lay
+        return (t, self.n_lay * layer_bytes(sp, n_past + self.n_new, self.n_new), self.n_lay,
+                self.n_lay * layer_flops(sp, n_past, self.n_new))
 
     def describe(self, steps):
         sp = self.sp
-        return ("%d decode step(s) x first %d of %d layers at n_kv from %d, %d threads; per-token time "
-                "extrapolated linearly to all layers" % (steps, self.n_lay, sp["n_layer"], sp["n_past"] + 1,
+        what = "decode step(s)" if self.n_new == 1 else "%d-token chunk(s)" % self.n_new
+        return ("%d %s x first %d of %d layers at n_past %d, %d threads; per-step time "
+                "extrapolated linearly to all layers" % (steps, what, self.n_lay, sp["n_layer"], sp["n_past"],
                                                        self.threads))
 
 
 def cpu_sample(sp, seconds, max_steps):
     """(GB/s, us per token, description, threads) of the CPU path over about `seconds`."""
     cp = CpuPath(sp, max_steps)
-    t_total, nbytes, nls, s = 0.0, 0, 0, 0
+    t_total, nbytes, nls, s, fl = 0.0, 0, 0, 0, 0
     while s < cp.max_steps and (t_total < seconds or s == 0):
-        t, b, n = cp.step(s)
+        t, b, n, f = cp.step(s)
         t_total += t
         nbytes += b
         nls += n
+        fl += f
         s += 1
-    return nbytes / t_total / 1e9, t_total / nls * sp["n_layer"] * 1e6, cp.describe(s), cp.threads
+    return (nbytes / t_total / 1e9, t_total / nls * sp["n_layer"] * 1e6, cp.describe(s), cp.threads,
+            fl / t_total / 1e12)
 
 
 def run_reference(args, sp):
@@ -226,14 +245,31 @@ def run_reference(args, sp):
     if rank != 0:
         return 0
     cp = CpuPath(sp, args.warmup + args.steps)
-    t_total, nbytes, nls = 0.0, 0, 0
+    t_total, nbytes, nls, fl = 0.0, 0, 0, 0
     for i in range(args.warmup + args.steps):
-        t, b, n = cp.step(i)
+        t, b, n, f = cp.step(i)
         if i >= args.warmup:
             t_total += t
             nbytes += b
             nls += n
+            fl += f
     gbs = nbytes / t_total / 1e9
+    if sp["n_new"] > 1:   # prefill: the tensor-bound metric
+        tf = fl / t_total / 1e12
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC_PREFILL, "value": round(tf, 5), "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_total / nls * sp["n_layer"] * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16 cache, f32 math",
+            "data": "synthetic (seeded generator, configuration shapes)",
+            "config": {"workload": sp["name"], "n_past": sp["n_past"], "n_new": sp["n_new"],
+                       "parallelism": "host threads"},
+            "cpu_baseline": {"value": round(tf, 5), "unit": "TFLOP/s", "cores": cp.threads, "kind": "port",
+                             "sample": "each step: " + cp.describe(1)},
+            "e2e": {"value": round(tf, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "CPU restatement of model.cpp:1382-1445 (ggml not vendored, reference backend unbuildable)"}),
+            flush=True)
+        return 0
     us = t_total / nls * sp["n_layer"] * 1e6
     desc = cp.describe(1)
     threads = cp.threads
@@ -363,6 +399,9 @@ def run_ours(args, sp):
     total_bytes = sum(step_bytes(sp, p, n_new) for p in pos)
     value = total_bytes / (ms / 1e3) / 1e9
     ms_step = ms / args.steps
+    prefill = n_new > 1
+    if prefill:   # tensor-bound: algorithmic attention TFLOP/s of the whole job
+        value = sum(step_flops(sp, p, n_new) for p in pos) / (ms / 1e3) / 1e12
 
     # per-kernel durations (separate pass, CUDA events around each launch)
     prof_steps = min(args.steps, 32)
@@ -373,7 +412,7 @@ def run_ours(args, sp):
         step(pfirst + i)
     torch.cuda.synchronize()
     kern = {}
-    for name in ("append", "attn", "gather"):
+    for name in ("append", "attn", "prefill", "pfold", "gather"):
         n, tms = ctx.profile_read(name)
         kern[name] = (n, tms)
     ctx.profile(False)
@@ -392,6 +431,16 @@ def run_ours(args, sp):
     n_dom, t_dom = kern[dom]
     peak, peak_kind = measured_peak()
     achieved = algo[dom] / (t_dom / n_dom / 1e3) / 1e9 if n_dom else None
+    if prefill:
+        # both passes of the tensor-core kernel per layer carry the layer's
+        # algorithmic FLOPs; timed per launch (burst peak)
+        dom = "prefill"
+        n_dom, t_dom = kern[dom]
+        peak, peak_kind = measured_peak("bf16_tflops")
+        lf = statistics.mean(layer_flops(sp, p, n_new, world) for p in ppos)
+        per_layer_ms = t_dom / max(1, n_dom // 2)
+        achieved = lf / (per_layer_ms / 1e3) / 1e12 if n_dom else None
+        algo[dom] = lf
     kernel_table = {k: {"launches": v[0], "total_ms": round(v[1], 4),
                         "avg_us": round(v[1] / v[0] * 1e3, 3) if v[0] else None} for k, v in kern.items()}
 
@@ -420,26 +469,32 @@ def run_ours(args, sp):
         e2e_ms = max_over_ranks(f0.elapsed_time(f1))
         epos = positions(sp, efirst, e2e_steps)
         e2e_value = sum(step_bytes(sp, p, n_new) for p in epos) / (e2e_ms / 1e3) / 1e9
-        e2e = {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+        if prefill:
+            e2e_value = sum(step_flops(sp, p, n_new) for p in epos) / (e2e_ms / 1e3) / 1e12
+        e2e = {"value": round(e2e_value, 2), "unit": "TFLOP/s" if prefill else "GB/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "us_per_token": round(e2e_ms / e2e_steps * 1e3, 2),
                "note": "pinned host inputs copied in and outputs copied out every step, host sync per step"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        gbs, us, desc, threads = cpu_sample(sp, args.cpu_seconds, 64)
-        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc,
-               "us_per_token": round(us, 1)}
+        gbs, us, desc, threads, tfs = cpu_sample(sp, args.cpu_seconds, 64)
+        cpu = {"value": round(tfs, 5) if prefill else round(gbs, 4), "unit": "TFLOP/s" if prefill else "GB/s",
+               "cores": threads, "kind": "port", "sample": desc, "us_per_token": round(us, 1)}
 
     clocks = sampler.summary() if rank == 0 else None
     barrier()
     if rank == 0:
         us_tok = ms_step * 1e3
         ideal_us = statistics.mean(step_bytes(sp, p, n_new) for p in pos) / (peak * world * 1e9) * 1e6
+        if prefill:
+            ideal_us = statistics.mean(step_flops(sp, p, n_new) for p in pos) / (peak * world * 1e12) * 1e6
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC_PREFILL if prefill else METRIC, "value": round(value, 2),
+            "unit": "TFLOP/s" if prefill else "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "us_per_token": round(us_tok, 2),
             "pct_of_roofline": round(100.0 * value / (peak * world), 2),
-            "pct_of_nominal_8tbs": round(100.0 * value / (NOMINAL_HBM_GBS * world), 2),
+            ("pct_of_nominal_2250tflops" if prefill else "pct_of_nominal_8tbs"):
+                round(100.0 * value / ((2250.0 if prefill else NOMINAL_HBM_GBS) * world), 2),
             "ideal_us_per_token": round(ideal_us, 2),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f16 cache, f32 math",
@@ -451,10 +506,12 @@ def run_ours(args, sp):
                        else "single GPU",
                        "l2": "no flush: each step reads %.2f GB of cache (> 126 MB L2)" % (
                            statistics.mean(step_bytes(sp, p, n_new) for p in pos) / 1e9)},
-            "roofline": {"bound": "hbm", "kernel": "kv_" + dom, "achieved": round(achieved, 1) if achieved else None,
-                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None,
-                         "peak_source": peak_kind,
-                         "algorithmic_bytes_per_launch": int(algo[dom]),
+            "roofline": {"bound": "tensor" if prefill else "hbm", "kernel": "kv_" + dom,
+                         "achieved": round(achieved, 1) if achieved else None,
+                         "peak": peak, "unit": "TFLOP/s" if prefill else "GB/s",
+                         "frac": round(achieved / peak, 4) if achieved else None,
+                         "peak_source": peak_kind + (" dense bf16/f16 burst" if prefill else " copy bandwidth"),
+                         ("algorithmic_flops_per_layer" if prefill else "algorithmic_bytes_per_launch"): int(algo[dom]),
                          "traffic": committed_traffic(sp["name"], "kv_" + dom),
                          "kernels": kernel_table},
             "e2e": e2e,

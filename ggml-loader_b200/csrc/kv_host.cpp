@@ -597,7 +597,7 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
         const int kseg = kvb::prefill_max_segments();
         const size_t nblk = (size_t)(c.n_batch_max + ctx->pf_tb - 1) / ctx->pf_tb;
         const size_t slots = (size_t)ctx->sm_count * kseg * 128u;
-        e = cudaMalloc(&ctx->pf_stat, slots * 2u * sizeof(float));
+        e = cudaMalloc(&ctx->pf_stat, slots * 4u * 2u * sizeof(float));   // up to 4 column parts
         if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_rstat, (size_t)ctx->hkv_loc * nblk * 128u * sizeof(float2));
         if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_out, slots * (size_t)D * sizeof(float));
         if (e != cudaSuccess) return bail(fail(KV_E_OOM, "prefill scratch: %s", cudaGetErrorString(e)));
@@ -757,7 +757,7 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     static const char *what[4] = {"prefill statistics kernel", "prefill statistics fold", "prefill output kernel",
                                   "prefill output fold"};
     for (int which = 0; which < 4; which++) {
-        const int rc = launch(ctx, KV_K_PREFILL, st, what[which],
+        const int rc = launch(ctx, (which & 1) ? KV_K_PFOLD : KV_K_PREFILL, st, what[which],
                               [&] { return kvb::launch_prefill(ctx->D, which, ctx->qmap, km, vm, pp, st); });
         if (rc) return rc;
     }
@@ -1086,7 +1086,7 @@ int kv_profile_read(kv_ctx *ctx, int32_t kernel, int64_t *launches, double *tota
 
 const char *kv_kernel_name(int32_t kernel)
 {
-    static const char *names[KV_K_COUNT] = {"kv_append", "kv_attn", "kv_prefill", "kv_unshard"};
+    static const char *names[KV_K_COUNT] = {"kv_append", "kv_attn", "kv_prefill", "kv_prefill_fold", "kv_unshard"};
     return (kernel >= 0 && kernel < KV_K_COUNT) ? names[kernel] : "?";
 }
 

@@ -148,7 +148,7 @@ struct PrefillParams {
     int64_t s_all;     // key tiles of one KV head summed over its blocks
     int32_t n_cta, kseg;
     float scale;
-    float *pstat;      // [n_cta][kseg][128] (max, sum of exp) per segment and row
+    float *pstat;      // [n_cta][kseg][column part][128] (max, sum of exp) per segment, part and row
     float2 *rstat;     // [hkv * nblk][128] (max, 1/sum) per pair and row
     float *pout;       // [n_cta][kseg][128][D] partial outputs
     float *out;        // row t at out + t*out_stride, head h at (out_head0 + h)*D

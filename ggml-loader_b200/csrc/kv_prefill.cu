@@ -19,17 +19,18 @@
 // equal ranges (one CTA each, C <= SMs); a range holds one or more "segments"
 // (the part of one pair it covers).
 //
-// prefill_kernel<D, OUT> (192 threads):
+// prefill_kernel<D, OUT> (320 threads):
 //   warp 0     TMA: the pair's Q tile, then K tiles (and V tiles in pass 2) into
 //              mbarrier rings;
 //   warp 1     TMEM owner and MMA issuer (one thread): S = Q . K^T, M=128, N=128
 //              keys, K = D, into one of two 128-column TMEM buffers; in pass 2
-//              also O += P . V (M=128, N=D, K=128 keys, V read MN-major) into
-//              D more columns, one tile behind;
-//   warps 2-5  one query row per thread, read from TMEM with tcgen05.ld:
-//              pass 1 keeps the running row max / sum of exp; pass 2 writes p
-//              as F16 into a double-buffered, 128-byte-swizzled P tile (the A
-//              operand of the next MMA) and, at a segment's end, copies O out.
+//              also O += P . V (M=128, N=D, K=128 keys; P from TMEM, V read
+//              MN-major from shared memory) into D more columns, one tile behind;
+//   warps 2-9  a query row per lane and half of each tile's keys per warp,
+//              read from TMEM with tcgen05.ld: pass 1 keeps the running row max
+//              / sum of exp; pass 2 writes p as F16 pairs back into TMEM with
+//              tcgen05.st (double-buffered), the A operand of the P . V MMA,
+//              and at a segment's end copies O out.
 // prefill_stats_fold   (M, 1/Z) of every (pair, row) from the segments' partials
 // prefill_out_fold     sum of the segments' partial outputs, scattered to out
 // Every wait is bounded (limit_ns) and gives up when the CTA's abort flag is
@@ -44,21 +45,25 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kPThreads = 192;
+constexpr int kSW = 8;                      // softmax / epilogue warps (2..9)
+constexpr int kCP = kSW / 4;                // column parts of a tile
+constexpr int kPThreads = 64 + 32 * kSW;
 constexpr uint32_t kBox = 128 * 128;   // one [128 rows][64 halves] swizzled box
+// TMEM columns: S (two 128-column F32 buffers), O (up to 128 F32), P (two
+// 64-column buffers of F16 pairs) -- 512 in all
+constexpr uint32_t kTmO = 256, kTmP = 384;
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D, bool OUT>
 struct PL {
     static constexpr int NB = D / 64;                        // boxes per Q/K/V row
     static constexpr uint32_t kTile = (uint32_t)NB * kBox;   // 128 rows x D halves
-    static constexpr int KS = OUT ? (D == 128 ? 2 : 4) : (D == 128 ? 5 : 8);
-    static constexpr int VS = OUT ? (D == 128 ? 2 : 4) : 0;
+    static constexpr int KS = OUT ? (D == 128 ? 3 : 6) : (D == 128 ? 6 : 12);
+    static constexpr int VS = OUT ? (D == 128 ? 3 : 6) : 0;
     static constexpr size_t o_q = 0;
     static constexpr size_t o_k = o_q + kTile;
     static constexpr size_t o_v = o_k + (size_t)KS * kTile;
-    static constexpr size_t o_p = o_v + (size_t)VS * kTile;  // 2 buffers x 2 boxes (128 keys)
-    static constexpr size_t o_bar = o_p + (OUT ? 4 * (size_t)kBox : 0);
+    static constexpr size_t o_bar = o_v + (size_t)VS * kTile;
     // q_full, q_empty, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
     // s_full[2], s_free[2], p_full[2], p_empty[2], o_full, o_empty, drain
     static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 8 + 3;
@@ -162,11 +167,11 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
 
     if (tid == 0) {
         for (int i = 0; i < L::NBAR; i++) {
-            // the four softmax warps arrive on s_free, p_full and o_empty
+            // every softmax warp arrives on s_free, p_full and o_empty
             const uint64_t *bi = &bar[i];
             const bool four = bi == &s_free[0] || bi == &s_free[1] || bi == &p_full[0] || bi == &p_full[1] ||
                               bi == o_empty;
-            mbar_init(&bar[i], four ? 4 : 1);
+            mbar_init(&bar[i], four ? kSW : 1);
         }
         flags[0] = 0;
         fence_mbar_init();
@@ -233,7 +238,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
             constexpr uint32_t idS = idesc_f16_f32(128, 128, false);
             constexpr uint32_t idO = idesc_f16_f32(128, D, true);
             const uint32_t sq = smem_addr(smem + L::o_q), sk = smem_addr(smem + L::o_k);
-            const uint32_t sv = smem_addr(smem + L::o_v), sp = smem_addr(smem + L::o_p);
+            const uint32_t sv = smem_addr(smem + L::o_v);
             int j = 0;               // tiles issued (S)
             int pend = -1;           // tile whose P . V is still to issue
             bool pend_first = false, pend_last = false;
@@ -249,10 +254,9 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                 }
                 tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    const uint64_t a = sdesc_k_sw128(sp + pb * 2 * kBox + (kk >> 2) * kBox + (kk & 3) * 32);
+                for (int kk = 0; kk < 8; kk++) {   // 16 keys per step: 8 packed P columns
                     const uint64_t bd = sdesc_mn_sw128(sv + vs * kTile + kk * 2048, kBox);
-                    umma_ss(tmem + 256, a, bd, idO, !(pend_first && kk == 0));
+                    umma_ts(tmem + kTmO, tmem + kTmP + pb * 64 + kk * 8, bd, idO, !(pend_first && kk == 0));
                 }
                 umma_commit(&p_empty[pb]);
                 umma_commit(&v_empty[vs]);
@@ -298,27 +302,33 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
             mbar_wait(drain, 0, p.limit_ns);
         }
     } else {
-        // ================= softmax / epilogue: one query row per thread =================
-        const int q4 = warp & 3;                  // TMEM lane quarter of this warp
+        // ================= softmax / epilogue =================
+        // kSW warps: warp w reaches TMEM lanes 32*(w%4) .. +31 (its rows) and
+        // takes column part (w-2)/4 of every tile (kCP parts of 128/kCP keys)
+        const int q4 = warp & 3;
+        const int part = (warp - 2) >> 2;
         const int row = q4 * 32 + lane;           // query row of the tile = token*r + head
         const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-        const int tok_in = row / p.r, hd = row - tok_in * p.r;
+        const int tok_in = row / p.r;
         const bool row_ok = tok_in < p.tb;
+        constexpr int kCols = 128 / kCP;          // keys of a tile per part
+        constexpr int kLd = kCols / 32;           // tcgen05.ld x32 per tile
+        const float cs = p.scale * kLog2e;        // exp(s*scale - M) = 2^(acc*cs - M*log2e)
         int j = 0;
         for_segments(p, c, [&](int k, const Seg &sg) {
-            const int kvh = sg.pair / p.nblk, b = sg.pair % p.nblk;
+            const int b = sg.pair % p.nblk;
             const int tok = b * p.tb + tok_in;
             const bool valid = row_ok && tok < p.n_new;
             const int64_t lim = valid ? p.n_past + tok : -1;   // last visible key
-            float M = 0.0f, inv = 0.0f;
+            float nM = 0.0f, inv = 0.0f;         // -M*log2e and 1/Z of the row (pass 2)
             if constexpr (OUT) {
                 if (valid) {
                     const float2 st = p.rstat[(int64_t)sg.pair * 128 + row];
-                    M = st.x;
+                    nM = -st.x * kLog2e;
                     inv = st.y;
                 }
             }
-            float m = -INFINITY, z = 0.0f;
+            float am = -INFINITY, z = 0.0f;      // pass 1: running max of raw S, sum of exp
             for (int t = sg.t0; t < sg.t1; t++, j++) {
                 const int sb = j & 1, pb = j & 1;
                 if (!mbar_wait_ab(&s_full[sb], (j >> 1) & 1, p.limit_ns, flags)) {
@@ -326,99 +336,106 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                     return false;
                 }
                 tc_fence_after();
-                if constexpr (OUT) {
+                uint32_t v[kLd][32];
+#pragma unroll
+                for (int u = 0; u < kLd; u++) tmem_ld32(trow + sb * 128 + part * kCols + u * 32, v[u]);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[sb]);
+                const int64_t kc0 = (int64_t)t * 128 + part * kCols;
+                const int nvis = (int)max((int64_t)0, min((int64_t)kCols, lim - kc0 + 1));   // visible keys
+                if constexpr (!OUT) {
+                    float cm = -INFINITY;
+                    if (nvis == kCols) {
+#pragma unroll
+                        for (int u = 0; u < kLd; u++)
+#pragma unroll
+                            for (int e = 0; e < 32; e++) cm = fmaxf(cm, __uint_as_float(v[u][e]));
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < kLd; u++)
+#pragma unroll
+                            for (int e = 0; e < 32; e++)
+                                if (u * 32 + e < nvis) cm = fmaxf(cm, __uint_as_float(v[u][e]));
+                    }
+                    const float nm = fmaxf(am, cm);
+                    if (nm != -INFINITY) {
+                        const float nb = -nm * cs;
+                        float a4[4] = {am == -INFINITY ? 0.0f : z * ex2_approx(fmaf(am, cs, nb)), 0.0f, 0.0f, 0.0f};
+                        if (nvis == kCols) {
+#pragma unroll
+                            for (int u = 0; u < kLd; u++)
+#pragma unroll
+                                for (int e = 0; e < 32; e++)
+                                    a4[e & 3] += ex2_approx(fmaf(__uint_as_float(v[u][e]), cs, nb));
+                        } else {
+#pragma unroll
+                            for (int u = 0; u < kLd; u++)
+#pragma unroll
+                                for (int e = 0; e < 32; e++) {
+                                    const float x = ex2_approx(fmaf(__uint_as_float(v[u][e]), cs, nb));
+                                    a4[e & 3] += u * 32 + e < nvis ? x : 0.0f;
+                                }
+                        }
+                        z = (a4[0] + a4[1]) + (a4[2] + a4[3]);
+                        am = nm;
+                    }
+                } else {
                     if (j >= 2 && !mbar_wait_ab(&p_empty[pb], ((j - 2) >> 1) & 1, p.limit_ns, flags)) {
                         give_up(p, flags, 1u);
                         return false;
                     }
-                }
-                const int64_t key0 = (int64_t)t * 128;
-                unsigned char *prow = smem + L::o_p + pb * 2 * kBox + row * 128;
-#pragma unroll 1
-                for (int ch = 0; ch < 4; ch++) {
-                    uint32_t v[32];
-                    tmem_ld32(trow + sb * 128 + ch * 32, v);
-                    tmem_wait_ld();
-                    if (ch == 3) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&s_free[sb]);
-                    }
-                    const int64_t kc = key0 + ch * 32;
-                    const int nvis = (int)max((int64_t)0, min((int64_t)32, lim - kc + 1));   // keys of the chunk visible
-                    if constexpr (!OUT) {
-                        float cm = -INFINITY;
 #pragma unroll
-                        for (int e = 0; e < 32; e++) {
-                            const float s = __fmul_rn(__uint_as_float(v[e]), p.scale);
-                            v[e] = __float_as_uint(e < nvis ? s : -INFINITY);
-                            cm = fmaxf(cm, __uint_as_float(v[e]));
-                        }
-                        const float mn = fmaxf(m, cm);
-                        if (mn != -INFINITY) {
-                            const float nb = -mn * kLog2e;
-                            float acc = m == -INFINITY ? 0.0f : z * ex2_approx(fmaf(m, kLog2e, nb));
-#pragma unroll
-                            for (int e = 0; e < 32; e++)
-                                acc += ex2_approx(fmaf(__uint_as_float(v[e]), kLog2e, nb));
-                            z = acc;
-                            m = mn;
-                        }
-                    } else {
+                    for (int u = 0; u < kLd; u++) {
                         uint32_t pk[16];
 #pragma unroll
                         for (int e = 0; e < 16; e++) {
-                            float pe[2];
-#pragma unroll
-                            for (int u = 0; u < 2; u++) {
-                                const int ee = 2 * e + u;
-                                const float s = __fmul_rn(__uint_as_float(v[ee]), p.scale);
-                                pe[u] = ee < nvis ? __fmul_rn(ex2_approx(__fmul_rn(__fsub_rn(s, M), kLog2e)), inv) : 0.0f;
+                            float x0 = __fmul_rn(ex2_approx(fmaf(__uint_as_float(v[u][2 * e]), cs, nM)), inv);
+                            float x1 = __fmul_rn(ex2_approx(fmaf(__uint_as_float(v[u][2 * e + 1]), cs, nM)), inv);
+                            if (nvis < kCols) {
+                                x0 = u * 32 + 2 * e < nvis ? x0 : 0.0f;
+                                x1 = u * 32 + 2 * e + 1 < nvis ? x1 : 0.0f;
                             }
-                            pk[e] = pack_half2(__float2half_rn(pe[0]), __float2half_rn(pe[1]));
+                            const __half2 h2 = __floats2half2_rn(x0, x1);
+                            pk[e] = *reinterpret_cast<const uint32_t *>(&h2);
                         }
-                        // keys ch*32 .. +31: box ch/2, 16-byte chunks (ch%2)*4 .. +3, swizzled by row
-#pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            const int chunk = (ch & 1) * 4 + q;
-                            *reinterpret_cast<uint4 *>(prow + (ch >> 1) * kBox + ((chunk ^ (row & 7)) << 4)) =
-                                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-                        }
+                        // keys part*kCols + u*32 .. +31 -> 16 packed columns of P[pb]
+                        tmem_st16(trow + kTmP + pb * 64 + (part * kCols + u * 32) / 2, pk);
                     }
-                }
-                if constexpr (OUT) {
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // P feeds tcgen05.mma
+                    tmem_wait_st();
+                    tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&p_full[pb]);
                 }
             }
             if constexpr (!OUT) {
-                float2 *ps = reinterpret_cast<float2 *>(p.pstat) + ((int64_t)c * p.kseg + k) * 128 + row;
-                *ps = make_float2(m, z);
+                // this part's (max, sum) of the row: max in scaled units
+                float2 *ps = reinterpret_cast<float2 *>(p.pstat) + (((int64_t)c * p.kseg + k) * kCP + part) * 128 + row;
+                *ps = make_float2(am == -INFINITY ? -INFINITY : __fmul_rn(am, p.scale), z);
             } else {
                 if (!mbar_wait_ab(o_full, k & 1, p.limit_ns, flags)) {
                     give_up(p, flags, 1u);
                     return false;
                 }
                 tc_fence_after();
-                float *po = p.pout + (((int64_t)c * p.kseg + k) * 128 + row) * D;
+                constexpr int kOc = D / kCP;   // output dims per part
+                float *po = p.pout + (((int64_t)c * p.kseg + k) * 128 + row) * D + part * kOc;
 #pragma unroll 1
-                for (int ch = 0; ch < D / 32; ch++) {
-                    uint32_t v[32];
-                    tmem_ld32(trow + 256 + ch * 32, v);
+                for (int ch = 0; ch < kOc / 32; ch++) {
+                    uint32_t o[32];
+                    tmem_ld32(trow + kTmO + part * kOc + ch * 32, o);
                     tmem_wait_ld();
                     if (valid)
 #pragma unroll
                         for (int q = 0; q < 8; q++)
                             *reinterpret_cast<uint4 *>(po + ch * 32 + 4 * q) =
-                                make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                                make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(o_empty);
             }
-            (void)kvh;
-            (void)hd;
             return true;
         });
     }
@@ -462,38 +479,62 @@ __device__ __forceinline__ int seg_index(const PrefillParams &p, int cc, int pai
     return pair - pair_of(p, cta_lo(p, cc));
 }
 
-// (M, 1/Z) per (pair, row): one thread per row, CTAs in order
+// (M, 1/Z) per (pair, row) from every segment part: one thread per row
 __global__ void prefill_stats_fold(const PrefillParams p)
 {
     const int pair = blockIdx.x, row = threadIdx.x;
-    int ca, cb;
-    pair_ctas(p, pair, ca, cb);
+    __shared__ int span[2];
+    if (row == 0) pair_ctas(p, pair, span[0], span[1]);
+    __syncthreads();
     const float2 *ps = reinterpret_cast<const float2 *>(p.pstat);
     float M = -INFINITY;
-    for (int cc = ca; cc <= cb; cc++) M = fmaxf(M, ps[((int64_t)cc * p.kseg + seg_index(p, cc, pair)) * 128 + row].x);
+    for (int cc = span[0]; cc <= span[1]; cc++) {
+        const int64_t base = ((int64_t)cc * p.kseg + seg_index(p, cc, pair)) * kCP;
+        for (int q = 0; q < kCP; q++) M = fmaxf(M, ps[(base + q) * 128 + row].x);
+    }
     double Z = 0.0;
-    for (int cc = ca; cc <= cb; cc++) {
-        const float2 v = ps[((int64_t)cc * p.kseg + seg_index(p, cc, pair)) * 128 + row];
-        if (v.x != -INFINITY) Z += (double)v.y * (double)exp2f((v.x - M) * kLog2e);
+    for (int cc = span[0]; cc <= span[1]; cc++) {
+        const int64_t base = ((int64_t)cc * p.kseg + seg_index(p, cc, pair)) * kCP;
+        for (int q = 0; q < kCP; q++) {
+            const float2 v = ps[(base + q) * 128 + row];
+            if (v.x != -INFINITY) Z += (double)v.y * (double)exp2f((v.x - M) * kLog2e);
+        }
     }
     p.rstat[(int64_t)pair * 128 + row] = make_float2(M, Z > 0.0 ? __fdiv_rn(1.0f, (float)Z) : 0.0f);
 }
 
-// out row = sum of the pair's partial outputs (CTAs in order); one block per
-// (pair, row), one thread per dim
-__global__ void prefill_out_fold(const PrefillParams p)
+// out = the sum of the pair's partial outputs (CTAs in order), scattered to the
+// caller's [token][head][D] rows; one block per (pair, 8 rows), float4 per thread
+__global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
 {
-    const int pair = blockIdx.x / 128, row = blockIdx.x % 128, dd = threadIdx.x;
-    const int tok_in = row / p.r, hd = row - tok_in * p.r;
+    const int pair = blockIdx.x >> 4, row0 = (blockIdx.x & 15) * 8;
+    __shared__ int span[2];
+    __shared__ int segi[160];
+    if (threadIdx.x == 0) pair_ctas(p, pair, span[0], span[1]);
+    __syncthreads();
+    for (int cc = span[0] + (int)threadIdx.x; cc <= span[1]; cc += blockDim.x)
+        if (cc - span[0] < 160) segi[cc - span[0]] = seg_index(p, cc, pair);
+    __syncthreads();
+    const int per_row = p.D / 4;
     const int b = pair % p.nblk, kvh = pair / p.nblk;
-    const int tok = b * p.tb + tok_in;
-    if (tok_in >= p.tb || tok >= p.n_new) return;
-    int ca, cb;
-    pair_ctas(p, pair, ca, cb);
-    float sum = 0.0f;
-    for (int cc = ca; cc <= cb; cc++)
-        sum += __ldg(p.pout + (((int64_t)cc * p.kseg + seg_index(p, cc, pair)) * 128 + row) * p.D + dd);
-    p.out[(int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * p.D + dd] = sum;
+    for (int idx = threadIdx.x; idx < 8 * per_row; idx += blockDim.x) {
+        const int row = row0 + idx / per_row, d4 = idx % per_row;
+        const int tok_in = row / p.r, hd = row - tok_in * p.r;
+        const int tok = b * p.tb + tok_in;
+        if (tok_in >= p.tb || tok >= p.n_new) continue;
+        float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int cc = span[0]; cc <= span[1]; cc++) {
+            const int sgi = cc - span[0] < 160 ? segi[cc - span[0]] : seg_index(p, cc, pair);
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(
+                p.pout + (((int64_t)cc * p.kseg + sgi) * 128 + row) * p.D) + d4);
+            sum.x += v.x;
+            sum.y += v.y;
+            sum.z += v.z;
+            sum.w += v.w;
+        }
+        *reinterpret_cast<float4 *>(p.out + (int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * p.D +
+                                    4 * d4) = sum;
+    }
 }
 
 template <int D>
@@ -518,7 +559,7 @@ cudaError_t launch_pf(int which, const CUtensorMap &qmap, const CUtensorMap &kma
     case 2:
         prefill_kernel<D, true><<<p.n_cta, kPThreads, PL<D, true>::bytes, st>>>(qmap, kmap, vmap, p);
         break;
-    default: prefill_out_fold<<<p.hkv * p.nblk * 128, D, 0, st>>>(p); break;
+    default: prefill_out_fold<<<p.hkv * p.nblk * 16, 256, 0, st>>>(p); break;
     }
     return cudaGetLastError();
 }

@@ -24,7 +24,7 @@ KV_E_TIMEOUT = -6
 KV_E_STATE = -7
 KV_E_UNSUPPORTED = -8
 
-KERNELS = {"append": 0, "attn": 1, "prefill": 2, "gather": 3}
+KERNELS = {"append": 0, "attn": 1, "prefill": 2, "pfold": 3, "gather": 4}
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32

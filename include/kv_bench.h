@@ -32,9 +32,10 @@ int kv_gen_normal_device(float *dst, uint64_t seed, uint64_t stream,
  * launch; totals accumulate until kv_profile_reset. */
 #define KV_K_APPEND   0
 #define KV_K_ATTN     1
-#define KV_K_PREFILL  2
-#define KV_K_GATHER   3
-#define KV_K_COUNT    4
+#define KV_K_PREFILL  2   /* both tensor-core passes */
+#define KV_K_PFOLD    3   /* the prefill statistics / output folds */
+#define KV_K_GATHER   4
+#define KV_K_COUNT    5
 int kv_profile_enable(kv_ctx *ctx, int on);
 int kv_profile_reset(kv_ctx *ctx);
 /* Synchronizes the recorded events; returns launches and summed milliseconds. */
