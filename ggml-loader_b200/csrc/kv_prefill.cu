@@ -19,14 +19,14 @@
 // equal ranges (one CTA each, C <= SMs); a range holds one or more "segments"
 // (the part of one pair it covers).
 //
-// prefill_kernel<D, OUT> (320 threads):
+// prefill_kernel<D, OUT> (576 threads):
 //   warp 0     TMA: the pair's Q tile, then K tiles (and V tiles in pass 2) into
 //              mbarrier rings;
 //   warp 1     TMEM owner and MMA issuer (one thread): S = Q . K^T, M=128, N=128
 //              keys, K = D, into one of two 128-column TMEM buffers; in pass 2
 //              also O += P . V (M=128, N=D, K=128 keys; P from TMEM, V read
 //              MN-major from shared memory) into D more columns, one tile behind;
-//   warps 2-9  a query row per lane and half of each tile's keys per warp,
+//   warps 2-17 a query row per lane and a quarter of each tile's keys per warp,
 //              read from TMEM with tcgen05.ld: pass 1 keeps the running row max
 //              / sum of exp; pass 2 writes p as F16 pairs back into TMEM with
 //              tcgen05.st (double-buffered), the A operand of the P . V MMA,
@@ -45,8 +45,8 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kSW = 8;                      // softmax / epilogue warps (2..9)
-constexpr int kCP = kSW / 4;                // column parts of a tile
+constexpr int kSW = 16;                     // softmax / epilogue warps (2..17)
+constexpr int kCP = 4;                      // statistics parts of a row: 2 tile groups x 2 key halves
 constexpr int kPThreads = 64 + 32 * kSW;
 constexpr uint32_t kBox = 128 * 128;   // one [128 rows][64 halves] swizzled box
 // TMEM columns: S (two 128-column F32 buffers), O (up to 128 F32), P (two
@@ -167,11 +167,10 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
 
     if (tid == 0) {
         for (int i = 0; i < L::NBAR; i++) {
-            // every softmax warp arrives on s_free, p_full and o_empty
+            // a tile group's 8 warps arrive on s_free and p_full, all 16 on o_empty
             const uint64_t *bi = &bar[i];
-            const bool four = bi == &s_free[0] || bi == &s_free[1] || bi == &p_full[0] || bi == &p_full[1] ||
-                              bi == o_empty;
-            mbar_init(&bar[i], four ? kSW : 1);
+            const bool grp = bi == &s_free[0] || bi == &s_free[1] || bi == &p_full[0] || bi == &p_full[1];
+            mbar_init(&bar[i], grp ? kSW / 2 : bi == o_empty ? kSW : 1);
         }
         flags[0] = 0;
         fence_mbar_init();
@@ -240,15 +239,20 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
             const uint32_t sq = smem_addr(smem + L::o_q), sk = smem_addr(smem + L::o_k);
             const uint32_t sv = smem_addr(smem + L::o_v);
             int j = 0;               // tiles issued (S)
-            int pend = -1;           // tile whose P . V is still to issue
-            bool pend_first = false, pend_last = false;
-            int pend_seg = 0;
+            // tiles whose P . V is still to issue, oldest first; P . V runs two
+            // tiles behind S so the next S never queues behind a P . V
+            struct Pend {
+                int j, seg;
+                bool first, last;
+            };
+            Pend pq0{}, pq1{};
+            int npq = 0;
             bool ok = true;
-            auto issue_pv = [&]() -> bool {
-                const int jp = pend, pb = jp & 1, vs = jp % (VS > 0 ? VS : 1);
+            auto issue_pv = [&](const Pend &pe) -> bool {
+                const int jp = pe.j, pb = jp & 1, vs = jp % (VS > 0 ? VS : 1);
                 if (!mbar_wait_ab(&p_full[pb], (jp >> 1) & 1, p.limit_ns, flags) ||
                     !mbar_wait_ab(&v_full[vs], (jp / (VS > 0 ? VS : 1)) & 1, p.limit_ns, flags) ||
-                    (pend_first && pend_seg > 0 && !mbar_wait_ab(o_empty, (pend_seg - 1) & 1, p.limit_ns, flags))) {
+                    (pe.first && pe.seg > 0 && !mbar_wait_ab(o_empty, (pe.seg - 1) & 1, p.limit_ns, flags))) {
                     give_up(p, flags, 1u);
                     return false;
                 }
@@ -256,11 +260,11 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++) {   // 16 keys per step: 8 packed P columns
                     const uint64_t bd = sdesc_mn_sw128(sv + vs * kTile + kk * 2048, kBox);
-                    umma_ts(tmem + kTmO, tmem + kTmP + pb * 64 + kk * 8, bd, idO, !(pend_first && kk == 0));
+                    umma_ts(tmem + kTmO, tmem + kTmP + pb * 64 + kk * 8, bd, idO, !(pe.first && kk == 0));
                 }
                 umma_commit(&p_empty[pb]);
                 umma_commit(&v_empty[vs]);
-                if (pend_last) umma_commit(o_full);
+                if (pe.last) umma_commit(o_full);
                 return true;
             };
             for_segments(p, c, [&](int k, const Seg &sg) {
@@ -286,17 +290,22 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                     umma_commit(&k_empty[s]);
                     if (t == sg.t1 - 1) umma_commit(q_empty);
                     if constexpr (OUT) {
-                        if (pend >= 0 && !issue_pv()) return ok = false;
-                        pend = j;
-                        pend_first = t == sg.t0;
-                        pend_last = t == sg.t1 - 1;
-                        pend_seg = k;
+                        if (npq == 2) {
+                            if (!issue_pv(pq0)) return ok = false;
+                            pq0 = pq1;
+                            npq = 1;
+                        }
+                        const Pend pe{j, k, t == sg.t0, t == sg.t1 - 1};
+                        if (npq == 0) pq0 = pe;
+                        else pq1 = pe;
+                        npq++;
                     }
                     j++;
                 }
                 return true;
             });
-            if (OUT && ok && pend >= 0) issue_pv();
+            if (OUT && ok && npq > 0) ok = issue_pv(pq0);
+            if (OUT && ok && npq > 1) ok = issue_pv(pq1);
             // every MMA this thread issued has completed before TMEM is freed
             umma_commit(drain);
             mbar_wait(drain, 0, p.limit_ns);
@@ -305,13 +314,17 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
         // ================= softmax / epilogue =================
         // kSW warps: warp w reaches TMEM lanes 32*(w%4) .. +31 (its rows) and
         // takes column part (w-2)/4 of every tile (kCP parts of 128/kCP keys)
+        // two groups of 8 warps take alternate tiles (group g: tiles j with j%2 == g),
+        // so one group computes while the other waits on TMEM; in a group, warp w
+        // has TMEM lanes 32*(w%4).. (its rows) and one half of the tile's keys
+        const int sw = warp - 2, grp = sw >> 3, half = (sw >> 2) & 1;
         const int q4 = warp & 3;
-        const int part = (warp - 2) >> 2;
+        const int part = grp * 2 + half;          // statistics part of this warp
         const int row = q4 * 32 + lane;           // query row of the tile = token*r + head
         const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
         const int tok_in = row / p.r;
         const bool row_ok = tok_in < p.tb;
-        constexpr int kCols = 128 / kCP;          // keys of a tile per part
+        constexpr int kCols = 64;                 // keys of a tile per warp
         constexpr int kLd = kCols / 32;           // tcgen05.ld x32 per tile
         const float cs = p.scale * kLog2e;        // exp(s*scale - M) = 2^(acc*cs - M*log2e)
         int j = 0;
@@ -331,6 +344,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
             float am = -INFINITY, z = 0.0f;      // pass 1: running max of raw S, sum of exp
             for (int t = sg.t0; t < sg.t1; t++, j++) {
                 const int sb = j & 1, pb = j & 1;
+                if (sb != grp) continue;   // the other group's tile
                 if (!mbar_wait_ab(&s_full[sb], (j >> 1) & 1, p.limit_ns, flags)) {
                     give_up(p, flags, 1u);
                     return false;
@@ -338,47 +352,52 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                 tc_fence_after();
                 uint32_t v[kLd][32];
 #pragma unroll
-                for (int u = 0; u < kLd; u++) tmem_ld32(trow + sb * 128 + part * kCols + u * 32, v[u]);
+                for (int u = 0; u < kLd; u++) tmem_ld32(trow + sb * 128 + half * kCols + u * 32, v[u]);
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&s_free[sb]);
-                const int64_t kc0 = (int64_t)t * 128 + part * kCols;
+                const int64_t kc0 = (int64_t)t * 128 + half * kCols;
                 const int nvis = (int)max((int64_t)0, min((int64_t)kCols, lim - kc0 + 1));   // visible keys
                 if constexpr (!OUT) {
-                    float cm = -INFINITY;
+                    float m8[8];   // eight independent max chains
+#pragma unroll
+                    for (int i = 0; i < 8; i++) m8[i] = -INFINITY;
                     if (nvis == kCols) {
 #pragma unroll
                         for (int u = 0; u < kLd; u++)
 #pragma unroll
-                            for (int e = 0; e < 32; e++) cm = fmaxf(cm, __uint_as_float(v[u][e]));
+                            for (int e = 0; e < 32; e++) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(v[u][e]));
                     } else {
 #pragma unroll
                         for (int u = 0; u < kLd; u++)
 #pragma unroll
                             for (int e = 0; e < 32; e++)
-                                if (u * 32 + e < nvis) cm = fmaxf(cm, __uint_as_float(v[u][e]));
+                                if (u * 32 + e < nvis) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(v[u][e]));
                     }
+                    const float cm = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                           fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
                     const float nm = fmaxf(am, cm);
                     if (nm != -INFINITY) {
                         const float nb = -nm * cs;
-                        float a4[4] = {am == -INFINITY ? 0.0f : z * ex2_approx(fmaf(am, cs, nb)), 0.0f, 0.0f, 0.0f};
+                        float a8[8] = {am == -INFINITY ? 0.0f : z * ex2_approx(fmaf(am, cs, nb)), 0.0f, 0.0f, 0.0f,
+                                       0.0f, 0.0f, 0.0f, 0.0f};
                         if (nvis == kCols) {
 #pragma unroll
                             for (int u = 0; u < kLd; u++)
 #pragma unroll
                                 for (int e = 0; e < 32; e++)
-                                    a4[e & 3] += ex2_approx(fmaf(__uint_as_float(v[u][e]), cs, nb));
+                                    a8[e & 7] += ex2_approx(fmaf(__uint_as_float(v[u][e]), cs, nb));
                         } else {
 #pragma unroll
                             for (int u = 0; u < kLd; u++)
 #pragma unroll
                                 for (int e = 0; e < 32; e++) {
                                     const float x = ex2_approx(fmaf(__uint_as_float(v[u][e]), cs, nb));
-                                    a4[e & 3] += u * 32 + e < nvis ? x : 0.0f;
+                                    a8[e & 7] += u * 32 + e < nvis ? x : 0.0f;
                                 }
                         }
-                        z = (a4[0] + a4[1]) + (a4[2] + a4[3]);
+                        z = ((a8[0] + a8[1]) + (a8[2] + a8[3])) + ((a8[4] + a8[5]) + (a8[6] + a8[7]));
                         am = nm;
                     }
                 } else {
@@ -401,7 +420,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                             pk[e] = *reinterpret_cast<const uint32_t *>(&h2);
                         }
                         // keys part*kCols + u*32 .. +31 -> 16 packed columns of P[pb]
-                        tmem_st16(trow + kTmP + pb * 64 + (part * kCols + u * 32) / 2, pk);
+                        tmem_st16(trow + kTmP + pb * 64 + (half * kCols + u * 32) / 2, pk);
                     }
                     tmem_wait_st();
                     tc_fence_before();
@@ -419,17 +438,18 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                     return false;
                 }
                 tc_fence_after();
-                constexpr int kOc = D / kCP;   // output dims per part
-                float *po = p.pout + (((int64_t)c * p.kseg + k) * 128 + row) * D + part * kOc;
+                constexpr int kOc = D / 4;     // output dims per warp of a lane quarter (16 or 32)
+                const int oq = sw >> 2;        // 0..3
+                float *po = p.pout + (((int64_t)c * p.kseg + k) * 128 + row) * D + oq * kOc;
 #pragma unroll 1
-                for (int ch = 0; ch < kOc / 32; ch++) {
-                    uint32_t o[32];
-                    tmem_ld32(trow + kTmO + part * kOc + ch * 32, o);
+                for (int ch = 0; ch < kOc / 16; ch++) {
+                    uint32_t o[16];
+                    tmem_ld16(trow + kTmO + oq * kOc + ch * 16, o);
                     tmem_wait_ld();
                     if (valid)
 #pragma unroll
-                        for (int q = 0; q < 8; q++)
-                            *reinterpret_cast<uint4 *>(po + ch * 32 + 4 * q) =
+                        for (int q = 0; q < 4; q++)
+                            *reinterpret_cast<uint4 *>(po + ch * 16 + 4 * q) =
                                 make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
                 }
                 tc_fence_before();
