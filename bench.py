@@ -374,7 +374,7 @@ def run_ours(args, sp):
     sampler = ClockSampler(smi_index)
     if rank == 0:
         sampler.start()
-    lead = 100   # untimed steps on every rank while the sampler starts
+    lead = args.lead   # untimed steps on every rank while the sampler starts
     for s in range(args.warmup, args.warmup + lead):
         step(s)
     barrier()
@@ -537,6 +537,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) pass")
+    ap.add_argument("--lead", type=int, default=100,
+                    help="untimed steps between warm-up and the timed region (clock sampler start-up)")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the layer count (small profiling cases only; the bench line is invalid)")
     args = ap.parse_args()
