@@ -384,8 +384,10 @@ def run_ours(args, sp):
     barrier()
     sampler.mark("start")
     e0.record(stream)
+    h0 = time.perf_counter()
     for i in range(args.steps):
         step(first + i)
+    host_ms = (time.perf_counter() - h0) * 1e3   # host submission time of the timed steps
     e1.record(stream)
     e1.synchronize()
     sampler.mark("end")
@@ -516,6 +518,7 @@ def run_ours(args, sp):
                          "kernels": kernel_table},
             "e2e": e2e,
             "gpu_launches": int(launches),
+            "host_submit_ms_per_step": round(host_ms / args.steps, 4),
             "clocks": clocks,
             "cpu_baseline": cpu,
         }

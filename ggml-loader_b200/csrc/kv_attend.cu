@@ -213,7 +213,7 @@ struct Smem {
     static constexpr size_t o_kf = o_row + 4 * kRows * 4;                  // [D] f32
     static constexpr size_t o_knew = o_kf + (size_t)D * 4;                 // [D] f16
     static constexpr size_t o_vnew = o_knew + (size_t)D * 2;               // [D] f16
-    static constexpr size_t o_flags = o_vnew + (size_t)D * 2;              // abort, last(seg 0), last(seg 1)
+    static constexpr size_t o_flags = o_vnew + (size_t)D * 2;              // abort, last(seg 0), last(seg 1), collector
     static constexpr size_t bytes = o_flags + 16;
     static_assert(bytes <= 227 * 1024, "shared memory of the attention kernel");
     static_assert(kStage % 1024 == 0, "ring stages stay 1024-byte aligned");
@@ -635,17 +635,65 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         if (flags[1 + sl]) {
             __threadfence();
             const bool nan_out = __ldcg(&p.nonfin[h]) != 0u;
+            const int par = (int)(p.epoch & 1u);
             for (int idx = tid; idx < R * D; idx += kConsumers) {
                 const int row = idx / D, dd = idx - row * D;
                 const long long v = __ldcg(acc + idx);
                 acc[idx] = 0;
                 const int qrow = p.row0 + row;
-                p.out[(int64_t)(qrow / p.r) * p.out_stride + (int64_t)(p.out_head0 + h * p.r + qrow % p.r) * D + dd] =
-                    nan_out ? __int_as_float(0x7fc00000) : __fmul_rn(__ll2float_rn(v), kUnfix);
+                const int64_t o = (int64_t)(qrow / p.r) * p.out_stride + (int64_t)(p.out_head0 + h * p.r + qrow % p.r) * D + dd;
+                const float val = nan_out ? __int_as_float(0x7fc00000) : __fmul_rn(__ll2float_rn(v), kUnfix);
+                p.out[o] = val;
+                // KV-head shards: the same row into every peer's receive buffer (NVLink stores)
+                for (int g = 0; g < p.n_peers; g++)
+                    if (g != p.shard) p.rx[g][par * p.rx_stride + o] = val;
             }
             if (tid == 0) {
                 p.counters[h] = 0u;
                 p.nonfin[h] = 0u;
+            }
+            if (p.n_peers > 1) {
+                __threadfence_system();
+                named_sync(1, kConsumers);
+                if (tid == 0) {
+                    // this head's rows are visible: raise its flag on every peer, then
+                    // count the head in; the CTA that converts the last local head
+                    // collects the peers' heads
+                    for (int g = 0; g < p.n_peers; g++)
+                        if (g != p.shard)
+                            st_volatile_u32(p.rxflag[g] + ((int64_t)par * p.n_peers + p.shard) * p.hkv + h, p.epoch);
+                    flags[3] = atomicAdd(p.xticket, 1u) == (unsigned)(p.hkv - 1);
+                }
+                named_sync(1, kConsumers);
+                if (flags[3]) {
+                    bool late = false;
+                    const int nflag = (p.n_peers - 1) * p.hkv;
+                    if (tid < nflag) {
+                        const int gg = tid / p.hkv, hh = tid - gg * p.hkv;
+                        const int g = gg < p.shard ? gg : gg + 1;
+                        const unsigned *f = p.rxflag[p.shard] + ((int64_t)par * p.n_peers + g) * p.hkv + hh;
+                        const uint64_t t0 = globaltimer();
+                        while (ld_volatile_u32(f) != p.epoch)
+                            if (globaltimer() - t0 > p.limit_ns) {
+                                late = true;
+                                break;
+                            }
+                    }
+                    if (named_sync_or(1, kConsumers, late)) {
+                        if (tid == 0) atomicOr(p.err, 8u);
+                    } else {
+                        __threadfence_system();
+                        // the peers' heads: every column outside this shard's
+                        const float *src = p.rx[p.shard] + par * p.rx_stride;
+                        const int cols = p.hkv * p.r * D;   // this shard's columns
+                        for (int idx = tid; idx < p.n_peers * cols; idx += kConsumers) {
+                            const int o = idx;
+                            if (o >= p.out_head0 * D && o < p.out_head0 * D + cols) continue;
+                            p.out[o] = __ldcv(src + o);
+                        }
+                    }
+                    if (tid == 0) *p.xticket = 0u;
+                }
             }
         }
     };

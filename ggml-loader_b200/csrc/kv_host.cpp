@@ -201,9 +201,15 @@ struct kv_ctx {
     unsigned long long *stats = nullptr;  // [max_cta][2][8][2] epoch-tagged (max, sum) slots
     uint32_t epoch = 0;                   // tag of the last attention launch
     long long *acc = nullptr; // [hkv_loc][8][D] fixed-point output accumulators
-    unsigned *ctl = nullptr;  // [2][hkv_loc]: output tickets, non-finite flags
+    unsigned *ctl = nullptr;  // [2][hkv_loc]: output tickets, non-finite flags; then the peer-exchange ticket
     unsigned *err = nullptr;  // device error word of the bounded waits
     float *local_out = nullptr;   // sharded prefill: [n_batch_max][hq_loc*D]
+    // sharded decode over peer memory: this shard's receive buffer [2][n_head*D]
+    // F32 + flags [2][n_shards][hkv_loc], and every shard's buffer mapped here
+    float *rx = nullptr;
+    int64_t rx_stride = 0;
+    float *peer_rx[kvb::kMaxShards] = {};
+    bool peers = false;
     float *gathered = nullptr;    // [n_shards][n_batch_max][hq_loc*D]
     int max_cta = 0;
     std::vector<CUtensorMap> kmaps, vmaps;  // per layer: [n_ctx][hkv_loc][D] F16, swizzled column boxes
@@ -362,6 +368,8 @@ int encode_map(CUtensorMap *m, CUtensorMapDataType dt, int rank, void *base, con
     return KV_OK;
 }
 
+void unmap_peers(kv_ctx *ctx);
+
 void free_all(kv_ctx *ctx)
 {
     for (auto &r : ctx->recs) {
@@ -371,6 +379,18 @@ void free_all(kv_ctx *ctx)
     for (auto e : ctx->ev_pool) cudaEventDestroy(e);
     ctx->recs.clear();
     ctx->ev_pool.clear();
+    if (ctx->cfg.n_shards > 1 && ctx->comm) {
+        // no shard may still write into a buffer about to be unmapped: all
+        // shards reach this point with their work complete
+        cudaDeviceSynchronize();
+        int *d = nullptr;
+        if (cudaMalloc(&d, sizeof(int) * ctx->cfg.n_shards) == cudaSuccess) {
+            nccl().AllGather(d + ctx->cfg.shard, d, 1, 2, ctx->comm, nullptr);
+            cudaDeviceSynchronize();
+            cudaFree(d);
+        }
+    }
+    unmap_peers(ctx);
     if (ctx->comm && nccl().CommDestroy) nccl().CommDestroy(ctx->comm);
     ctx->comm = nullptr;
     void *ptrs[] = {ctx->cache, ctx->rope, ctx->qbuf, ctx->S, ctx->stats, ctx->acc, ctx->ctl, ctx->err,
@@ -379,6 +399,83 @@ void free_all(kv_ctx *ctx)
         if (p) cudaFree(p);
 }
 
+
+// Sharded decode exchanges head outputs over NVLink instead of an NCCL
+// all-gather: each shard allocates a receive buffer, its CUDA IPC handle goes to
+// every shard (one ncclAllGather at kv_alloc) and each shard maps the others'.
+// Returns KV_OK and leaves ctx->peers false (NCCL path) when the mapping is not
+// possible; an error code only for a failed collective.
+int map_peers(kv_ctx *ctx)
+{
+    const kv_config &c = ctx->cfg;
+    const int G = c.n_shards;
+    if (G > kvb::kMaxShards) return KV_OK;
+    ctx->rx_stride = (int64_t)c.n_head * ctx->D;
+    const size_t bytes = (size_t)2 * ctx->rx_stride * sizeof(float) + (size_t)2 * G * ctx->hkv_loc * sizeof(unsigned);
+    if (cudaMalloc(&ctx->rx, bytes) != cudaSuccess || cudaMemset(ctx->rx, 0, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(KV_E_OOM, "peer receive buffer");
+    }
+    cudaIpcMemHandle_t mine;
+    const bool have = cudaIpcGetMemHandle(&mine, ctx->rx) == cudaSuccess;
+    if (!have) cudaGetLastError();
+    // every shard's handle (a zeroed handle marks a shard without one)
+    std::vector<unsigned char> all((size_t)G * sizeof(cudaIpcMemHandle_t), 0);
+    unsigned char *dev = nullptr;
+    if (cudaMalloc(&dev, all.size()) != cudaSuccess) return fail(KV_E_OOM, "handle exchange buffer");
+    cudaMemset(dev, 0, all.size());
+    if (have)
+        cudaMemcpy(dev + (size_t)c.shard * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice);
+    const int nr = nccl().AllGather(dev + (size_t)c.shard * sizeof(mine), dev, sizeof(mine), 1 /* uint8 */,
+                                    ctx->comm, nullptr);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(all.data(), dev, all.size(), cudaMemcpyDeviceToHost);
+    cudaFree(dev);
+    if (nr != 0 || e != cudaSuccess) return fail(KV_E_COMM, "IPC handle exchange failed");
+    bool ok = true;
+    for (int g = 0; g < G && ok; g++) {
+        if (g == c.shard) {
+            ctx->peer_rx[g] = ctx->rx;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, all.data() + (size_t)g * sizeof(h), sizeof(h));
+        bool zero = true;
+        for (size_t i = 0; i < sizeof(h); i++) zero = zero && ((unsigned char *)&h)[i] == 0;
+        void *p = nullptr;
+        if (zero || cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+        } else {
+            ctx->peer_rx[g] = static_cast<float *>(p);
+        }
+    }
+    // every shard must agree: one that could not map its peers uses NCCL, so all do
+    int flag = ok ? 1 : 0;
+    int *dflag = nullptr;
+    std::vector<int> flags(G, 0);
+    if (cudaMalloc(&dflag, G * sizeof(int)) == cudaSuccess) {
+        cudaMemcpy(dflag + c.shard, &flag, sizeof(int), cudaMemcpyHostToDevice);
+        if (nccl().AllGather(dflag + c.shard, dflag, 1, 2 /* int32 */, ctx->comm, nullptr) == 0 &&
+            cudaDeviceSynchronize() == cudaSuccess)
+            cudaMemcpy(flags.data(), dflag, G * sizeof(int), cudaMemcpyDeviceToHost);
+        cudaFree(dflag);
+    }
+    ctx->peers = true;
+    for (int g = 0; g < G; g++) ctx->peers = ctx->peers && flags[g] == 1;
+    // KV_B200_EXCHANGE=nccl keeps the NCCL all-gather for decode as well
+    const char *env = getenv("KV_B200_EXCHANGE");
+    if (env && strcmp(env, "nccl") == 0) ctx->peers = false;
+    return KV_OK;
+}
+
+void unmap_peers(kv_ctx *ctx)
+{
+    for (int g = 0; g < kvb::kMaxShards; g++)
+        if (ctx->peer_rx[g] && ctx->peer_rx[g] != ctx->rx) cudaIpcCloseMemHandle(ctx->peer_rx[g]);
+    if (ctx->rx) cudaFree(ctx->rx);
+    ctx->rx = nullptr;
+}
 
 // The single-token append a kv_append deferred to the following kv_attend.
 int run_append(kv_ctx *ctx, const Pending &pd)
@@ -549,14 +646,14 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
         {(void **)&ctx->S, (size_t)ctx->S_floats * sizeof(float)},
         {(void **)&ctx->stats, n_part * 2u * sizeof(unsigned long long)},
         {(void **)&ctx->acc, (size_t)ctx->hkv_loc * 8u * (size_t)D * sizeof(long long)},
-        {(void **)&ctx->ctl, 2u * (size_t)ctx->hkv_loc * sizeof(unsigned)},
+        {(void **)&ctx->ctl, (2u * (size_t)ctx->hkv_loc + 1u) * sizeof(unsigned)},
         {(void **)&ctx->err, sizeof(unsigned)},
     };
     for (auto &a : allocs) {
         e = cudaMalloc(a.p, a.bytes);
         if (e != cudaSuccess) return bail(fail(KV_E_OOM, "scratch allocation (%zu bytes): %s", a.bytes, cudaGetErrorString(e)));
     }
-    e = cudaMemset(ctx->ctl, 0, 2u * (size_t)ctx->hkv_loc * sizeof(unsigned));
+    e = cudaMemset(ctx->ctl, 0, (2u * (size_t)ctx->hkv_loc + 1u) * sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(ctx->stats, 0, n_part * 2u * sizeof(unsigned long long));
     if (e == cudaSuccess) e = cudaMemset(ctx->acc, 0, (size_t)ctx->hkv_loc * 8u * (size_t)D * sizeof(long long));
     if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, sizeof(unsigned));
@@ -621,6 +718,8 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
             ctx->comm = nullptr;
             return bail(fail(KV_E_COMM, "ncclCommInitRank: %s", api.GetErrorString ? api.GetErrorString(rc) : "error"));
         }
+        const int prc = map_peers(ctx);
+        if (prc) return bail(prc);
     }
     e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return bail(cuda_fail(e, "kv_alloc sync"));
@@ -833,6 +932,18 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     ap.out = dst;
     ap.out_stride = dst_stride;
     ap.out_head0 = dst_head0;
+    const bool via_peers = sharded && ctx->peers && n_new == 1 && ctx->r <= kvb::attn_rows() &&
+                           !(!fused && ctx->pf && n_new * ctx->r >= 32);
+    ap.n_peers = via_peers ? c.n_shards : 0;
+    ap.shard = c.shard;
+    ap.rx_stride = ctx->rx_stride;
+    ap.xticket = ctx->ctl + 2 * ctx->hkv_loc;
+    for (int g = 0; g < kvb::kMaxShards; g++) {
+        ap.rx[g] = via_peers ? ctx->peer_rx[g] : nullptr;
+        ap.rxflag[g] = via_peers && ctx->peer_rx[g]
+                           ? reinterpret_cast<unsigned *>(ctx->peer_rx[g] + 2 * ctx->rx_stride)
+                           : nullptr;
+    }
     if (ap.n_cta > ctx->max_cta) return fail(KV_E_RANGE, "internal: %d CTAs > %d", ap.n_cta, ctx->max_cta);
     {
         // score tiles of the longest CTA range: ceil(ceil(T/C)/128) + 1 (a range
@@ -886,7 +997,7 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     ctx->hz_layer = fused ? layer : -1;
     ctx->hz_row = fused ? n_past : -1;
 
-    if (sharded) {
+    if (sharded && !via_peers) {
         NcclApi &api = nccl();
         const size_t cols = (size_t)ctx->hq_loc * D;
         int nr;
@@ -998,7 +1109,7 @@ int kv_status(kv_ctx *ctx, void *stream)
     if (word == 0) return KV_OK;
     // a CTA that left early never counted itself in: restart the per-head
     // tickets and clear the output accumulators
-    KV_CUDA(cudaMemset(ctx->ctl, 0, 2u * (size_t)ctx->hkv_loc * sizeof(unsigned)));
+    KV_CUDA(cudaMemset(ctx->ctl, 0, (2u * (size_t)ctx->hkv_loc + 1u) * sizeof(unsigned)));
     KV_CUDA(cudaMemset(ctx->acc, 0, (size_t)ctx->hkv_loc * 8u * (size_t)ctx->D * sizeof(long long)));
     KV_CUDA(cudaMemset(ctx->err, 0, sizeof(unsigned)));
     return fail(KV_E_TIMEOUT, "a device-side wait expired (error word 0x%x); the outputs of that call are invalid",

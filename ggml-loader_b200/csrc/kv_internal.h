@@ -79,6 +79,7 @@ cudaError_t launch_pv(int D, const PVParams &p, int hkv_loc, cudaStream_t st);
 // layer and group of <= 8 query rows, chained with programmatic dependent launch
 // ---------------------------------------------------------------------------
 constexpr int kMaxLocalHeads = 64;   // KV heads one context may own
+constexpr int kMaxShards = 8;        // KV-head shards exchanging outputs over peer memory
 
 struct AttnParams {
     int32_t hkv, r, hq_loc;          // local KV heads, GQA group, local query heads
@@ -117,6 +118,16 @@ struct AttnParams {
     float *out;
     int64_t out_stride;
     int32_t out_head0;
+    // KV-head shards exchanging decode outputs over NVLink (n_peers = shards, 0 = none):
+    // rx[g] = shard g's receive buffer, 2 parities x out_stride floats (the
+    // full output row, written by the shard that owns each head); rxflag[g] =
+    // shard g's flags [2 parities][n_peers][hkv] = epoch of the writer's launch;
+    // xticket counts this launch's converted local heads
+    int32_t n_peers, shard;
+    float *rx[kMaxShards];
+    unsigned *rxflag[kMaxShards];
+    int64_t rx_stride;
+    unsigned *xticket;
     // CTAs [span_a[h], span_b[h]] cover local head h; span_slot[h] is the
     // segment index head h has in CTA span_a[h] (1 when that CTA starts in head h-1)
     int16_t span_a[kMaxLocalHeads], span_b[kMaxLocalHeads];

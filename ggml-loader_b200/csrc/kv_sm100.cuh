@@ -184,6 +184,18 @@ __device__ __forceinline__ void cp_async_wait()
 }
 
 // ---- cross-CTA slots ------------------------------------------------------------
+__device__ __forceinline__ unsigned ld_volatile_u32(const unsigned *p)
+{
+    unsigned v;
+    asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_volatile_u32(unsigned *p, unsigned v)
+{
+    asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // 16-byte stores / loads of two 64-bit words for cross-CTA slots; each word is
 // single-copy atomic, the pair is not (readers check both words).
 __device__ __forceinline__ void st_volatile_v2(unsigned long long *p, unsigned long long a, unsigned long long b)
