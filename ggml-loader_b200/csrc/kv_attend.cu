@@ -274,6 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             prefetch_tmap(&vmap);
             const int total = 2 * g.nt;
             bool waited = false;
+            const uint64_t pol = policy_evict_first();   // K/V are read once per launch
             for (int j = 0; j < total; j++) {
                 if (p.inject == 1 && j == 1) break;   // test hook: withhold tile 1
                 const int s = j % NS;
@@ -299,7 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 mbar_arrive_expect_tx(&full[s], kStage);
 #pragma unroll
                 for (int b = 0; b < NB; b++)
-                    tma_load_3d(smem + s * kStage + b * kSub, isv ? &vmap : &kmap, &full[s], b * BW, h, (int)k0);
+                    tma_load_3d_hint(smem + s * kStage + b * kSub, isv ? &vmap : &kmap, &full[s], b * BW, h, (int)k0,
+                                     pol);
                 issued = j + 1;
             }
             if (!waited) pdl_wait();   // complete only after the previous kernel
@@ -322,7 +324,19 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     float *const Scta = p.S + (int64_t)c * p.S_tiles * kTileScores;
 
     float2 csr[(D + 31) / 32];
-    if (p.fused) rope_prefetch<D>(p, csr);
+    if (p.fused) {
+        rope_prefetch<D>(p, csr);
+        // the query rows (and the new K row) into L2 while the previous kernel
+        // finishes: L2 is coherent, so a row it still writes is read fresh below
+        const int nq = R * (two ? 2 : 1);
+        for (int it = warp; it < nq + (owns_new ? 1 : 0); it += 8)
+            if (lane < D / 32) {
+                const float *src = it < nq ? p.q + (int64_t)((p.row0 + it % R) / p.r) * p.q_stride +
+                                                 (int64_t)(p.hq0 + (g.h0 + it / R) * p.r + (p.row0 + it % R) % p.r) * D
+                                           : p.k + (int64_t)(p.hkv0 + g.h0) * D;
+                l2_prefetch(src + lane * 32);
+            }
+    }
     pdl_wait();   // inputs, qbuf and the rows below may come from the previous kernel
     pdl_launch_dependents();   // only now: the next kernel may rely on every kernel before this one
 
@@ -762,6 +776,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     }
     cp_async_wait<0>();
     flush_out(two ? 1 : 0);
+    // every consumer has read its scores (flush_out opens with a barrier): the
+    // scratch is dead until the next launch rewrites it, so it leaves L2
+    // without a write-back
+    for (int ln = tid; ln < g.nt * (kTileScores / 32); ln += kConsumers) l2_discard(Scta + ln * 32);
     named_sync(2, kThreads);
 }
 

@@ -103,6 +103,36 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *m, uin
         : "memory");
 }
 
+// L2 policy for data read once (streamed K/V tiles): evicted before other lines
+__device__ __forceinline__ uint64_t policy_evict_first()
+{
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ void tma_load_3d_hint(void *dst, const CUtensorMap *m, uint64_t *bar, int x, int y, int z,
+                                                 uint64_t pol)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+        "[%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z), "l"(pol)
+        : "memory");
+}
+
+// drop a dead 128-byte line from L2 without writing it back (scratch that is
+// rewritten before it is read again)
+__device__ __forceinline__ void l2_discard(const void *p)
+{
+    asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
+}
+
+__device__ __forceinline__ void l2_prefetch(const void *p)
+{
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *m, uint64_t *bar, int x, int y)
 {
     asm volatile(
