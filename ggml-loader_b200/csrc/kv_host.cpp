@@ -221,15 +221,14 @@ struct kv_ctx {
     int last_layer = -1;
     int64_t last_n_past = -1;
     int last_n_new = 0;
-    // the cache row the last fused attention launch appended (stream, layer):
-    // the next launch on that stream for that layer must not read it early
     // chunked prefill on the tensor cores (head_dim 64/128, chunks of >= 32 query rows)
     bool pf = false;
     int pf_tb = 0;                          // tokens per 128-row query tile
     CUtensorMap qmap{};                     // qbuf [n_batch_max][hq_loc][D], box 64 x r x tb
-    float *pf_stat = nullptr;               // [sm_count][kseg][128][2]
-    float2 *pf_rstat = nullptr;             // [hkv_loc * blocks][128]
-    float *pf_out = nullptr;                // [sm_count][kseg][128][D]
+    float *pf_stat = nullptr;               // [sm_count][kseg][2 tiles][128][2]
+    float *pf_out = nullptr;                // [sm_count][kseg][2 tiles][128][D]
+    // the cache row the last fused attention launch appended (stream, layer):
+    // the next launch on that stream for that layer must not read it early
     cudaStream_t hz_stream = nullptr;
     int hz_layer = -1;
     int64_t hz_row = -1;
@@ -394,7 +393,7 @@ void free_all(kv_ctx *ctx)
     if (ctx->comm && nccl().CommDestroy) nccl().CommDestroy(ctx->comm);
     ctx->comm = nullptr;
     void *ptrs[] = {ctx->cache, ctx->rope, ctx->qbuf, ctx->S, ctx->stats, ctx->acc, ctx->ctl, ctx->err,
-                    ctx->local_out, ctx->gathered, ctx->pf_stat, ctx->pf_rstat, ctx->pf_out};
+                    ctx->local_out, ctx->gathered, ctx->pf_stat, ctx->pf_out};
     for (void *p : ptrs)
         if (p) cudaFree(p);
 }
@@ -692,10 +691,8 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
                             CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc != KV_OK) return bail(rc);
         const int kseg = kvb::prefill_max_segments();
-        const size_t nblk = (size_t)(c.n_batch_max + ctx->pf_tb - 1) / ctx->pf_tb;
-        const size_t slots = (size_t)ctx->sm_count * kseg * 128u;
-        e = cudaMalloc(&ctx->pf_stat, slots * 4u * 2u * sizeof(float));   // up to 4 column parts
-        if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_rstat, (size_t)ctx->hkv_loc * nblk * 128u * sizeof(float2));
+        const size_t slots = (size_t)ctx->sm_count * kseg * 256u;   // segments x two 128-row tiles
+        e = cudaMalloc(&ctx->pf_stat, slots * 2u * sizeof(float));
         if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_out, slots * (size_t)D * sizeof(float));
         if (e != cudaSuccess) return bail(fail(KV_E_OOM, "prefill scratch: %s", cudaGetErrorString(e)));
         e = kvb::prefill_prepare(ctx->D);
@@ -804,10 +801,11 @@ int kv_append(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
 
 namespace {
 
-// Chunked-prefill attention on the tensor cores: statistics pass, statistics
-// fold, output pass, output fold (kv_prefill.cu).  The pairs' key tiles, laid
-// end to end, are cut into C equal ranges; C is the SM count, lowered until no
-// range holds more than prefill_max_segments() pairs.
+// Chunked-prefill attention on the tensor cores: the one-pass attention kernel,
+// then the fold of pairs split over CTAs (kv_prefill.cu).  A pair is (KV head,
+// block of two 128-row query tiles); the pairs' key tiles, laid end to end, are
+// cut into C equal ranges; C is the SM count, lowered until no range holds more
+// than prefill_max_segments() pairs.
 int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n_past, int32_t n_new, float *dst,
             int64_t dst_stride, int dst_head0, cudaStream_t st)
 {
@@ -819,11 +817,11 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     pp.n_past = n_past;
     pp.n_new = n_new;
     pp.tb = ctx->pf_tb;
-    pp.nblk = (n_new + pp.tb - 1) / pp.tb;
+    pp.nblk = (n_new + 2 * pp.tb - 1) / (2 * pp.tb);
     std::vector<int64_t> nt(pp.nblk);
     pp.s_all = 0;
     for (int b = 0; b < pp.nblk; b++) {
-        nt[b] = (n_past + std::min<int64_t>(n_new, (int64_t)(b + 1) * pp.tb) + 127) / 128;
+        nt[b] = (n_past + std::min<int64_t>(n_new, (int64_t)(2 * b + 2) * pp.tb) + 127) / 128;
         pp.s_all += nt[b];
     }
     const int64_t W = (int64_t)pp.hkv * pp.s_all;
@@ -846,17 +844,15 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     pp.kseg = kseg;
     pp.scale = ctx->scale;
     pp.pstat = ctx->pf_stat;
-    pp.rstat = ctx->pf_rstat;
     pp.pout = ctx->pf_out;
     pp.out = dst;
     pp.out_stride = dst_stride;
     pp.out_head0 = dst_head0;
     pp.err = ctx->err;
     pp.limit_ns = ctx->limit_ns;
-    static const char *what[4] = {"prefill statistics kernel", "prefill statistics fold", "prefill output kernel",
-                                  "prefill output fold"};
-    for (int which = 0; which < 4; which++) {
-        const int rc = launch(ctx, (which & 1) ? KV_K_PFOLD : KV_K_PREFILL, st, what[which],
+    static const char *what[2] = {"prefill attention kernel", "prefill output fold"};
+    for (int which = 0; which < 2; which++) {
+        const int rc = launch(ctx, which ? KV_K_PFOLD : KV_K_PREFILL, st, what[which],
                               [&] { return kvb::launch_prefill(ctx->D, which, ctx->qmap, km, vm, pp, st); });
         if (rc) return rc;
     }

@@ -155,13 +155,12 @@ struct PrefillParams {
     int64_t n_past;
     int32_t n_new;
     int32_t tb;        // tokens per 128-row query tile (tb * r <= 128)
-    int32_t nblk;      // token blocks: ceil(n_new / tb); pair = kv head * nblk + block
+    int32_t nblk;      // blocks of two query tiles: ceil(n_new / (2 tb)); pair = kv head * nblk + block
     int64_t s_all;     // key tiles of one KV head summed over its blocks
     int32_t n_cta, kseg;
     float scale;
-    float *pstat;      // [n_cta][kseg][column part][128] (max, sum of exp) per segment, part and row
-    float2 *rstat;     // [hkv * nblk][128] (max, 1/sum) per pair and row
-    float *pout;       // [n_cta][kseg][128][D] partial outputs
+    float *pstat;      // [n_cta][kseg][2 tiles][128] (m, l) per segment and row (split pairs)
+    float *pout;       // [n_cta][kseg][2 tiles][128][D] unnormalised partial outputs
     float *out;        // row t at out + t*out_stride, head h at (out_head0 + h)*D
     int64_t out_stride;
     int32_t out_head0;
@@ -172,7 +171,7 @@ struct PrefillParams {
 bool prefill_supported(int D);
 int prefill_max_segments();
 cudaError_t prefill_prepare(int D);
-// which: 0 statistics pass, 1 statistics fold, 2 output pass, 3 output fold
+// which: 0 the attention kernel, 1 the fold of pairs split over CTAs
 cudaError_t launch_prefill(int D, int which, const CUtensorMap &qmap, const CUtensorMap &kmap,
                            const CUtensorMap &vmap, const PrefillParams &p, cudaStream_t st);
 

@@ -2,37 +2,47 @@
 // generation tensor cores: tcgen05.mma with TMEM accumulators, operands staged
 // in shared memory by TMA.
 //
-// Numerics: the reference's attention branch (src/model.cpp:1416-1445) for
-// n_new query tokens: S = F16(q) . K (F32 accumulation), causal mask (key <=
-// n_past + token), softmax with the global row max M and sum Z, p = F16(exp(s
-// - M) / Z), O = p . V (F32 accumulation).  ggml rounds the normalised p to
-// F16, so every p needs the final M and Z of its row: pass 1 computes S and
-// the row statistics, pass 2 computes S again, forms p and accumulates P . V.
-// exp is 2^(x log2 e) on the SFU (ex2.approx): within a few F32 ulps of expf,
-// far inside the attention tolerance.
+// What it computes: the reference's attention branch (src/model.cpp:1416-1445)
+// for n_new query tokens: S = F16(q) . K (F32 accumulation), causal mask (key <=
+// n_past + token), scale, softmax over the keys, O = P . V with the weights P
+// rounded to F16 (ggml converts the mul_mat operand to the F16 vec-dot type).
 //
-// Work: query rows are packed GQA-group-major: one 128-row tile holds tb =
+// How: one pass over the keys with an online softmax.  Per query row the kernel
+// keeps a running maximum m (log2 units: s * log2 e), the F32 sum l of
+// 2^(s*log2e - m) and O = sum F16(2^(s*log2e - m)) . V in TMEM; the output is
+// O / l.  ggml rounds the normalised weight exp(s - M) / Z to F16 instead; the
+// two roundings differ by at most one F16 ulp of each weight (2^-11 relative),
+// far inside the attention tolerance.  m is raised lazily: only when a tile's
+// maximum exceeds it by more than 2^8 are l and the row of O rescaled, so the
+// weights stay <= 256 (exact range of F16) and O is rarely read back.  exp is
+// 2^x on the SFU (ex2.approx, a few F32 ulps from expf).
+//
+// Work: query rows are packed GQA-group-major: a 128-row tile holds tb =
 // floor(128 / r) tokens x the r query heads of one KV head (row = token*r +
-// head), so a K/V tile staged once serves every head of the group.  A "pair" is
-// (KV head, block of tb tokens); its keys are the tiles of 128 keys up to the
-// block's last visible key.  The pairs' tiles, laid end to end, are cut into C
-// equal ranges (one CTA each, C <= SMs); a range holds one or more "segments"
-// (the part of one pair it covers).
+// head), and a CTA holds two such tiles, A and B (2*tb consecutive tokens), so
+// a K/V tile staged once feeds four MMAs.  A "pair" is (KV head, block of 2*tb
+// tokens); its keys are the tiles of 128 keys up to the block's last visible
+// key.  The pairs' tiles, laid end to end, are cut into C equal ranges (one CTA
+// each, C <= SMs); a range holds one or more "segments" (the part of one pair
+// it covers).  A pair that one segment covers is written to the output by the
+// kernel; otherwise each segment leaves its (m, l, O) and prefill_out_fold
+// merges them (weights 2^(m_i - max m), CTAs in order).
 //
-// prefill_kernel<D, OUT> (576 threads):
-//   warp 0     TMA: the pair's Q tile, then K tiles (and V tiles in pass 2) into
-//              mbarrier rings;
-//   warp 1     TMEM owner and MMA issuer (one thread): S = Q . K^T, M=128, N=128
-//              keys, K = D, into one of two 128-column TMEM buffers; in pass 2
-//              also O += P . V (M=128, N=D, K=128 keys; P from TMEM, V read
-//              MN-major from shared memory) into D more columns, one tile behind;
-//   warps 2-17 a query row per lane and a quarter of each tile's keys per warp,
-//              read from TMEM with tcgen05.ld: pass 1 keeps the running row max
-//              / sum of exp; pass 2 writes p as F16 pairs back into TMEM with
-//              tcgen05.st (double-buffered), the A operand of the P . V MMA,
-//              and at a segment's end copies O out.
-// prefill_stats_fold   (M, 1/Z) of every (pair, row) from the segments' partials
-// prefill_out_fold     sum of the segments' partial outputs, scattered to out
+// prefill_kernel<D> (320 threads):
+//   warp 0     TMA: the pair's two Q tiles, then K and V tiles into mbarrier rings
+//   warp 1     TMEM owner and MMA issuer (one thread), in sub-tiles of 64 keys
+//              (half a K/V tile).  TMEM columns: two S buffers per query tile
+//              (64 F32 columns each; P, F16 pairs, overwrites the first 32
+//              columns of its S), then O_A, O_B (D each).  Issue order:
+//                S_A(i) S_B(i) S_A(i+1) S_B(i+1) PV_A(i) S_A(i+2) PV_B(i) S_B(i+2) ..
+//              so the tensor cores compute S(i+1) while sub-tile i is in the
+//              softmax.  The MMAs of one thread run in issue order: S_X(i+2)
+//              cannot overwrite P_X(i) before PV_X(i) has read it
+//   warps 2-5  softmax of tile A, warps 6-9 of tile B: one query row per thread,
+//              a sub-tile's 64 keys read with tcgen05.ld; P written back with
+//              tcgen05.st; the rare O rescale (after the previous P . V, which
+//              the barrier o_ready reports); at a segment's end O out
+// prefill_out_fold   merges the segments of pairs split over CTAs
 // Every wait is bounded (limit_ns) and gives up when the CTA's abort flag is
 // set; the CTA drains its TMA loads and MMAs and frees TMEM before leaving.
 #include <math.h>
@@ -45,28 +55,26 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kSW = 16;                     // softmax / epilogue warps (2..17)
-constexpr int kCP = 4;                      // statistics parts of a row: 2 tile groups x 2 key halves
-constexpr int kPThreads = 64 + 32 * kSW;
-constexpr uint32_t kBox = 128 * 128;   // one [128 rows][64 halves] swizzled box
-// TMEM columns: S (two 128-column F32 buffers), O (up to 128 F32), P (two
-// 64-column buffers of F16 pairs) -- 512 in all
-constexpr uint32_t kTmO = 256, kTmP = 384;
+constexpr int kGW = 4;                         // softmax warps per query tile
+constexpr int kPThreads = 32 * (4 + 2 * kGW);  // TMA warp, three MMA issuers, two softmax groups
+constexpr uint32_t kBox = 128 * 128;           // one [128 rows][64 halves] swizzled box
+constexpr uint32_t kTmO = 256;                 // TMEM column of O_A (O_B follows at +D)
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLazy = 8.0f;                  // raise m only past 2^8 growth
 
-template <int D, bool OUT>
+template <int D>
 struct PL {
     static constexpr int NB = D / 64;                        // boxes per Q/K/V row
     static constexpr uint32_t kTile = (uint32_t)NB * kBox;   // 128 rows x D halves
-    static constexpr int KS = OUT ? (D == 128 ? 3 : 6) : (D == 128 ? 6 : 12);
-    static constexpr int VS = OUT ? (D == 128 ? 3 : 6) : 0;
-    static constexpr size_t o_q = 0;
-    static constexpr size_t o_k = o_q + kTile;
+    static constexpr int KS = D == 128 ? 3 : 6;              // K ring
+    static constexpr int VS = D == 128 ? 2 : 5;              // V ring
+    static constexpr size_t o_q = 0;                         // Q tiles A, B
+    static constexpr size_t o_k = o_q + 2 * (size_t)kTile;
     static constexpr size_t o_v = o_k + (size_t)KS * kTile;
     static constexpr size_t o_bar = o_v + (size_t)VS * kTile;
     // q_full, q_empty, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
-    // s_full[2], s_free[2], p_full[2], p_empty[2], o_full, o_empty, drain
-    static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 8 + 3;
+    // s_full[2][2], p_full[2][2], o_ready[2][2], o_full, o_empty, drain[3]
+    static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 12 + 5;
     static constexpr size_t o_tm = o_bar + (size_t)NBAR * 8;
     static constexpr size_t o_flags = o_tm + 16;
     static constexpr size_t bytes = o_flags + 16;
@@ -74,9 +82,10 @@ struct PL {
 };
 
 // ---- the work split ------------------------------------------------------------
+// key tiles of block b (tokens [2b*tb, 2b*tb + 2*tb))
 __device__ __forceinline__ int nt_of(const PrefillParams &p, int b)
 {
-    const int64_t last = p.n_past + min(p.n_new, (b + 1) * p.tb);   // keys [0, last)
+    const int64_t last = p.n_past + min((int64_t)p.n_new, (int64_t)(2 * b + 2) * p.tb);   // keys [0, last)
     return (int)((last + 127) / 128);
 }
 
@@ -141,15 +150,56 @@ __device__ __forceinline__ void give_up(const PrefillParams &p, volatile int *fl
 }
 
 // ---------------------------------------------------------------------------
-// pass 1 (OUT = false) and pass 2 (OUT = true)
+// softmax arithmetic: three-input max and packed F32 pairs (sm_100)
 // ---------------------------------------------------------------------------
-template <int D, bool OUT>
+__device__ __forceinline__ float max3(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t pk2(float lo, float hi)
+{
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+
+__device__ __forceinline__ float2 up2(uint64_t v)
+{
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+
+// (a.x*b.x + c.x, a.y*b.y + c.y), each rounded once
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+// 12 warps put 3 on each of the SM's four 16K-register quarters: at most 168
+// registers a thread
+template <int D>
 __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                  const __grid_constant__ CUtensorMap kmap,
                                                                  const __grid_constant__ CUtensorMap vmap,
                                                                  const PrefillParams p)
 {
-    using L = PL<D, OUT>;
+    using L = PL<D>;
     constexpr int NB = L::NB, KS = L::KS, VS = L::VS;
     constexpr uint32_t kTile = L::kTile;
     extern __shared__ __align__(1024) unsigned char smem[];
@@ -157,9 +207,11 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
     uint64_t *q_full = bar, *q_empty = bar + 1;
     uint64_t *k_full = bar + 2, *k_empty = k_full + KS;
     uint64_t *v_full = k_empty + KS, *v_empty = v_full + VS;
-    uint64_t *s_full = v_empty + VS, *s_free = s_full + 2;
-    uint64_t *p_full = s_free + 2, *p_empty = p_full + 2;
-    uint64_t *o_full = p_empty + 2, *o_empty = o_full + 1, *drain = o_empty + 1;
+    uint64_t *s_full = v_empty + VS;   // [tile g][buffer]: S_g of a sub-tile is in TMEM
+    uint64_t *p_full = s_full + 4;     // [tile g][buffer]: P_g of a sub-tile is in TMEM
+    uint64_t *o_ready = p_full + 4;    // [tile g][buffer]: the P_g . V of a sub-tile has completed
+    uint64_t *o_full = o_ready + 4, *o_empty = o_full + 1;
+    uint64_t *drain = o_empty + 1;     // [issuer]
     uint32_t *tm_slot = reinterpret_cast<uint32_t *>(smem + L::o_tm);
     volatile int *flags = reinterpret_cast<volatile int *>(smem + L::o_flags);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, c = blockIdx.x;
@@ -167,10 +219,11 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
 
     if (tid == 0) {
         for (int i = 0; i < L::NBAR; i++) {
-            // a tile group's 8 warps arrive on s_free and p_full, all 16 on o_empty
+            // a softmax group's warps arrive on its p_full, both groups' on
+            // o_empty; both S issuers commit to k_empty and q_empty
             const uint64_t *bi = &bar[i];
-            const bool grp = bi == &s_free[0] || bi == &s_free[1] || bi == &p_full[0] || bi == &p_full[1];
-            mbar_init(&bar[i], grp ? kSW / 2 : bi == o_empty ? kSW : 1);
+            const bool two = bi == q_empty || (bi >= k_empty && bi < k_empty + KS);
+            mbar_init(&bar[i], (bi >= p_full && bi < p_full + 4) ? kGW : bi == o_empty ? 2 * kGW : two ? 2 : 1);
         }
         flags[0] = 0;
         fence_mbar_init();
@@ -183,24 +236,28 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tm_slot;
+    pdl_launch_dependents();   // the fold may start its set-up (it waits for this grid)
 
     if (warp == 0) {
         // ================= TMA =================
         if (lane == 0) {
             prefetch_tmap(&qmap);
             prefetch_tmap(&kmap);
-            if (OUT) prefetch_tmap(&vmap);
-            const uint32_t qbytes = (uint32_t)(p.r * p.tb) * 128u * NB;
+            prefetch_tmap(&vmap);
+            const uint32_t qbytes = (uint32_t)(p.r * p.tb) * 128u * NB;   // one Q tile (zero fill counts)
             for_segments(p, c, [&](int k, const Seg &sg) {
                 const int kvh = sg.pair / p.nblk, b = sg.pair % p.nblk;
                 if (k > 0 && !mbar_wait_ab(q_empty, (k - 1) & 1, p.limit_ns, flags)) {
                     give_up(p, flags, 2u);
                     return false;
                 }
-                mbar_arrive_expect_tx(q_full, qbytes);
+                mbar_arrive_expect_tx(q_full, 2 * qbytes);
 #pragma unroll
-                for (int bx = 0; bx < NB; bx++)
-                    tma_load_3d(smem + L::o_q + bx * kBox, &qmap, q_full, bx * 64, kvh * p.r, b * p.tb);
+                for (int g = 0; g < 2; g++)
+#pragma unroll
+                    for (int bx = 0; bx < NB; bx++)
+                        tma_load_3d(smem + L::o_q + g * kTile + bx * kBox, &qmap, q_full, bx * 64, kvh * p.r,
+                                    (2 * b + g) * p.tb);
                 issued_q++;
                 for (int t = sg.t0; t < sg.t1; t++) {
                     const int s = issued_k % KS;
@@ -213,249 +270,244 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                     for (int bx = 0; bx < NB; bx++)
                         tma_load_3d(smem + L::o_k + s * kTile + bx * kBox, &kmap, &k_full[s], bx * 64, kvh, t * 128);
                     issued_k++;
-                    if constexpr (OUT) {
-                        const int sv = issued_v % VS;
-                        if (issued_v >= VS &&
-                            !mbar_wait_ab(&v_empty[sv], ((issued_v / VS) - 1) & 1, p.limit_ns, flags)) {
-                            give_up(p, flags, 2u);
-                            return false;
-                        }
-                        mbar_arrive_expect_tx(&v_full[sv], kTile);
-#pragma unroll
-                        for (int bx = 0; bx < NB; bx++)
-                            tma_load_3d(smem + L::o_v + sv * kTile + bx * kBox, &vmap, &v_full[sv], bx * 64, kvh,
-                                        t * 128);
-                        issued_v++;
+                    const int sv = issued_v % VS;
+                    if (issued_v >= VS && !mbar_wait_ab(&v_empty[sv], ((issued_v / VS) - 1) & 1, p.limit_ns, flags)) {
+                        give_up(p, flags, 2u);
+                        return false;
                     }
+                    mbar_arrive_expect_tx(&v_full[sv], kTile);
+#pragma unroll
+                    for (int bx = 0; bx < NB; bx++)
+                        tma_load_3d(smem + L::o_v + sv * kTile + bx * kBox, &vmap, &v_full[sv], bx * 64, kvh, t * 128);
+                    issued_v++;
                 }
                 return true;
             });
         }
-    } else if (warp == 1) {
+    } else if (warp == 1 || warp >= 2 + 2 * kGW) {
         // ================= MMA issue =================
+        // Sub-tile i = 64 keys (half of K/V tile i/2; i counts across
+        // segments), S buffer i&1.  Three issuing warps, since one thread's
+        // tcgen05.mma issue, not the tensor cores, limits narrow MMAs:
+        //   S issuer of tile g (warps 1, 10): S_g(i) once PV_g(i-2) has read
+        //     the buffer's P (o_ready) -- so S runs two sub-tiles ahead
+        //   PV issuer (warp 11): PV_A(i), PV_B(i) once the softmax reports P
+        const int role = warp == 1 ? 0 : warp - (1 + 2 * kGW);   // 0: S_A, 1: S_B, 2: PV
         if (lane == 0) {
-            constexpr uint32_t idS = idesc_f16_f32(128, 128, false);
+            constexpr uint32_t idS = idesc_f16_f32(128, 64, false);
             constexpr uint32_t idO = idesc_f16_f32(128, D, true);
             const uint32_t sq = smem_addr(smem + L::o_q), sk = smem_addr(smem + L::o_k);
             const uint32_t sv = smem_addr(smem + L::o_v);
-            int j = 0;               // tiles issued (S)
-            // tiles whose P . V is still to issue, oldest first; P . V runs two
-            // tiles behind S so the next S never queues behind a P . V
-            struct Pend {
-                int j, seg;
-                bool first, last;
-            };
-            Pend pq0{}, pq1{};
-            int npq = 0;
             bool ok = true;
-            auto issue_pv = [&](const Pend &pe) -> bool {
-                const int jp = pe.j, pb = jp & 1, vs = jp % (VS > 0 ? VS : 1);
-                if (!mbar_wait_ab(&p_full[pb], (jp >> 1) & 1, p.limit_ns, flags) ||
-                    !mbar_wait_ab(&v_full[vs], (jp / (VS > 0 ? VS : 1)) & 1, p.limit_ns, flags) ||
-                    (pe.first && pe.seg > 0 && !mbar_wait_ab(o_empty, (pe.seg - 1) & 1, p.limit_ns, flags))) {
+            auto wt = [&](uint64_t *b, uint32_t par) {
+                if (ok && !mbar_wait_ab(b, par, p.limit_ns, flags)) {
                     give_up(p, flags, 1u);
-                    return false;
+                    ok = false;
                 }
-                tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < 8; kk++) {   // 16 keys per step: 8 packed P columns
-                    const uint64_t bd = sdesc_mn_sw128(sv + vs * kTile + kk * 2048, kBox);
-                    umma_ts(tmem + kTmO, tmem + kTmP + pb * 64 + kk * 8, bd, idO, !(pe.first && kk == 0));
-                }
-                umma_commit(&p_empty[pb]);
-                umma_commit(&v_empty[vs]);
-                if (pe.last) umma_commit(o_full);
-                return true;
+                return ok;
             };
-            for_segments(p, c, [&](int k, const Seg &sg) {
-                if (!mbar_wait_ab(q_full, k & 1, p.limit_ns, flags)) {
-                    give_up(p, flags, 1u);
-                    return ok = false;
-                }
-                for (int t = sg.t0; t < sg.t1; t++) {
-                    const int s = j % KS, sb = j & 1;
-                    if (!mbar_wait_ab(&k_full[s], (j / KS) & 1, p.limit_ns, flags) ||
-                        (j >= 2 && !mbar_wait_ab(&s_free[sb], ((j - 2) >> 1) & 1, p.limit_ns, flags))) {
-                        give_up(p, flags, 1u);
-                        return ok = false;
-                    }
-                    tc_fence_after();
+            int i = 0;   // sub-tiles consumed
+            if (role < 2) {
+                const int g = role;
+                for_segments(p, c, [&](int k, const Seg &sg) {
+                    const int i1 = i + 2 * (sg.t1 - sg.t0);
+                    if (!wt(q_full, k & 1)) return false;
+                    for (; i < i1; i++) {
+                        const int tile = i >> 1;
+                        if (!(i & 1) && !wt(&k_full[tile % KS], (tile / KS) & 1)) return false;
+                        if (i >= 2 && !wt(&o_ready[g * 2 + (i & 1)], ((i - 2) >> 1) & 1)) return false;
+                        tc_fence_after();
+                        // S_g(i) = Q_g . K(64 of the tile's 128 rows)^T
+                        const uint32_t kt = sk + (tile % KS) * kTile + (i & 1) * 8192;
 #pragma unroll
-                    for (int kk = 0; kk < D / 16; kk++) {
-                        const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
-                        umma_ss(tmem + sb * 128, sdesc_k_sw128(sq + off), sdesc_k_sw128(sk + s * kTile + off), idS,
-                                kk > 0);
-                    }
-                    umma_commit(&s_full[sb]);
-                    umma_commit(&k_empty[s]);
-                    if (t == sg.t1 - 1) umma_commit(q_empty);
-                    if constexpr (OUT) {
-                        if (npq == 2) {
-                            if (!issue_pv(pq0)) return ok = false;
-                            pq0 = pq1;
-                            npq = 1;
+                        for (int kk = 0; kk < D / 16; kk++) {
+                            const uint32_t off = (kk >> 2) * kBox + (kk & 3) * 32;
+                            umma_ss(tmem + g * 128 + (i & 1) * 64, sdesc_k_sw128(sq + g * kTile + off),
+                                    sdesc_k_sw128(kt + off), idS, kk > 0);
                         }
-                        const Pend pe{j, k, t == sg.t0, t == sg.t1 - 1};
-                        if (npq == 0) pq0 = pe;
-                        else pq1 = pe;
-                        npq++;
+                        umma_commit(&s_full[g * 2 + (i & 1)]);
+                        if (i & 1) umma_commit(&k_empty[tile % KS]);   // both halves of the K tile read
+                        if (i == i1 - 1) umma_commit(q_empty);
                     }
-                    j++;
-                }
-                return true;
-            });
-            if (OUT && ok && npq > 0) ok = issue_pv(pq0);
-            if (OUT && ok && npq > 1) ok = issue_pv(pq1);
+                    return true;
+                });
+            } else {
+                for_segments(p, c, [&](int k, const Seg &sg) {
+                    const int i0 = i, i1 = i + 2 * (sg.t1 - sg.t0);
+                    for (; i < i1; i++) {
+                        const int tile = i >> 1;
+#pragma unroll
+                        for (int g = 0; g < 2; g++) {
+                            if (!wt(&p_full[g * 2 + (i & 1)], (i >> 1) & 1)) return false;
+                            if (g == 0 && !(i & 1) && !wt(&v_full[tile % VS], (tile / VS) & 1)) return false;
+                            if (g == 0 && i == i0 && k > 0 && !wt(o_empty, (k - 1) & 1)) return false;
+                            tc_fence_after();
+                            // O_g (+)= P_g(i) . V(64 of the tile's 128 rows)
+                            const uint32_t vt = sv + (tile % VS) * kTile + (i & 1) * 8192;
+#pragma unroll
+                            for (int kk = 0; kk < 4; kk++) {   // 16 keys per step: 8 packed P columns
+                                const uint64_t bd = sdesc_mn_sw128(vt + kk * 2048, kBox);
+                                umma_ts(tmem + kTmO + g * D, tmem + g * 128 + (i & 1) * 64 + kk * 8, bd, idO,
+                                        !(i == i0 && kk == 0));
+                            }
+                            umma_commit(&o_ready[g * 2 + (i & 1)]);
+                        }
+                        if (i & 1) umma_commit(&v_empty[tile % VS]);   // both halves of the V tile read
+                        if (i == i1 - 1) umma_commit(o_full);
+                    }
+                    return true;
+                });
+            }
             // every MMA this thread issued has completed before TMEM is freed
-            umma_commit(drain);
-            mbar_wait(drain, 0, p.limit_ns);
+            umma_commit(&drain[role]);
+            mbar_wait(&drain[role], 0, p.limit_ns);
         }
     } else {
         // ================= softmax / epilogue =================
-        // kSW warps: warp w reaches TMEM lanes 32*(w%4) .. +31 (its rows) and
-        // takes column part (w-2)/4 of every tile (kCP parts of 128/kCP keys)
-        // two groups of 8 warps take alternate tiles (group g: tiles j with j%2 == g),
-        // so one group computes while the other waits on TMEM; in a group, warp w
-        // has TMEM lanes 32*(w%4).. (its rows) and one half of the tile's keys
-        const int sw = warp - 2, grp = sw >> 3, half = (sw >> 2) & 1;
+        // group grp (0: tile A, 1: tile B) of kGW warps; warp w reaches TMEM
+        // lanes 32*(w%4) .. +31, one query row per thread, 64 keys a sub-tile
+        const int grp = (warp - 2) / kGW;
         const int q4 = warp & 3;
-        const int part = grp * 2 + half;          // statistics part of this warp
         const int row = q4 * 32 + lane;           // query row of the tile = token*r + head
         const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-        const int tok_in = row / p.r;
+        const uint32_t tS = trow + grp * 128, tO = trow + kTmO + grp * D;
+        const int tok_in = row / p.r, hd = row - tok_in * p.r;
         const bool row_ok = tok_in < p.tb;
-        constexpr int kCols = 64;                 // keys of a tile per warp
-        constexpr int kLd = kCols / 32;           // tcgen05.ld x32 per tile
-        const float cs = p.scale * kLog2e;        // exp(s*scale - M) = 2^(acc*cs - M*log2e)
-        int j = 0;
+        const float cs = p.scale * kLog2e;        // s * log2 e = acc * cs
+        const uint64_t cs2 = pk2(cs, cs);
+        int i = 0;
         for_segments(p, c, [&](int k, const Seg &sg) {
-            const int b = sg.pair % p.nblk;
-            const int tok = b * p.tb + tok_in;
+            const int b = sg.pair % p.nblk, kvh = sg.pair / p.nblk;
+            const int tok = (2 * b + grp) * p.tb + tok_in;
             const bool valid = row_ok && tok < p.n_new;
             const int64_t lim = valid ? p.n_past + tok : -1;   // last visible key
-            float nM = 0.0f, inv = 0.0f;         // -M*log2e and 1/Z of the row (pass 2)
-            if constexpr (OUT) {
-                if (valid) {
-                    const float2 st = p.rstat[(int64_t)sg.pair * 128 + row];
-                    nM = -st.x * kLog2e;
-                    inv = st.y;
-                }
-            }
-            float am = -INFINITY, z = 0.0f;      // pass 1: running max of raw S, sum of exp
-            for (int t = sg.t0; t < sg.t1; t++, j++) {
-                const int sb = j & 1, pb = j & 1;
-                if (sb != grp) continue;   // the other group's tile
-                if (!mbar_wait_ab(&s_full[sb], (j >> 1) & 1, p.limit_ns, flags)) {
+            const int i0 = i, i1 = i + 2 * (sg.t1 - sg.t0);
+            float m = -INFINITY, l = 0.0f;
+            for (; i < i1; i++) {
+                const int bf = i & 1;
+                if (!mbar_wait_ab(&s_full[grp * 2 + bf], (i >> 1) & 1, p.limit_ns, flags)) {
                     give_up(p, flags, 1u);
                     return false;
                 }
                 tc_fence_after();
-                uint32_t v[kLd][32];
-#pragma unroll
-                for (int u = 0; u < kLd; u++) tmem_ld32(trow + sb * 128 + half * kCols + u * 32, v[u]);
+                uint32_t v[64];
+                tmem_ld32(tS + bf * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
+                tmem_ld32(tS + bf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
                 tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_free[sb]);
-                const int64_t kc0 = (int64_t)t * 128 + half * kCols;
-                const int nvis = (int)max((int64_t)0, min((int64_t)kCols, lim - kc0 + 1));   // visible keys
-                if constexpr (!OUT) {
-                    float m8[8];   // eight independent max chains
+                const int64_t kb = (int64_t)(2 * sg.t0 + (i - i0)) * 64;   // first key of the sub-tile
+                const int nvis = (int)max((int64_t)0, min((int64_t)64, lim - kb + 1));
+                const bool full = __all_sync(0xffffffffu, nvis == 64);
+                float mx;
+                if (full) {
+                    float m4[4];
 #pragma unroll
-                    for (int i = 0; i < 8; i++) m8[i] = -INFINITY;
-                    if (nvis == kCols) {
+                    for (int a = 0; a < 4; a++) m4[a] = fmaxf(__uint_as_float(v[a]), __uint_as_float(v[4 + a]));
 #pragma unroll
-                        for (int u = 0; u < kLd; u++)
+                    for (int e = 8; e < 64; e += 8)
 #pragma unroll
-                            for (int e = 0; e < 32; e++) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(v[u][e]));
-                    } else {
-#pragma unroll
-                        for (int u = 0; u < kLd; u++)
-#pragma unroll
-                            for (int e = 0; e < 32; e++)
-                                if (u * 32 + e < nvis) m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(v[u][e]));
-                    }
-                    const float cm = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                           fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-                    const float nm = fmaxf(am, cm);
-                    if (nm != -INFINITY) {
-                        const float nb = -nm * cs;
-                        float a8[8] = {am == -INFINITY ? 0.0f : z * ex2_approx(fmaf(am, cs, nb)), 0.0f, 0.0f, 0.0f,
-                                       0.0f, 0.0f, 0.0f, 0.0f};
-                        if (nvis == kCols) {
-#pragma unroll
-                            for (int u = 0; u < kLd; u++)
-#pragma unroll
-                                for (int e = 0; e < 32; e++)
-                                    a8[e & 7] += ex2_approx(fmaf(__uint_as_float(v[u][e]), cs, nb));
-                        } else {
-#pragma unroll
-                            for (int u = 0; u < kLd; u++)
-#pragma unroll
-                                for (int e = 0; e < 32; e++) {
-                                    const float x = ex2_approx(fmaf(__uint_as_float(v[u][e]), cs, nb));
-                                    a8[e & 7] += u * 32 + e < nvis ? x : 0.0f;
-                                }
-                        }
-                        z = ((a8[0] + a8[1]) + (a8[2] + a8[3])) + ((a8[4] + a8[5]) + (a8[6] + a8[7]));
-                        am = nm;
-                    }
+                        for (int a = 0; a < 4; a++)
+                            m4[a] = max3(m4[a], __uint_as_float(v[e + a]), __uint_as_float(v[e + 4 + a]));
+                    mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
                 } else {
-                    if (j >= 2 && !mbar_wait_ab(&p_empty[pb], ((j - 2) >> 1) & 1, p.limit_ns, flags)) {
+#pragma unroll
+                    for (int e = 0; e < 64; e++)
+                        if (e >= nvis) v[e] = __float_as_uint(-INFINITY);
+                    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                    for (int e = 0; e < 64; e += 8)
+#pragma unroll
+                        for (int a = 0; a < 4; a++)
+                            m4[a] = max3(m4[a], __uint_as_float(v[e + a]), __uint_as_float(v[e + 4 + a]));
+                    mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+                }
+                const float xm = mx * cs;
+                float f = 1.0f;
+                bool resc = false;
+                if (xm > m + kLazy) {   // never for a sub-tile without visible keys (xm = -inf)
+                    f = ex2_approx(m - xm);   // 0 while m = -inf
+                    resc = m != -INFINITY;
+                    l *= f;
+                    m = xm;
+                }
+                // p = 2^(acc*cs - m): masked keys hold -inf (2^-inf = 0); rows
+                // without a visible key yet have m = -inf and every key masked
+                const float nm = m == -INFINITY ? 0.0f : -m;
+                const uint64_t nm2 = pk2(nm, nm);
+                uint64_t s2[2] = {0ull, 0ull};
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    uint32_t pkd[16];
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        const float2 xy = up2(fma2(pk2(__uint_as_float(v[u * 32 + 2 * e]),
+                                                       __uint_as_float(v[u * 32 + 2 * e + 1])), cs2, nm2));
+                        const float x0 = ex2_approx(xy.x), x1 = ex2_approx(xy.y);
+                        s2[e & 1] = add2(s2[e & 1], pk2(x0, x1));
+                        const __half2 h2 = __floats2half2_rn(x0, x1);
+                        pkd[e] = *reinterpret_cast<const uint32_t *>(&h2);
+                    }
+                    // keys 32u .. 32u+31 -> packed columns 16u .. 16u+15 of the buffer
+                    tmem_st16(tS + bf * 64 + u * 16, pkd);
+                }
+                const float2 sa = up2(add2(s2[0], s2[1]));
+                l += sa.x + sa.y;
+                // O holds this segment's earlier sub-tiles: once the last P . V
+                // into it has completed, scale the raised rows (before P(i) is
+                // reported, so before PV(i) adds to O)
+                if (i > i0 && __any_sync(0xffffffffu, resc)) {
+                    if (!mbar_wait_ab(&o_ready[grp * 2 + ((i - 1) & 1)], ((i - 1) >> 1) & 1, p.limit_ns, flags)) {
                         give_up(p, flags, 1u);
                         return false;
                     }
-#pragma unroll
-                    for (int u = 0; u < kLd; u++) {
-                        uint32_t pk[16];
-#pragma unroll
-                        for (int e = 0; e < 16; e++) {
-                            float x0 = __fmul_rn(ex2_approx(fmaf(__uint_as_float(v[u][2 * e]), cs, nM)), inv);
-                            float x1 = __fmul_rn(ex2_approx(fmaf(__uint_as_float(v[u][2 * e + 1]), cs, nM)), inv);
-                            if (nvis < kCols) {
-                                x0 = u * 32 + 2 * e < nvis ? x0 : 0.0f;
-                                x1 = u * 32 + 2 * e + 1 < nvis ? x1 : 0.0f;
-                            }
-                            const __half2 h2 = __floats2half2_rn(x0, x1);
-                            pk[e] = *reinterpret_cast<const uint32_t *>(&h2);
-                        }
-                        // keys part*kCols + u*32 .. +31 -> 16 packed columns of P[pb]
-                        tmem_st16(trow + kTmP + pb * 64 + (half * kCols + u * 32) / 2, pk);
-                    }
-                    tmem_wait_st();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&p_full[pb]);
-                }
-            }
-            if constexpr (!OUT) {
-                // this part's (max, sum) of the row: max in scaled units
-                float2 *ps = reinterpret_cast<float2 *>(p.pstat) + (((int64_t)c * p.kseg + k) * kCP + part) * 128 + row;
-                *ps = make_float2(am == -INFINITY ? -INFINITY : __fmul_rn(am, p.scale), z);
-            } else {
-                if (!mbar_wait_ab(o_full, k & 1, p.limit_ns, flags)) {
-                    give_up(p, flags, 1u);
-                    return false;
-                }
-                tc_fence_after();
-                constexpr int kOc = D / 4;     // output dims per warp of a lane quarter (16 or 32)
-                const int oq = sw >> 2;        // 0..3
-                float *po = p.pout + (((int64_t)c * p.kseg + k) * 128 + row) * D + oq * kOc;
+                    tc_fence_after();
+                    const float fo = resc ? f : 1.0f;
 #pragma unroll 1
-                for (int ch = 0; ch < kOc / 16; ch++) {
-                    uint32_t o[16];
-                    tmem_ld16(trow + kTmO + oq * kOc + ch * 16, o);
-                    tmem_wait_ld();
-                    if (valid)
+                    for (int ch = 0; ch < D / 16; ch++) {
+                        uint32_t o[16];
+                        tmem_ld16(tO + ch * 16, o);
+                        tmem_wait_ld();
 #pragma unroll
-                        for (int q = 0; q < 4; q++)
-                            *reinterpret_cast<uint4 *>(po + ch * 16 + 4 * q) =
-                                make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                        for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * fo);
+                        tmem_st16(tO + ch * 16, o);
+                    }
                 }
+                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(o_empty);
+                if (lane == 0) mbar_arrive(&p_full[grp * 2 + bf]);
             }
+            // ---- the segment's output ----
+            if (!mbar_wait_ab(o_full, k & 1, p.limit_ns, flags)) {
+                give_up(p, flags, 1u);
+                return false;
+            }
+            tc_fence_after();
+            const bool whole = sg.t0 == 0 && sg.t1 == nt_of(p, b);   // no other CTA holds this pair
+            float *dst;
+            float scl = 1.0f;
+            if (whole) {
+                dst = p.out + (int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * D;
+                scl = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;
+            } else {
+                const int64_t slot = (((int64_t)c * p.kseg + k) * 2 + grp) * 128 + row;
+                reinterpret_cast<float2 *>(p.pstat)[slot] = make_float2(m, l);
+                dst = p.pout + slot * D;
+            }
+#pragma unroll 1
+            for (int ch = 0; ch < D / 32; ch++) {
+                uint32_t o[32];
+                tmem_ld32(tO + ch * 32, o);
+                tmem_wait_ld();
+                if (valid)
+#pragma unroll
+                    for (int q = 0; q < 8; q++)
+                        *reinterpret_cast<float4 *>(dst + ch * 32 + 4 * q) =
+                            make_float4(__uint_as_float(o[4 * q]) * scl, __uint_as_float(o[4 * q + 1]) * scl,
+                                        __uint_as_float(o[4 * q + 2]) * scl, __uint_as_float(o[4 * q + 3]) * scl);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(o_empty);
             return true;
         });
     }
@@ -465,9 +517,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
         // the CTA gave up: loads nobody waited for may still be landing
         for (int j = issued_k > KS ? issued_k - KS : 0; j < issued_k; j++)
             mbar_wait(&k_full[j % KS], (j / KS) & 1, p.limit_ns);
-        if constexpr (OUT)
-            for (int j = issued_v > VS ? issued_v - VS : 0; j < issued_v; j++)
-                mbar_wait(&v_full[j % VS], (j / VS) & 1, p.limit_ns);
+        for (int j = issued_v > VS ? issued_v - VS : 0; j < issued_v; j++)
+            mbar_wait(&v_full[j % VS], (j / VS) & 1, p.limit_ns);
         if (issued_q > 0) mbar_wait(q_full, (issued_q - 1) & 1, p.limit_ns);
     }
     if (warp == 1) {
@@ -477,7 +528,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------------------
-// folds
+// the fold of split pairs
 // ---------------------------------------------------------------------------
 // CTAs [ca, cb] hold pair `pair`; its segment index in CTA cc
 __device__ __forceinline__ void pair_ctas(const PrefillParams &p, int pair, int &ca, int &cb)
@@ -499,89 +550,94 @@ __device__ __forceinline__ int seg_index(const PrefillParams &p, int cc, int pai
     return pair - pair_of(p, cta_lo(p, cc));
 }
 
-// (M, 1/Z) per (pair, row) from every segment part: one thread per row
-__global__ void prefill_stats_fold(const PrefillParams p)
-{
-    const int pair = blockIdx.x, row = threadIdx.x;
-    __shared__ int span[2];
-    if (row == 0) pair_ctas(p, pair, span[0], span[1]);
-    __syncthreads();
-    const float2 *ps = reinterpret_cast<const float2 *>(p.pstat);
-    float M = -INFINITY;
-    for (int cc = span[0]; cc <= span[1]; cc++) {
-        const int64_t base = ((int64_t)cc * p.kseg + seg_index(p, cc, pair)) * kCP;
-        for (int q = 0; q < kCP; q++) M = fmaxf(M, ps[(base + q) * 128 + row].x);
-    }
-    double Z = 0.0;
-    for (int cc = span[0]; cc <= span[1]; cc++) {
-        const int64_t base = ((int64_t)cc * p.kseg + seg_index(p, cc, pair)) * kCP;
-        for (int q = 0; q < kCP; q++) {
-            const float2 v = ps[(base + q) * 128 + row];
-            if (v.x != -INFINITY) Z += (double)v.y * (double)exp2f((v.x - M) * kLog2e);
-        }
-    }
-    p.rstat[(int64_t)pair * 128 + row] = make_float2(M, Z > 0.0 ? __fdiv_rn(1.0f, (float)Z) : 0.0f);
-}
+// out = sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i over the pair's segments
+// (CTAs in order), scattered to the caller's [token][head][D] rows.  One block
+// per (pair, 32 of its 256 rows), 8 threads a row, D/8 floats a thread.  The
+// block finds the pair's CTAs before its grid-dependency wait, so with a
+// programmatic launch that work overlaps the attention kernel's tail.
+constexpr int kFoldSpan = 160;   // CTAs of a pair kept in shared memory
 
-// out = the sum of the pair's partial outputs (CTAs in order), scattered to the
-// caller's [token][head][D] rows; one block per (pair, 8 rows), float4 per thread
+template <int D>
 __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
 {
-    const int pair = blockIdx.x >> 4, row0 = (blockIdx.x & 15) * 8;
+    constexpr int F4 = D / 32;   // float4s of a thread
+    const int pair = blockIdx.x >> 3, row0 = (blockIdx.x & 7) * 32;
     __shared__ int span[2];
-    __shared__ int segi[160];
+    __shared__ int segi[kFoldSpan];
     if (threadIdx.x == 0) pair_ctas(p, pair, span[0], span[1]);
     __syncthreads();
-    for (int cc = span[0] + (int)threadIdx.x; cc <= span[1]; cc += blockDim.x)
-        if (cc - span[0] < 160) segi[cc - span[0]] = seg_index(p, cc, pair);
+    const int ca = span[0], cb = span[1];
+    for (int cc = ca + (int)threadIdx.x; cc <= cb && cc - ca < kFoldSpan; cc += blockDim.x)
+        segi[cc - ca] = seg_index(p, cc, pair);
     __syncthreads();
-    const int per_row = p.D / 4;
+    pdl_wait();   // the attention kernel's partials
+    if (ca == cb) return;   // one segment: the attention kernel wrote the rows
+    const int rr = row0 + (int)(threadIdx.x >> 3), part = threadIdx.x & 7;
+    const int grp = rr >> 7, row = rr & 127;
+    const int tok_in = row / p.r, hd = row - tok_in * p.r;
     const int b = pair % p.nblk, kvh = pair / p.nblk;
-    for (int idx = threadIdx.x; idx < 8 * per_row; idx += blockDim.x) {
-        const int row = row0 + idx / per_row, d4 = idx % per_row;
-        const int tok_in = row / p.r, hd = row - tok_in * p.r;
-        const int tok = b * p.tb + tok_in;
-        if (tok_in >= p.tb || tok >= p.n_new) continue;
-        float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        for (int cc = span[0]; cc <= span[1]; cc++) {
-            const int sgi = cc - span[0] < 160 ? segi[cc - span[0]] : seg_index(p, cc, pair);
-            const float4 v = __ldg(reinterpret_cast<const float4 *>(
-                p.pout + (((int64_t)cc * p.kseg + sgi) * 128 + row) * p.D) + d4);
-            sum.x += v.x;
-            sum.y += v.y;
-            sum.z += v.z;
-            sum.w += v.w;
+    const int tok = (2 * b + grp) * p.tb + tok_in;
+    if (tok_in >= p.tb || tok >= p.n_new) return;
+    auto slot = [&](int cc) {
+        const int sgi = cc - ca < kFoldSpan ? segi[cc - ca] : seg_index(p, cc, pair);
+        return (((int64_t)cc * p.kseg + sgi) * 2 + grp) * 128 + row;
+    };
+    const float2 *ps = reinterpret_cast<const float2 *>(p.pstat);
+    float M = -INFINITY;
+    for (int cc = ca; cc <= cb; cc++) M = fmaxf(M, __ldcg(ps + slot(cc)).x);
+    float lsum = 0.0f;
+    float4 acc[F4];
+#pragma unroll
+    for (int q = 0; q < F4; q++) acc[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int cc = ca; cc <= cb; cc++) {
+        const int64_t sl = slot(cc);
+        const float2 st = __ldcg(ps + sl);
+        if (st.x == -INFINITY) continue;   // no visible key in this segment
+        const float w = exp2f(st.x - M);
+        lsum += st.y * w;
+        const float4 *src = reinterpret_cast<const float4 *>(p.pout + sl * D) + part * F4;
+#pragma unroll
+        for (int q = 0; q < F4; q++) {
+            const float4 v = __ldcg(src + q);
+            acc[q].x += v.x * w;
+            acc[q].y += v.y * w;
+            acc[q].z += v.z * w;
+            acc[q].w += v.w * w;
         }
-        *reinterpret_cast<float4 *>(p.out + (int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * p.D +
-                                    4 * d4) = sum;
     }
+    const float inv = lsum > 0.0f ? __fdiv_rn(1.0f, lsum) : 0.0f;
+    float4 *dst = reinterpret_cast<float4 *>(p.out + (int64_t)tok * p.out_stride +
+                                             (int64_t)(p.out_head0 + kvh * p.r + hd) * D) + part * F4;
+#pragma unroll
+    for (int q = 0; q < F4; q++)
+        dst[q] = make_float4(acc[q].x * inv, acc[q].y * inv, acc[q].z * inv, acc[q].w * inv);
 }
 
 template <int D>
 cudaError_t prep_pf()
 {
-    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)PL<D, false>::bytes);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(prefill_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)PL<D, true>::bytes);
+    return cudaFuncSetAttribute(prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PL<D>::bytes);
 }
 
 template <int D>
 cudaError_t launch_pf(int which, const CUtensorMap &qmap, const CUtensorMap &kmap, const CUtensorMap &vmap,
                       const PrefillParams &p, cudaStream_t st)
 {
-    switch (which) {
-    case 0:
-        prefill_kernel<D, false><<<p.n_cta, kPThreads, PL<D, false>::bytes, st>>>(qmap, kmap, vmap, p);
-        break;
-    case 1: prefill_stats_fold<<<p.hkv * p.nblk, 128, 0, st>>>(p); break;
-    case 2:
-        prefill_kernel<D, true><<<p.n_cta, kPThreads, PL<D, true>::bytes, st>>>(qmap, kmap, vmap, p);
-        break;
-    default: prefill_out_fold<<<p.hkv * p.nblk * 16, 256, 0, st>>>(p); break;
+    if (which == 0) {
+        prefill_kernel<D><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p);
+        return cudaGetLastError();
     }
-    return cudaGetLastError();
+    // the fold may be scheduled once every attention CTA has started
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(p.hkv * p.nblk * 8));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, prefill_out_fold<D>, p);
 }
 
 }  // namespace

@@ -203,6 +203,35 @@ def test_mid_size_matches_oracle(name, n_past, n_new, cuda):
     assert_close(out, orc.attend(kc, vc, n_past, qr))
 
 
+@pytest.mark.parametrize("name,n_past,n_new", [
+    ("qwen3-8b-prefill", 64, 8),       # one key tile per pair: every pair written by its own CTA
+    ("qwen3-8b-prefill", 300, 200),    # pairs split over CTAs (fold), a last block with an empty tile B
+    ("llama3.2-3b", 1000, 40),         # r = 3: 42 tokens per tile, 2 rows of each tile unused
+    ("qwen2-0.5b", 150, 5),            # head_dim 64, r = 7
+    ("qwen3-8b-prefill", 16384, 512),  # the benchmark chunk
+])
+def test_prefill_chunk_matches_oracle(name, n_past, n_new, cuda):
+    """The tensor-core chunk path (one-pass online softmax) against the oracle's
+    two-pass ggml softmax, within the attention tolerance."""
+    sp = specs.get(name)
+    sp["n_layer"] = 1
+    n_ctx = n_past + n_new + 64
+    case = dict(name=name, spec=name, n_ctx=n_ctx, n_past=n_past, n_new=n_new)
+    run = Run(case, cuda, n_batch_max=max(64, n_new))
+    run.sp = sp
+    kc, vc = _oracle_layer(sp, n_ctx, n_past)
+    rows = synth.qkv_rows(sp, 3, 0, n_new)
+    run.ctx.profile(True)
+    out = run.step(rows, n_past)
+    assert run.ctx.profile_read("prefill")[0] == 1   # the tensor-core path ran
+    q, k, v = _split(sp, rows)
+    qn, kn = synth.norm_weights(sp, 0) if sp["qk_norm"] else (None, None)
+    orc = O.Oracle(sp)
+    qr = orc.append(kc, vc, n_past, q, k, v, qn, kn)
+    assert np.array_equal(run.rows(0, n_past, n_new), kc[n_past:n_past + n_new])
+    assert_close(out, orc.attend(kc, vc, n_past, qr))
+
+
 @pytest.mark.parametrize("name", ["llama3.2-3b", "llama3.1-8b-128k"])
 def test_full_context_decode_matches_oracle(name, cuda):
     """One layer at the benchmark's full context (32001 / 131001 keys)."""
