@@ -8,20 +8,22 @@
 //
 // Bit-exactness: every product and sum is a separately rounded IEEE float op
 // (__fmul_rn / __fadd_rn / __fsub_rn: nothing is contracted into an FMA); the
-// RMSNorm sum of squares is sequential in double; sqrt and the reciprocal are
-// correctly rounded; the (cos, sin) table is built on the host with the same
-// libm calls as the CPU path.  So the cache bytes equal the CPU path's.
+// RMSNorm mean equals that of the sequential double sum of the float squares
+// (exact_mean, with the sequential sum itself as the fallback); sqrt and the
+// reciprocal are correctly rounded; the (cos, sin) table is built on the host
+// with the same libm calls as the CPU path.  So the cache bytes equal the CPU
+// path's.
 //
 // Work decomposition: a "row" is one (token, head) vector of D floats of Q, K
 // or V.  D/8 threads own a row, each thread 8 consecutive elements, so a
 // thread stores its 8 halves with one 16-byte st.global and a row group writes
-// a contiguous D*2-byte cache segment.  8 rows per block.
+// a contiguous D*2-byte cache segment.  32 rows per block.
 #include "kv_internal.h"
 
 namespace kvb {
 namespace {
 
-constexpr int kRowsPerBlock = 8;
+constexpr int kRowsPerBlock = 32;
 
 __device__ __forceinline__ void load8(const float *src, bool vec, float x[8])
 {
@@ -44,27 +46,94 @@ __device__ __forceinline__ void store8_f16(__half *dst, const float x[8])
     *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(h);
 }
 
+// row -> (token, kind 0 Q / 1 K / 2 V, head); false past the last row
+__device__ __forceinline__ bool row_of(const AppendParams &p, int64_t row, int &t, int &kind, int &h)
+{
+    const int rows_per_tok = p.hq_loc + 2 * p.hkv_loc;
+    t = 0;
+    kind = 2;
+    h = 0;
+    if (row >= (int64_t)p.n_new * rows_per_tok) return false;
+    t = (int)(row / rows_per_tok);
+    const int slot = (int)(row % rows_per_tok);
+    if (slot < p.hq_loc) { kind = 0; h = slot; }
+    else if (slot < p.hq_loc + p.hkv_loc) { kind = 1; h = slot - p.hq_loc; }
+    else { kind = 2; h = slot - p.hq_loc - p.hkv_loc; }
+    return true;
+}
+
+// The mean of a row's squares exactly as ggml computes it, from the G threads'
+// 8 squares each (G a power of two: the row's threads are one aligned group of
+// lanes).  Each square m * 2^(e-150) (m the 24-bit significand) is aligned to
+// the row's largest exponent E as m * 2^(e - E + 31) in a 64-bit integer
+// (terms more than 31 binades below E are truncated: < 128 * 2^(E-181) in
+// all, under 2^-47 of the sum); the sum fits in 62 bits.  Returns false when
+// the rounding test cannot decide (the caller then sums sequentially).
+template <int G, int D>
+__device__ __forceinline__ bool exact_mean(const float (&sq)[8], float &mean)
+{
+    unsigned emax = 1u;
+    bool special = false;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const unsigned eb = (__float_as_uint(sq[e]) >> 23) & 0xFFu;
+        special |= eb == 0xFFu;
+        emax = max(emax, eb);
+    }
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
+    unsigned long long acc = 0ull;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const unsigned u = __float_as_uint(sq[e]);
+        const unsigned eb = (u >> 23) & 0xFFu;
+        const unsigned long long m = (u & 0x7FFFFFu) | (eb ? 0x800000u : 0u);
+        const int sh = (int)max(eb, 1u) - (int)emax + 31;
+        acc += sh >= 0 ? m << sh : (sh > -64 ? m >> (-sh) : 0ull);
+    }
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    special = __any_sync(0xffffffffu, special);   // (a warp holds whole rows: any row's inf/nan sends the warp's rows to the chain)
+    if (special) return false;
+    if (acc == 0ull) {   // every square is zero: so is the sequential sum
+        mean = 0.0f;
+        return true;
+    }
+    const double T = ldexp((double)acc, (int)emax - 181);
+    if (T < 0x1p-100) return false;   // keep (float)(T / D) far from the subnormal range
+    const float f = __double2float_rn(T);
+    const double up = 0.5 * ((double)f + (double)nextafterf(f, INFINITY));
+    const double dn = 0.5 * ((double)f + (double)nextafterf(f, 0.0f));
+    const double tol = T * 0x1p-44;
+    if (fabs(T - up) <= tol || fabs(T - dn) <= tol) return false;
+    mean = f * (1.0f / (float)D);   // D is a power of two: exact
+    return true;
+}
+
+template <int D>
+struct AppendSmem {
+    static constexpr int LDD = D + 1;   // doubles a row (odd: rows fall on different banks)
+    static constexpr int LDX = D + 4;   // floats a row (16-byte aligned rows)
+    static constexpr size_t sq = (size_t)kRowsPerBlock * LDD * 8;
+    static constexpr size_t xs = (size_t)kRowsPerBlock * LDX * 4;
+    static constexpr size_t bytes = sq > xs ? sq : xs;   // the squares, then the normed rows
+};
+
 template <int D, bool VEC>
 __global__ void __launch_bounds__(kRowsPerBlock *(D / 8)) append_kernel(const AppendParams p)
 {
     constexpr int G = D / 8;  // threads per row
-    __shared__ float xs[kRowsPerBlock][D];
+    using S = AppendSmem<D>;
+    __shared__ __align__(16) unsigned char sm[S::bytes];
     __shared__ float rscale[kRowsPerBlock];
+    double *sq = reinterpret_cast<double *>(sm);
+    float *xs = reinterpret_cast<float *>(sm);
 
     const int rloc = threadIdx.x / G;
     const int tig = threadIdx.x % G;
-    const int rows_per_tok = p.hq_loc + 2 * p.hkv_loc;
-    const int64_t row = (int64_t)blockIdx.x * kRowsPerBlock + rloc;
-    const bool active = row < (int64_t)p.n_new * rows_per_tok;
-
-    int t = 0, kind = 2, h = 0;
-    if (active) {
-        t = (int)(row / rows_per_tok);
-        const int slot = (int)(row % rows_per_tok);
-        if (slot < p.hq_loc) { kind = 0; h = slot; }
-        else if (slot < p.hq_loc + p.hkv_loc) { kind = 1; h = slot - p.hq_loc; }
-        else { kind = 2; h = slot - p.hq_loc - p.hkv_loc; }
-    }
+    const int64_t row0 = (int64_t)blockIdx.x * kRowsPerBlock;
+    int t, kind, h;
+    const bool active = row_of(p, row0 + rloc, t, kind, h);
     const bool rotates = active && kind < 2;
 
     float x[8];
@@ -79,19 +148,40 @@ __global__ void __launch_bounds__(kRowsPerBlock *(D / 8)) append_kernel(const Ap
     }
 
     // ---- QK-Norm: y = (x * (1/sqrt(mean(x*x) + eps))) * gamma --------------
+    // ggml's mean: the float squares summed in double in element order, then
+    // (float)(sum / D).  Fast path: the exact sum T from 64-bit integers (see
+    // exact_mean); the sequential double sum s is within 2^-46 T of T,
+    // so (float)s == (float)T whenever no float rounding midpoint lies within
+    // 2^-44 T of T -- then the mean is (float)T / D.  Rows that fail the test
+    // (about one in a million) or hold inf/nan or tiny sums run the sequential
+    // double sum itself (warp 0, a row per lane).
     if (p.qk_norm) {
+        float sqv[8];
 #pragma unroll
-        for (int e = 0; e < 8; e++) xs[rloc][tig * 8 + e] = __fmul_rn(x[e], x[e]);
-        __syncthreads();
-        if (rotates && tig == 0) {
-            double sum = 0.0;
-            for (int i = 0; i < D; i++) sum = __dadd_rn(sum, (double)xs[rloc][i]);
-            const float mean = __double2float_rn(__ddiv_rn(sum, (double)D));
-            rscale[rloc] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+        for (int e = 0; e < 8; e++) sqv[e] = __fmul_rn(x[e], x[e]);
+        float fast_mean = 0.0f;
+        const bool need_chain = (G & (G - 1)) != 0 || !exact_mean<G, D>(sqv, fast_mean);
+        if (__syncthreads_or(rotates && need_chain)) {
+            if (need_chain) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) sq[rloc * S::LDD + tig * 8 + e] = (double)sqv[e];
+            }
+            __syncthreads();
+            if (threadIdx.x < kRowsPerBlock) {
+                int tr, kr, hr;
+                if (row_of(p, row0 + threadIdx.x, tr, kr, hr) && kr < 2) {
+                    const double *r = sq + threadIdx.x * S::LDD;
+                    double sum = 0.0;
+#pragma unroll 16
+                    for (int i = 0; i < D; i++) sum = __dadd_rn(sum, r[i]);
+                    rscale[threadIdx.x] = __double2float_rn(__ddiv_rn(sum, (double)D));
+                }
+            }
+            __syncthreads();
+            if (need_chain) fast_mean = rscale[rloc];
         }
-        __syncthreads();
         if (rotates) {
-            const float sc = rscale[rloc];
+            const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(fast_mean, p.eps)));
             const float *w = (kind == 0 ? p.q_norm_w : p.k_norm_w) + tig * 8;
 #pragma unroll
             for (int e = 0; e < 8; e++) x[e] = __fmul_rn(__fmul_rn(x[e], sc), __ldg(w + e));
@@ -100,31 +190,59 @@ __global__ void __launch_bounds__(kRowsPerBlock *(D / 8)) append_kernel(const Ap
 
     // ---- RoPE on the first n_rot dims (NEOX halves / NORMAL pairs) --------
     if (p.n_rot > 0) {
-        __syncthreads();
+        const int half = p.n_rot >> 1;
+        const int i0 = tig * 8;
+        if (p.rope_mode == 2) {
+            // NEOX: element i pairs with i +- half, held by another thread (the
+            // squares' last reader, warp 0, has passed the norm's barrier)
+            float *xr = xs + rloc * S::LDX;
+            *reinterpret_cast<float4 *>(xr + i0) = make_float4(x[0], x[1], x[2], x[3]);
+            *reinterpret_cast<float4 *>(xr + i0 + 4) = make_float4(x[4], x[5], x[6], x[7]);
+            __syncthreads();
+            if (rotates && i0 < p.n_rot) {
+                const float2 *cs = p.rope + (p.n_past + t) * (int64_t)half;
+                if ((half & 7) == 0 && i0 + 8 <= p.n_rot) {
+                    // the thread's 8 elements sit in one half: vector loads
+                    const bool lo = i0 < half;
+                    const int j0 = lo ? i0 : i0 - half;          // table index of element 0
+                    const int pj = lo ? i0 + half : i0 - half;   // partner of element 0
+                    float y[8];
+                    *reinterpret_cast<float4 *>(y) = *reinterpret_cast<const float4 *>(xr + pj);
+                    *reinterpret_cast<float4 *>(y + 4) = *reinterpret_cast<const float4 *>(xr + pj + 4);
+                    float2 c[8];
 #pragma unroll
-        for (int e = 0; e < 8; e++) xs[rloc][tig * 8 + e] = x[e];
-        __syncthreads();
-        if (rotates) {
-            const int half = p.n_rot >> 1;
-            const float2 *cs = p.rope + (p.n_past + t) * (int64_t)half;
-            const float *xr = xs[rloc];
+                    for (int q = 0; q < 4; q++)
+                        *reinterpret_cast<float4 *>(c + 2 * q) = __ldg(reinterpret_cast<const float4 *>(cs + j0) + q);
 #pragma unroll
-            for (int e = 0; e < 8; e++) {
-                const int i = tig * 8 + e;
-                if (i >= p.n_rot) continue;
-                if (p.rope_mode == 2) {
-                    if (i < half) {
-                        const float2 c = __ldg(cs + i);
-                        x[e] = __fsub_rn(__fmul_rn(xr[i], c.x), __fmul_rn(xr[i + half], c.y));
-                    } else {
-                        const float2 c = __ldg(cs + (i - half));
-                        x[e] = __fadd_rn(__fmul_rn(xr[i - half], c.y), __fmul_rn(xr[i], c.x));
-                    }
+                    for (int e = 0; e < 8; e++)
+                        x[e] = lo ? __fsub_rn(__fmul_rn(x[e], c[e].x), __fmul_rn(y[e], c[e].y))
+                                  : __fadd_rn(__fmul_rn(y[e], c[e].y), __fmul_rn(x[e], c[e].x));
                 } else {
-                    const float2 c = __ldg(cs + (i >> 1));
-                    if ((i & 1) == 0) x[e] = __fsub_rn(__fmul_rn(xr[i], c.x), __fmul_rn(xr[i + 1], c.y));
-                    else x[e] = __fadd_rn(__fmul_rn(xr[i - 1], c.y), __fmul_rn(xr[i], c.x));
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        const int i = i0 + e;
+                        if (i >= p.n_rot) continue;
+                        if (i < half) {
+                            const float2 c = __ldg(cs + i);
+                            x[e] = __fsub_rn(__fmul_rn(xr[i], c.x), __fmul_rn(xr[i + half], c.y));
+                        } else {
+                            const float2 c = __ldg(cs + (i - half));
+                            x[e] = __fadd_rn(__fmul_rn(xr[i - half], c.y), __fmul_rn(xr[i], c.x));
+                        }
+                    }
                 }
+            }
+        } else if (rotates) {
+            // NORMAL: pairs (2k, 2k+1) inside the thread's 8 elements
+            const float2 *cs = p.rope + (p.n_past + t) * (int64_t)half;
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+                const int i = i0 + e;
+                if (i >= p.n_rot) continue;
+                const float2 c = __ldg(cs + (i >> 1));
+                const float a = x[e], b = x[e + 1];
+                x[e] = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
+                x[e + 1] = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
             }
         }
     }

@@ -25,23 +25,25 @@
 // key.  The pairs' tiles, laid end to end, are cut into C equal ranges (one CTA
 // each, C <= SMs); a range holds one or more "segments" (the part of one pair
 // it covers).  A pair that one segment covers is written to the output by the
-// kernel; otherwise each segment leaves its (m, l, O) and prefill_out_fold
-// merges them (weights 2^(m_i - max m), CTAs in order).
+// kernel; otherwise each segment leaves its (m, l, O) rows in scratch and
+// prefill_out_fold merges them (weights 2^(m_i - max m), CTAs in order).
 //
-// prefill_kernel<D> (320 threads):
+// prefill_kernel<D> (384 threads):
 //   warp 0     TMA: the pair's two Q tiles, then K and V tiles into mbarrier rings
-//   warp 1     TMEM owner and MMA issuer (one thread), in sub-tiles of 64 keys
-//              (half a K/V tile).  TMEM columns: two S buffers per query tile
-//              (64 F32 columns each; P, F16 pairs, overwrites the first 32
-//              columns of its S), then O_A, O_B (D each).  Issue order:
-//                S_A(i) S_B(i) S_A(i+1) S_B(i+1) PV_A(i) S_A(i+2) PV_B(i) S_B(i+2) ..
-//              so the tensor cores compute S(i+1) while sub-tile i is in the
-//              softmax.  The MMAs of one thread run in issue order: S_X(i+2)
-//              cannot overwrite P_X(i) before PV_X(i) has read it
+//   warps 1,10,11  MMA issuers (one thread each; warp 1 also owns TMEM), in
+//              sub-tiles of 64 keys (half a K/V tile).  TMEM columns: two S
+//              buffers per query tile (64 F32 columns each; P, F16 pairs,
+//              overwrites the first 32 columns of its S), then O_A, O_B (D
+//              each).  Warp 1 issues S_A, warp 10 S_B -- sub-tile i+2 into the
+//              buffer of i once PV(i) has read its P (barrier o_ready), so the
+//              tensor cores compute S two sub-tiles ahead of the softmax --
+//              and warp 11 issues PV_A(i), PV_B(i) as the softmax reports P.
+//              One thread's tcgen05.mma issue rate, not the tensor cores, bounds
+//              these narrow MMAs, hence three issuers
 //   warps 2-5  softmax of tile A, warps 6-9 of tile B: one query row per thread,
 //              a sub-tile's 64 keys read with tcgen05.ld; P written back with
 //              tcgen05.st; the rare O rescale (after the previous P . V, which
-//              the barrier o_ready reports); at a segment's end O out
+//              o_ready reports); at a segment's end O out
 // prefill_out_fold   merges the segments of pairs split over CTAs
 // Every wait is bounded (limit_ns) and gives up when the CTA's abort flag is
 // set; the CTA drains its TMA loads and MMAs and frees TMEM before leaving.
@@ -147,6 +149,21 @@ __device__ __forceinline__ void give_up(const PrefillParams &p, volatile int *fl
         atomicOr(p.err, bit);
         flags[0] = 1;
     }
+}
+
+// CTAs [ca, cb] hold pair `pair`
+__device__ __forceinline__ void pair_ctas(const PrefillParams &p, int pair, int &ca, int &cb)
+{
+    const int64_t W = (int64_t)p.hkv * p.s_all;
+    const int64_t x0 = pair_start(p, pair), x1 = x0 + nt_of(p, pair % p.nblk) - 1;
+    auto cta_of = [&](int64_t x) {
+        int cc = (int)min((int64_t)p.n_cta - 1, x * p.n_cta / W);
+        while (cc + 1 < p.n_cta && cta_lo(p, cc + 1) <= x) cc++;
+        while (cc > 0 && cta_lo(p, cc) > x) cc--;
+        return cc;
+    };
+    ca = cta_of(x0);
+    cb = cta_of(x1);
 }
 
 // ---------------------------------------------------------------------------
@@ -483,10 +500,9 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
             }
             tc_fence_after();
             const bool whole = sg.t0 == 0 && sg.t1 == nt_of(p, b);   // no other CTA holds this pair
-            float *dst;
+            float *dst = p.out + (int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * D;
             float scl = 1.0f;
             if (whole) {
-                dst = p.out + (int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * D;
                 scl = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;
             } else {
                 const int64_t slot = (((int64_t)c * p.kseg + k) * 2 + grp) * 128 + row;
@@ -530,46 +546,28 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
 // ---------------------------------------------------------------------------
 // the fold of split pairs
 // ---------------------------------------------------------------------------
-// CTAs [ca, cb] hold pair `pair`; its segment index in CTA cc
-__device__ __forceinline__ void pair_ctas(const PrefillParams &p, int pair, int &ca, int &cb)
-{
-    const int64_t W = (int64_t)p.hkv * p.s_all;
-    const int64_t x0 = pair_start(p, pair), x1 = x0 + nt_of(p, pair % p.nblk) - 1;
-    auto cta_of = [&](int64_t x) {
-        int cc = (int)min((int64_t)p.n_cta - 1, x * p.n_cta / W);
-        while (cc + 1 < p.n_cta && cta_lo(p, cc + 1) <= x) cc++;
-        while (cc > 0 && cta_lo(p, cc) > x) cc--;
-        return cc;
-    };
-    ca = cta_of(x0);
-    cb = cta_of(x1);
-}
-
-__device__ __forceinline__ int seg_index(const PrefillParams &p, int cc, int pair)
-{
-    return pair - pair_of(p, cta_lo(p, cc));
-}
-
 // out = sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i over the pair's segments
-// (CTAs in order), scattered to the caller's [token][head][D] rows.  One block
-// per (pair, 32 of its 256 rows), 8 threads a row, D/8 floats a thread.  The
-// block finds the pair's CTAs before its grid-dependency wait, so with a
-// programmatic launch that work overlaps the attention kernel's tail.
-constexpr int kFoldSpan = 160;   // CTAs of a pair kept in shared memory
-
+// (CTAs ca..cb in order; the pair is segment 0 of every CTA after ca),
+// scattered to the caller's [token][head][D] rows.  One block per (pair, 32 of
+// its 256 rows), 8 threads a row, D/8 floats a thread; loads go out four
+// segments at a time.  The block finds the pair's CTAs before its
+// grid-dependency wait, so with a programmatic launch that overlaps the
+// attention kernel's tail.
 template <int D>
 __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
 {
     constexpr int F4 = D / 32;   // float4s of a thread
     const int pair = blockIdx.x >> 3, row0 = (blockIdx.x & 7) * 32;
-    __shared__ int span[2];
-    __shared__ int segi[kFoldSpan];
-    if (threadIdx.x == 0) pair_ctas(p, pair, span[0], span[1]);
+    __shared__ int info[3];
+    if (threadIdx.x == 0) {
+        int ca, cb;
+        pair_ctas(p, pair, ca, cb);
+        info[0] = ca;
+        info[1] = cb;
+        info[2] = pair - pair_of(p, cta_lo(p, ca));
+    }
     __syncthreads();
-    const int ca = span[0], cb = span[1];
-    for (int cc = ca + (int)threadIdx.x; cc <= cb && cc - ca < kFoldSpan; cc += blockDim.x)
-        segi[cc - ca] = seg_index(p, cc, pair);
-    __syncthreads();
+    const int ca = info[0], cb = info[1], seg_a = info[2];
     pdl_wait();   // the attention kernel's partials
     if (ca == cb) return;   // one segment: the attention kernel wrote the rows
     const int rr = row0 + (int)(threadIdx.x >> 3), part = threadIdx.x & 7;
@@ -578,31 +576,42 @@ __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
     const int b = pair % p.nblk, kvh = pair / p.nblk;
     const int tok = (2 * b + grp) * p.tb + tok_in;
     if (tok_in >= p.tb || tok >= p.n_new) return;
-    auto slot = [&](int cc) {
-        const int sgi = cc - ca < kFoldSpan ? segi[cc - ca] : seg_index(p, cc, pair);
-        return (((int64_t)cc * p.kseg + sgi) * 2 + grp) * 128 + row;
-    };
+    auto slot = [&](int cc) { return (((int64_t)cc * p.kseg + (cc == ca ? seg_a : 0)) * 2 + grp) * 128 + row; };
     const float2 *ps = reinterpret_cast<const float2 *>(p.pstat);
     float M = -INFINITY;
-    for (int cc = ca; cc <= cb; cc++) M = fmaxf(M, __ldcg(ps + slot(cc)).x);
+    for (int c0 = ca; c0 <= cb; c0 += 4) {
+        float m4[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) m4[u] = c0 + u <= cb ? __ldcg(ps + slot(c0 + u)).x : -INFINITY;
+        M = fmaxf(M, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+    }
     float lsum = 0.0f;
     float4 acc[F4];
 #pragma unroll
     for (int q = 0; q < F4; q++) acc[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int cc = ca; cc <= cb; cc++) {
-        const int64_t sl = slot(cc);
-        const float2 st = __ldcg(ps + sl);
-        if (st.x == -INFINITY) continue;   // no visible key in this segment
-        const float w = exp2f(st.x - M);
-        lsum += st.y * w;
-        const float4 *src = reinterpret_cast<const float4 *>(p.pout + sl * D) + part * F4;
+    for (int c0 = ca; c0 <= cb; c0 += 4) {
+        float2 st[4];
+        float4 v[4][F4];
 #pragma unroll
-        for (int q = 0; q < F4; q++) {
-            const float4 v = __ldcg(src + q);
-            acc[q].x += v.x * w;
-            acc[q].y += v.y * w;
-            acc[q].z += v.z * w;
-            acc[q].w += v.w * w;
+        for (int u = 0; u < 4; u++) {
+            const bool in = c0 + u <= cb;
+            const int64_t sl = slot(in ? c0 + u : c0);
+            st[u] = in ? __ldcg(ps + sl) : make_float2(-INFINITY, 0.0f);
+            const float4 *src = reinterpret_cast<const float4 *>(p.pout + sl * D) + part * F4;
+#pragma unroll
+            for (int q = 0; q < F4; q++) v[u][q] = __ldcg(src + q);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const float w = st[u].x == -INFINITY ? 0.0f : exp2f(st[u].x - M);   // no visible key: weight 0
+            lsum += st[u].y * w;
+#pragma unroll
+            for (int q = 0; q < F4; q++) {
+                acc[q].x += v[u][q].x * w;
+                acc[q].y += v[u][q].y * w;
+                acc[q].z += v[u][q].z * w;
+                acc[q].w += v[u][q].w * w;
+            }
         }
     }
     const float inv = lsum > 0.0f ? __fdiv_rn(1.0f, lsum) : 0.0f;

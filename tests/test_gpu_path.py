@@ -232,6 +232,35 @@ def test_prefill_chunk_matches_oracle(name, n_past, n_new, cuda):
     assert_close(out, orc.attend(kc, vc, n_past, qr))
 
 
+def test_qk_norm_fallback_rows_match_oracle_bits(cuda):
+    """QK-Norm rows whose sum of squares is tiny, or whose squares span many
+    binades, leave the exact-integer fast path for the sequential double sum;
+    the cache bytes still equal the oracle's."""
+    sp = specs.get("qwen3-8b-prefill")
+    sp["n_layer"] = 1
+    n_past, n_new = 100, 40
+    case = dict(name="qkn", spec="qwen3-8b-prefill", n_ctx=256, n_past=n_past, n_new=n_new)
+    run = Run(case, cuda, n_batch_max=64)
+    run.sp = sp
+    hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+    rows = synth.qkv_rows(sp, 11, 0, n_new).astype(np.float32)
+    k0 = hq * d
+    rows[0:8, k0:k0 + hkv * d] *= np.float32(1e-17)            # tiny sums: below the fast path's range
+    rows[8:16, :hq * d] *= np.float32(1e-19)
+    rows[16:24, k0:k0 + d] = np.float32(1e-30)                   # squares 2^-200 apart from ...
+    rows[16:24, k0] = np.float32(3.0)                            # ... one large element
+    rows[24:32, k0 + 3 * d:k0 + 4 * d:2] = 0.0                   # half the elements zero
+    kc, vc = _oracle_layer(sp, case["n_ctx"], n_past)
+    out = run.step(rows, n_past)
+    q, k, v = _split(sp, rows)
+    qn, kn = synth.norm_weights(sp, 0)
+    orc = O.Oracle(sp)
+    qr = orc.append(kc, vc, n_past, q, k, v, qn, kn)
+    assert np.array_equal(run.rows(0, n_past, n_new), kc[n_past:n_past + n_new])
+    assert np.array_equal(run.rows(1, n_past, n_new), vc[n_past:n_past + n_new])
+    assert np.all(np.isfinite(out))
+
+
 @pytest.mark.parametrize("name", ["llama3.2-3b", "llama3.1-8b-128k"])
 def test_full_context_decode_matches_oracle(name, cuda):
     """One layer at the benchmark's full context (32001 / 131001 keys)."""
