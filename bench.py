@@ -256,7 +256,7 @@ def run_reference(args, sp):
     gbs = nbytes / t_total / 1e9
     if sp["n_new"] > 1:   # prefill: the tensor-bound metric
         tf = fl / t_total / 1e12
-        print(json.dumps({
+        emit({
             "impl": "reference", "metric": METRIC_PREFILL, "value": round(tf, 5), "unit": "TFLOP/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t_total / nls * sp["n_layer"] * 1e3, 3),
@@ -267,8 +267,7 @@ def run_reference(args, sp):
             "cpu_baseline": {"value": round(tf, 5), "unit": "TFLOP/s", "cores": cp.threads, "kind": "port",
                              "sample": "each step: " + cp.describe(1)},
             "e2e": {"value": round(tf, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "CPU restatement of model.cpp:1382-1445 (ggml not vendored, reference backend unbuildable)"}),
-            flush=True)
+            "note": "CPU restatement of model.cpp:1382-1445 (ggml not vendored, reference backend unbuildable)"})
         return 0
     us = t_total / nls * sp["n_layer"] * 1e6
     desc = cp.describe(1)
@@ -286,7 +285,7 @@ def run_reference(args, sp):
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "CPU restatement of model.cpp:1382-1445 (ggml not vendored, reference backend unbuildable)",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -539,7 +538,7 @@ def run_ours(args, sp):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     ctx.close()
     if dist:
         dist.barrier()
@@ -547,7 +546,24 @@ def run_ours(args, sp):
     return 0
 
 
+_JSON_OUT = None
+
+
+def emit(line):
+    """The one JSON line, on the process's original standard output."""
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    global _JSON_OUT
+    # Everything else printed at any level (NCCL's version banner, library
+    # messages) goes to standard error, so standard output carries only the
+    # JSON line.
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[1])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)

@@ -658,54 +658,58 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 const int64_t o = (int64_t)(qrow / p.r) * p.out_stride + (int64_t)(p.out_head0 + h * p.r + qrow % p.r) * D + dd;
                 const float val = nan_out ? __int_as_float(0x7fc00000) : __fmul_rn(__ll2float_rn(v), kUnfix);
                 p.out[o] = val;
-                // KV-head shards: the same row into every peer's receive buffer (NVLink stores)
+                // KV-head shards: the same value, tagged with this launch, into
+                // every peer's receive buffer (NVLink stores; no fence or flag:
+                // the reader checks each word's tag)
+                const unsigned long long word = ((unsigned long long)p.epoch << 32) | __float_as_uint(val);
                 for (int g = 0; g < p.n_peers; g++)
-                    if (g != p.shard) p.rx[g][par * p.rx_stride + o] = val;
+                    if (g != p.shard) p.rx[g][par * p.rx_stride + o] = word;
             }
             if (tid == 0) {
                 p.counters[h] = 0u;
                 p.nonfin[h] = 0u;
             }
             if (p.n_peers > 1) {
-                __threadfence_system();
                 named_sync(1, kConsumers);
-                if (tid == 0) {
-                    // this head's rows are visible: raise its flag on every peer, then
-                    // count the head in; the CTA that converts the last local head
-                    // collects the peers' heads
-                    for (int g = 0; g < p.n_peers; g++)
-                        if (g != p.shard)
-                            st_volatile_u32(p.rxflag[g] + ((int64_t)par * p.n_peers + p.shard) * p.hkv + h, p.epoch);
-                    flags[3] = atomicAdd(p.xticket, 1u) == (unsigned)(p.hkv - 1);
-                }
+                // count the head in; the CTA that converts the last local head
+                // collects the peers' heads
+                if (tid == 0) flags[3] = atomicAdd(p.xticket, 1u) == (unsigned)(p.hkv - 1);
                 named_sync(1, kConsumers);
                 if (flags[3]) {
+                    // every column outside this shard's, once its word carries
+                    // this launch's tag; a thread keeps up to 8 words' loads in
+                    // flight per poll
+                    const unsigned long long *src = p.rx[p.shard] + par * p.rx_stride;
+                    const int cols = p.hkv * p.r * D;   // this shard's columns
+                    const int lo = p.out_head0 * D, all = p.n_peers * cols;
+                    const unsigned ep = p.epoch;
                     bool late = false;
-                    const int nflag = (p.n_peers - 1) * p.hkv;
-                    if (tid < nflag) {
-                        const int gg = tid / p.hkv, hh = tid - gg * p.hkv;
-                        const int g = gg < p.shard ? gg : gg + 1;
-                        const unsigned *f = p.rxflag[p.shard] + ((int64_t)par * p.n_peers + g) * p.hkv + hh;
-                        const uint64_t t0 = globaltimer();
-                        while (ld_volatile_u32(f) != p.epoch)
-                            if (globaltimer() - t0 > p.limit_ns) {
+                    const uint64_t t0 = globaltimer();
+                    for (int base = 0; base < all && !late; base += 8 * kConsumers) {
+                        unsigned pend = 0u;
+#pragma unroll
+                        for (int u = 0; u < 8; u++) {
+                            const int o = base + u * kConsumers + tid;
+                            if (o < all && (o < lo || o >= lo + cols)) pend |= 1u << u;
+                        }
+                        while (pend) {
+                            unsigned long long w[8];
+#pragma unroll
+                            for (int u = 0; u < 8; u++)   // all loads out before any is used
+                                w[u] = (pend & (1u << u)) ? ld_volatile_u64(src + base + u * kConsumers + tid) : 0ull;
+#pragma unroll
+                            for (int u = 0; u < 8; u++)
+                                if ((pend & (1u << u)) && (unsigned)(w[u] >> 32) == ep) {
+                                    p.out[base + u * kConsumers + tid] = __uint_as_float((unsigned)w[u]);
+                                    pend &= ~(1u << u);
+                                }
+                            if (pend && globaltimer() - t0 > p.limit_ns) {
                                 late = true;
                                 break;
                             }
-                    }
-                    if (named_sync_or(1, kConsumers, late)) {
-                        if (tid == 0) atomicOr(p.err, 8u);
-                    } else {
-                        __threadfence_system();
-                        // the peers' heads: every column outside this shard's
-                        const float *src = p.rx[p.shard] + par * p.rx_stride;
-                        const int cols = p.hkv * p.r * D;   // this shard's columns
-                        for (int idx = tid; idx < p.n_peers * cols; idx += kConsumers) {
-                            const int o = idx;
-                            if (o >= p.out_head0 * D && o < p.out_head0 * D + cols) continue;
-                            p.out[o] = __ldcv(src + o);
                         }
                     }
+                    if (named_sync_or(1, kConsumers, late) && tid == 0) atomicOr(p.err, 8u);
                     if (tid == 0) *p.xticket = 0u;
                 }
             }

@@ -206,9 +206,9 @@ struct kv_ctx {
     float *local_out = nullptr;   // sharded prefill: [n_batch_max][hq_loc*D]
     // sharded decode over peer memory: this shard's receive buffer [2][n_head*D]
     // F32 + flags [2][n_shards][hkv_loc], and every shard's buffer mapped here
-    float *rx = nullptr;
+    unsigned long long *rx = nullptr;   // this shard's receive buffer [2][rx_stride] tagged words
     int64_t rx_stride = 0;
-    float *peer_rx[kvb::kMaxShards] = {};
+    unsigned long long *peer_rx[kvb::kMaxShards] = {};
     bool peers = false;
     float *gathered = nullptr;    // [n_shards][n_batch_max][hq_loc*D]
     int max_cta = 0;
@@ -410,7 +410,7 @@ int map_peers(kv_ctx *ctx)
     const int G = c.n_shards;
     if (G > kvb::kMaxShards) return KV_OK;
     ctx->rx_stride = (int64_t)c.n_head * ctx->D;
-    const size_t bytes = (size_t)2 * ctx->rx_stride * sizeof(float) + (size_t)2 * G * ctx->hkv_loc * sizeof(unsigned);
+    const size_t bytes = (size_t)2 * ctx->rx_stride * sizeof(unsigned long long);
     if (cudaMalloc(&ctx->rx, bytes) != cudaSuccess || cudaMemset(ctx->rx, 0, bytes) != cudaSuccess) {
         cudaGetLastError();
         return fail(KV_E_OOM, "peer receive buffer");
@@ -446,7 +446,7 @@ int map_peers(kv_ctx *ctx)
             cudaGetLastError();
             ok = false;
         } else {
-            ctx->peer_rx[g] = static_cast<float *>(p);
+            ctx->peer_rx[g] = static_cast<unsigned long long *>(p);
         }
     }
     // every shard must agree: one that could not map its peers uses NCCL, so all do
@@ -936,9 +936,6 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     ap.xticket = ctx->ctl + 2 * ctx->hkv_loc;
     for (int g = 0; g < kvb::kMaxShards; g++) {
         ap.rx[g] = via_peers ? ctx->peer_rx[g] : nullptr;
-        ap.rxflag[g] = via_peers && ctx->peer_rx[g]
-                           ? reinterpret_cast<unsigned *>(ctx->peer_rx[g] + 2 * ctx->rx_stride)
-                           : nullptr;
     }
     if (ap.n_cta > ctx->max_cta) return fail(KV_E_RANGE, "internal: %d CTAs > %d", ap.n_cta, ctx->max_cta);
     {

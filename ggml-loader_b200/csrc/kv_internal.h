@@ -119,13 +119,12 @@ struct AttnParams {
     int64_t out_stride;
     int32_t out_head0;
     // KV-head shards exchanging decode outputs over NVLink (n_peers = shards, 0 = none):
-    // rx[g] = shard g's receive buffer, 2 parities x out_stride floats (the
-    // full output row, written by the shard that owns each head); rxflag[g] =
-    // shard g's flags [2 parities][n_peers][hkv] = epoch of the writer's launch;
-    // xticket counts this launch's converted local heads
+    // rx[g] = shard g's receive buffer, 2 parities x rx_stride words, one word
+    // per output float of the full row (written by the shard that owns each
+    // head) = epoch << 32 | float bits, so a word is valid once its tag shows
+    // the launch; xticket counts this launch's converted local heads
     int32_t n_peers, shard;
-    float *rx[kMaxShards];
-    unsigned *rxflag[kMaxShards];
+    unsigned long long *rx[kMaxShards];
     int64_t rx_stride;
     unsigned *xticket;
     // CTAs [span_a[h], span_b[h]] cover local head h; span_slot[h] is the

@@ -221,6 +221,13 @@ __device__ __forceinline__ unsigned ld_volatile_u32(const unsigned *p)
     return v;
 }
 
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void st_volatile_u32(unsigned *p, unsigned v)
 {
     asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
