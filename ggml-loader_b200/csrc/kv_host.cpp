@@ -227,6 +227,7 @@ struct kv_ctx {
     CUtensorMap qmap{};                     // qbuf [n_batch_max][hq_loc][D], box 64 x r x tb
     float *pf_stat = nullptr;               // [sm_count][kseg][2 tiles][128][2]
     float *pf_out = nullptr;                // [sm_count][kseg][2 tiles][128][D]
+    float2 *pf_rstat = nullptr;             // [hkv_loc * blocks][256] (M, 1/Z) of the exact passes
     // the cache row the last fused attention launch appended (stream, layer):
     // the next launch on that stream for that layer must not read it early
     cudaStream_t hz_stream = nullptr;
@@ -393,7 +394,7 @@ void free_all(kv_ctx *ctx)
     if (ctx->comm && nccl().CommDestroy) nccl().CommDestroy(ctx->comm);
     ctx->comm = nullptr;
     void *ptrs[] = {ctx->cache, ctx->rope, ctx->qbuf, ctx->S, ctx->stats, ctx->acc, ctx->ctl, ctx->err,
-                    ctx->local_out, ctx->gathered, ctx->pf_stat, ctx->pf_out};
+                    ctx->local_out, ctx->gathered, ctx->pf_stat, ctx->pf_out, ctx->pf_rstat};
     for (void *p : ptrs)
         if (p) cudaFree(p);
 }
@@ -694,6 +695,8 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
         const size_t slots = (size_t)ctx->sm_count * kseg * 256u;   // segments x two 128-row tiles
         e = cudaMalloc(&ctx->pf_stat, slots * 2u * sizeof(float));
         if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_out, slots * (size_t)D * sizeof(float));
+        const size_t nblk = (size_t)(c.n_batch_max + 2 * ctx->pf_tb - 1) / (2 * ctx->pf_tb);
+        if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_rstat, (size_t)ctx->hkv_loc * nblk * 256u * sizeof(float2));
         if (e != cudaSuccess) return bail(fail(KV_E_OOM, "prefill scratch: %s", cudaGetErrorString(e)));
         e = kvb::prefill_prepare(ctx->D);
         if (e != cudaSuccess) return bail(cuda_fail(e, "prefill_prepare"));
@@ -801,8 +804,17 @@ int kv_append(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
 
 namespace {
 
+// Chunks whose keys go beyond this take the exact two passes: the one-pass
+// kernel rounds unnormalised weights to F16 while ggml rounds the normalised
+// ones, which at long context fall in F16's subnormal range -- measured on
+// the oracle, rel-L2 3e-4 at 16k keys, 7e-4 at 64k, 1.3e-3 at 131k (the
+// tolerance is 1e-3).
+constexpr int64_t kOnePassKeys = 32768;
+
 // Chunked-prefill attention on the tensor cores: the one-pass attention kernel,
-// then the fold of pairs split over CTAs (kv_prefill.cu).  A pair is (KV head,
+// then the fold of pairs split over CTAs; past kOnePassKeys keys the exact
+// passes instead (statistics kernel, statistics fold, output kernel, fold)
+// (kv_prefill.cu).  A pair is (KV head,
 // block of two 128-row query tiles); the pairs' key tiles, laid end to end, are
 // cut into C equal ranges; C is the SM count, lowered until no range holds more
 // than prefill_max_segments() pairs.
@@ -843,16 +855,23 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     pp.n_cta = C;
     pp.kseg = kseg;
     pp.scale = ctx->scale;
+    pp.mode = n_past + n_new > kOnePassKeys ? 2 : 0;
     pp.pstat = ctx->pf_stat;
     pp.pout = ctx->pf_out;
+    pp.rstat = ctx->pf_rstat;
     pp.out = dst;
     pp.out_stride = dst_stride;
     pp.out_head0 = dst_head0;
     pp.err = ctx->err;
     pp.limit_ns = ctx->limit_ns;
-    static const char *what[2] = {"prefill attention kernel", "prefill output fold"};
-    for (int which = 0; which < 2; which++) {
-        const int rc = launch(ctx, which ? KV_K_PFOLD : KV_K_PREFILL, st, what[which],
+    static const char *what[5] = {"prefill attention kernel", "prefill output fold", "prefill statistics kernel",
+                                  "prefill statistics fold", "prefill output kernel"};
+    static const int one_pass[] = {0, 1}, exact[] = {2, 3, 4, 1};
+    const int *seq = pp.mode ? exact : one_pass;
+    const int nseq = pp.mode ? 4 : 2;
+    for (int n = 0; n < nseq; n++) {
+        const int which = seq[n];
+        const int rc = launch(ctx, (which == 1 || which == 3) ? KV_K_PFOLD : KV_K_PREFILL, st, what[which],
                               [&] { return kvb::launch_prefill(ctx->D, which, ctx->qmap, km, vm, pp, st); });
         if (rc) return rc;
     }

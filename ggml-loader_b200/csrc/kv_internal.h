@@ -158,8 +158,10 @@ struct PrefillParams {
     int64_t s_all;     // key tiles of one KV head summed over its blocks
     int32_t n_cta, kseg;
     float scale;
-    float *pstat;      // [n_cta][kseg][2 tiles][128] (m, l) per segment and row (split pairs)
-    float *pout;       // [n_cta][kseg][2 tiles][128][D] unnormalised partial outputs
+    int32_t mode;      // 0 one pass (online softmax), 2 the exact two passes (long contexts)
+    float *pstat;      // [n_cta][kseg][2 tiles][128] (m, l) per segment and row
+    float *pout;       // [n_cta][kseg][2 tiles][128][D] partial outputs of split pairs
+    float2 *rstat;     // [hkv * nblk][256] (M, 1/Z) per pair and row (exact passes)
     float *out;        // row t at out + t*out_stride, head h at (out_head0 + h)*D
     int64_t out_stride;
     int32_t out_head0;
@@ -170,7 +172,8 @@ struct PrefillParams {
 bool prefill_supported(int D);
 int prefill_max_segments();
 cudaError_t prefill_prepare(int D);
-// which: 0 the attention kernel, 1 the fold of pairs split over CTAs
+// which: 0 the one-pass attention kernel, 1 the fold of pairs split over CTAs;
+// the exact two passes: 2 statistics kernel, 3 statistics fold, 4 output kernel
 cudaError_t launch_prefill(int D, int which, const CUtensorMap &qmap, const CUtensorMap &kmap,
                            const CUtensorMap &vmap, const PrefillParams &p, cudaStream_t st);
 

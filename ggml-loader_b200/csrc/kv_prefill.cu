@@ -63,6 +63,9 @@ constexpr uint32_t kBox = 128 * 128;           // one [128 rows][64 halves] swiz
 constexpr uint32_t kTmO = 256;                 // TMEM column of O_A (O_B follows at +D)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLazy = 8.0f;                  // raise m only past 2^8 growth
+// kernel modes: one pass (online softmax), or the exact two passes for long
+// contexts: statistics (S, row max and sum), then output (ggml's normalised p)
+constexpr int kOnePass = 0, kStats = 1, kExact = 2;
 
 template <int D>
 struct PL {
@@ -210,7 +213,7 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b)
 // ---------------------------------------------------------------------------
 // 12 warps put 3 on each of the SM's four 16K-register quarters: at most 168
 // registers a thread
-template <int D>
+template <int D, int MODE>
 __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                  const __grid_constant__ CUtensorMap kmap,
                                                                  const __grid_constant__ CUtensorMap vmap,
@@ -260,7 +263,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
         if (lane == 0) {
             prefetch_tmap(&qmap);
             prefetch_tmap(&kmap);
-            prefetch_tmap(&vmap);
+            if (MODE != kStats) prefetch_tmap(&vmap);
             const uint32_t qbytes = (uint32_t)(p.r * p.tb) * 128u * NB;   // one Q tile (zero fill counts)
             for_segments(p, c, [&](int k, const Seg &sg) {
                 const int kvh = sg.pair / p.nblk, b = sg.pair % p.nblk;
@@ -287,16 +290,20 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                     for (int bx = 0; bx < NB; bx++)
                         tma_load_3d(smem + L::o_k + s * kTile + bx * kBox, &kmap, &k_full[s], bx * 64, kvh, t * 128);
                     issued_k++;
-                    const int sv = issued_v % VS;
-                    if (issued_v >= VS && !mbar_wait_ab(&v_empty[sv], ((issued_v / VS) - 1) & 1, p.limit_ns, flags)) {
-                        give_up(p, flags, 2u);
-                        return false;
-                    }
-                    mbar_arrive_expect_tx(&v_full[sv], kTile);
+                    if constexpr (MODE != kStats) {
+                        const int sv = issued_v % VS;
+                        if (issued_v >= VS &&
+                            !mbar_wait_ab(&v_empty[sv], ((issued_v / VS) - 1) & 1, p.limit_ns, flags)) {
+                            give_up(p, flags, 2u);
+                            return false;
+                        }
+                        mbar_arrive_expect_tx(&v_full[sv], kTile);
 #pragma unroll
-                    for (int bx = 0; bx < NB; bx++)
-                        tma_load_3d(smem + L::o_v + sv * kTile + bx * kBox, &vmap, &v_full[sv], bx * 64, kvh, t * 128);
-                    issued_v++;
+                        for (int bx = 0; bx < NB; bx++)
+                            tma_load_3d(smem + L::o_v + sv * kTile + bx * kBox, &vmap, &v_full[sv], bx * 64, kvh,
+                                        t * 128);
+                        issued_v++;
+                    }
                 }
                 return true;
             });
@@ -332,7 +339,11 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                     for (; i < i1; i++) {
                         const int tile = i >> 1;
                         if (!(i & 1) && !wt(&k_full[tile % KS], (tile / KS) & 1)) return false;
-                        if (i >= 2 && !wt(&o_ready[g * 2 + (i & 1)], ((i - 2) >> 1) & 1)) return false;
+                        // the buffer is free once PV_g(i-2) has read its P (the
+                        // statistics pass: once the softmax has read S_g(i-2))
+                        if (i >= 2 && !wt(MODE == kStats ? &p_full[g * 2 + (i & 1)] : &o_ready[g * 2 + (i & 1)],
+                                          ((i - 2) >> 1) & 1))
+                            return false;
                         tc_fence_after();
                         // S_g(i) = Q_g . K(64 of the tile's 128 rows)^T
                         const uint32_t kt = sk + (tile % KS) * kTile + (i & 1) * 8192;
@@ -348,7 +359,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                     }
                     return true;
                 });
-            } else {
+            } else if (MODE != kStats) {
                 for_segments(p, c, [&](int k, const Seg &sg) {
                     const int i0 = i, i1 = i + 2 * (sg.t1 - sg.t0);
                     for (; i < i1; i++) {
@@ -399,7 +410,15 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
             const bool valid = row_ok && tok < p.n_new;
             const int64_t lim = valid ? p.n_past + tok : -1;   // last visible key
             const int i0 = i, i1 = i + 2 * (sg.t1 - sg.t0);
-            float m = -INFINITY, l = 0.0f;
+            float m = -INFINITY, l = 0.0f;   // one pass: running max (log2 units), sum; statistics: raw max, sum
+            float nMx = 0.0f, inv = 0.0f;     // exact pass: -M * log2 e and 1/Z of the row
+            if constexpr (MODE == kExact) {
+                if (valid) {
+                    const float2 st = p.rstat[(int64_t)sg.pair * 256 + grp * 128 + row];
+                    nMx = -st.x * kLog2e;
+                    inv = st.y;
+                }
+            }
             for (; i < i1; i++) {
                 const int bf = i & 1;
                 if (!mbar_wait_ab(&s_full[grp * 2 + bf], (i >> 1) & 1, p.limit_ns, flags)) {
@@ -411,11 +430,21 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                 tmem_ld32(tS + bf * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
                 tmem_ld32(tS + bf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
                 tmem_wait_ld();
+                if constexpr (MODE == kStats) {   // S is in registers: the buffer may be refilled
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&p_full[grp * 2 + bf]);
+                }
                 const int64_t kb = (int64_t)(2 * sg.t0 + (i - i0)) * 64;   // first key of the sub-tile
                 const int nvis = (int)max((int64_t)0, min((int64_t)64, lim - kb + 1));
                 const bool full = __all_sync(0xffffffffu, nvis == 64);
-                float mx;
-                if (full) {
+                if (!full) {
+#pragma unroll
+                    for (int e = 0; e < 64; e++)
+                        if (e >= nvis) v[e] = __float_as_uint(-INFINITY);
+                }
+                float mx = 0.0f;
+                if constexpr (MODE != kExact) {
                     float m4[4];
 #pragma unroll
                     for (int a = 0; a < 4; a++) m4[a] = fmaxf(__uint_as_float(v[a]), __uint_as_float(v[4 + a]));
@@ -425,31 +454,44 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                         for (int a = 0; a < 4; a++)
                             m4[a] = max3(m4[a], __uint_as_float(v[e + a]), __uint_as_float(v[e + 4 + a]));
                     mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 64; e++)
-                        if (e >= nvis) v[e] = __float_as_uint(-INFINITY);
-                    float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-                    for (int e = 0; e < 64; e += 8)
-#pragma unroll
-                        for (int a = 0; a < 4; a++)
-                            m4[a] = max3(m4[a], __uint_as_float(v[e + a]), __uint_as_float(v[e + 4 + a]));
-                    mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
                 }
-                const float xm = mx * cs;
+                if constexpr (MODE == kStats) {
+                    // running raw max and sum of 2^((acc - max) * cs), exact online rescale
+                    const float nmax = fmaxf(m, mx);
+                    if (nmax != -INFINITY) {
+                        const float nb = -nmax * cs;
+                        const uint64_t nb2 = pk2(nb, nb);
+                        uint64_t s2[2] = {0ull, 0ull};
+#pragma unroll
+                        for (int e = 0; e < 32; e++) {
+                            const float2 xy = up2(fma2(pk2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])),
+                                                       cs2, nb2));
+                            s2[e & 1] = add2(s2[e & 1], pk2(ex2_approx(xy.x), ex2_approx(xy.y)));
+                        }
+                        const float2 sa = up2(add2(s2[0], s2[1]));
+                        l = (m == -INFINITY ? 0.0f : l * ex2_approx(fmaf(m, cs, nb))) + (sa.x + sa.y);
+                        m = nmax;
+                    }
+                    continue;
+                }
                 float f = 1.0f;
                 bool resc = false;
-                if (xm > m + kLazy) {   // never for a sub-tile without visible keys (xm = -inf)
-                    f = ex2_approx(m - xm);   // 0 while m = -inf
-                    resc = m != -INFINITY;
-                    l *= f;
-                    m = xm;
+                uint64_t nm2;
+                if constexpr (MODE == kOnePass) {
+                    const float xm = mx * cs;
+                    if (xm > m + kLazy) {   // never for a sub-tile without visible keys (xm = -inf)
+                        f = ex2_approx(m - xm);   // 0 while m = -inf
+                        resc = m != -INFINITY;
+                        l *= f;
+                        m = xm;
+                    }
+                    // p = 2^(acc*cs - m): masked keys hold -inf (2^-inf = 0); rows
+                    // without a visible key yet have m = -inf and every key masked
+                    const float nm = m == -INFINITY ? 0.0f : -m;
+                    nm2 = pk2(nm, nm);
+                } else {
+                    nm2 = pk2(nMx, nMx);   // p = F16(2^(acc*cs - M*log2e) * (1/Z)), ggml's rounding
                 }
-                // p = 2^(acc*cs - m): masked keys hold -inf (2^-inf = 0); rows
-                // without a visible key yet have m = -inf and every key masked
-                const float nm = m == -INFINITY ? 0.0f : -m;
-                const uint64_t nm2 = pk2(nm, nm);
                 uint64_t s2[2] = {0ull, 0ull};
 #pragma unroll
                 for (int u = 0; u < 2; u++) {
@@ -458,34 +500,41 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                     for (int e = 0; e < 16; e++) {
                         const float2 xy = up2(fma2(pk2(__uint_as_float(v[u * 32 + 2 * e]),
                                                        __uint_as_float(v[u * 32 + 2 * e + 1])), cs2, nm2));
-                        const float x0 = ex2_approx(xy.x), x1 = ex2_approx(xy.y);
-                        s2[e & 1] = add2(s2[e & 1], pk2(x0, x1));
+                        float x0 = ex2_approx(xy.x), x1 = ex2_approx(xy.y);
+                        if constexpr (MODE == kOnePass) {
+                            s2[e & 1] = add2(s2[e & 1], pk2(x0, x1));
+                        } else {
+                            x0 = __fmul_rn(x0, inv);
+                            x1 = __fmul_rn(x1, inv);
+                        }
                         const __half2 h2 = __floats2half2_rn(x0, x1);
                         pkd[e] = *reinterpret_cast<const uint32_t *>(&h2);
                     }
                     // keys 32u .. 32u+31 -> packed columns 16u .. 16u+15 of the buffer
                     tmem_st16(tS + bf * 64 + u * 16, pkd);
                 }
-                const float2 sa = up2(add2(s2[0], s2[1]));
-                l += sa.x + sa.y;
-                // O holds this segment's earlier sub-tiles: once the last P . V
-                // into it has completed, scale the raised rows (before P(i) is
-                // reported, so before PV(i) adds to O)
-                if (i > i0 && __any_sync(0xffffffffu, resc)) {
-                    if (!mbar_wait_ab(&o_ready[grp * 2 + ((i - 1) & 1)], ((i - 1) >> 1) & 1, p.limit_ns, flags)) {
-                        give_up(p, flags, 1u);
-                        return false;
-                    }
-                    tc_fence_after();
-                    const float fo = resc ? f : 1.0f;
+                if constexpr (MODE == kOnePass) {
+                    const float2 sa = up2(add2(s2[0], s2[1]));
+                    l += sa.x + sa.y;
+                    // O holds this segment's earlier sub-tiles: once the last P . V
+                    // into it has completed, scale the raised rows (before P(i) is
+                    // reported, so before PV(i) adds to O)
+                    if (i > i0 && __any_sync(0xffffffffu, resc)) {
+                        if (!mbar_wait_ab(&o_ready[grp * 2 + ((i - 1) & 1)], ((i - 1) >> 1) & 1, p.limit_ns, flags)) {
+                            give_up(p, flags, 1u);
+                            return false;
+                        }
+                        tc_fence_after();
+                        const float fo = resc ? f : 1.0f;
 #pragma unroll 1
-                    for (int ch = 0; ch < D / 16; ch++) {
-                        uint32_t o[16];
-                        tmem_ld16(tO + ch * 16, o);
-                        tmem_wait_ld();
+                        for (int ch = 0; ch < D / 16; ch++) {
+                            uint32_t o[16];
+                            tmem_ld16(tO + ch * 16, o);
+                            tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * fo);
-                        tmem_st16(tO + ch * 16, o);
+                            for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * fo);
+                            tmem_st16(tO + ch * 16, o);
+                        }
                     }
                 }
                 tmem_wait_st();
@@ -493,20 +542,26 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[grp * 2 + bf]);
             }
+            const bool whole = sg.t0 == 0 && sg.t1 == nt_of(p, b);   // no other CTA holds this pair
+            const int64_t slot = (((int64_t)c * p.kseg + k) * 2 + grp) * 128 + row;
+            if constexpr (MODE == kStats) {
+                // (max in scaled units, sum) of every segment, split or not
+                reinterpret_cast<float2 *>(p.pstat)[slot] =
+                    make_float2(m == -INFINITY ? -INFINITY : __fmul_rn(m, p.scale), l);
+                return true;
+            }
             // ---- the segment's output ----
             if (!mbar_wait_ab(o_full, k & 1, p.limit_ns, flags)) {
                 give_up(p, flags, 1u);
                 return false;
             }
             tc_fence_after();
-            const bool whole = sg.t0 == 0 && sg.t1 == nt_of(p, b);   // no other CTA holds this pair
             float *dst = p.out + (int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * D;
-            float scl = 1.0f;
+            float scl = 1.0f;   // the exact pass's O is final (p carries 1/Z)
             if (whole) {
-                scl = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;
+                if (MODE == kOnePass) scl = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;
             } else {
-                const int64_t slot = (((int64_t)c * p.kseg + k) * 2 + grp) * 128 + row;
-                reinterpret_cast<float2 *>(p.pstat)[slot] = make_float2(m, l);
+                if (MODE == kOnePass) reinterpret_cast<float2 *>(p.pstat)[slot] = make_float2(m, l);
                 dst = p.pout + slot * D;
             }
 #pragma unroll 1
@@ -533,8 +588,9 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
         // the CTA gave up: loads nobody waited for may still be landing
         for (int j = issued_k > KS ? issued_k - KS : 0; j < issued_k; j++)
             mbar_wait(&k_full[j % KS], (j / KS) & 1, p.limit_ns);
-        for (int j = issued_v > VS ? issued_v - VS : 0; j < issued_v; j++)
-            mbar_wait(&v_full[j % VS], (j / VS) & 1, p.limit_ns);
+        if constexpr (MODE != kStats)
+            for (int j = issued_v > VS ? issued_v - VS : 0; j < issued_v; j++)
+                mbar_wait(&v_full[j % VS], (j / VS) & 1, p.limit_ns);
         if (issued_q > 0) mbar_wait(q_full, (issued_q - 1) & 1, p.limit_ns);
     }
     if (warp == 1) {
@@ -577,6 +633,36 @@ __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
     const int tok = (2 * b + grp) * p.tb + tok_in;
     if (tok_in >= p.tb || tok >= p.n_new) return;
     auto slot = [&](int cc) { return (((int64_t)cc * p.kseg + (cc == ca ? seg_a : 0)) * 2 + grp) * 128 + row; };
+    float4 *dst = reinterpret_cast<float4 *>(p.out + (int64_t)tok * p.out_stride +
+                                             (int64_t)(p.out_head0 + kvh * p.r + hd) * D) + part * F4;
+    if (p.mode == kExact) {   // the segments' rows are final: their sum, CTAs in order
+        float4 acc[F4];
+#pragma unroll
+        for (int q = 0; q < F4; q++) acc[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int c0 = ca; c0 <= cb; c0 += 4) {
+            float4 v[4][F4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float4 *src = reinterpret_cast<const float4 *>(p.pout + slot(c0 + u <= cb ? c0 + u : c0) * D) +
+                                    part * F4;
+#pragma unroll
+                for (int q = 0; q < F4; q++) v[u][q] = __ldcg(src + q);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (c0 + u <= cb)
+#pragma unroll
+                    for (int q = 0; q < F4; q++) {
+                        acc[q].x += v[u][q].x;
+                        acc[q].y += v[u][q].y;
+                        acc[q].z += v[u][q].z;
+                        acc[q].w += v[u][q].w;
+                    }
+        }
+#pragma unroll
+        for (int q = 0; q < F4; q++) dst[q] = acc[q];
+        return;
+    }
     const float2 *ps = reinterpret_cast<const float2 *>(p.pstat);
     float M = -INFINITY;
     for (int c0 = ca; c0 <= cb; c0 += 4) {
@@ -615,38 +701,77 @@ __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
         }
     }
     const float inv = lsum > 0.0f ? __fdiv_rn(1.0f, lsum) : 0.0f;
-    float4 *dst = reinterpret_cast<float4 *>(p.out + (int64_t)tok * p.out_stride +
-                                             (int64_t)(p.out_head0 + kvh * p.r + hd) * D) + part * F4;
 #pragma unroll
     for (int q = 0; q < F4; q++)
         dst[q] = make_float4(acc[q].x * inv, acc[q].y * inv, acc[q].z * inv, acc[q].w * inv);
 }
 
+// (M, 1/Z) per (pair, row) for the exact output pass: M = the largest segment
+// maximum, Z = sum_i l_i exp(m_i - M) in double, CTAs in order; one block per
+// pair, a thread per row of its two tiles
+__global__ void __launch_bounds__(256) prefill_stats_fold(const PrefillParams p)
+{
+    const int pair = blockIdx.x, rr = threadIdx.x, grp = rr >> 7, row = rr & 127;
+    __shared__ int info[3];
+    if (threadIdx.x == 0) {
+        int ca, cb;
+        pair_ctas(p, pair, ca, cb);
+        info[0] = ca;
+        info[1] = cb;
+        info[2] = pair - pair_of(p, cta_lo(p, ca));
+    }
+    __syncthreads();
+    const int ca = info[0], cb = info[1], seg_a = info[2];
+    auto slot = [&](int cc) { return (((int64_t)cc * p.kseg + (cc == ca ? seg_a : 0)) * 2 + grp) * 128 + row; };
+    const float2 *ps = reinterpret_cast<const float2 *>(p.pstat);
+    float M = -INFINITY;
+    for (int cc = ca; cc <= cb; cc++) M = fmaxf(M, __ldcg(ps + slot(cc)).x);
+    double Z = 0.0;
+    for (int cc = ca; cc <= cb; cc++) {
+        const float2 v = __ldcg(ps + slot(cc));
+        if (v.x != -INFINITY) Z += (double)v.y * (double)exp2f((v.x - M) * kLog2e);
+    }
+    p.rstat[(int64_t)pair * 256 + rr] = make_float2(M, Z > 0.0 ? __fdiv_rn(1.0f, (float)Z) : 0.0f);
+}
+
 template <int D>
 cudaError_t prep_pf()
 {
-    return cudaFuncSetAttribute(prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PL<D>::bytes);
+    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<D, kOnePass>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)PL<D>::bytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill_kernel<D, kStats>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)PL<D>::bytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill_kernel<D, kExact>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)PL<D>::bytes);
+    return e;
 }
 
 template <int D>
 cudaError_t launch_pf(int which, const CUtensorMap &qmap, const CUtensorMap &kmap, const CUtensorMap &vmap,
                       const PrefillParams &p, cudaStream_t st)
 {
-    if (which == 0) {
-        prefill_kernel<D><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p);
-        return cudaGetLastError();
+    switch (which) {
+    case 0: prefill_kernel<D, kOnePass><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p); break;
+    case 2: prefill_kernel<D, kStats><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p); break;
+    case 3: prefill_stats_fold<<<p.hkv * p.nblk, 256, 0, st>>>(p); break;
+    case 4: prefill_kernel<D, kExact><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p); break;
+    default: {
+        // the fold may be scheduled once every attention CTA has started
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(p.hkv * p.nblk * 8));
+        cfg.blockDim = dim3(256);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, prefill_out_fold<D>, p);
     }
-    // the fold may be scheduled once every attention CTA has started
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(p.hkv * p.nblk * 8));
-    cfg.blockDim = dim3(256);
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, prefill_out_fold<D>, p);
+    }
+    return cudaGetLastError();
 }
 
 }  // namespace

@@ -209,10 +209,14 @@ def test_mid_size_matches_oracle(name, n_past, n_new, cuda):
     ("llama3.2-3b", 1000, 40),         # r = 3: 42 tokens per tile, 2 rows of each tile unused
     ("qwen2-0.5b", 150, 5),            # head_dim 64, r = 7
     ("qwen3-8b-prefill", 16384, 512),  # the benchmark chunk
+    ("qwen3-8b-prefill", 40000, 40),   # past 32k keys: the exact two passes
+    ("llama3.1-8b-128k", 120000, 33),  # 128k-class context, exact passes, pairs over many CTAs
 ])
 def test_prefill_chunk_matches_oracle(name, n_past, n_new, cuda):
-    """The tensor-core chunk path (one-pass online softmax) against the oracle's
-    two-pass ggml softmax, within the attention tolerance."""
+    """The tensor-core chunk path against the oracle's ggml softmax, within the
+    attention tolerance: the one-pass online softmax up to 32k keys, the exact
+    statistics + output passes beyond (where ggml's F16 rounding of normalised
+    weights, subnormal at long context, matters)."""
     sp = specs.get(name)
     sp["n_layer"] = 1
     n_ctx = n_past + n_new + 64
@@ -223,7 +227,7 @@ def test_prefill_chunk_matches_oracle(name, n_past, n_new, cuda):
     rows = synth.qkv_rows(sp, 3, 0, n_new)
     run.ctx.profile(True)
     out = run.step(rows, n_past)
-    assert run.ctx.profile_read("prefill")[0] == 1   # the tensor-core path ran
+    assert run.ctx.profile_read("prefill")[0] == (1 if n_past + n_new <= 32768 else 2)   # the tensor-core path ran
     q, k, v = _split(sp, rows)
     qn, kn = synth.norm_weights(sp, 0) if sp["qk_norm"] else (None, None)
     orc = O.Oracle(sp)
