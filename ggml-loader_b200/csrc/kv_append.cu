@@ -1,6 +1,7 @@
 // kv_append.cu -- fused QK-Norm + RoPE + F32->F16 (RNE) append of one layer.
 //
 // Replaces, for one layer, the reference's (src/model.cpp):
+//   QKV projection bias (qwen2), ggml_add      model.cpp:1099-1102
 //   per-head RMSNorm * gamma on Q and K        model.cpp:1382-1387 (rms_norm_mul 1071-1074)
 //   ggml_rope_ext on Q and K                   model.cpp:1389-1404
 //   ggml_cpy(K/V -> cache rows [n_past, +n_new)) model.cpp:1406-1414
@@ -140,11 +141,21 @@ __global__ void __launch_bounds__(kRowsPerBlock *(D / 8)) append_kernel(const Ap
 #pragma unroll
     for (int e = 0; e < 8; e++) x[e] = 0.0f;
     if (active) {
-        const float *src;
-        if (kind == 0) src = p.q + (int64_t)t * p.q_stride + (int64_t)(p.hq0 + h) * D;
-        else if (kind == 1) src = p.k + (int64_t)t * p.k_stride + (int64_t)(p.hkv0 + h) * D;
-        else src = p.v + (int64_t)t * p.v_stride + (int64_t)(p.hkv0 + h) * D;
+        const float *src, *bias;
+        if (kind == 0) {
+            src = p.q + (int64_t)t * p.q_stride + (int64_t)(p.hq0 + h) * D;
+            bias = p.q_bias ? p.q_bias + (int64_t)(p.hq0 + h) * D : nullptr;
+        } else if (kind == 1) {
+            src = p.k + (int64_t)t * p.k_stride + (int64_t)(p.hkv0 + h) * D;
+            bias = p.k_bias ? p.k_bias + (int64_t)(p.hkv0 + h) * D : nullptr;
+        } else {
+            src = p.v + (int64_t)t * p.v_stride + (int64_t)(p.hkv0 + h) * D;
+            bias = p.v_bias ? p.v_bias + (int64_t)(p.hkv0 + h) * D : nullptr;
+        }
         load8(src + tig * 8, VEC, x);
+        if (bias)   // ggml_add of the projection bias (model.cpp:1099-1102): one rounded add
+#pragma unroll
+            for (int e = 0; e < 8; e++) x[e] = __fadd_rn(x[e], __ldg(bias + tig * 8 + e));
     }
 
     // ---- QK-Norm: y = (x * (1/sqrt(mean(x*x) + eps))) * gamma --------------

@@ -125,8 +125,8 @@ __device__ __forceinline__ void rope_prefetch(const AttnParams &p, float2 (&csr)
 // RMS-normalised form in xs[] (shared), with the separately rounded arithmetic of
 // kv_append (kv_append.cu) so the bits agree.
 template <int D>
-__device__ void warp_rotate(const float *src, const float *gamma, const AttnParams &p, float *xs, float *tmp,
-                            const float2 (&csr)[(D + 31) / 32])
+__device__ void warp_rotate(const float *src, const float *bias, const float *gamma, const AttnParams &p, float *xs,
+                            float *tmp, const float2 (&csr)[(D + 31) / 32])
 {
     constexpr int E = (D + 31) / 32;
     const int lane = threadIdx.x & 31;
@@ -135,6 +135,7 @@ __device__ void warp_rotate(const float *src, const float *gamma, const AttnPara
     for (int e = 0; e < E; e++) {
         const int i = lane + 32 * e;
         x[e] = i < D ? __ldg(src + i) : 0.0f;
+        if (bias && i < D) x[e] = __fadd_rn(x[e], __ldg(bias + i));   // the projection bias, first
         w[e] = (gamma && i < D) ? __ldg(gamma + i) : 1.0f;
     }
 #pragma unroll
@@ -348,11 +349,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 const int hs = it / R, row = p.row0 + it % R;
                 const float *src = p.q + (int64_t)(row / p.r) * p.q_stride +
                                    (int64_t)(p.hq0 + (g.h0 + hs) * p.r + row % p.r) * D;
-                warp_rotate<D>(src, p.qk_norm ? p.q_norm_w : nullptr, p, qs + (hs * kRows + it % R) * D,
+                const float *bq = p.q_bias ? p.q_bias + (int64_t)(p.hq0 + (g.h0 + hs) * p.r + row % p.r) * D
+                                           : nullptr;
+                warp_rotate<D>(src, bq, p.qk_norm ? p.q_norm_w : nullptr, p, qs + (hs * kRows + it % R) * D,
                                tmp + warp * D, csr);
             } else {
-                warp_rotate<D>(p.k + (int64_t)(p.hkv0 + g.h0) * D, p.qk_norm ? p.k_norm_w : nullptr, p, kf,
-                               tmp + warp * D, csr);
+                warp_rotate<D>(p.k + (int64_t)(p.hkv0 + g.h0) * D,
+                               p.k_bias ? p.k_bias + (int64_t)(p.hkv0 + g.h0) * D : nullptr,
+                               p.qk_norm ? p.k_norm_w : nullptr, p, kf, tmp + warp * D, csr);
                 __half *dst = p.kc + (p.n_past * (int64_t)p.hkv + g.h0) * D;
                 for (int i = lane; i < D; i += 32) {
                     const __half h16 = __float2half_rn(kf[i]);
@@ -511,9 +515,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     // decode: the new V row of head h0 goes to the cache now, while others finish
     if (owns_new && warp == 7) {
         const float *src = p.v + (int64_t)(p.hkv0 + g.h0) * D;
+        const float *bv = p.v_bias ? p.v_bias + (int64_t)(p.hkv0 + g.h0) * D : nullptr;
         __half *dst = p.vc + (p.n_past * (int64_t)p.hkv + g.h0) * D;
         for (int i = lane; i < D; i += 32) {
-            const __half h16 = __float2half_rn(__ldg(src + i));
+            const __half h16 = __float2half_rn(bv ? __fadd_rn(__ldg(src + i), __ldg(bv + i)) : __ldg(src + i));
             vnew[i] = h16;
             dst[i] = h16;
         }

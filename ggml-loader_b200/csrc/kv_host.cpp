@@ -179,6 +179,7 @@ struct Pending {
     const float *q = nullptr, *k = nullptr, *v = nullptr;
     int64_t q_stride = 0, k_stride = 0, v_stride = 0;
     const float *qn = nullptr, *kn = nullptr;
+    const float *qb = nullptr, *kb = nullptr, *vb = nullptr;   // projection biases or null
     cudaStream_t st = nullptr;
 };
 
@@ -485,6 +486,7 @@ int run_append(kv_ctx *ctx, const Pending &pd)
     p.q = pd.q; p.k = pd.k; p.v = pd.v;
     p.q_stride = pd.q_stride; p.k_stride = pd.k_stride; p.v_stride = pd.v_stride;
     p.q_norm_w = pd.qn; p.k_norm_w = pd.kn;
+    p.q_bias = pd.qb; p.k_bias = pd.kb; p.v_bias = pd.vb;
     p.n_new = pd.n_new; p.n_past = pd.n_past;
     p.hq_loc = ctx->hq_loc; p.hkv_loc = ctx->hkv_loc; p.hq0 = ctx->hq0; p.hkv0 = ctx->hkv0;
     p.n_rot = c.n_rot; p.rope_mode = c.rope_mode; p.qk_norm = c.qk_norm; p.eps = c.rms_eps;
@@ -763,6 +765,15 @@ int kv_append(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
               const float *v, int64_t v_stride, const float *q_norm_w, const float *k_norm_w,
               void *stream)
 {
+    return kv_append_bias(ctx, layer, n_past, n_new, q, q_stride, k, k_stride, v, v_stride, q_norm_w, k_norm_w,
+                          nullptr, nullptr, nullptr, stream);
+}
+
+int kv_append_bias(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
+                   const float *q, int64_t q_stride, const float *k, int64_t k_stride,
+                   const float *v, int64_t v_stride, const float *q_norm_w, const float *k_norm_w,
+                   const float *q_bias, const float *k_bias, const float *v_bias, void *stream)
+{
     if (!ctx) return fail(KV_E_ARG, "NULL context");
     const kv_config &c = ctx->cfg;
     if (layer < 0 || layer >= c.n_layer) return fail(KV_E_ARG, "layer %d out of range", layer);
@@ -789,6 +800,7 @@ int kv_append(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
     pd.q = q; pd.k = k; pd.v = v;
     pd.q_stride = q_stride; pd.k_stride = k_stride; pd.v_stride = v_stride;
     pd.qn = q_norm_w; pd.kn = k_norm_w;
+    pd.qb = q_bias; pd.kb = k_bias; pd.vb = v_bias;
     pd.st = to_stream(stream);
     ctx->last_layer = layer;
     ctx->last_n_past = n_past;
@@ -926,6 +938,9 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     ap.q_stride = pd.q_stride;
     ap.q_norm_w = pd.qn;
     ap.k_norm_w = pd.kn;
+    ap.q_bias = pd.qb;
+    ap.k_bias = pd.kb;
+    ap.v_bias = pd.vb;
     ap.qk_norm = c.qk_norm;
     ap.n_rot = c.n_rot;
     ap.rope_mode = c.rope_mode;

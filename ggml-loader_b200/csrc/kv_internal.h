@@ -16,6 +16,7 @@ struct AppendParams {
     const float *q, *k, *v;          // token 0 of each block (global heads)
     int64_t q_stride, k_stride, v_stride;
     const float *q_norm_w, *k_norm_w; // [D] or null
+    const float *q_bias, *k_bias, *v_bias;   // [heads*D] (global heads) or null: added first
     int32_t n_new;
     int64_t n_past;
     int32_t hq_loc, hkv_loc;         // heads owned by this context
@@ -93,6 +94,7 @@ struct AttnParams {
     const float *q, *k, *v;          // token 0's Q/K/V blocks (global heads)
     int64_t q_stride;
     const float *q_norm_w, *k_norm_w;
+    const float *q_bias, *k_bias, *v_bias;   // [heads*D] (global heads) or null: added first
     int32_t qk_norm, n_rot, rope_mode;
     float eps;
     const float2 *rope;              // [n_ctx][n_rot/2]

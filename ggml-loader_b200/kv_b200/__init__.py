@@ -77,6 +77,8 @@ def lib():
         "kv_free": (ctypes.c_int, [_vp]),
         "kv_n_ctx": (ctypes.c_int, [_vp, ctypes.POINTER(_i64)]),
         "kv_append": (ctypes.c_int, [_vp, _i32, _i64, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp]),
+        "kv_append_bias": (ctypes.c_int, [_vp, _i32, _i64, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp,
+                                          _vp, _vp, _vp, _vp]),
         "kv_attend": (ctypes.c_int, [_vp, _i32, _i64, _i32, _vp, _vp]),
         "kv_forward": (ctypes.c_int, [_vp, _i64, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _vp, _vp, _i64,
                                       _vp, _i64, _vp]),
@@ -246,6 +248,14 @@ class Context:
         return _check(lib().kv_append(self.h, layer, n_past, n_new, _ptr(q), q_stride, _ptr(k), k_stride,
                                       _ptr(v), v_stride, _ptr(q_norm_w), _ptr(k_norm_w), _stream(stream)),
                       "kv_append")
+
+    def append_bias(self, layer, n_past, n_new, q, q_stride, k, k_stride, v, v_stride,
+                    q_norm_w=None, k_norm_w=None, q_bias=None, k_bias=None, v_bias=None, stream=None):
+        """kv_append with the qwen2 QKV projection biases added in the load."""
+        return _check(lib().kv_append_bias(self.h, layer, n_past, n_new, _ptr(q), q_stride, _ptr(k), k_stride,
+                                           _ptr(v), v_stride, _ptr(q_norm_w), _ptr(k_norm_w), _ptr(q_bias),
+                                           _ptr(k_bias), _ptr(v_bias), _stream(stream)),
+                      "kv_append_bias")
 
     def attend(self, layer, n_past, n_new, out, stream=None):
         return _check(lib().kv_attend(self.h, layer, n_past, n_new, _ptr(out), _stream(stream)), "kv_attend")

@@ -142,6 +142,22 @@ int kv_append(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
               void *stream);
 
 /*
+ * kv_append with the QKV bias of qwen2-style layers (model.cpp:1099-1102,
+ * ggml_add of attn_q/k/v.bias to the projections) added inside the append's
+ * load: q_bias [n_head*head_dim], k_bias and v_bias [n_head_kv*head_dim], F32
+ * device pointers of this layer, or NULL (no bias).  Each element is one
+ * rounded F32 add before QK-Norm and RoPE, as ggml_add is.  kv_append is this
+ * call with three NULL biases.
+ */
+int kv_append_bias(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
+                   const float *q, int64_t q_stride,
+                   const float *k, int64_t k_stride,
+                   const float *v, int64_t v_stride,
+                   const float *q_norm_w, const float *k_norm_w,
+                   const float *q_bias, const float *k_bias, const float *v_bias,
+                   void *stream);
+
+/*
  * Attention of the n_new tokens last appended to `layer` (same layer, n_past
  * and n_new as that kv_append) over cache rows [0, n_past+n_new) with the
  * causal mask k <= n_past+t (model.cpp:1579-1586) and scale 1/sqrt(head_dim).

@@ -236,6 +236,43 @@ def test_prefill_chunk_matches_oracle(name, n_past, n_new, cuda):
     assert_close(out, orc.attend(kc, vc, n_past, qr))
 
 
+@pytest.mark.parametrize("n_new", [1, 40])
+def test_qkv_bias_matches_oracle(n_new, cuda):
+    """kv_append_bias: qwen2's projection biases (model.cpp:1099-1102, ggml_add
+    in F32) added inside the append -- the fused decode append (one token) and
+    the chunk kernel -- give the oracle's cache bytes after the same add."""
+    import torch
+    sp = specs.get("qwen2-0.5b")
+    sp["n_layer"] = 1
+    n_past = 700
+    case = dict(name="bias", spec="qwen2-0.5b", n_ctx=1024, n_past=n_past, n_new=n_new)
+    run = Run(case, cuda, n_batch_max=64)
+    run.sp = sp
+    hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+    rng = np.random.default_rng(7)
+    bq = rng.uniform(-2, 2, hq * d).astype(np.float32)
+    bk = rng.uniform(-2, 2, hkv * d).astype(np.float32)
+    bv = rng.uniform(-2, 2, hkv * d).astype(np.float32)
+    rows = synth.qkv_rows(sp, 5, 0, n_new)
+    t = torch.from_numpy(np.ascontiguousarray(rows, np.float32)).to(cuda)
+    tb = [torch.from_numpy(x).to(cuda) for x in (bq, bk, bv)]
+    b, w = t.data_ptr(), rows.shape[1]
+    run.ctx.append_bias(0, n_past, n_new, b, w, b + 4 * hq * d, w, b + 4 * (hq + hkv) * d, w,
+                        None, None, tb[0], tb[1], tb[2], stream=run.stream)
+    out = torch.full((n_new, hq * d), float("nan"), device=cuda)
+    run.ctx.attend(0, n_past, n_new, out, stream=run.stream)
+    torch.cuda.synchronize()
+    kc, vc = _oracle_layer(sp, case["n_ctx"], n_past)
+    q, k, v = _split(sp, rows)
+    # ggml_add: one F32 add per element, before RoPE
+    q, k, v = (np.ascontiguousarray(x + bb, np.float32) for x, bb in ((q, bq), (k, bk), (v, bv)))
+    orc = O.Oracle(sp)
+    qr = orc.append(kc, vc, n_past, q, k, v)
+    assert np.array_equal(run.rows(0, n_past, n_new), kc[n_past:n_past + n_new])
+    assert np.array_equal(run.rows(1, n_past, n_new), vc[n_past:n_past + n_new])
+    assert_close(out.cpu().numpy(), orc.attend(kc, vc, n_past, qr))
+
+
 def test_qk_norm_fallback_rows_match_oracle_bits(cuda):
     """QK-Norm rows whose sum of squares is tiny, or whose squares span many
     binades, leave the exact-integer fast path for the sequential double sum;
