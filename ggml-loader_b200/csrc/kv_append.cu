@@ -100,11 +100,12 @@ __device__ __forceinline__ bool exact_mean(const float (&sq)[8], float &mean)
         mean = 0.0f;
         return true;
     }
-    const double T = ldexp((double)acc, (int)emax - 181);
+    // T = acc * 2^(emax - 181), the power of two built in the exponent field
+    const double T = (double)acc * __longlong_as_double((long long)((int)emax - 181 + 1023) << 52);
     if (T < 0x1p-100) return false;   // keep (float)(T / D) far from the subnormal range
-    const float f = __double2float_rn(T);
-    const double up = 0.5 * ((double)f + (double)nextafterf(f, INFINITY));
-    const double dn = 0.5 * ((double)f + (double)nextafterf(f, 0.0f));
+    const float f = __double2float_rn(T);   // positive and finite: its neighbours are +-1 ulp
+    const double up = 0.5 * ((double)f + (double)__uint_as_float(__float_as_uint(f) + 1u));
+    const double dn = 0.5 * ((double)f + (double)__uint_as_float(__float_as_uint(f) - 1u));
     const double tol = T * 0x1p-44;
     if (fabs(T - up) <= tol || fabs(T - dn) <= tol) return false;
     mean = f * (1.0f / (float)D);   // D is a power of two: exact
@@ -266,12 +267,133 @@ __global__ void __launch_bounds__(kRowsPerBlock *(D / 8)) append_kernel(const Ap
     store8_f16(dst + tig * 8, x);
 }
 
+// The common shapes (head_dim 64 or 128, RoPE over the whole head or none): a
+// row's D/8 threads are one aligned group of lanes, so the NEOX
+// partners, the norm's sum and its rare sequential fallback move by shuffles
+// -- no shared memory, no block barrier.  Same arithmetic as append_kernel.
+template <int D, bool VEC>
+__global__ void __launch_bounds__(256) append_kernel_warp(const AppendParams p)
+{
+    constexpr int G = D / 8;               // threads per row (16 or 8)
+    const int lane = threadIdx.x & 31;
+    const int tig = lane % G;
+    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / G;
+    int t, kind, h;
+    const bool active = row_of(p, row, t, kind, h);
+    const bool rotates = active && kind < 2;
+    const int half = p.n_rot >> 1, i0 = tig * 8;
+    const bool neox = p.rope_mode == 2;
+
+    // RoPE entries first: they do not depend on the row's values
+    float2 c[8];
+    if (rotates && p.n_rot > 0) {
+        const float2 *cs = p.rope + (p.n_past + t) * (int64_t)half;
+        if (neox) {
+            const int j0 = i0 < half ? i0 : i0 - half;
+#pragma unroll
+            for (int q = 0; q < 4; q++) *reinterpret_cast<float4 *>(c + 2 * q) = __ldg(reinterpret_cast<const float4 *>(cs + j0) + q);
+        } else {
+#pragma unroll
+            for (int q = 0; q < 2; q++) *reinterpret_cast<float4 *>(c + 2 * q) = __ldg(reinterpret_cast<const float4 *>(cs + i0 / 2) + q);
+        }
+    }
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) x[e] = 0.0f;
+    if (active) {
+        const float *src, *bias;
+        if (kind == 0) {
+            src = p.q + (int64_t)t * p.q_stride + (int64_t)(p.hq0 + h) * D;
+            bias = p.q_bias ? p.q_bias + (int64_t)(p.hq0 + h) * D : nullptr;
+        } else if (kind == 1) {
+            src = p.k + (int64_t)t * p.k_stride + (int64_t)(p.hkv0 + h) * D;
+            bias = p.k_bias ? p.k_bias + (int64_t)(p.hkv0 + h) * D : nullptr;
+        } else {
+            src = p.v + (int64_t)t * p.v_stride + (int64_t)(p.hkv0 + h) * D;
+            bias = p.v_bias ? p.v_bias + (int64_t)(p.hkv0 + h) * D : nullptr;
+        }
+        load8(src + i0, VEC, x);
+        if (bias)   // ggml_add of the projection bias (model.cpp:1099-1102): one rounded add
+#pragma unroll
+            for (int e = 0; e < 8; e++) x[e] = __fadd_rn(x[e], __ldg(bias + i0 + e));
+    }
+
+    // ---- QK-Norm (see append_kernel) ------------------------------------------
+    if (p.qk_norm) {
+        float sqv[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) sqv[e] = __fmul_rn(x[e], x[e]);
+        float mean = 0.0f;
+        const bool need = !exact_mean<G, D>(sqv, mean);
+        if (__any_sync(0xffffffffu, rotates && need)) {
+            // the sequential double sum, lane 0 of the row's group gathering the
+            // squares in element order
+            const int base = (lane / G) * G;
+            double sum = 0.0;
+#pragma unroll 1
+            for (int s2 = 0; s2 < G; s2++)
+#pragma unroll
+                for (int e = 0; e < 8; e++) sum = __dadd_rn(sum, (double)__shfl_sync(0xffffffffu, sqv[e], base + s2));
+            const float cm = __double2float_rn(__ddiv_rn(sum, (double)D));
+            if (need) mean = cm;
+        }
+        if (rotates) {
+            const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+            const float *w = (kind == 0 ? p.q_norm_w : p.k_norm_w) + i0;
+#pragma unroll
+            for (int e = 0; e < 8; e++) x[e] = __fmul_rn(__fmul_rn(x[e], sc), __ldg(w + e));
+        }
+    }
+
+    // ---- RoPE ---------------------------------------------------------------
+    if (p.n_rot > 0) {
+        if (neox) {
+            // partner of element i is i +- D/2: the thread D/16 lanes away
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) y[e] = __shfl_xor_sync(0xffffffffu, x[e], G / 2);
+            if (rotates) {
+                const bool lo = i0 < half;
+#pragma unroll
+                for (int e = 0; e < 8; e++)
+                    x[e] = lo ? __fsub_rn(__fmul_rn(x[e], c[e].x), __fmul_rn(y[e], c[e].y))
+                              : __fadd_rn(__fmul_rn(y[e], c[e].y), __fmul_rn(x[e], c[e].x));
+            }
+        } else if (rotates) {
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+                const float2 cc = c[e / 2];
+                const float a = x[e], b = x[e + 1];
+                x[e] = __fsub_rn(__fmul_rn(a, cc.x), __fmul_rn(b, cc.y));
+                x[e + 1] = __fadd_rn(__fmul_rn(a, cc.y), __fmul_rn(b, cc.x));
+            }
+        }
+    }
+
+    if (!active) return;
+    __half *dst;
+    if (kind == 0) dst = p.qbuf + ((int64_t)t * p.hq_loc + h) * D;
+    else if (kind == 1) dst = p.kc + ((p.n_past + t) * (int64_t)p.hkv_loc + h) * D;
+    else dst = p.vc + ((p.n_past + t) * (int64_t)p.hkv_loc + h) * D;
+    store8_f16(dst + i0, x);
+}
+
 template <int D>
 cudaError_t launch_append_d(bool vec, const AppendParams &p, cudaStream_t st)
 {
     const int64_t rows = (int64_t)p.n_new * (p.hq_loc + 2 * p.hkv_loc);
     const int64_t blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
     if (blocks <= 0) return cudaSuccess;
+    if constexpr (D == 64 || D == 128) {
+        // shuffle-only kernel: RoPE over the whole head (or none); partial
+        // rotary takes append_kernel
+        if (p.n_rot == 0 || p.n_rot == D) {
+            const int64_t wblocks = (rows * (D / 8) + 255) / 256;
+            if (vec) append_kernel_warp<D, true><<<(unsigned)wblocks, 256, 0, st>>>(p);
+            else append_kernel_warp<D, false><<<(unsigned)wblocks, 256, 0, st>>>(p);
+            return cudaGetLastError();
+        }
+    }
     const dim3 grid((unsigned)blocks), block(kRowsPerBlock * (D / 8));
     if (vec) append_kernel<D, true><<<grid, block, 0, st>>>(p);
     else append_kernel<D, false><<<grid, block, 0, st>>>(p);
