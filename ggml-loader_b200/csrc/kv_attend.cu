@@ -549,20 +549,27 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         const unsigned ep = p.epoch;
         const uint64_t t_start = globaltimer();
         for (;;) {
+            // every pending slot's load goes out before any is checked: one L2
+            // round trip a poll, however many CTAs span the head
+            unsigned long long w0[2][kPU], w1[2][kPU];
+#pragma unroll
+            for (int sl = 0; sl < 2; sl++)
+#pragma unroll
+                for (int u = 0; u < kPU; u++) {
+                    w0[sl][u] = w1[sl][u] = 0ull;
+                    if (pend & (1u << (sl * kPU + u)))
+                        ld_volatile_v2(p.stats + 2 * (part_slot(p, g.h0 + sl, ca[sl] + lane + 32 * u) * kRows + warp),
+                                       w0[sl][u], w1[sl][u]);
+                }
 #pragma unroll
             for (int sl = 0; sl < 2; sl++)
 #pragma unroll
                 for (int u = 0; u < kPU; u++) {
                     const unsigned bit = 1u << (sl * kPU + u);
-                    if (pend & bit) {
-                        const int cc = ca[sl] + lane + 32 * u;
-                        unsigned long long w0, w1;
-                        ld_volatile_v2(p.stats + 2 * (part_slot(p, g.h0 + sl, cc) * kRows + warp), w0, w1);
-                        if ((unsigned)(w0 >> 32) == ep && (unsigned)(w1 >> 32) == ep) {
-                            mm[sl][u] = __uint_as_float((unsigned)w0);
-                            zz[sl][u] = __uint_as_float((unsigned)w1);
-                            pend &= ~bit;
-                        }
+                    if ((pend & bit) && (unsigned)(w0[sl][u] >> 32) == ep && (unsigned)(w1[sl][u] >> 32) == ep) {
+                        mm[sl][u] = __uint_as_float((unsigned)w0[sl][u]);
+                        zz[sl][u] = __uint_as_float((unsigned)w1[sl][u]);
+                        pend &= ~bit;
                     }
                 }
             if (!__any_sync(0xffffffffu, pend != 0u)) break;
