@@ -497,15 +497,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     // -- a slot is valid once both tags match
     if (tid < 2 * kRows) {
         const int sl = tid / kRows, row = tid % kRows;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < 8; w++) M = fmaxf(M, red_m[(sl * 8 + w) * kRows + row]);
-        double Z = 0.0;
+        float mw[8], zw[8];
 #pragma unroll
         for (int w = 0; w < 8; w++) {
-            const float mw = red_m[(sl * 8 + w) * kRows + row];
-            if (mw != -INFINITY) Z += (double)red_z[(sl * 8 + w) * kRows + row] * (double)__expf(mw - M);
+            mw[w] = red_m[(sl * 8 + w) * kRows + row];
+            zw[w] = red_z[(sl * 8 + w) * kRows + row];
         }
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 8; w++) M = fmaxf(M, mw[w]);
+        // the 8 warps' sums (F32: this slot is on the head's critical path;
+        // the rounding is ~1e-7 of Z)
+        float Z = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; w++)
+            if (mw[w] != -INFINITY) Z = fmaf(zw[w], __expf(mw[w] - M), Z);
         // an aborted CTA publishes empty statistics, so no other CTA waits for it
         const unsigned long long tag = (unsigned long long)p.epoch << 32;
         st_volatile_v2(p.stats + 2 * (((int64_t)c * 2 + sl) * kRows + row),
