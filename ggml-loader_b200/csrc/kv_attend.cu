@@ -659,13 +659,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 bad = true;
         }
         if (bad) atomicOr(&p.nonfin[h], 1u);
-        __threadfence();
+        // the CTA's atomics, ordered by the barrier, are released by the ticket
+        // (cumulativity); the last CTA's ticket acquires every other CTA's
         named_sync(1, kConsumers);
         if (tid == 0)
-            flags[1 + sl] = atomicAdd(&p.counters[h], 1u) == (unsigned)(p.span_b[h] - p.span_a[h]);
+            flags[1 + sl] = atom_add_acq_rel_gpu(&p.counters[h], 1u) == (unsigned)(p.span_b[h] - p.span_a[h]);
         named_sync(1, kConsumers);
         if (flags[1 + sl]) {
-            __threadfence();
             const bool nan_out = __ldcg(&p.nonfin[h]) != 0u;
             const int par = (int)(p.epoch & 1u);
             for (int idx = tid; idx < R * D; idx += kConsumers) {

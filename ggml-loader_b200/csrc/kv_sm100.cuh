@@ -228,6 +228,16 @@ __device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned lon
     return v;
 }
 
+// Ticket: an add with release (everything this CTA wrote before the barrier
+// that precedes it) and acquire (what the CTAs counted in before wrote)
+// semantics at GPU scope.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned *p, unsigned v)
+{
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 __device__ __forceinline__ void st_volatile_u32(unsigned *p, unsigned v)
 {
     asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
