@@ -99,6 +99,14 @@ __device__ __forceinline__ void tile_of(const Range &g, int i, int &h, int64_t &
     else { h = g.h0 + 1; k0 = (int64_t)(i - g.nt0) * kTK; kend = g.e1; }
 }
 
+// the caller's additive mask at (token, key)
+__device__ __forceinline__ float mask_at(const AttnParams &p, int tok, int64_t key)
+{
+    const int64_t i = (int64_t)tok * p.mask_stride + key;
+    return p.mask_f16 ? __half2float(__ldg(reinterpret_cast<const __half *>(p.mask) + i))
+                      : __ldg(reinterpret_cast<const float *>(p.mask) + i);
+}
+
 // index of the (CTA, segment) statistics of local head h held by CTA cc
 __device__ __forceinline__ int64_t part_slot(const AttnParams &p, int h, int cc)
 {
@@ -223,7 +231,9 @@ struct Smem {
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int D>
+// EXT: the instance for kv_attend_mask (the caller's mask and/or the flash
+// branch); the plain causal instance is compiled without that code
+template <int D, bool EXT>
 __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                     const __grid_constant__ CUtensorMap vmap,
                                                                     const AttnParams p)
@@ -320,8 +330,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     const int gq = lane >> 2, cq = lane & 3;
     const int R = p.nrows;
     const int row_a = 2 * cq, row_b = 2 * cq + 1;
-    const int64_t lim_a = p.n_past + (p.row0 + min(row_a, R - 1)) / p.r;
-    const int64_t lim_b = p.n_past + (p.row0 + min(row_b, R - 1)) / p.r;
+    const int tok_a = (p.row0 + min(row_a, R - 1)) / p.r, tok_b = (p.row0 + min(row_b, R - 1)) / p.r;
+    // the last visible key of each row: the causal bound, or every key with a mask
+    const bool masked = EXT && p.mask;
+    const bool flash = EXT && p.flash;
+    const int64_t lim_a = masked ? p.n_kv : p.n_past + tok_a;
+    const int64_t lim_b = masked ? p.n_kv : p.n_past + tok_b;
     float *const Scta = p.S + (int64_t)c * p.S_tiles * kTileScores;
 
     float2 csr[(D + 31) / 32];
@@ -420,6 +434,24 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 load_q(1);
             }
             const int s = i % NS;
+            int h;
+            int64_t k0, kend;
+            tile_of(g, i, h, k0, kend);
+            // (key gq, row 2cq), (key gq, row 2cq+1), (key gq+8, row 2cq), (key gq+8, row 2cq+1)
+            const int64_t key0 = k0 + warp * 16 + gq, key1 = key0 + 8;
+            const bool v0 = key0 < kend, v1 = key1 < kend;
+            // the caller's mask: loaded before the tile wait, which hides the latency
+            float mk[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (masked) {
+                if (v0) {
+                    mk[0] = mask_at(p, tok_a, key0);
+                    mk[1] = mask_at(p, tok_b, key0);
+                }
+                if (v1) {
+                    mk[2] = mask_at(p, tok_a, key1);
+                    mk[3] = mask_at(p, tok_b, key1);
+                }
+            }
             const bool ok = mbar_wait(&full[s], (i / NS) & 1, p.limit_ns);
             if (__any_sync(0xffffffffu, !ok)) {
                 if (lane == 0) {
@@ -429,9 +461,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 aborted = true;
                 break;
             }
-            int h;
-            int64_t k0, kend;
-            tile_of(g, i, h, k0, kend);
             if (i == it_new && (int)((p.n_past - k0) >> 4) == warp)
                 patch_row<D, BW>(smem + s * kStage, (int)(p.n_past - k0), knew);
 
@@ -448,13 +477,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
 
-            // (key gq, row 2cq), (key gq, row 2cq+1), (key gq+8, row 2cq), (key gq+8, row 2cq+1)
-            const int64_t key0 = k0 + warp * 16 + gq, key1 = key0 + 8;
-            const bool v0 = key0 < kend, v1 = key1 < kend;
-            const float sa0 = v0 && key0 <= lim_a ? __fmul_rn(acc0[0] + acc1[0], p.scale) : -INFINITY;
-            const float sb0 = v0 && key0 <= lim_b ? __fmul_rn(acc0[1] + acc1[1], p.scale) : -INFINITY;
-            const float sa1 = v1 && key1 <= lim_a ? __fmul_rn(acc0[2] + acc1[2], p.scale) : -INFINITY;
-            const float sb1 = v1 && key1 <= lim_b ? __fmul_rn(acc0[3] + acc1[3], p.scale) : -INFINITY;
+            // s = dot*scale (+ mask), rounded separately as ggml_soft_max_ext does
+            auto score = [&](float dot, bool vis, float m) {
+                return vis ? (masked ? __fadd_rn(__fmul_rn(dot, p.scale), m) : __fmul_rn(dot, p.scale)) : -INFINITY;
+            };
+            const float sa0 = score(acc0[0] + acc1[0], v0 && key0 <= lim_a, mk[0]);
+            const float sb0 = score(acc0[1] + acc1[1], v0 && key0 <= lim_b, mk[1]);
+            const float sa1 = score(acc0[2] + acc1[2], v1 && key1 <= lim_a, mk[2]);
+            const float sb1 = score(acc0[3] + acc1[3], v1 && key1 <= lim_b, mk[3]);
             float *Sw = Scta + (int64_t)i * kTileScores + warp * 128;
             if (row_a < R) {
                 if (v0) Sw[so_a] = sa0;
@@ -646,19 +676,20 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         }
         named_sync(1, kConsumers);
         long long *acc = p.acc + (int64_t)h * kRows * D;
-        bool bad = false;
+        unsigned bad = 0u;   // rows with a non-finite partial
         for (int idx = tid; idx < R * D; idx += kConsumers) {
             const int row = idx / D, dd = idx - row * D;
             float sum = 0.0f;
 #pragma unroll
             for (int w = 0; w < 8; w++) sum += red[(w * kRows + row) * RED_LD + dd];
+            if (flash) sum = __fmul_rn(sum, rowInv[sl * kRows + row]);   // flash: normalised here
             if (isfinite(sum))
                 atomicAdd(reinterpret_cast<unsigned long long *>(acc + idx),
                           (unsigned long long)__float2ll_rn(__fmul_rn(sum, kFix)));
             else
-                bad = true;
+                bad |= 1u << row;
         }
-        if (bad) atomicOr(&p.nonfin[h], 1u);
+        if (bad) atomicOr(&p.nonfin[h], bad);
         // the CTA's atomics, ordered by the barrier, are released by the ticket
         // (cumulativity); the last CTA's ticket acquires every other CTA's
         named_sync(1, kConsumers);
@@ -666,7 +697,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             flags[1 + sl] = atom_add_acq_rel_gpu(&p.counters[h], 1u) == (unsigned)(p.span_b[h] - p.span_a[h]);
         named_sync(1, kConsumers);
         if (flags[1 + sl]) {
-            const bool nan_out = __ldcg(&p.nonfin[h]) != 0u;
+            const unsigned nan_rows = __ldcg(&p.nonfin[h]);
             const int par = (int)(p.epoch & 1u);
             for (int idx = tid; idx < R * D; idx += kConsumers) {
                 const int row = idx / D, dd = idx - row * D;
@@ -674,7 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 acc[idx] = 0;
                 const int qrow = p.row0 + row;
                 const int64_t o = (int64_t)(qrow / p.r) * p.out_stride + (int64_t)(p.out_head0 + h * p.r + qrow % p.r) * D + dd;
-                const float val = nan_out ? __int_as_float(0x7fc00000) : __fmul_rn(__ll2float_rn(v), kUnfix);
+                const float val = (nan_rows >> row) & 1u ? __int_as_float(0x7fc00000) : __fmul_rn(__ll2float_rn(v), kUnfix);
                 p.out[o] = val;
                 // KV-head shards: the same value, tagged with this launch, into
                 // every peer's receive buffer (NVLink stores; no fence or flag:
@@ -778,7 +809,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         for (int e = 0; e < 4; e++) {
             const int kk = kw + 2 * cq + (e & 1) + 8 * (e >> 1);
             const bool valid = gq < R && kk < n_valid;
-            const float pe = __fmul_rn(expf(sc[e] - M), inv);
+            // default branch: F16(exp(s - M) * (1/Z)), ggml's rounding of the
+            // normalised weight; flash branch: F16(exp(s - M)), scaled by 1/Z at
+            // the output, and 0 for a row without a visible key
+            const float pe = flash ? (M == -INFINITY ? 0.0f : expf(sc[e] - M)) : __fmul_rn(expf(sc[e] - M), inv);
             pv[e] = valid ? __float2half_rn(pe) : __ushort_as_half((unsigned short)0);
         }
         const uint32_t b0 = pack_half2(pv[0], pv[1]), b1 = pack_half2(pv[2], pv[3]);
@@ -811,7 +845,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
 template <int D>
 cudaError_t prep()
 {
-    return cudaFuncSetAttribute(attn_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    const cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)Smem<D>::bytes);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(attn_decode_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)Smem<D>::bytes);
 }
 
@@ -828,7 +865,8 @@ cudaError_t launch(const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnP
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D>, kmap, vmap, p);
+    if (p.mask || p.flash) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true>, kmap, vmap, p);
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, false>, kmap, vmap, p);
 }
 
 }  // namespace

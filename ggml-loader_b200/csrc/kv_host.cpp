@@ -830,8 +830,16 @@ constexpr int64_t kOnePassKeys = 32768;
 // block of two 128-row query tiles); the pairs' key tiles, laid end to end, are
 // cut into C equal ranges; C is the SM count, lowered until no range holds more
 // than prefill_max_segments() pairs.
+// the caller's mask of kv_attend_mask (ptr nullptr: the implicit causal mask)
+struct MaskArg {
+    const void *ptr = nullptr;
+    int64_t stride = 0;
+    bool f16 = false;
+    bool flash = false;
+};
+
 int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n_past, int32_t n_new, float *dst,
-            int64_t dst_stride, int dst_head0, cudaStream_t st)
+            int64_t dst_stride, int dst_head0, const MaskArg &mk, cudaStream_t st)
 {
     kvb::PrefillParams pp{};
     pp.hkv = ctx->hkv_loc;
@@ -845,7 +853,7 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     std::vector<int64_t> nt(pp.nblk);
     pp.s_all = 0;
     for (int b = 0; b < pp.nblk; b++) {
-        nt[b] = (n_past + std::min<int64_t>(n_new, (int64_t)(2 * b + 2) * pp.tb) + 127) / 128;
+        nt[b] = (n_past + (mk.ptr ? (int64_t)n_new : std::min<int64_t>(n_new, (int64_t)(2 * b + 2) * pp.tb)) + 127) / 128;
         pp.s_all += nt[b];
     }
     const int64_t W = (int64_t)pp.hkv * pp.s_all;
@@ -867,7 +875,15 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     pp.n_cta = C;
     pp.kseg = kseg;
     pp.scale = ctx->scale;
-    pp.mode = n_past + n_new > kOnePassKeys ? 2 : 0;
+    // the exact two passes reproduce the default branch's rounding at long
+    // contexts; the flash-attn branch is one online softmax at any length
+    pp.mode = !mk.flash && n_past + n_new > kOnePassKeys ? 2 : 0;
+    pp.mask = mk.ptr;
+    pp.mask_stride = mk.stride;
+    pp.mask_f16 = mk.f16 ? 1 : 0;
+    pp.mask_vec = mk.ptr && reinterpret_cast<uintptr_t>(mk.ptr) % 16 == 0 &&
+                  (mk.stride * (mk.f16 ? 2 : 4)) % 16 == 0;
+    pp.flash = mk.flash ? 1 : 0;
     pp.pstat = ctx->pf_stat;
     pp.pout = ctx->pf_out;
     pp.rstat = ctx->pf_rstat;
@@ -892,7 +908,8 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
 
 }  // namespace
 
-int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *out, void *stream)
+static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, const MaskArg &mk, float *out,
+                void *stream)
 {
     if (!ctx) return fail(KV_E_ARG, "NULL context");
     if (!out) return fail(KV_E_ARG, "out is NULL");
@@ -962,6 +979,10 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     ap.out = dst;
     ap.out_stride = dst_stride;
     ap.out_head0 = dst_head0;
+    ap.mask = mk.ptr;
+    ap.mask_stride = mk.stride;
+    ap.mask_f16 = mk.f16 ? 1 : 0;
+    ap.flash = mk.flash ? 1 : 0;
     const bool via_peers = sharded && ctx->peers && n_new == 1 && ctx->r <= kvb::attn_rows() &&
                            !(!fused && ctx->pf && n_new * ctx->r >= 32);
     ap.n_peers = via_peers ? c.n_shards : 0;
@@ -1003,7 +1024,7 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     const int rows_per = kvb::attn_rows();
     const CUtensorMap &km = ctx->kmaps[layer], &vm = ctx->vmaps[layer];
     if (!fused && ctx->pf && rows >= 32) {
-        rc = prefill(ctx, km, vm, n_past, n_new, dst, dst_stride, dst_head0, st);
+        rc = prefill(ctx, km, vm, n_past, n_new, dst, dst_stride, dst_head0, mk, st);
         if (rc) return rc;
     }
     for (int row0 = 0; row0 < rows && !(!fused && ctx->pf && rows >= 32); row0 += rows_per) {
@@ -1043,6 +1064,28 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
         }
     }
     return KV_OK;
+}
+
+int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *out, void *stream)
+{
+    return attend_impl(ctx, layer, n_past, n_new, MaskArg{}, out, stream);
+}
+
+int kv_attend_mask(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, const void *mask, int32_t mask_type,
+                   int64_t mask_stride, uint32_t flags, float *out, void *stream)
+{
+    if (mask_type != KV_MASK_F32 && mask_type != KV_MASK_F16)
+        return fail(KV_E_ARG, "unknown mask type %d", mask_type);
+    if ((flags & ~(uint32_t)KV_ATTN_FLASH) != 0) return fail(KV_E_ARG, "unknown flags 0x%x", flags);
+    if (mask && mask_stride < n_past + n_new)
+        return fail(KV_E_ARG, "mask_stride %lld < n_past + n_new (%lld)", (long long)mask_stride,
+                    (long long)(n_past + n_new));
+    MaskArg mk;
+    mk.ptr = mask;
+    mk.stride = mask ? mask_stride : 0;
+    mk.f16 = mask_type == KV_MASK_F16;
+    mk.flash = (flags & KV_ATTN_FLASH) != 0;
+    return attend_impl(ctx, layer, n_past, n_new, mk, out, stream);
 }
 
 int kv_forward(kv_ctx *ctx, int64_t n_past, int32_t n_new,

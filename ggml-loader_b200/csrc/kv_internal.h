@@ -112,10 +112,18 @@ struct AttnParams {
     uint32_t epoch;                  // tag of this launch's statistics (never 0)
     long long *acc;                  // [hkv][8][D] output accumulators, fixed point 2^-40, zero between calls
     unsigned *counters;              // [hkv] output tickets, zero between calls
-    unsigned *nonfin;                // [hkv] a non-finite partial output was seen, zero between calls
+    unsigned *nonfin;                // [hkv] rows (bit per row) with a non-finite partial output, zero between calls
     unsigned *err;                   // error word (1: consumer tile wait, 2: producer, 4: statistics wait)
     uint64_t limit_ns;               // bound of every device-side wait
     int32_t inject;                  // test hook: 1 = producers withhold tile 1
+    // the caller's additive mask (nullptr: the implicit causal mask): score =
+    // dot*scale + mask[token*mask_stride + key], F16 when mask_f16
+    const void *mask;
+    int64_t mask_stride;
+    int32_t mask_f16;
+    // 1: the flash-attn branch -- weights exp(s - M) rounded to F16 unnormalised,
+    // the partial output scaled by 1/Z; a row without a visible key gives 0
+    int32_t flash;
     // output
     float *out;
     int64_t out_stride;
@@ -167,6 +175,11 @@ struct PrefillParams {
     float *out;        // row t at out + t*out_stride, head h at (out_head0 + h)*D
     int64_t out_stride;
     int32_t out_head0;
+    const void *mask;  // as AttnParams: the caller's additive mask, nullptr = causal
+    int64_t mask_stride;
+    int32_t mask_f16;
+    int32_t mask_vec;  // mask rows start on 16-byte boundaries: vector loads
+    int32_t flash;     // the flash-attn branch: a row without a visible key gives 0
     unsigned *err;
     uint64_t limit_ns;
 };

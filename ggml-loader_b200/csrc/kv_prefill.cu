@@ -45,6 +45,11 @@
 //              tcgen05.st; the rare O rescale (after the previous P . V, which
 //              o_ready reports); at a segment's end O out
 // prefill_out_fold   merges the segments of pairs split over CTAs
+// With the caller's additive mask (kv_attend_mask) every pair covers all keys,
+// the mask is added to each score (acc + mask/scale, so s*log2e = acc*cs +
+// mask*log2e) and the causal bound is not applied; the flash-attn branch runs
+// the one-pass mode at any length and gives 0 for a row without a visible key
+// (the default branch: NaN, as ggml's soft_max of an all -inf row).
 // Every wait is bounded (limit_ns) and gives up when the CTA's abort flag is
 // set; the CTA drains its TMA loads and MMAs and frees TMEM before leaving.
 #include <math.h>
@@ -86,11 +91,70 @@ struct PL {
     static_assert(bytes <= 227 * 1024, "shared memory of the prefill kernel");
 };
 
+// ---- the caller's mask -----------------------------------------------------------
+// v[e] (raw dots of keys kb + e, e < nvis) += mask[tok][kb + e] / scale; 16-byte
+// loads when the rows allow them (mask_vec), else one element at a time
+__device__ __forceinline__ void add_mask(const PrefillParams &p, int tok, int64_t kb, int nvis, float mscl,
+                                         uint32_t (&v)[64])
+{
+    const int64_t base = (int64_t)tok * p.mask_stride + kb;
+    if (p.mask_vec && nvis == 64) {
+        if (p.mask_f16) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const __half *>(p.mask) + base);
+            uint4 u[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) u[q] = __ldg(src + q);
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                const uint32_t w4[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w4[t]));
+                    v[8 * q + 2 * t] = __float_as_uint(fmaf(f.x, mscl, __uint_as_float(v[8 * q + 2 * t])));
+                    v[8 * q + 2 * t + 1] = __float_as_uint(fmaf(f.y, mscl, __uint_as_float(v[8 * q + 2 * t + 1])));
+                }
+            }
+        } else {
+            const float4 *src = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p.mask) + base);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                float4 f[8];
+#pragma unroll
+                for (int q = 0; q < 8; q++) f[q] = __ldg(src + 8 * h + q);
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    const int e = 32 * h + 4 * q;
+                    v[e] = __float_as_uint(fmaf(f[q].x, mscl, __uint_as_float(v[e])));
+                    v[e + 1] = __float_as_uint(fmaf(f[q].y, mscl, __uint_as_float(v[e + 1])));
+                    v[e + 2] = __float_as_uint(fmaf(f[q].z, mscl, __uint_as_float(v[e + 2])));
+                    v[e + 3] = __float_as_uint(fmaf(f[q].w, mscl, __uint_as_float(v[e + 3])));
+                }
+            }
+        }
+        return;
+    }
+#pragma unroll
+    for (int e = 0; e < 64; e++)
+        if (e < nvis) {
+            const float m = p.mask_f16 ? __half2float(__ldg(reinterpret_cast<const __half *>(p.mask) + base + e))
+                                       : __ldg(reinterpret_cast<const float *>(p.mask) + base + e);
+            v[e] = __float_as_uint(fmaf(m, mscl, __uint_as_float(v[e])));
+        }
+}
+
+// output scale of a row without a visible key: 0 in the flash-attn branch,
+// NaN in the default one (ggml's soft_max of an all -inf row)
+__device__ __forceinline__ float no_key_scale(const PrefillParams &p)
+{
+    return p.flash ? 0.0f : __int_as_float(0x7fc00000);
+}
+
 // ---- the work split ------------------------------------------------------------
 // key tiles of block b (tokens [2b*tb, 2b*tb + 2*tb))
 __device__ __forceinline__ int nt_of(const PrefillParams &p, int b)
 {
-    const int64_t last = p.n_past + min((int64_t)p.n_new, (int64_t)(2 * b + 2) * p.tb);   // keys [0, last)
+    // keys [0, last): the causal bound of the block's last token, or all keys with a mask
+    const int64_t last = p.n_past + (p.mask ? (int64_t)p.n_new : min((int64_t)p.n_new, (int64_t)(2 * b + 2) * p.tb));
     return (int)((last + 127) / 128);
 }
 
@@ -213,7 +277,7 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b)
 // ---------------------------------------------------------------------------
 // 12 warps put 3 on each of the SM's four 16K-register quarters: at most 168
 // registers a thread
-template <int D, int MODE>
+template <int D, int MODE, bool MASKED>
 __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                  const __grid_constant__ CUtensorMap kmap,
                                                                  const __grid_constant__ CUtensorMap vmap,
@@ -408,7 +472,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
             const int b = sg.pair % p.nblk, kvh = sg.pair / p.nblk;
             const int tok = (2 * b + grp) * p.tb + tok_in;
             const bool valid = row_ok && tok < p.n_new;
-            const int64_t lim = valid ? p.n_past + tok : -1;   // last visible key
+            const int64_t lim = !valid ? -1 : p.mask ? p.n_past + p.n_new - 1 : p.n_past + tok;   // last visible key
+            const float mscl = p.mask ? __fdiv_rn(1.0f, p.scale) : 0.0f;   // mask / scale adds to the raw dot
             const int i0 = i, i1 = i + 2 * (sg.t1 - sg.t0);
             float m = -INFINITY, l = 0.0f;   // one pass: running max (log2 units), sum; statistics: raw max, sum
             float nMx = 0.0f, inv = 0.0f;     // exact pass: -M * log2 e and 1/Z of the row
@@ -443,6 +508,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                     for (int e = 0; e < 64; e++)
                         if (e >= nvis) v[e] = __float_as_uint(-INFINITY);
                 }
+                if constexpr (MASKED)   // (a separate instance: the causal one keeps its registers)
+                    if (valid) add_mask(p, tok, kb, nvis, mscl, v);
                 float mx = 0.0f;
                 if constexpr (MODE != kExact) {
                     float m4[4];
@@ -559,7 +626,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
             float *dst = p.out + (int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * D;
             float scl = 1.0f;   // the exact pass's O is final (p carries 1/Z)
             if (whole) {
-                if (MODE == kOnePass) scl = l > 0.0f ? __fdiv_rn(1.0f, l) : 0.0f;
+                if (MODE == kOnePass) scl = l > 0.0f ? __fdiv_rn(1.0f, l) : no_key_scale(p);
             } else {
                 if (MODE == kOnePass) reinterpret_cast<float2 *>(p.pstat)[slot] = make_float2(m, l);
                 dst = p.pout + slot * D;
@@ -700,7 +767,7 @@ __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
             }
         }
     }
-    const float inv = lsum > 0.0f ? __fdiv_rn(1.0f, lsum) : 0.0f;
+    const float inv = lsum > 0.0f ? __fdiv_rn(1.0f, lsum) : no_key_scale(p);
 #pragma unroll
     for (int q = 0; q < F4; q++)
         dst[q] = make_float4(acc[q].x * inv, acc[q].y * inv, acc[q].z * inv, acc[q].w * inv);
@@ -734,18 +801,34 @@ __global__ void __launch_bounds__(256) prefill_stats_fold(const PrefillParams p)
     p.rstat[(int64_t)pair * 256 + rr] = make_float2(M, Z > 0.0 ? __fdiv_rn(1.0f, (float)Z) : 0.0f);
 }
 
+template <int D, bool MASKED>
+cudaError_t prep_pf_m()
+{
+    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<D, kOnePass, MASKED>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PL<D>::bytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill_kernel<D, kStats, MASKED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)PL<D>::bytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill_kernel<D, kExact, MASKED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)PL<D>::bytes);
+    return e;
+}
+
 template <int D>
 cudaError_t prep_pf()
 {
-    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<D, kOnePass>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)PL<D>::bytes);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(prefill_kernel<D, kStats>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)PL<D>::bytes);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(prefill_kernel<D, kExact>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)PL<D>::bytes);
-    return e;
+    const cudaError_t e = prep_pf_m<D, false>();
+    return e == cudaSuccess ? prep_pf_m<D, true>() : e;
+}
+
+template <int D, bool MASKED>
+void launch_pf_kernel(int which, const CUtensorMap &qmap, const CUtensorMap &kmap, const CUtensorMap &vmap,
+                      const PrefillParams &p, cudaStream_t st)
+{
+    if (which == 0) prefill_kernel<D, kOnePass, MASKED><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p);
+    else if (which == 2) prefill_kernel<D, kStats, MASKED><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p);
+    else prefill_kernel<D, kExact, MASKED><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p);
 }
 
 template <int D>
@@ -753,10 +836,13 @@ cudaError_t launch_pf(int which, const CUtensorMap &qmap, const CUtensorMap &kma
                       const PrefillParams &p, cudaStream_t st)
 {
     switch (which) {
-    case 0: prefill_kernel<D, kOnePass><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p); break;
-    case 2: prefill_kernel<D, kStats><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p); break;
+    case 0:
+    case 2:
+    case 4:
+        if (p.mask) launch_pf_kernel<D, true>(which, qmap, kmap, vmap, p, st);
+        else launch_pf_kernel<D, false>(which, qmap, kmap, vmap, p, st);
+        break;
     case 3: prefill_stats_fold<<<p.hkv * p.nblk, 256, 0, st>>>(p); break;
-    case 4: prefill_kernel<D, kExact><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p); break;
     default: {
         // the fold may be scheduled once every attention CTA has started
         cudaLaunchConfig_t cfg = {};

@@ -80,6 +80,7 @@ def lib():
         "kv_append_bias": (ctypes.c_int, [_vp, _i32, _i64, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp,
                                           _vp, _vp, _vp, _vp]),
         "kv_attend": (ctypes.c_int, [_vp, _i32, _i64, _i32, _vp, _vp]),
+        "kv_attend_mask": (ctypes.c_int, [_vp, _i32, _i64, _i32, _vp, _i32, _i64, ctypes.c_uint32, _vp, _vp]),
         "kv_forward": (ctypes.c_int, [_vp, _i64, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _vp, _vp, _i64,
                                       _vp, _i64, _vp]),
         "kv_export_rows": (ctypes.c_int, [_vp, _i32, _i32, _i64, _i64, _vp]),
@@ -259,6 +260,18 @@ class Context:
 
     def attend(self, layer, n_past, n_new, out, stream=None):
         return _check(lib().kv_attend(self.h, layer, n_past, n_new, _ptr(out), _stream(stream)), "kv_attend")
+
+    def attend_mask(self, layer, n_past, n_new, mask, out, flash=False, stream=None):
+        """kv_attend with the caller's additive mask (a CUDA tensor of n_new rows,
+        float32 or float16, row stride mask.stride(0); None = the implicit causal
+        mask) and the flash-attn branch when flash is true."""
+        mtype, mstride = 0, 0
+        if mask is not None:
+            import torch
+            assert mask.dim() == 2 and mask.stride(1) == 1 and mask.dtype in (torch.float32, torch.float16)
+            mtype, mstride = int(mask.dtype == torch.float16), mask.stride(0)
+        return _check(lib().kv_attend_mask(self.h, layer, n_past, n_new, _ptr(mask), mtype, mstride,
+                                           1 if flash else 0, _ptr(out), _stream(stream)), "kv_attend_mask")
 
     def forward(self, n_past, n_new, q, q_stride, k, k_stride, v, v_stride, in_layer_stride,
                 q_norm_w, k_norm_w, norm_layer_stride, out, out_layer_stride, stream=None):

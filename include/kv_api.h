@@ -169,6 +169,37 @@ int kv_append_bias(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
 int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
               float *out, void *stream);
 
+/* Mask element types and flags of kv_attend_mask. */
+#define KV_MASK_F32    0   /* ggml_soft_max_ext's mask (model.cpp:1437)          */
+#define KV_MASK_F16    1   /* the flash branch's ggml_cast mask (model.cpp:1431) */
+#define KV_ATTN_FLASH  1u  /* the ggml_flash_attn_ext branch (model.cpp:1426-1434) */
+
+/*
+ * kv_attend with the reference's explicit additive mask in place of the
+ * implicit causal one, and the choice of the reference's two attention
+ * branches (decode_session::use_flash_attn, model.h:381-384).  Same call order
+ * and output as kv_attend.
+ *
+ * mask: DEVICE pointer to n_new rows of at least n_past+n_new elements,
+ * mask_stride elements apart (the [n_kv, n_new] mask model.cpp:1579-1586
+ * builds, rows padded as ggml pads them), F32 (KV_MASK_F32) or F16
+ * (KV_MASK_F16); the score of token t and key k is dot*scale + mask[t][k], so
+ * -inf removes the key.  NULL keeps the implicit causal mask.  Rows starting on
+ * 16-byte boundaries are read with vector loads.
+ * flags: 0 = the default branch (ggml_soft_max_ext then ggml_mul_mat: the
+ * normalised weights rounded to F16); KV_ATTN_FLASH = the ggml_flash_attn_ext
+ * branch: the weights exp(s - max) are not normalised before the F16 rounding
+ * (the output is divided by their sum), and a row whose keys are all masked
+ * gives 0 (the default branch gives NaN, as ggml's soft_max of an all -inf
+ * row).  The flash branch's output layout [head_dim, n_head, n_new] is the
+ * same memory order as `out` here.
+ * Returns KV_OK, KV_E_ARG (unknown type or flag, mask_stride < n_past+n_new)
+ * or the codes of kv_attend.
+ */
+int kv_attend_mask(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
+                   const void *mask, int32_t mask_type, int64_t mask_stride,
+                   uint32_t flags, float *out, void *stream);
+
 /*
  * One step of the path over every layer: for layer l in [0, n_layer),
  * kv_append then kv_attend with inputs at q + l*in_layer_stride (likewise k,

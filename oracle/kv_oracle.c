@@ -416,7 +416,16 @@ typedef struct {
     float *w;                /* [n_new][hq][n_kv]  scores, then F16-rounded P */
     float *part;             /* [n_new][hq][n_blocks][d] */
     float *out;
+    const void *mask;        /* NULL: causal; else [n_new] rows of mask_stride (A6) */
+    int64_t mask_stride;
+    int32_t mask_f16, flash;
 } kvo_att;
+
+static float kvo_mask_at(const kvo_att *a, int32_t t, int64_t kk)
+{
+    const int64_t i = (int64_t)t * a->mask_stride + kk;
+    return a->mask_f16 ? kvo_f16_to_f32(((const uint16_t *)a->mask)[i]) : ((const float *)a->mask)[i];
+}
 
 /* phase 1: scores for one (token, kv head, key block), all r heads of the group */
 static void kvo_att_scores(void *vctx, int64_t task)
@@ -428,7 +437,8 @@ static void kvo_att_scores(void *vctx, int64_t task)
     const int64_t rest = task / a->n_blocks;
     const int32_t kvh = (int32_t)(rest % hkv);
     const int32_t t = (int32_t)(rest / hkv);
-    const int64_t lim = a->n_past + t;            /* keys <= lim are visible */
+    /* keys <= lim are visible (causal), or every key with a mask */
+    const int64_t lim = a->mask ? a->n_kv - 1 : a->n_past + t;
     const int64_t k0 = blk * KVO_KEY_BLOCK;
     int64_t k1 = k0 + KVO_KEY_BLOCK;
     if (k1 > a->n_kv) k1 = a->n_kv;
@@ -440,17 +450,33 @@ static void kvo_att_scores(void *vctx, int64_t task)
             if (kk > lim) { w[kk] = -INFINITY; continue; }
             const uint16_t *qrow = a->q16 + ((size_t)t * (size_t)hq + (size_t)h) * (size_t)d;
             w[kk] = kvo_dot16(krow, qrow, d) * a->scale;
+            if (a->mask) w[kk] += kvo_mask_at(a, t, kk);   /* A5: w = s*scale + mask, two roundings */
         }
     }
 }
 
-/* phase 2: softmax of one (token, head) row (A5), then P rounded to F16 (A4) */
+/* phase 2: softmax of one (token, head) row (A5), then P rounded to F16 (A4);
+ * the flash branch (A6) keeps exact weights e/sum in float */
 static void kvo_att_softmax(void *vctx, int64_t task)
 {
     kvo_att *a = (kvo_att *)vctx;
     float *w = a->w + (size_t)task * (size_t)a->n_kv;
     float mx = -INFINITY;
     for (int64_t kk = 0; kk < a->n_kv; kk++) if (w[kk] > mx) mx = w[kk];
+    if (a->flash) {
+        if (mx == -INFINITY) {   /* no visible key: the flash branch's output is 0 */
+            for (int64_t kk = 0; kk < a->n_kv; kk++) w[kk] = 0.0f;
+            return;
+        }
+        double sum = 0.0;
+        for (int64_t kk = 0; kk < a->n_kv; kk++) {
+            const double e = exp((double)w[kk] - (double)mx);
+            w[kk] = (float)e;
+            sum += e;
+        }
+        for (int64_t kk = 0; kk < a->n_kv; kk++) w[kk] = (float)((double)w[kk] / sum);
+        return;
+    }
     double sum = 0.0;
     for (int64_t kk = 0; kk < a->n_kv; kk++) {
         const float e = expf(w[kk] - mx);
@@ -472,7 +498,7 @@ static void kvo_att_pv(void *vctx, int64_t task)
     const int64_t rest = task / a->n_blocks;
     const int32_t kvh = (int32_t)(rest % hkv);
     const int32_t t = (int32_t)(rest / hkv);
-    const int64_t lim = a->n_past + t;
+    const int64_t lim = a->mask ? a->n_kv - 1 : a->n_past + t;
     const int64_t k0 = blk * KVO_KEY_BLOCK;
     int64_t k1 = k0 + KVO_KEY_BLOCK;
     if (k1 > a->n_kv) k1 = a->n_kv;
@@ -506,7 +532,16 @@ int kvo_attend(const kvo_cfg *c, int64_t n_past, int32_t n_new,
                const float *q_roped, const uint16_t *kcache, const uint16_t *vcache,
                float *out, int32_t n_threads)
 {
+    return kvo_attend_ex(c, n_past, n_new, q_roped, kcache, vcache, NULL, 0, 0, 0, out, n_threads);
+}
+
+int kvo_attend_ex(const kvo_cfg *c, int64_t n_past, int32_t n_new,
+                  const float *q_roped, const uint16_t *kcache, const uint16_t *vcache,
+                  const void *mask, int32_t mask_f16, int64_t mask_stride, int32_t flash,
+                  float *out, int32_t n_threads)
+{
     if (!kvo_cfg_ok(c) || n_past < 0 || n_new <= 0) return -1;
+    if (mask && mask_stride < n_past + n_new) return -1;
     const int32_t d = c->head_dim, hq = c->n_head, hkv = c->n_head_kv;
     kvo_att a;
     a.c = c;
@@ -519,6 +554,10 @@ int kvo_attend(const kvo_cfg *c, int64_t n_past, int32_t n_new,
     a.kc = kcache;
     a.vc = vcache;
     a.out = out;
+    a.mask = mask;
+    a.mask_stride = mask_stride;
+    a.mask_f16 = mask_f16;
+    a.flash = flash;
     const size_t nq = (size_t)n_new * (size_t)hq * (size_t)d;
     uint16_t *q16 = (uint16_t *)malloc(sizeof(uint16_t) * nq);
     float *w = (float *)malloc(sizeof(float) * (size_t)n_new * (size_t)hq * (size_t)a.n_kv);

@@ -38,7 +38,14 @@
  *      accumulates products in F32 (summation order is implementation-defined;
  *      parity on attention outputs is therefore judged within a tolerance).
  *   A5 soft_max_ext: w = s*scale + mask, m = max w, e = expf(w - m) in float,
- *      sum accumulated in double, p = e * (float)(1.0/sum).
+ *      sum accumulated in double, p = e * (float)(1.0/sum); a row whose w are
+ *      all -inf gives NaN (expf(-inf - -inf)).
+ *   A6 flash_attn_ext (the opt-in branch, model.cpp:1426-1434) computes the
+ *      same softmax(w) . V with an online softmax and never rounds the
+ *      normalised weights to F16; its CPU kernel's own accumulation order and
+ *      precision are not restated -- the oracle takes the exact weights
+ *      exp(w - m) / sum in double, rounded once to float, with F32 accumulation
+ *      of P . V, and a row whose w are all -inf gives 0 (its sum is 0).
  * The NEOX pairing, the RMSNorm formula and the softmax formula are also
  * cross-checked against the reference's own scalar backend
  * (src/moe_stream/compute_backend.c:42-86), compiled from its sources by
@@ -116,6 +123,15 @@ int kvo_append(const kvo_cfg *c, int64_t n_ctx, int64_t n_past, int32_t n_new,
 int kvo_attend(const kvo_cfg *c, int64_t n_past, int32_t n_new,
                const float *q_roped, const uint16_t *kcache, const uint16_t *vcache,
                float *out, int32_t n_threads);
+
+/* kvo_attend_ex: kvo_attend with the caller's additive mask (NULL: causal) of
+ * n_new rows, mask_stride elements apart, F16 (mask_f16) or F32, added to each
+ * scaled score (A5), and flash != 0 for the ggml_flash_attn_ext branch
+ * (model.cpp:1426-1434) under A6. */
+int kvo_attend_ex(const kvo_cfg *c, int64_t n_past, int32_t n_new,
+                  const float *q_roped, const uint16_t *kcache, const uint16_t *vcache,
+                  const void *mask, int32_t mask_f16, int64_t mask_stride, int32_t flash,
+                  float *out, int32_t n_threads);
 
 /* ---- context sizing (model.cpp:869-885, 1002-1059) ----------------------- */
 uint64_t kvo_kv_cache_bytes(int32_t n_layer, int32_t n_head_kv, int32_t head_dim, int64_t n_ctx);

@@ -65,6 +65,10 @@ def lib():
         L.kvo_attend.restype = ctypes.c_int
         L.kvo_attend.argtypes = [ctypes.POINTER(KvoCfg), ctypes.c_int64, ctypes.c_int32,
                                  _f32p, _u16p, _u16p, _f32p, ctypes.c_int32]
+        L.kvo_attend_ex.restype = ctypes.c_int
+        L.kvo_attend_ex.argtypes = [ctypes.POINTER(KvoCfg), ctypes.c_int64, ctypes.c_int32, _f32p, _u16p, _u16p,
+                                    ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, _f32p,
+                                    ctypes.c_int32]
         L.kvo_kv_cache_bytes.restype = ctypes.c_uint64
         L.kvo_kv_cache_bytes.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64]
         L.kvo_auto_n_ctx.restype = ctypes.c_int64
@@ -161,6 +165,24 @@ class Oracle:
         out = np.zeros((n_new, self.cfg.n_head * self.cfg.head_dim), np.float32)
         rc = lib().kvo_attend(ctypes.byref(self.cfg), n_past, n_new, _p(q_roped),
                               _p(kcache, _u16p), _p(vcache, _u16p), _p(out), n_threads)
+        assert rc == 0, rc
+        return out
+
+
+    def attend_ex(self, kcache, vcache, n_past, q_roped, mask=None, flash=False, n_threads=0):
+        """attend() with the caller's additive mask (a float32 or float16 array of
+        n_new rows of >= n_past+n_new keys; None = causal) and the flash-attn
+        branch (kv_oracle.h A5, A6)."""
+        q_roped = np.ascontiguousarray(q_roped, np.float32)
+        n_new = q_roped.shape[0]
+        out = np.zeros((n_new, self.cfg.n_head * self.cfg.head_dim), np.float32)
+        mptr, mf16, mstride = None, 0, 0
+        if mask is not None:
+            mask = np.ascontiguousarray(mask)
+            assert mask.dtype in (np.float32, np.float16) and mask.shape[0] == n_new
+            mptr, mf16, mstride = mask.ctypes.data, int(mask.dtype == np.float16), mask.shape[1]
+        rc = lib().kvo_attend_ex(ctypes.byref(self.cfg), n_past, n_new, _p(q_roped), _p(kcache, _u16p),
+                                 _p(vcache, _u16p), mptr, mf16, mstride, int(bool(flash)), _p(out), n_threads)
         assert rc == 0, rc
         return out
 

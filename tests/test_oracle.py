@@ -263,6 +263,97 @@ def test_softmax_semantics_against_reference_scalar_backend():
         assert np.allclose(o, got[0, h * d:(h + 1) * d], rtol=0, atol=2e-5)
 
 
+def _causal_mask(n_past, n_new, stride, dtype):
+    m = np.full((n_new, stride), -np.inf, dtype)
+    for t in range(n_new):
+        m[t, : n_past + t + 1] = 0
+    return m
+
+
+def _np_attention_masked(sp, n_past, q_roped, kc, vc, mask, flash):
+    """float64 restatement with an explicit additive mask: the default branch
+    (A5, F16-rounded normalised weights) or the flash branch (A6, exact)."""
+    hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+    r = hq // hkv
+    n_new = q_roped.shape[0]
+    n_kv = n_past + n_new
+    scale = np.float32(1.0) / np.sqrt(np.float32(d))
+    K = kc[:n_kv].view(np.float16).astype(np.float64)
+    V = vc[:n_kv].view(np.float16).astype(np.float64)
+    q16 = q_roped.astype(np.float16).astype(np.float64)
+    out = np.zeros((n_new, hq * d))
+    for t in range(n_new):
+        mrow = mask[t, :n_kv].astype(np.float32)
+        for h in range(hq):
+            kv = h // r
+            s = ((K[:, kv] @ q16[t, h]).astype(np.float32) * scale + mrow).astype(np.float32)
+            if flash:
+                if s.max() == -np.inf:
+                    continue
+                e = np.exp(s.astype(np.float64) - float(s.max()))
+                out[t, h * d:(h + 1) * d] = (e / e.sum()) @ V[:, kv]
+            else:
+                e = np.exp((s - s.max()).astype(np.float64)).astype(np.float32)
+                p = (e * np.float32(1.0 / e.astype(np.float64).sum())).astype(np.float16).astype(np.float64)
+                out[t, h * d:(h + 1) * d] = p @ V[:, kv]
+    return out
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float16])
+def test_explicit_causal_mask_equals_implicit(dtype):
+    """kvo_attend_ex with the causal mask of model.cpp:1579-1586 (padded rows)
+    is kvo_attend bit for bit: adding 0 after the scale changes no score."""
+    case = G.CASES[6]
+    sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
+    orc = O.Oracle(sp)
+    n_past = case["n_past"]
+    q_roped = orc.append(kc, vc, n_past, q, k, v, qn, kn)
+    n_new = q_roped.shape[0]
+    mask = _causal_mask(n_past, n_new, n_past + n_new + 13, dtype)
+    a = orc.attend(kc, vc, n_past, q_roped)
+    b = orc.attend_ex(kc, vc, n_past, q_roped, mask=mask)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.mark.parametrize("flash", [False, True])
+def test_window_mask_matches_float64_restatement(flash):
+    """A sliding-window F16 mask (keys in (pos - 96, pos]) in both branches."""
+    case = G.CASES[6]
+    sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
+    orc = O.Oracle(sp)
+    n_past = case["n_past"]
+    q_roped = orc.append(kc, vc, n_past, q, k, v, qn, kn)
+    n_new = q_roped.shape[0]
+    mask = np.full((n_new, n_past + n_new), -np.inf, np.float16)
+    for t in range(n_new):
+        pos = n_past + t
+        mask[t, max(0, pos - 95): pos + 1] = 0
+    got = orc.attend_ex(kc, vc, n_past, q_roped, mask=mask, flash=flash)
+    want = _np_attention_masked(sp, n_past, q_roped, kc, vc, mask, flash)
+    assert np.abs(got - want).max() < 1e-4
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) < 3e-5
+
+
+def test_flash_branch_and_fully_masked_rows():
+    """The flash branch equals exact softmax(s) . V; a row whose keys are all
+    masked gives 0 there and NaN in the default branch (ggml's soft_max)."""
+    case = G.CASES[6]
+    sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
+    orc = O.Oracle(sp)
+    n_past = case["n_past"]
+    q_roped = orc.append(kc, vc, n_past, q, k, v, qn, kn)
+    n_new = q_roped.shape[0]
+    mask = _causal_mask(n_past, n_new, n_past + n_new, np.float32)
+    mask[0, :] = -np.inf                      # token 0 sees nothing
+    fl = orc.attend_ex(kc, vc, n_past, q_roped, mask=mask, flash=True)
+    de = orc.attend_ex(kc, vc, n_past, q_roped, mask=mask, flash=False)
+    assert np.all(fl[0] == 0.0) and np.all(np.isnan(de[0]))
+    want = _np_attention_masked(sp, n_past, q_roped, kc, vc, mask, True)
+    assert np.abs(fl[1:] - want[1:]).max() < 2e-6
+    # the two branches differ by the F16 rounding of the normalised weights only
+    assert np.abs(fl[1:] - de[1:]).max() < 1e-3
+
+
 def test_attention_thread_count_invariant():
     case = G.CASES[6]
     sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
