@@ -1,7 +1,7 @@
 /*
  * kv_oracle.c -- CPU oracle for the KV-cache append + attention path.
  * TEST INFRASTRUCTURE ONLY (see kv_oracle.h for scope, sources and the
- * assumptions A1-A5 under which it restates ggml's op semantics).
+ * assumptions A1-A6 under which it restates ggml's op semantics).
  *
  * Build: oracle/build.sh (gcc -O3 -ffp-contract=off -pthread).  Contraction
  * must stay off: RoPE and RMSNorm are compared bit-for-bit and their reference

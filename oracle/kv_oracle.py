@@ -3,7 +3,7 @@
 TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
 CPU legs of bench.py, never by the product package.  See kv_oracle.h for what
 is restated from the reference (src/model.cpp:1382-1445, 821-885, 1002-1059)
-and for the assumptions A1-A5 (parity unpinned: ggml is not vendored).
+and for the assumptions A1-A6 (parity unpinned: ggml is not vendored).
 """
 import ctypes
 import os
