@@ -55,8 +55,9 @@ __device__ __forceinline__ bool row_of(const AppendParams &p, int64_t row, int &
     kind = 2;
     h = 0;
     if (row >= (int64_t)p.n_new * rows_per_tok) return false;
-    t = (int)(row / rows_per_tok);
-    const int slot = (int)(row % rows_per_tok);
+    const int r32 = (int)row;   // rows of one call < 2^31: 32-bit division
+    t = r32 / rows_per_tok;
+    const int slot = r32 - t * rows_per_tok;
     if (slot < p.hq_loc) { kind = 0; h = slot; }
     else if (slot < p.hq_loc + p.hkv_loc) { kind = 1; h = slot - p.hq_loc; }
     else { kind = 2; h = slot - p.hq_loc - p.hkv_loc; }
@@ -65,43 +66,26 @@ __device__ __forceinline__ bool row_of(const AppendParams &p, int64_t row, int &
 
 // The mean of a row's squares exactly as ggml computes it, from the G threads'
 // 8 squares each (G a power of two: the row's threads are one aligned group of
-// lanes).  Each square m * 2^(e-150) (m the 24-bit significand) is aligned to
-// the row's largest exponent E as m * 2^(e - E + 31) in a 64-bit integer
-// (terms more than 31 binades below E are truncated: < 128 * 2^(E-181) in
-// all, under 2^-47 of the sum); the sum fits in 62 bits.  Returns false when
-// the rounding test cannot decide (the caller then sums sequentially).
+// lanes).  T = the squares summed in double as a tree (pairs within the
+// thread, then the row's threads by shuffles): every term is >= 0, so T is
+// within log2(8 G) * 2^-53 < 2^-49 of the exact sum.  ggml's sequential double
+// sum is within (D - 1) * 2^-53 < 2^-45.9 of it.  When no float rounding
+// boundary lies within 2^-44 T of T, both round to the same float and the
+// mean is that float / D (D a power of two).  Returns false when the test
+// cannot decide (the caller then sums sequentially).
 template <int G, int D>
 __device__ __forceinline__ bool exact_mean(const float (&sq)[8], float &mean)
 {
-    unsigned emax = 1u;
-    bool special = false;
+    double T = (((double)sq[0] + (double)sq[1]) + ((double)sq[2] + (double)sq[3])) +
+               (((double)sq[4] + (double)sq[5]) + ((double)sq[6] + (double)sq[7]));
 #pragma unroll
-    for (int e = 0; e < 8; e++) {
-        const unsigned eb = (__float_as_uint(sq[e]) >> 23) & 0xFFu;
-        special |= eb == 0xFFu;
-        emax = max(emax, eb);
-    }
-#pragma unroll
-    for (int o = G / 2; o > 0; o >>= 1) emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, o));
-    unsigned long long acc = 0ull;
-#pragma unroll
-    for (int e = 0; e < 8; e++) {
-        const unsigned u = __float_as_uint(sq[e]);
-        const unsigned eb = (u >> 23) & 0xFFu;
-        const unsigned long long m = (u & 0x7FFFFFu) | (eb ? 0x800000u : 0u);
-        const int sh = (int)max(eb, 1u) - (int)emax + 31;
-        acc += sh >= 0 ? m << sh : (sh > -64 ? m >> (-sh) : 0ull);
-    }
-#pragma unroll
-    for (int o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    special = __any_sync(0xffffffffu, special);   // (a warp holds whole rows: any row's inf/nan sends the warp's rows to the chain)
-    if (special) return false;
-    if (acc == 0ull) {   // every square is zero: so is the sequential sum
+    for (int o = 1; o < G; o <<= 1) T += __shfl_xor_sync(0xffffffffu, T, o);
+    // (a warp holds whole rows: any row's inf/nan sends the warp's rows to the chain)
+    if (__any_sync(0xffffffffu, !(T < INFINITY))) return false;
+    if (T == 0.0) {   // every square is zero: so is the sequential sum
         mean = 0.0f;
         return true;
     }
-    // T = acc * 2^(emax - 181), the power of two built in the exponent field
-    const double T = (double)acc * __longlong_as_double((long long)((int)emax - 181 + 1023) << 52);
     if (T < 0x1p-100) return false;   // keep (float)(T / D) far from the subnormal range
     const float f = __double2float_rn(T);   // positive and finite: its neighbours are +-1 ulp
     const double up = 0.5 * ((double)f + (double)__uint_as_float(__float_as_uint(f) + 1u));
@@ -318,8 +302,8 @@ __global__ void __launch_bounds__(256) append_kernel_warp(const AppendParams p)
             for (int e = 0; e < 8; e++) x[e] = __fadd_rn(x[e], __ldg(bias + i0 + e));
     }
 
-    // ---- QK-Norm (see append_kernel) ------------------------------------------
-    if (p.qk_norm) {
+    // ---- QK-Norm (see append_kernel); warps of V rows only skip it --------------
+    if (p.qk_norm && __any_sync(0xffffffffu, rotates)) {
         float sqv[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) sqv[e] = __fmul_rn(x[e], x[e]);
@@ -339,9 +323,10 @@ __global__ void __launch_bounds__(256) append_kernel_warp(const AppendParams p)
         }
         if (rotates) {
             const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-            const float *w = (kind == 0 ? p.q_norm_w : p.k_norm_w) + i0;
+            float wv[8];
+            load8((kind == 0 ? p.q_norm_w : p.k_norm_w) + i0, VEC, wv);   // (VEC: gammas 16-byte aligned too)
 #pragma unroll
-            for (int e = 0; e < 8; e++) x[e] = __fmul_rn(__fmul_rn(x[e], sc), __ldg(w + e));
+            for (int e = 0; e < 8; e++) x[e] = __fmul_rn(__fmul_rn(x[e], sc), wv[e]);
         }
     }
 

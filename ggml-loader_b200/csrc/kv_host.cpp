@@ -497,7 +497,7 @@ int run_append(kv_ctx *ctx, const Pending &pd)
     p.kc = ctx->k_layer(pd.layer); p.vc = ctx->v_layer(pd.layer);
     p.qbuf = ctx->qbuf;
     auto al16 = [](const void *x) { return ((uintptr_t)x & 15u) == 0; };
-    const bool vec = al16(pd.q) && al16(pd.k) && al16(pd.v) &&
+    const bool vec = al16(pd.q) && al16(pd.k) && al16(pd.v) && al16(pd.qn) && al16(pd.kn) &&
                      (pd.n_new == 1 || ((pd.q_stride | pd.k_stride | pd.v_stride) & 3) == 0);
     return launch(ctx, KV_K_APPEND, pd.st, "append kernel", [&] { return kvb::launch_append(ctx->D, vec, p, pd.st); });
 }

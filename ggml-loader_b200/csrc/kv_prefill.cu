@@ -223,12 +223,8 @@ __device__ __forceinline__ void pair_ctas(const PrefillParams &p, int pair, int 
 {
     const int64_t W = (int64_t)p.hkv * p.s_all;
     const int64_t x0 = pair_start(p, pair), x1 = x0 + nt_of(p, pair % p.nblk) - 1;
-    auto cta_of = [&](int64_t x) {
-        int cc = (int)min((int64_t)p.n_cta - 1, x * p.n_cta / W);
-        while (cc + 1 < p.n_cta && cta_lo(p, cc + 1) <= x) cc++;
-        while (cc > 0 && cta_lo(p, cc) > x) cc--;
-        return cc;
-    };
+    // the CTA holding tile x: the largest c with floor(c W / C) <= x
+    auto cta_of = [&](int64_t x) { return (int)(((x + 1) * p.n_cta - 1) / W); };
     ca = cta_of(x0);
     cb = cta_of(x1);
 }
@@ -631,6 +627,9 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                 if (MODE == kOnePass) reinterpret_cast<float2 *>(p.pstat)[slot] = make_float2(m, l);
                 dst = p.pout + slot * D;
             }
+            // a split segment's rows stay in L2 (evict-last) for the fold, past the
+            // K/V tiles other CTAs stream meanwhile
+            const uint64_t pol = policy_evict_last();
 #pragma unroll 1
             for (int ch = 0; ch < D / 32; ch++) {
                 uint32_t o[32];
@@ -638,10 +637,13 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                 tmem_wait_ld();
                 if (valid)
 #pragma unroll
-                    for (int q = 0; q < 8; q++)
-                        *reinterpret_cast<float4 *>(dst + ch * 32 + 4 * q) =
-                            make_float4(__uint_as_float(o[4 * q]) * scl, __uint_as_float(o[4 * q + 1]) * scl,
-                                        __uint_as_float(o[4 * q + 2]) * scl, __uint_as_float(o[4 * q + 3]) * scl);
+                    for (int q = 0; q < 8; q++) {
+                        const float4 val = make_float4(__uint_as_float(o[4 * q]) * scl, __uint_as_float(o[4 * q + 1]) * scl,
+                                                       __uint_as_float(o[4 * q + 2]) * scl,
+                                                       __uint_as_float(o[4 * q + 3]) * scl);
+                        if (whole) *reinterpret_cast<float4 *>(dst + ch * 32 + 4 * q) = val;
+                        else st_v4_hint(dst + ch * 32 + 4 * q, val, pol);
+                    }
             }
             tc_fence_before();
             __syncwarp();
@@ -671,16 +673,18 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
 // ---------------------------------------------------------------------------
 // out = sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i over the pair's segments
 // (CTAs ca..cb in order; the pair is segment 0 of every CTA after ca),
-// scattered to the caller's [token][head][D] rows.  One block per (pair, 32 of
-// its 256 rows), 8 threads a row, D/8 floats a thread; loads go out four
-// segments at a time.  The block finds the pair's CTAs before its
-// grid-dependency wait, so with a programmatic launch that overlaps the
-// attention kernel's tail.
+// scattered to the caller's [token][head][D] rows.  One block per (pair, 16 of
+// its 256 rows), 16 threads a row, D/16 floats a thread.  The statistics and
+// the partial rows of four segments are loaded together (one round trip for
+// the common 2-4 segments; M is raised between groups of four, rescaling what
+// was summed, so the order of the sums is fixed).  The block finds the pair's
+// CTAs before its grid-dependency wait, so with a programmatic launch that
+// overlaps the attention kernel's tail.
 template <int D>
 __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
 {
-    constexpr int F4 = D / 32;   // float4s of a thread
-    const int pair = blockIdx.x >> 3, row0 = (blockIdx.x & 7) * 32;
+    constexpr int F4 = D / 64;   // float4s of a thread
+    const int pair = blockIdx.x >> 4, row0 = (blockIdx.x & 15) * 16;
     __shared__ int info[3];
     if (threadIdx.x == 0) {
         int ca, cb;
@@ -693,7 +697,7 @@ __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
     const int ca = info[0], cb = info[1], seg_a = info[2];
     pdl_wait();   // the attention kernel's partials
     if (ca == cb) return;   // one segment: the attention kernel wrote the rows
-    const int rr = row0 + (int)(threadIdx.x >> 3), part = threadIdx.x & 7;
+    const int rr = row0 + (int)(threadIdx.x >> 4), part = threadIdx.x & 15;
     const int grp = rr >> 7, row = rr & 127;
     const int tok_in = row / p.r, hd = row - tok_in * p.r;
     const int b = pair % p.nblk, kvh = pair / p.nblk;
@@ -702,43 +706,10 @@ __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
     auto slot = [&](int cc) { return (((int64_t)cc * p.kseg + (cc == ca ? seg_a : 0)) * 2 + grp) * 128 + row; };
     float4 *dst = reinterpret_cast<float4 *>(p.out + (int64_t)tok * p.out_stride +
                                              (int64_t)(p.out_head0 + kvh * p.r + hd) * D) + part * F4;
-    if (p.mode == kExact) {   // the segments' rows are final: their sum, CTAs in order
-        float4 acc[F4];
-#pragma unroll
-        for (int q = 0; q < F4; q++) acc[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        for (int c0 = ca; c0 <= cb; c0 += 4) {
-            float4 v[4][F4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const float4 *src = reinterpret_cast<const float4 *>(p.pout + slot(c0 + u <= cb ? c0 + u : c0) * D) +
-                                    part * F4;
-#pragma unroll
-                for (int q = 0; q < F4; q++) v[u][q] = __ldcg(src + q);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-                if (c0 + u <= cb)
-#pragma unroll
-                    for (int q = 0; q < F4; q++) {
-                        acc[q].x += v[u][q].x;
-                        acc[q].y += v[u][q].y;
-                        acc[q].z += v[u][q].z;
-                        acc[q].w += v[u][q].w;
-                    }
-        }
-#pragma unroll
-        for (int q = 0; q < F4; q++) dst[q] = acc[q];
-        return;
-    }
+    const bool exact = p.mode == kExact;   // the segments' rows are final: their sum, CTAs in order
     const float2 *ps = reinterpret_cast<const float2 *>(p.pstat);
-    float M = -INFINITY;
-    for (int c0 = ca; c0 <= cb; c0 += 4) {
-        float m4[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) m4[u] = c0 + u <= cb ? __ldcg(ps + slot(c0 + u)).x : -INFINITY;
-        M = fmaxf(M, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
-    }
-    float lsum = 0.0f;
+    const uint64_t pol = policy_evict_first();
+    float M = -INFINITY, lsum = 0.0f;
     float4 acc[F4];
 #pragma unroll
     for (int q = 0; q < F4; q++) acc[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -749,10 +720,31 @@ __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
         for (int u = 0; u < 4; u++) {
             const bool in = c0 + u <= cb;
             const int64_t sl = slot(in ? c0 + u : c0);
-            st[u] = in ? __ldcg(ps + sl) : make_float2(-INFINITY, 0.0f);
-            const float4 *src = reinterpret_cast<const float4 *>(p.pout + sl * D) + part * F4;
+            st[u] = in && !exact ? __ldcg(ps + sl) : make_float2(-INFINITY, 0.0f);
+            const float *src = p.pout + sl * D + part * F4 * 4;
 #pragma unroll
-            for (int q = 0; q < F4; q++) v[u][q] = __ldcg(src + q);
+            for (int q = 0; q < F4; q++) v[u][q] = ld_cg_v4_hint(src + 4 * q, pol);   // read once: evict first
+        }
+        if (exact) {
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (c0 + u <= cb)
+#pragma unroll
+                    for (int q = 0; q < F4; q++) {
+                        acc[q].x += v[u][q].x;
+                        acc[q].y += v[u][q].y;
+                        acc[q].z += v[u][q].z;
+                        acc[q].w += v[u][q].w;
+                    }
+            continue;
+        }
+        const float mx = fmaxf(fmaxf(M, fmaxf(st[0].x, st[1].x)), fmaxf(st[2].x, st[3].x));
+        if (mx > M) {   // raise M: what was summed is rescaled (never in the first group)
+            const float f = M == -INFINITY ? 0.0f : exp2f(M - mx);
+            lsum *= f;
+#pragma unroll
+            for (int q = 0; q < F4; q++) acc[q] = make_float4(acc[q].x * f, acc[q].y * f, acc[q].z * f, acc[q].w * f);
+            M = mx;
         }
 #pragma unroll
         for (int u = 0; u < 4; u++) {
@@ -766,6 +758,11 @@ __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
                 acc[q].w += v[u][q].w * w;
             }
         }
+    }
+    if (exact) {
+#pragma unroll
+        for (int q = 0; q < F4; q++) dst[q] = acc[q];
+        return;
     }
     const float inv = lsum > 0.0f ? __fdiv_rn(1.0f, lsum) : no_key_scale(p);
 #pragma unroll
@@ -846,7 +843,7 @@ cudaError_t launch_pf(int which, const CUtensorMap &qmap, const CUtensorMap &kma
     default: {
         // the fold may be scheduled once every attention CTA has started
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)(p.hkv * p.nblk * 8));
+        cfg.gridDim = dim3((unsigned)(p.hkv * p.nblk * 16));
         cfg.blockDim = dim3(256);
         cfg.stream = st;
         cudaLaunchAttribute attr[1];

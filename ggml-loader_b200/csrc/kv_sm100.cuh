@@ -111,6 +111,30 @@ __device__ __forceinline__ uint64_t policy_evict_first()
     return pol;
 }
 
+__device__ __forceinline__ uint64_t policy_evict_last()
+{
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// 16-byte store / L2-only load with an L2 eviction-priority policy
+__device__ __forceinline__ void st_v4_hint(float *p, float4 v, uint64_t pol)
+{
+    asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "f"(v.x), "f"(v.y),
+                 "f"(v.z), "f"(v.w), "l"(pol)
+                 : "memory");
+}
+
+__device__ __forceinline__ float4 ld_cg_v4_hint(const float *p, uint64_t pol)
+{
+    float4 v;
+    asm volatile("ld.global.cg.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p), "l"(pol));
+    return v;
+}
+
 __device__ __forceinline__ void tma_load_3d_hint(void *dst, const CUtensorMap *m, uint64_t *bar, int x, int y, int z,
                                                  uint64_t pol)
 {
