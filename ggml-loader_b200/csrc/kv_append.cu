@@ -19,6 +19,8 @@
 // or V.  D/8 threads own a row, each thread 8 consecutive elements, so a
 // thread stores its 8 halves with one 16-byte st.global and a row group writes
 // a contiguous D*2-byte cache segment.  32 rows per block.
+#include <algorithm>
+
 #include "kv_internal.h"
 
 namespace kvb {
@@ -45,6 +47,14 @@ __device__ __forceinline__ void store8_f16(__half *dst, const float x[8])
 #pragma unroll
     for (int e = 0; e < 4; e++) h[e] = __halves2half2(__float2half_rn(x[2 * e]), __float2half_rn(x[2 * e + 1]));
     *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(h);
+}
+
+// cache row of token t: its position, or the position modulo the ring's cells
+// (a ring cache, dory.c:459-472)
+__device__ __forceinline__ int64_t cache_row(const AppendParams &p, int t)
+{
+    const int64_t pos = p.n_past + t;
+    return p.ring ? pos % p.ring : pos;
 }
 
 // row -> (token, kind 0 Q / 1 K / 2 V, head); false past the last row
@@ -246,8 +256,8 @@ __global__ void __launch_bounds__(kRowsPerBlock *(D / 8)) append_kernel(const Ap
     if (!active) return;
     __half *dst;
     if (kind == 0) dst = p.qbuf + ((int64_t)t * p.hq_loc + h) * D;
-    else if (kind == 1) dst = p.kc + ((p.n_past + t) * (int64_t)p.hkv_loc + h) * D;
-    else dst = p.vc + ((p.n_past + t) * (int64_t)p.hkv_loc + h) * D;
+    else if (kind == 1) dst = p.kc + (cache_row(p, t) * p.hkv_loc + h) * D;
+    else dst = p.vc + (cache_row(p, t) * p.hkv_loc + h) * D;
     store8_f16(dst + tig * 8, x);
 }
 
@@ -358,8 +368,8 @@ __global__ void __launch_bounds__(256) append_kernel_warp(const AppendParams p)
     if (!active) return;
     __half *dst;
     if (kind == 0) dst = p.qbuf + ((int64_t)t * p.hq_loc + h) * D;
-    else if (kind == 1) dst = p.kc + ((p.n_past + t) * (int64_t)p.hkv_loc + h) * D;
-    else dst = p.vc + ((p.n_past + t) * (int64_t)p.hkv_loc + h) * D;
+    else if (kind == 1) dst = p.kc + (cache_row(p, t) * p.hkv_loc + h) * D;
+    else dst = p.vc + (cache_row(p, t) * p.hkv_loc + h) * D;
     store8_f16(dst + i0, x);
 }
 
@@ -385,7 +395,34 @@ cudaError_t launch_append_d(bool vec, const AppendParams &p, cudaStream_t st)
     return cudaGetLastError();
 }
 
+// dory_fill_attn_mask (dory.c:553-575) over the n_used cells a ring attention
+// reads: with head = pos0 + n_tokens - 1, cell c was last written at
+// head - ((head - c) mod n_cells) = base + c (- n_cells when c > head mod
+// n_cells), base = head - head mod n_cells; visible (0) to the query at pos0 + q
+// when that write is a real position no later than it, else -inf.  F16 rows of
+// `stride` elements.
+__global__ void __launch_bounds__(256) ring_mask_kernel(__half *dst, int64_t stride, int64_t n_cells, int64_t pos0,
+                                                        int n_tokens, int64_t n_used)
+{
+    const int q = blockIdx.y;
+    const int64_t head = pos0 + n_tokens - 1, hm = head % n_cells, base = head - hm;
+    const __half vis = __float2half_rn(0.0f), hid = __float2half_rn(-INFINITY);
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < n_used; c += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t lw = base + c - (c > hm ? n_cells : 0);
+        dst[(int64_t)q * stride + c] = (lw >= 0 && lw <= pos0 + q) ? vis : hid;
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_ring_mask(__half *dst, int64_t stride, int64_t n_cells, int64_t pos0, int n_tokens, int64_t n_used,
+                             cudaStream_t st)
+{
+    if (n_tokens <= 0 || n_used <= 0) return cudaSuccess;
+    const unsigned bx = (unsigned)std::min<int64_t>((n_used + 255) / 256, 64);
+    ring_mask_kernel<<<dim3(bx, (unsigned)n_tokens), 256, 0, st>>>(dst, stride, n_cells, pos0, n_tokens, n_used);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_append(int D, bool vec_loads, const AppendParams &p, cudaStream_t st)
 {

@@ -304,7 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 // need its completion; every older kernel has completed,
                 // since the previous one let this one start only after its
                 // own griddepcontrol.wait
-                if (!waited && ((!p.fused && k0 + kTK > p.n_past) || (p.hz_row >= k0 && p.hz_row < k0 + kTK))) {
+                if (!waited && (p.wait_first || (!p.fused && k0 + kTK > p.n_past) ||
+                                (p.hz_row >= k0 && p.hz_row < k0 + kTK))) {
                     pdl_wait();
                     waited = true;
                 }
@@ -334,8 +335,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     // the last visible key of each row: the causal bound, or every key with a mask
     const bool masked = EXT && p.mask;
     const bool flash = EXT && p.flash;
-    const int64_t lim_a = masked ? p.n_kv : p.n_past + tok_a;
-    const int64_t lim_b = masked ? p.n_kv : p.n_past + tok_b;
+    const bool all = masked || (EXT && p.all_keys);
+    const int64_t lim_a = all ? p.n_kv : p.n_past + tok_a;
+    const int64_t lim_b = all ? p.n_kv : p.n_past + tok_b;
     float *const Scta = p.S + (int64_t)c * p.S_tiles * kTileScores;
 
     float2 csr[(D + 31) / 32];
@@ -865,7 +867,7 @@ cudaError_t launch(const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnP
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (p.mask || p.flash) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true>, kmap, vmap, p);
+    if (p.mask || p.flash || p.all_keys) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true>, kmap, vmap, p);
     return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, false>, kmap, vmap, p);
 }
 

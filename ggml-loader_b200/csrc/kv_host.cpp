@@ -188,13 +188,16 @@ struct kv_ctx {
     std::vector<float> freq_factors;
     int device = 0;
     int sm_count = 148;
-    int64_t n_ctx = 0;
+    int64_t n_ctx = 0;        // positions (the RoPE table)
+    int64_t rows = 0;         // cache rows: n_ctx, or the ring's cells
+    int64_t ring = 0;         // ring cells (0: linear cache)
+    __half *ring_mask = nullptr;   // ring caches: [n_batch_max][rows] F16 visibility of a chunk
     int D = 0, hq_loc = 0, hkv_loc = 0, r = 1, hq0 = 0, hkv0 = 0;
     int rmax = 0, split_max = 0, max_splits = 0;
     float scale = 1.0f;
 
-    __half *cache = nullptr;  // [n_layer][2][n_ctx][hkv_loc][D]
-    int64_t layer_elems = 0;  // n_ctx * hkv_loc * D
+    __half *cache = nullptr;  // [n_layer][2][rows][hkv_loc][D]
+    int64_t layer_elems = 0;  // rows * hkv_loc * D
     float2 *rope = nullptr;   // [n_ctx][n_rot/2]
     __half *qbuf = nullptr;   // [n_batch_max][hq_loc][D]
     float *S = nullptr;       // score scratch, attn_tile_scores() floats per (CTA, tile)
@@ -398,7 +401,7 @@ void free_all(kv_ctx *ctx)
     if (ctx->comm && nccl().CommDestroy) nccl().CommDestroy(ctx->comm);
     ctx->comm = nullptr;
     void *ptrs[] = {ctx->cache, ctx->rope, ctx->qbuf, ctx->S, ctx->stats, ctx->acc, ctx->ctl, ctx->err,
-                    ctx->local_out, ctx->gathered, ctx->pf_stat, ctx->pf_out, ctx->pf_rstat};
+                    ctx->local_out, ctx->gathered, ctx->pf_stat, ctx->pf_out, ctx->pf_rstat, ctx->ring_mask};
     for (void *p : ptrs)
         if (p) cudaFree(p);
 }
@@ -495,6 +498,7 @@ int run_append(kv_ctx *ctx, const Pending &pd)
     p.n_rot = c.n_rot; p.rope_mode = c.rope_mode; p.qk_norm = c.qk_norm; p.eps = c.rms_eps;
     p.rope = ctx->rope;
     p.kc = ctx->k_layer(pd.layer); p.vc = ctx->v_layer(pd.layer);
+    p.ring = ctx->ring;
     p.qbuf = ctx->qbuf;
     auto al16 = [](const void *x) { return ((uintptr_t)x & 15u) == 0; };
     const bool vec = al16(pd.q) && al16(pd.k) && al16(pd.v) && al16(pd.qn) && al16(pd.kn) &&
@@ -615,15 +619,18 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
         ctx->n_ctx = c.n_ctx;
     }
     c.n_ctx = ctx->n_ctx;
-    if (c.n_batch_max > ctx->n_ctx) c.n_batch_max = (int32_t)ctx->n_ctx;
+    ctx->ring = c.ring_cells > 0 ? std::min<int64_t>(c.ring_cells, ctx->n_ctx) : 0;
+    ctx->rows = ctx->ring ? ctx->ring : ctx->n_ctx;
+    c.ring_cells = ctx->ring;
+    if (c.n_batch_max > ctx->rows) c.n_batch_max = (int32_t)ctx->rows;
 
     const int64_t D = ctx->D;
-    ctx->layer_elems = ctx->n_ctx * ctx->hkv_loc * D;
+    ctx->layer_elems = ctx->rows * ctx->hkv_loc * D;
     const size_t cache_bytes = (size_t)c.n_layer * 2u * (size_t)ctx->layer_elems * sizeof(__half);
     e = cudaMalloc(&ctx->cache, cache_bytes);
     if (e != cudaSuccess) {
-        return bail(fail(KV_E_OOM, "failed to allocate KV cache (%lld positions x %d layers, %.0f MiB requested): %s",
-                         (long long)ctx->n_ctx, c.n_layer, (double)cache_bytes / (1024.0 * 1024.0),
+        return bail(fail(KV_E_OOM, "failed to allocate KV cache (%lld rows x %d layers, %.0f MiB requested): %s",
+                         (long long)ctx->rows, c.n_layer, (double)cache_bytes / (1024.0 * 1024.0),
                          cudaGetErrorString(e)));
     }
     cudaGetLastError();
@@ -643,7 +650,7 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
     // score scratch: CTA c of a launch owns S_tiles(n_kv) tiles from
     // c*S_tiles on; C*S_tiles <= T/128 + 3C for T = hkv_loc*n_kv rows
     ctx->max_cta = std::max(std::min(ctx->sm_count, kvb::attn_max_ctas()), ctx->hkv_loc);
-    ctx->S_floats = ((int64_t)ctx->hkv_loc * ctx->n_ctx / kvb::attn_tile_keys() + 3 * (int64_t)ctx->max_cta + 1) *
+    ctx->S_floats = ((int64_t)ctx->hkv_loc * ctx->rows / kvb::attn_tile_keys() + 3 * (int64_t)ctx->max_cta + 1) *
                     kvb::attn_tile_scores();
     const size_t n_part = (size_t)ctx->max_cta * 2u * 8u;
     struct { void **p; size_t bytes; } allocs[] = {
@@ -653,8 +660,10 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
         {(void **)&ctx->acc, (size_t)ctx->hkv_loc * 8u * (size_t)D * sizeof(long long)},
         {(void **)&ctx->ctl, (2u * (size_t)ctx->hkv_loc + 1u) * sizeof(unsigned)},
         {(void **)&ctx->err, sizeof(unsigned)},
+        {(void **)&ctx->ring_mask, ctx->ring ? (size_t)c.n_batch_max * (size_t)ctx->rows * sizeof(__half) : 0},
     };
     for (auto &a : allocs) {
+        if (a.bytes == 0) continue;
         e = cudaMalloc(a.p, a.bytes);
         if (e != cudaSuccess) return bail(fail(KV_E_OOM, "scratch allocation (%zu bytes): %s", a.bytes, cudaGetErrorString(e)));
     }
@@ -674,7 +683,7 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
     {
         const int bw = kvb::attn_box_width(ctx->D);
         const CUtensorMapSwizzle sw = bw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-        const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)ctx->hkv_loc, (cuuint64_t)ctx->n_ctx};
+        const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)ctx->hkv_loc, (cuuint64_t)ctx->rows};
         const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)ctx->hkv_loc * D * 2};
         const cuuint32_t box[3] = {(cuuint32_t)bw, 1, (cuuint32_t)kvb::attn_tile_keys()};
         for (int l = 0; l < c.n_layer; l++) {
@@ -783,8 +792,10 @@ int kv_append_bias(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
     if (n_new <= 0 || n_past < 0) return fail(KV_E_ARG, "n_new must be > 0 and n_past >= 0");
     if (n_new > c.n_batch_max) return fail(KV_E_RANGE, "n_new %d exceeds n_batch_max %d", n_new, c.n_batch_max);
     if (n_past + n_new > ctx->n_ctx)
-        return fail(KV_E_RANGE, "rows [%lld, %lld) exceed n_ctx %lld", (long long)n_past,
+        return fail(KV_E_RANGE, "positions [%lld, %lld) exceed n_ctx %lld", (long long)n_past,
                     (long long)(n_past + n_new), (long long)ctx->n_ctx);
+    if (ctx->ring && n_new > ctx->ring)   // a batch longer than the ring would overwrite its own rows
+        return fail(KV_E_RANGE, "n_new %d exceeds the ring's %lld cells", n_new, (long long)ctx->ring);
     if (!q || !k || !v) return fail(KV_E_ARG, "q, k and v are required");
     const int64_t D = ctx->D;
     if (n_new > 1 && (q_stride < c.n_head * D || k_stride < c.n_head_kv * D || v_stride < c.n_head_kv * D))
@@ -808,7 +819,7 @@ int kv_append_bias(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
     ctx->last_layer = layer;
     ctx->last_n_past = n_past;
     ctx->last_n_new = n_new;
-    if (n_new == 1 && ctx->r <= kvb::attn_rows()) {
+    if (n_new == 1 && ctx->r <= kvb::attn_rows() && !ctx->ring) {
         // one token: the attention kernels do the append themselves (same bits);
         // any other call on this context first performs it with the append kernel
         ctx->pend = pd;
@@ -911,7 +922,7 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
 
 }  // namespace
 
-static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, const MaskArg &mk, float *out,
+static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, const MaskArg &mk_in, float *out,
                 void *stream)
 {
     if (!ctx) return fail(KV_E_ARG, "NULL context");
@@ -934,7 +945,25 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
         if (rc) return rc;
     }
     const int64_t D = ctx->D;
-    const int64_t n_kv = n_past + n_new;
+    // a ring cache attends over its cells in use: the kernels see them as keys
+    // [0, n_kv), the new tokens' rows among them, under a mask (the caller's,
+    // or dory's visibility built here) or, for one token, every key
+    const int64_t n_kv = ctx->ring ? std::min<int64_t>(ctx->ring, n_past + n_new) : n_past + n_new;
+    const int64_t kpast = n_kv - n_new;   // the kernels' n_past
+    MaskArg mk = mk_in;
+    if (mk.ptr && mk.stride < n_kv)
+        return fail(KV_E_ARG, "mask_stride %lld < the %lld keys attended", (long long)mk.stride, (long long)n_kv);
+    bool all_keys = false;
+    if (ctx->ring && !mk.ptr) {
+        if (n_new == 1) {
+            all_keys = true;
+        } else {
+            KV_CUDA(kvb::launch_ring_mask(ctx->ring_mask, ctx->rows, ctx->ring, n_past, n_new, n_kv, st));
+            mk.ptr = ctx->ring_mask;
+            mk.stride = ctx->rows;
+            mk.f16 = true;
+        }
+    }
     const bool sharded = c.n_shards > 1;
     const bool direct = !sharded || n_new == 1;
     float *dst = direct ? out : ctx->local_out;
@@ -948,7 +977,7 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
     ap.hq0 = ctx->hq0;
     ap.hkv0 = ctx->hkv0;
     ap.n_kv = n_kv;
-    ap.n_past = n_past;
+    ap.n_past = kpast;
     ap.n_cta = decode_ctas(ctx, n_kv);
     ap.scale = ctx->scale;
     ap.fused = fused ? 1 : 0;
@@ -986,6 +1015,8 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
     ap.mask_stride = mk.stride;
     ap.mask_f16 = mk.f16 ? 1 : 0;
     ap.flash = mk.flash ? 1 : 0;
+    ap.all_keys = all_keys ? 1 : 0;
+    ap.wait_first = ctx->ring ? 1 : 0;
     const bool via_peers = sharded && ctx->peers && n_new == 1 && ctx->r <= kvb::attn_rows() &&
                            !(!fused && ctx->pf && n_new * ctx->r >= 32);
     ap.n_peers = via_peers ? c.n_shards : 0;
@@ -1027,7 +1058,7 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
     const int rows_per = kvb::attn_rows();
     const CUtensorMap &km = ctx->kmaps[layer], &vm = ctx->vmaps[layer];
     if (!fused && ctx->pf && rows >= 32) {
-        rc = prefill(ctx, km, vm, n_past, n_new, dst, dst_stride, dst_head0, mk, st);
+        rc = prefill(ctx, km, vm, kpast, n_new, dst, dst_stride, dst_head0, mk, st);
         if (rc) return rc;
     }
     for (int row0 = 0; row0 < rows && !(!fused && ctx->pf && rows >= 32); row0 += rows_per) {
@@ -1080,9 +1111,6 @@ int kv_attend_mask(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, co
     if (mask_type != KV_MASK_F32 && mask_type != KV_MASK_F16)
         return fail(KV_E_ARG, "unknown mask type %d", mask_type);
     if ((flags & ~(uint32_t)KV_ATTN_FLASH) != 0) return fail(KV_E_ARG, "unknown flags 0x%x", flags);
-    if (mask && mask_stride < n_past + n_new)
-        return fail(KV_E_ARG, "mask_stride %lld < n_past + n_new (%lld)", (long long)mask_stride,
-                    (long long)(n_past + n_new));
     MaskArg mk;
     mk.ptr = mask;
     mk.stride = mask ? mask_stride : 0;
@@ -1115,7 +1143,7 @@ static int rows_io(kv_ctx *ctx, int32_t layer, int32_t which, int64_t row0, int6
     if (!ctx || !host) return fail(KV_E_ARG, "NULL argument");
     if (layer < 0 || layer >= ctx->cfg.n_layer || (which != 0 && which != 1))
         return fail(KV_E_ARG, "bad layer or which");
-    if (row0 < 0 || nrows < 0 || row0 + nrows > ctx->n_ctx) return fail(KV_E_RANGE, "rows outside the cache");
+    if (row0 < 0 || nrows < 0 || row0 + nrows > ctx->rows) return fail(KV_E_RANGE, "rows outside the cache");
     int rc = ensure_device(ctx);
     if (rc) return rc;
     rc = flush_pending(ctx);
@@ -1203,7 +1231,7 @@ int kv_debug_inject(kv_ctx *ctx, int32_t what, uint64_t limit_ns)
 int kv_fill_synthetic(kv_ctx *ctx, uint64_t seed, uint64_t stream_base, int64_t row0, int64_t nrows, void *stream)
 {
     if (!ctx) return fail(KV_E_ARG, "NULL context");
-    if (row0 < 0 || nrows < 0 || row0 + nrows > ctx->n_ctx) return fail(KV_E_RANGE, "rows outside the cache");
+    if (row0 < 0 || nrows < 0 || row0 + nrows > ctx->rows) return fail(KV_E_RANGE, "rows outside the cache");
     int rc = ensure_device(ctx);
     if (rc) return rc;
     rc = flush_pending(ctx);
@@ -1215,7 +1243,7 @@ int kv_fill_synthetic(kv_ctx *ctx, uint64_t seed, uint64_t stream_base, int64_t 
     p.hkv_loc = ctx->hkv_loc;
     p.hkv_total = ctx->cfg.n_head_kv;
     p.hkv0 = ctx->hkv0;
-    p.n_ctx = ctx->n_ctx;
+    p.n_ctx = ctx->rows;
     p.row0 = row0;
     p.nrows = nrows;
     p.seed = seed;

@@ -24,11 +24,16 @@ struct AppendParams {
     int32_t n_rot, rope_mode, qk_norm;
     float eps;
     const float2 *rope;              // [n_ctx][n_rot/2] (cos, sin)
-    __half *kc, *vc;                 // layer cache [n_ctx][hkv_loc][D]
+    __half *kc, *vc;                 // layer cache [rows][hkv_loc][D]
     __half *qbuf;                    // [n_new][hq_loc][D]  rotated Q, F16
+    int64_t ring;                    // 0: position p in row p; > 0: in row p % ring (ring cache)
 };
 
 cudaError_t launch_append(int D, bool vec_loads, const AppendParams &p, cudaStream_t st);
+// a ring cache's visibility mask for a chunk at positions [pos0, pos0+n_tokens):
+// [n_tokens] F16 rows of `stride` elements over its n_used cells
+cudaError_t launch_ring_mask(__half *dst, int64_t stride, int64_t n_cells, int64_t pos0, int n_tokens, int64_t n_used,
+                             cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // decode attention (CUDA cores, two passes): scores, then P.V + combine
@@ -124,6 +129,11 @@ struct AttnParams {
     // 1: the flash-attn branch -- weights exp(s - M) rounded to F16 unnormalised,
     // the partial output scaled by 1/Z; a row without a visible key gives 0
     int32_t flash;
+    // 1: every key < n_kv is visible (a ring cache's single token), no causal bound
+    int32_t all_keys;
+    // 1: the producer waits for the previous kernel before its first tile (a ring
+    // cache's new rows may sit in any tile)
+    int32_t wait_first;
     // output
     float *out;
     int64_t out_stride;

@@ -47,6 +47,7 @@ class KvConfig(ctypes.Structure):
         ("longrope_clamp", _i32), ("n_batch_max", _i32), ("device", _i32),
         ("n_shards", _i32), ("shard", _i32),
         ("comm_id", _vp),
+        ("ring_cells", _i64),
     ]
 
 
@@ -145,9 +146,10 @@ def _stream(s):
     return s.cuda_stream
 
 
-def make_config(spec, n_ctx=None, n_batch_max=None, device=-1, n_shards=1, shard=0, comm_id=None):
+def make_config(spec, n_ctx=None, n_batch_max=None, device=-1, n_shards=1, shard=0, comm_id=None, ring_cells=0):
     """A KvConfig from a specs.py dict.  Keeps referenced buffers alive on the
-    returned object (freq factors, comm id)."""
+    returned object (freq factors, comm id).  ring_cells > 0 makes a ring cache
+    (positions bounded by n_ctx, rows = ring_cells)."""
     import numpy as np
     c = KvConfig()
     lib().kv_config_init(ctypes.byref(c))
@@ -176,6 +178,7 @@ def make_config(spec, n_ctx=None, n_batch_max=None, device=-1, n_shards=1, shard
     c.device = device
     c.n_shards = n_shards
     c.shard = shard
+    c.ring_cells = ring_cells
     if comm_id is not None:
         c._id = ctypes.create_string_buffer(bytes(comm_id), 128)
         c.comm_id = ctypes.cast(c._id, _vp)

@@ -88,10 +88,24 @@ typedef struct kv_config {
     int32_t shard;              /* this context's shard index in [0, n_shards)    */
     const void *comm_id;        /* 128-byte id from kv_comm_unique_id() on shard 0,
                                    the same bytes on every shard; n_shards > 1    */
+    int64_t ring_cells;         /* 0: linear cache, position p in row p.  > 0: a
+                                   ring of ring_cells rows (dory.c:391-522), the
+                                   token at position p in row p % ring_cells;
+                                   n_ctx then bounds the positions (RoPE table)  */
 } kv_config;
 
 /* Defaults: NEOX RoPE, base 10000, scale 1, attn factor 1, no YaRN, eps 1e-6,
- * n_ctx 0 (auto), n_batch_max 512, device -1, one shard.  Shape fields 0. */
+ * n_ctx 0 (auto), n_batch_max 512, device -1, one shard, linear cache.  Shape
+ * fields 0.
+ *
+ * Ring caches (ring_cells > 0; dory's sliding and global rings, one context
+ * per ring size, per-loop slots as extra layers): kv_append's n_past is the
+ * position of the first new token (RoPE and the cell p % ring_cells; n_new <=
+ * ring_cells), and kv_attend attends over the min(ring_cells, n_past + n_new)
+ * cells in use with dory_fill_attn_mask's visibility (dory.c:553-575: a cell
+ * is visible to the query at p when its newest write is a real position <= p),
+ * built on the device; kv_attend_mask takes the caller's mask over those cells
+ * instead (mask_stride >= the cells in use). */
 int kv_config_init(kv_config *cfg);
 
 /* Bytes of the whole K+V cache at n_ctx positions, all layers and all shards:

@@ -258,7 +258,22 @@ int kvo_append(const kvo_cfg *c, int64_t n_ctx, int64_t n_past, int32_t n_new,
                const float *q_norm_w, const float *k_norm_w,
                uint16_t *kcache, uint16_t *vcache, float *q_out)
 {
-    if (!kvo_cfg_ok(c) || n_past < 0 || n_new < 0 || n_past + n_new > n_ctx) return -1;
+    if (n_past + n_new > n_ctx) return -1;
+    return kvo_append_ring(c, 0, n_past, n_new, q, q_stride, k, k_stride, v, v_stride, q_norm_w, k_norm_w,
+                           kcache, vcache, q_out);
+}
+
+/* dory_kv_write (dory.c:477-522): the token at position pos goes to cell
+ * pos mod n_cells (dory_kv_runs splits a batch into at most two contiguous
+ * runs; the rows written are the same); n_cells = 0 is the linear cache. */
+int kvo_append_ring(const kvo_cfg *c, int64_t n_cells, int64_t n_past, int32_t n_new,
+                    const float *q, int64_t q_stride,
+                    const float *k, int64_t k_stride,
+                    const float *v, int64_t v_stride,
+                    const float *q_norm_w, const float *k_norm_w,
+                    uint16_t *kcache, uint16_t *vcache, float *q_out)
+{
+    if (!kvo_cfg_ok(c) || n_past < 0 || n_new < 0 || n_cells < 0 || (n_cells > 0 && n_new > n_cells)) return -1;
     if (c->qk_norm && (!q_norm_w || !k_norm_w)) return -1;
     const int32_t d = c->head_dim;
     const int32_t hq = c->n_head, hkv = c->n_head_kv;
@@ -285,10 +300,11 @@ int kvo_append(const kvo_cfg *c, int64_t n_ctx, int64_t n_past, int32_t n_new,
             if (c->qk_norm) { kvo_rms_norm_mul(x, k_norm_w, d, c->rms_eps, tmp); src = tmp; }
             if (half > 0) kvo_rope_row(c, cs, src, rot);
             else memcpy(rot, src, sizeof(float) * (size_t)d);
-            uint16_t *kd = kcache + ((size_t)pos * (size_t)hkv + (size_t)h) * (size_t)d;
+            const int64_t row = n_cells > 0 ? pos % n_cells : pos;
+            uint16_t *kd = kcache + ((size_t)row * (size_t)hkv + (size_t)h) * (size_t)d;
             kvo_f32_to_f16_n(rot, kd, d);
             const float *vx = v + (size_t)t * (size_t)v_stride + (size_t)h * (size_t)d;
-            uint16_t *vd = vcache + ((size_t)pos * (size_t)hkv + (size_t)h) * (size_t)d;
+            uint16_t *vd = vcache + ((size_t)row * (size_t)hkv + (size_t)h) * (size_t)d;
             kvo_f32_to_f16_n(vx, vd, d);
         }
     }
@@ -576,6 +592,23 @@ int kvo_attend_ex(const kvo_cfg *c, int64_t n_past, int32_t n_new,
     free(w);
     free(part);
     return 0;
+}
+
+/* dory_fill_attn_mask (dory.c:553-575): with head = pos0 + n_tokens - 1, cell c
+ * is visible to the query at p = pos0 + q iff the newest write into it,
+ * head - ((head - c) mod n_cells), is a real position (>= 0) no later than p. */
+void kvo_ring_mask(int64_t n_cells, int64_t pos0, int32_t n_tokens, float *dst)
+{
+    const int64_t head = pos0 + n_tokens - 1;
+    for (int32_t q = 0; q < n_tokens; q++) {
+        const int64_t p = pos0 + q;
+        for (int64_t cc = 0; cc < n_cells; cc++) {
+            int64_t m = (head - cc) % n_cells;
+            if (m < 0) m += n_cells;
+            const int64_t last_write = head - m;
+            dst[(size_t)q * (size_t)n_cells + (size_t)cc] = (last_write >= 0 && last_write <= p) ? 0.0f : -INFINITY;
+        }
+    }
 }
 
 /* ======================================================================== */

@@ -124,6 +124,18 @@ int kvo_attend(const kvo_cfg *c, int64_t n_past, int32_t n_new,
                const float *q_roped, const uint16_t *kcache, const uint16_t *vcache,
                float *out, int32_t n_threads);
 
+/* Ring cache (dory.c:391-575): kvo_append_ring writes the token at position p
+ * to cell p mod n_cells (0: the linear cache, as kvo_append), RoPE at p;
+ * kvo_ring_mask fills dory_fill_attn_mask's [n_tokens][n_cells] F32 0/-inf
+ * visibility for a batch at positions [pos0, pos0+n_tokens). */
+int kvo_append_ring(const kvo_cfg *c, int64_t n_cells, int64_t n_past, int32_t n_new,
+                    const float *q, int64_t q_stride,
+                    const float *k, int64_t k_stride,
+                    const float *v, int64_t v_stride,
+                    const float *q_norm_w, const float *k_norm_w,
+                    uint16_t *kcache, uint16_t *vcache, float *q_out);
+void kvo_ring_mask(int64_t n_cells, int64_t pos0, int32_t n_tokens, float *dst);
+
 /* kvo_attend_ex: kvo_attend with the caller's additive mask (NULL: causal) of
  * n_new rows, mask_stride elements apart, F16 (mask_f16) or F32, added to each
  * scaled score (A5), and flash != 0 for the ggml_flash_attn_ext branch

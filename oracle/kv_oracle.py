@@ -65,6 +65,12 @@ def lib():
         L.kvo_attend.restype = ctypes.c_int
         L.kvo_attend.argtypes = [ctypes.POINTER(KvoCfg), ctypes.c_int64, ctypes.c_int32,
                                  _f32p, _u16p, _u16p, _f32p, ctypes.c_int32]
+        L.kvo_append_ring.restype = ctypes.c_int
+        L.kvo_append_ring.argtypes = [ctypes.POINTER(KvoCfg), ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                      _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, _f32p, ctypes.c_int64,
+                                      _f32p, _f32p, _u16p, _u16p, _f32p]
+        L.kvo_ring_mask.restype = None
+        L.kvo_ring_mask.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, _f32p]
         L.kvo_attend_ex.restype = ctypes.c_int
         L.kvo_attend_ex.argtypes = [ctypes.POINTER(KvoCfg), ctypes.c_int64, ctypes.c_int32, _f32p, _u16p, _u16p,
                                     ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, _f32p,
@@ -159,6 +165,34 @@ class Oracle:
         assert rc == 0, rc
         return q_out
 
+    def append_ring(self, kcache, vcache, pos0, q, k, v, q_norm_w=None, k_norm_w=None):
+        """append() into a ring cache: kcache/vcache are uint16 [n_cells, hkv, d];
+        the token at position p goes to cell p % n_cells (dory.c:459-522)."""
+        n_new = q.shape[0]
+        for a in (q, k, v):
+            assert a.dtype == np.float32 and a.strides[1] == 4
+        assert kcache.flags.c_contiguous and vcache.flags.c_contiguous
+        d, hq = self.cfg.head_dim, self.cfg.n_head
+        q_out = np.zeros((n_new, hq, d), np.float32)
+        qn = None if q_norm_w is None else np.ascontiguousarray(q_norm_w, np.float32)
+        kn = None if k_norm_w is None else np.ascontiguousarray(k_norm_w, np.float32)
+        rc = lib().kvo_append_ring(ctypes.byref(self.cfg), kcache.shape[0], pos0, n_new,
+                                   _p(q), q.strides[0] // 4, _p(k), k.strides[0] // 4, _p(v), v.strides[0] // 4,
+                                   _p(qn), _p(kn), _p(kcache, _u16p), _p(vcache, _u16p), _p(q_out))
+        assert rc == 0, rc
+        return q_out
+
+    def attend_ring(self, kcache, vcache, pos0, q_roped, mask=None, flash=False, n_threads=0):
+        """Attention over a ring cache's cells in use (min(n_cells, pos0 + n_new))
+        with dory's visibility mask (ring_mask), or the caller's mask over them."""
+        n_new = q_roped.shape[0]
+        n_cells = kcache.shape[0]
+        n_used = min(n_cells, pos0 + n_new)
+        if mask is None:
+            mask = np.ascontiguousarray(ring_mask(n_cells, pos0, n_new)[:, :n_used])
+        return self.attend_ex(kcache, vcache, n_used - n_new, q_roped, mask=mask, flash=flash,
+                              n_threads=n_threads)
+
     def attend(self, kcache, vcache, n_past, q_roped, n_threads=0):
         q_roped = np.ascontiguousarray(q_roped, np.float32)
         n_new = q_roped.shape[0]
@@ -188,6 +222,13 @@ class Oracle:
 
 
 # -- generators and helpers --------------------------------------------------
+
+def ring_mask(n_cells, pos0, n_tokens):
+    """dory_fill_attn_mask (dory.c:553-575) as F32 [n_tokens][n_cells] 0 / -inf."""
+    out = np.empty((n_tokens, n_cells), np.float32)
+    lib().kvo_ring_mask(n_cells, pos0, n_tokens, _p(out))
+    return out
+
 
 def f32_to_f16_bits(x):
     x = np.ascontiguousarray(x, np.float32)

@@ -166,4 +166,9 @@ def test_mask_arguments_are_checked(cuda):
     lib = K.lib()
     assert lib.kv_attend_mask(run.ctx.h, 0, 100, 1, m.data_ptr(), 7, 101, 0, out.data_ptr(), None) == K.KV_E_ARG
     assert lib.kv_attend_mask(run.ctx.h, 0, 100, 1, m.data_ptr(), 0, 101, 4, out.data_ptr(), None) == K.KV_E_ARG
+    # a stride shorter than the keys attended (checked once the call follows its append)
+    rows = torch.zeros((1, (sp["n_head"] + 2 * sp["n_head_kv"]) * sp["head_dim"]), device=cuda)
+    base, w, hd = rows.data_ptr(), rows.shape[1], sp["head_dim"]
+    run.ctx.append(0, 100, 1, base, w, base + 4 * sp["n_head"] * hd, w,
+                   base + 4 * (sp["n_head"] + sp["n_head_kv"]) * hd, w)
     assert lib.kv_attend_mask(run.ctx.h, 0, 100, 1, m.data_ptr(), 0, 50, 0, out.data_ptr(), None) == K.KV_E_ARG

@@ -354,6 +354,57 @@ def test_flash_branch_and_fully_masked_rows():
     assert np.abs(fl[1:] - de[1:]).max() < 1e-3
 
 
+def _dory_mask(n_cells, pos0, n_tokens):
+    """dory_fill_attn_mask (dory.c:553-575), restated with Python's floor mod."""
+    head = pos0 + n_tokens - 1
+    m = np.full((n_tokens, n_cells), -np.inf, np.float32)
+    for q in range(n_tokens):
+        for c in range(n_cells):
+            lw = head - ((head - c) % n_cells)
+            if 0 <= lw <= pos0 + q:
+                m[q, c] = 0.0
+    return m
+
+
+@pytest.mark.parametrize("n_cells,pos0,n_tokens", [(8, 0, 1), (8, 5, 3), (4, 6, 3), (16, 40, 16), (7, 3, 7),
+                                                   (32, 100, 1), (1, 9, 1)])
+def test_ring_mask_matches_dory_rule(n_cells, pos0, n_tokens):
+    assert np.array_equal(O.ring_mask(n_cells, pos0, n_tokens), _dory_mask(n_cells, pos0, n_tokens))
+
+
+def test_ring_append_rows_and_attention():
+    """kvo_append_ring puts position p in cell p % n_cells with the linear
+    append's bits; attend_ring over the cells equals the linear attention
+    restricted to the visible positions (a ring holding the last n_cells)."""
+    case = G.CASES[6]
+    sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
+    orc = O.Oracle(sp)
+    hkv, d = sp["n_head_kv"], sp["head_dim"]
+    n_cells, n_pos = 16, 40
+    lin_k = np.zeros((n_pos, hkv, d), np.uint16)
+    lin_v = np.zeros((n_pos, hkv, d), np.uint16)
+    ring_k = np.zeros((n_cells, hkv, d), np.uint16)
+    ring_v = np.zeros((n_cells, hkv, d), np.uint16)
+    for pos0 in range(0, n_pos, 5):
+        rr = synth.qkv_rows(sp, pos0, 0, 5)
+        hq = sp["n_head"]
+        qq, kk, vv = rr[:, :hq * d], rr[:, hq * d:(hq + hkv) * d], rr[:, (hq + hkv) * d:]
+        a = orc.append(lin_k, lin_v, pos0, qq, kk, vv, qn, kn)
+        b = orc.append_ring(ring_k, ring_v, pos0, qq, kk, vv, qn, kn)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+        for t in range(5):
+            assert np.array_equal(ring_k[(pos0 + t) % n_cells], lin_k[pos0 + t])
+            assert np.array_equal(ring_v[(pos0 + t) % n_cells], lin_v[pos0 + t])
+        got = orc.attend_ring(ring_k, ring_v, pos0, b)
+        # the same attention on the linear cache: keys (head - n_cells, p] visible
+        head = pos0 + 4
+        mask = np.full((5, pos0 + 5), -np.inf, np.float32)
+        for t in range(5):
+            mask[t, max(0, head - n_cells + 1): pos0 + t + 1] = 0
+        want = orc.attend_ex(lin_k, lin_v, pos0, b, mask=mask)
+        assert np.abs(got - want).max() < 2e-6
+
+
 def test_attention_thread_count_invariant():
     case = G.CASES[6]
     sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
