@@ -265,6 +265,31 @@ __global__ void __launch_bounds__(kRowsPerBlock *(D / 8)) append_kernel(const Ap
 // row's D/8 threads are one aligned group of lanes, so the NEOX
 // partners, the norm's sum and its rare sequential fallback move by shuffles
 // -- no shared memory, no block barrier.  Same arithmetic as append_kernel.
+// ggml's mean of a row's squares (A1) for the G threads holding it, 8 values
+// each: exact_mean, else (one row in about a million) the sequential double sum
+// with lane 0 of the row's group gathering the squares in element order.  Every
+// lane of the warp calls it.
+template <int G, int D>
+__device__ __forceinline__ float row_mean(const float (&x)[8], bool rotates, int lane)
+{
+    float sqv[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) sqv[e] = __fmul_rn(x[e], x[e]);
+    float mean = 0.0f;
+    const bool need = !exact_mean<G, D>(sqv, mean);
+    if (__any_sync(0xffffffffu, rotates && need)) {
+        const int base = (lane / G) * G;
+        double sum = 0.0;
+#pragma unroll 1
+        for (int s2 = 0; s2 < G; s2++)
+#pragma unroll
+            for (int e = 0; e < 8; e++) sum = __dadd_rn(sum, (double)__shfl_sync(0xffffffffu, sqv[e], base + s2));
+        const float cm = __double2float_rn(__ddiv_rn(sum, (double)D));
+        if (need) mean = cm;
+    }
+    return mean;
+}
+
 template <int D, bool VEC>
 __global__ void __launch_bounds__(256) append_kernel_warp(const AppendParams p)
 {
@@ -313,24 +338,8 @@ __global__ void __launch_bounds__(256) append_kernel_warp(const AppendParams p)
     }
 
     // ---- QK-Norm (see append_kernel); warps of V rows only skip it --------------
-    if (p.qk_norm && __any_sync(0xffffffffu, rotates)) {
-        float sqv[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) sqv[e] = __fmul_rn(x[e], x[e]);
-        float mean = 0.0f;
-        const bool need = !exact_mean<G, D>(sqv, mean);
-        if (__any_sync(0xffffffffu, rotates && need)) {
-            // the sequential double sum, lane 0 of the row's group gathering the
-            // squares in element order
-            const int base = (lane / G) * G;
-            double sum = 0.0;
-#pragma unroll 1
-            for (int s2 = 0; s2 < G; s2++)
-#pragma unroll
-                for (int e = 0; e < 8; e++) sum = __dadd_rn(sum, (double)__shfl_sync(0xffffffffu, sqv[e], base + s2));
-            const float cm = __double2float_rn(__ddiv_rn(sum, (double)D));
-            if (need) mean = cm;
-        }
+    if (p.qk_norm == 1 && __any_sync(0xffffffffu, rotates)) {
+        const float mean = row_mean<G, D>(x, rotates, lane);
         if (rotates) {
             const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
             float wv[8];
@@ -365,6 +374,24 @@ __global__ void __launch_bounds__(256) append_kernel_warp(const AppendParams p)
         }
     }
 
+    // ---- nGPT (dory, qk_norm 2; dory.c:577-580, 646-649): after RoPE,
+    // rms_norm(x, 1e-6/D) (ggml's arithmetic, as QK-Norm) times 1/sqrt(D), then
+    // Q times its per-head, per-channel scale (q_norm_w [n_head][D]); K unscaled
+    if (p.qk_norm == 2 && __any_sync(0xffffffffu, rotates)) {
+        const float mean = row_mean<G, D>(x, rotates, lane);
+        if (rotates) {
+            const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+#pragma unroll
+            for (int e = 0; e < 8; e++) x[e] = __fmul_rn(__fmul_rn(x[e], sc), p.post);
+            if (kind == 0) {
+                float wv[8];
+                load8(p.q_norm_w + (int64_t)(p.hq0 + h) * D + i0, VEC, wv);
+#pragma unroll
+                for (int e = 0; e < 8; e++) x[e] = __fmul_rn(x[e], wv[e]);
+            }
+        }
+    }
+
     if (!active) return;
     __half *dst;
     if (kind == 0) dst = p.qbuf + ((int64_t)t * p.hq_loc + h) * D;
@@ -379,9 +406,10 @@ cudaError_t launch_append_d(bool vec, const AppendParams &p, cudaStream_t st)
     const int64_t rows = (int64_t)p.n_new * (p.hq_loc + 2 * p.hkv_loc);
     const int64_t blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
     if (blocks <= 0) return cudaSuccess;
-    if constexpr (D == 64 || D == 128) {
+    if constexpr (D == 64 || D == 128 || D == 256) {
         // shuffle-only kernel: RoPE over the whole head (or none); partial
-        // rotary takes append_kernel
+        // rotary takes append_kernel (head_dim <= 128), as does a partial
+        // rotation with the nGPT norm nowhere (dory rotates whole heads)
         if (p.n_rot == 0 || p.n_rot == D) {
             const int64_t wblocks = (rows * (D / 8) + 255) / 256;
             if (vec) append_kernel_warp<D, true><<<(unsigned)wblocks, 256, 0, st>>>(p);
@@ -389,10 +417,15 @@ cudaError_t launch_append_d(bool vec, const AppendParams &p, cudaStream_t st)
             return cudaGetLastError();
         }
     }
+    if constexpr (D == 256) {
+        return cudaErrorInvalidValue;   // partial rotation at head_dim 256: not built
+    } else {
+    if (p.qk_norm == 2) return cudaErrorInvalidValue;   // the nGPT norm needs whole-head rotation
     const dim3 grid((unsigned)blocks), block(kRowsPerBlock * (D / 8));
     if (vec) append_kernel<D, true><<<grid, block, 0, st>>>(p);
     else append_kernel<D, false><<<grid, block, 0, st>>>(p);
     return cudaGetLastError();
+    }
 }
 
 // dory_fill_attn_mask (dory.c:553-575) over the n_used cells a ring attention
@@ -430,6 +463,7 @@ cudaError_t launch_append(int D, bool vec_loads, const AppendParams &p, cudaStre
     case 64: return launch_append_d<64>(vec_loads, p, st);
     case 96: return launch_append_d<96>(vec_loads, p, st);
     case 128: return launch_append_d<128>(vec_loads, p, st);
+    case 256: return launch_append_d<256>(vec_loads, p, st);
     default: return cudaErrorInvalidValue;
     }
 }

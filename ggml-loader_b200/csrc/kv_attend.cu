@@ -64,6 +64,7 @@ template <int D> struct G4;
 template <> struct G4<64>  { static constexpr int BW = 64, NS = 11; };
 template <> struct G4<96>  { static constexpr int BW = 32, NS = 7; };
 template <> struct G4<128> { static constexpr int BW = 64, NS = 5; };
+template <> struct G4<256> { static constexpr int BW = 64, NS = 2; };   // 64 KB stages; the V-phase buffer takes 66 KB
 
 template <int BW>
 __device__ __forceinline__ uint32_t swz(int row, int chunk)
@@ -885,6 +886,7 @@ cudaError_t attn_prepare(int D)
     case 64: return prep<64>();
     case 96: return prep<96>();
     case 128: return prep<128>();
+    case 256: return prep<256>();
     default: return cudaErrorInvalidValue;
     }
 }
@@ -897,6 +899,7 @@ cudaError_t launch_attn(int D, const CUtensorMap &kmap, const CUtensorMap &vmap,
     case 64: return launch<64>(kmap, vmap, p, st, pdl);
     case 96: return launch<96>(kmap, vmap, p, st, pdl);
     case 128: return launch<128>(kmap, vmap, p, st, pdl);
+    case 256: return launch<256>(kmap, vmap, p, st, pdl);
     default: return cudaErrorInvalidValue;
     }
 }

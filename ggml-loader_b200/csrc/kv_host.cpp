@@ -259,8 +259,8 @@ bool shape_ok(const kv_config *c, std::string &why)
 {
     char buf[256];
     if (c->n_layer <= 0 || c->n_head <= 0 || c->n_head_kv <= 0) { why = "n_layer, n_head and n_head_kv must be > 0"; return false; }
-    if (c->head_dim != 64 && c->head_dim != 96 && c->head_dim != 128) {
-        snprintf(buf, sizeof(buf), "head_dim %d unsupported (64, 96, 128)", c->head_dim);
+    if (c->head_dim != 64 && c->head_dim != 96 && c->head_dim != 128 && c->head_dim != 256) {
+        snprintf(buf, sizeof(buf), "head_dim %d unsupported (64, 96, 128, 256)", c->head_dim);
         why = buf;
         return false;
     }
@@ -268,6 +268,11 @@ bool shape_ok(const kv_config *c, std::string &why)
     if (c->n_rot < 0 || c->n_rot > c->head_dim || (c->n_rot & 1)) { why = "n_rot must be even and <= head_dim"; return false; }
     if (c->rope_mode != KV_ROPE_NORMAL && c->rope_mode != KV_ROPE_NEOX) { why = "rope_mode must be 0 (NORMAL) or 2 (NEOX)"; return false; }
     if (c->n_rot > 0 && !(c->rope_base > 0.0f)) { why = "rope_base must be > 0"; return false; }
+    if (c->qk_norm < 0 || c->qk_norm > 2) { why = "qk_norm must be 0, 1 (RMSNorm) or 2 (nGPT)"; return false; }
+    if ((c->head_dim == 256 || c->qk_norm == 2) && c->n_rot != 0 && c->n_rot != c->head_dim) {
+        why = "head_dim 256 and the nGPT norm rotate whole heads (n_rot 0 or head_dim)";
+        return false;
+    }
     if (c->rope_ext_factor != 0.0f && c->n_ctx_orig <= 0) { why = "YaRN (ext_factor != 0) needs n_ctx_orig > 0"; return false; }
     const int ns = c->n_shards <= 1 ? 1 : c->n_shards;
     if (c->n_head_kv % ns != 0) { why = "n_head_kv must be a multiple of n_shards"; return false; }
@@ -495,7 +500,10 @@ int run_append(kv_ctx *ctx, const Pending &pd)
     p.q_bias = pd.qb; p.k_bias = pd.kb; p.v_bias = pd.vb;
     p.n_new = pd.n_new; p.n_past = pd.n_past;
     p.hq_loc = ctx->hq_loc; p.hkv_loc = ctx->hkv_loc; p.hq0 = ctx->hq0; p.hkv0 = ctx->hkv0;
-    p.n_rot = c.n_rot; p.rope_mode = c.rope_mode; p.qk_norm = c.qk_norm; p.eps = c.rms_eps;
+    p.n_rot = c.n_rot; p.rope_mode = c.rope_mode; p.qk_norm = c.qk_norm;
+    // nGPT's L2 norm is rms_norm(x, 1e-6 / D) * (1 / sqrt(D)) (dory.c:577-580)
+    p.eps = c.qk_norm == 2 ? c.rms_eps / (float)ctx->D : c.rms_eps;
+    p.post = 1.0f / sqrtf((float)ctx->D);
     p.rope = ctx->rope;
     p.kc = ctx->k_layer(pd.layer); p.vc = ctx->v_layer(pd.layer);
     p.ring = ctx->ring;
@@ -800,7 +808,8 @@ int kv_append_bias(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
     const int64_t D = ctx->D;
     if (n_new > 1 && (q_stride < c.n_head * D || k_stride < c.n_head_kv * D || v_stride < c.n_head_kv * D))
         return fail(KV_E_ARG, "row strides shorter than a token's heads");
-    if (c.qk_norm && (!q_norm_w || !k_norm_w)) return fail(KV_E_ARG, "qk_norm needs q_norm_w and k_norm_w");
+    if (c.qk_norm == 1 && (!q_norm_w || !k_norm_w)) return fail(KV_E_ARG, "qk_norm needs q_norm_w and k_norm_w");
+    if (c.qk_norm == 2 && !q_norm_w) return fail(KV_E_ARG, "the nGPT norm needs q_norm_w (Q's per-channel scale)");
     int rc = ensure_device(ctx);
     if (rc) return rc;
     rc = flush_pending(ctx);
@@ -819,7 +828,7 @@ int kv_append_bias(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
     ctx->last_layer = layer;
     ctx->last_n_past = n_past;
     ctx->last_n_new = n_new;
-    if (n_new == 1 && ctx->r <= kvb::attn_rows() && !ctx->ring) {
+    if (n_new == 1 && ctx->r <= kvb::attn_rows() && !ctx->ring && c.qk_norm != 2) {
         // one token: the attention kernels do the append themselves (same bits);
         // any other call on this context first performs it with the append kernel
         ctx->pend = pd;

@@ -21,8 +21,9 @@ struct AppendParams {
     int64_t n_past;
     int32_t hq_loc, hkv_loc;         // heads owned by this context
     int32_t hq0, hkv0;               // first owned global head
-    int32_t n_rot, rope_mode, qk_norm;
-    float eps;
+    int32_t n_rot, rope_mode, qk_norm;   // qk_norm: 0 none, 1 RMSNorm * gamma before RoPE, 2 nGPT after RoPE
+    float eps;                       // RMSNorm's eps (nGPT: 1e-6 / D)
+    float post;                      // nGPT: 1 / sqrt(D)
     const float2 *rope;              // [n_ctx][n_rot/2] (cos, sin)
     __half *kc, *vc;                 // layer cache [rows][hkv_loc][D]
     __half *qbuf;                    // [n_new][hq_loc][D]  rotated Q, F16

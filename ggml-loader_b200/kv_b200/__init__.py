@@ -169,7 +169,7 @@ def make_config(spec, n_ctx=None, n_batch_max=None, device=-1, n_shards=1, shard
     ff = spec.get("rope_freq_factors")
     c._ff = None if ff is None else np.ascontiguousarray(ff, dtype=np.float32)
     c.rope_freq_factors = None if c._ff is None else c._ff.ctypes.data_as(_f32p)
-    c.qk_norm = 1 if spec.get("qk_norm") else 0
+    c.qk_norm = int(spec.get("qk_norm") or 0)   # True -> 1 (RMSNorm); 2 = nGPT
     c.rms_eps = spec.get("rms_eps", 1e-6)
     c.n_ctx = spec.get("n_ctx", 0) if n_ctx is None else n_ctx
     c.n_ctx_train = spec.get("n_ctx_train", 0)

@@ -63,7 +63,9 @@ typedef struct kv_config {
     int32_t n_layer;            /* hparams::n_layer                               */
     int32_t n_head;             /* hparams::n_head (query heads, whole model)     */
     int32_t n_head_kv;          /* hparams::n_head_kv                             */
-    int32_t head_dim;           /* hparams::n_embd_head; 64, 96 or 128            */
+    int32_t head_dim;           /* hparams::n_embd_head; 64, 96, 128 or 256 (256:
+                                   whole-head RoPE; chunks run on the decode
+                                   kernel, the tensor-core kernel takes 64/128)  */
     int32_t n_rot;              /* hparams::n_rot (even, <= head_dim)             */
     int32_t rope_mode;          /* KV_ROPE_NORMAL (llama) / KV_ROPE_NEOX (others) */
     float   rope_base;          /* hparams::rope_freq_base                        */
@@ -76,7 +78,12 @@ typedef struct kv_config {
     const float *rope_freq_factors; /* HOST [n_rot/2] or NULL; copied by kv_alloc.
                                    phi3 rope_factors_short (model.cpp:555-557) or
                                    llama3 rope_freqs                             */
-    int32_t qk_norm;            /* hparams::has_qk_norm (qwen3)                   */
+    int32_t qk_norm;            /* 1: hparams::has_qk_norm (qwen3): RMSNorm * gamma
+                                   before RoPE.  2: dory's nGPT handling
+                                   (dory.c:577-580, 646-649): after RoPE,
+                                   rms_norm(x, rms_eps/head_dim) / sqrt(head_dim),
+                                   Q then times q_norm_w [n_head][head_dim] (the
+                                   squared learned scale); k_norm_w unused     */
     float   rms_eps;            /* hparams::rms_eps                               */
     int64_t n_ctx;              /* cache positions; 0 = auto from free HBM         */
     int64_t n_ctx_train;        /* auto-sizing clamp; 0 = 262144 cap              */

@@ -237,6 +237,25 @@ void kvo_rms_norm_mul(const float *x, const float *w, int32_t n, float eps, floa
     }
 }
 
+/* dory's L2 norm (dory.c:577-580): ggml_scale(ggml_rms_norm(x, 1e-6f/n),
+ * 1.0f/sqrtf(n)) -- A1's rms_norm with eps/n, then a float multiply -- and, for
+ * Q, ggml_mul by the squared learned scale w (NULL for K; dory.c:646-649). */
+void kvo_ngpt_norm(const float *x, const float *w, int32_t n, float eps, float *y)
+{
+    double sum = 0.0;
+    for (int32_t i = 0; i < n; i++) {
+        const float sq = x[i] * x[i];
+        sum += (double)sq;
+    }
+    const float mean = (float)(sum / (double)n);
+    const float scale = 1.0f / sqrtf(mean + eps / (float)n);
+    const float post = 1.0f / sqrtf((float)n);
+    for (int32_t i = 0; i < n; i++) {
+        const float t = (x[i] * scale) * post;
+        y[i] = w ? t * w[i] : t;
+    }
+}
+
 /* ======================================================================== */
 /* append: model.cpp:1382-1414                                               */
 /* ======================================================================== */
@@ -248,6 +267,7 @@ static int kvo_cfg_ok(const kvo_cfg *c)
     if (c->n_head % c->n_head_kv != 0) return 0;
     if (c->n_rot < 0 || c->n_rot > c->head_dim || (c->n_rot & 1)) return 0;
     if (c->rope_mode != 0 && c->rope_mode != 2) return 0;
+    if (c->qk_norm < 0 || c->qk_norm > 2) return 0;
     return 1;
 }
 
@@ -274,7 +294,8 @@ int kvo_append_ring(const kvo_cfg *c, int64_t n_cells, int64_t n_past, int32_t n
                     uint16_t *kcache, uint16_t *vcache, float *q_out)
 {
     if (!kvo_cfg_ok(c) || n_past < 0 || n_new < 0 || n_cells < 0 || (n_cells > 0 && n_new > n_cells)) return -1;
-    if (c->qk_norm && (!q_norm_w || !k_norm_w)) return -1;
+    if (c->qk_norm == 1 && (!q_norm_w || !k_norm_w)) return -1;
+    if (c->qk_norm == 2 && !q_norm_w) return -1;
     const int32_t d = c->head_dim;
     const int32_t hq = c->n_head, hkv = c->n_head_kv;
     const int32_t half = c->n_rot / 2;
@@ -288,18 +309,26 @@ int kvo_append_ring(const kvo_cfg *c, int64_t n_cells, int64_t n_past, int32_t n
         for (int32_t h = 0; h < hq; h++) {
             const float *x = q + (size_t)t * (size_t)q_stride + (size_t)h * (size_t)d;
             const float *src = x;
-            if (c->qk_norm) { kvo_rms_norm_mul(x, q_norm_w, d, c->rms_eps, tmp); src = tmp; }
+            if (c->qk_norm == 1) { kvo_rms_norm_mul(x, q_norm_w, d, c->rms_eps, tmp); src = tmp; }
             float *dst = q_out + ((size_t)t * (size_t)hq + (size_t)h) * (size_t)d;
             if (half > 0) kvo_rope_row(c, cs, src, dst);
             else memcpy(dst, src, sizeof(float) * (size_t)d);
+            if (c->qk_norm == 2) {   /* nGPT: after RoPE, Q's own per-head scale */
+                memcpy(tmp, dst, sizeof(float) * (size_t)d);
+                kvo_ngpt_norm(tmp, q_norm_w + (size_t)h * (size_t)d, d, c->rms_eps, dst);
+            }
         }
         /* K: norm -> rope -> F16 cache row; V: F16 cache row */
         for (int32_t h = 0; h < hkv; h++) {
             const float *x = k + (size_t)t * (size_t)k_stride + (size_t)h * (size_t)d;
             const float *src = x;
-            if (c->qk_norm) { kvo_rms_norm_mul(x, k_norm_w, d, c->rms_eps, tmp); src = tmp; }
+            if (c->qk_norm == 1) { kvo_rms_norm_mul(x, k_norm_w, d, c->rms_eps, tmp); src = tmp; }
             if (half > 0) kvo_rope_row(c, cs, src, rot);
             else memcpy(rot, src, sizeof(float) * (size_t)d);
+            if (c->qk_norm == 2) {
+                memcpy(tmp, rot, sizeof(float) * (size_t)d);
+                kvo_ngpt_norm(tmp, NULL, d, c->rms_eps, rot);
+            }
             const int64_t row = n_cells > 0 ? pos % n_cells : pos;
             uint16_t *kd = kcache + ((size_t)row * (size_t)hkv + (size_t)h) * (size_t)d;
             kvo_f32_to_f16_n(rot, kd, d);

@@ -77,7 +77,8 @@ typedef struct {
     float   rope_beta_fast;
     float   rope_beta_slow;
     const float *rope_freq_factors; /* [n_rot/2] or NULL                      */
-    int32_t qk_norm;         /* 1: per-head RMSNorm on Q and K before RoPE     */
+    int32_t qk_norm;         /* 1: per-head RMSNorm on Q and K before RoPE;
+                                2: dory's nGPT L2 norm after RoPE (Q scaled) */
     float   rms_eps;
 } kvo_cfg;
 
@@ -135,6 +136,9 @@ int kvo_append_ring(const kvo_cfg *c, int64_t n_cells, int64_t n_past, int32_t n
                     const float *q_norm_w, const float *k_norm_w,
                     uint16_t *kcache, uint16_t *vcache, float *q_out);
 void kvo_ring_mask(int64_t n_cells, int64_t pos0, int32_t n_tokens, float *dst);
+/* dory's L2 norm (dory.c:577-580) of one head vector, times w (Q's squared
+ * learned scale, dory.c:646-649) when w != NULL. */
+void kvo_ngpt_norm(const float *x, const float *w, int32_t n, float eps, float *y);
 
 /* kvo_attend_ex: kvo_attend with the caller's additive mask (NULL: causal) of
  * n_new rows, mask_stride elements apart, F16 (mask_f16) or F32, added to each

@@ -69,6 +69,8 @@ def lib():
         L.kvo_append_ring.argtypes = [ctypes.POINTER(KvoCfg), ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
                                       _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, _f32p, ctypes.c_int64,
                                       _f32p, _f32p, _u16p, _u16p, _f32p]
+        L.kvo_ngpt_norm.restype = None
+        L.kvo_ngpt_norm.argtypes = [_f32p, _f32p, ctypes.c_int32, ctypes.c_float, _f32p]
         L.kvo_ring_mask.restype = None
         L.kvo_ring_mask.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, _f32p]
         L.kvo_attend_ex.restype = ctypes.c_int
@@ -123,7 +125,7 @@ class Oracle:
         c.rope_beta_fast = spec.get("rope_beta_fast", 0.0)
         c.rope_beta_slow = spec.get("rope_beta_slow", 0.0)
         c.rope_freq_factors = _p(self._ff)
-        c.qk_norm = 1 if spec.get("qk_norm") else 0
+        c.qk_norm = int(spec.get("qk_norm") or 0)   # True -> 1 (RMSNorm); 2 = nGPT
         c.rms_eps = spec.get("rms_eps", 1e-6)
         self.cfg = c
 

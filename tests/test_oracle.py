@@ -405,6 +405,42 @@ def test_ring_append_rows_and_attention():
         assert np.abs(got - want).max() < 2e-6
 
 
+def test_ngpt_norm_matches_ggml_arithmetic():
+    """dory's L2 norm (dory.c:577-580) as ggml computes it: A1's rms_norm with
+    eps 1e-6/n (float squares summed in double), then * (1/sqrt(n)) and the
+    squared scale, each a rounded float multiply."""
+    rng = np.random.default_rng(5)
+    n = 256
+    x = rng.standard_normal(n).astype(np.float32)
+    w = rng.uniform(2.0, 6.0, n).astype(np.float32)
+    sq = (x * x).astype(np.float32)
+    mean = np.float32(np.cumsum(sq.astype(np.float64))[-1] / n)
+    sc = np.float32(1.0) / np.sqrt(np.float32(mean + np.float32(np.float32(1e-6) / np.float32(n))))
+    post = np.float32(1.0) / np.sqrt(np.float32(n))
+    want = (((x * sc).astype(np.float32) * post).astype(np.float32) * w).astype(np.float32)
+    got = np.zeros(n, np.float32)
+    O.lib().kvo_ngpt_norm(_fp(x), _fp(w), n, 1e-6, _fp(got))
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_ngpt_append_rotates_then_normalises():
+    """qk_norm 2: the cached K row is rope(k) normalised (unit RMS * 1/16 at
+    head_dim 256: L2 norm 1), Q additionally scaled."""
+    sp = specs.get("llama3.2-3b")
+    sp.update(n_layer=1, n_head=16, n_head_kv=4, head_dim=256, n_rot=256, rope_mode=2, rope_base=1e4,
+              rope_freq_factors=None, qk_norm=2)
+    orc = O.Oracle(sp)
+    kc = np.zeros((8, 4, 256), np.uint16)
+    vc = np.zeros((8, 4, 256), np.uint16)
+    rows = synth.qkv_rows(sp, 1, 0, 3)
+    q, k, v = rows[:, :16 * 256], rows[:, 16 * 256:20 * 256], rows[:, 20 * 256:]
+    qs = np.full(16 * 256, 3.0, np.float32)
+    qr = orc.append_ring(kc, vc, 5, q, k, v, qs, None)
+    kn = np.linalg.norm(kc[5:8].view(np.float16).astype(np.float64), axis=-1)
+    assert np.allclose(kn, 1.0, atol=2e-3)
+    assert np.allclose(np.linalg.norm(qr.astype(np.float64), axis=-1), 3.0, atol=1e-4)
+
+
 def test_attention_thread_count_invariant():
     case = G.CASES[6]
     sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
