@@ -279,6 +279,8 @@ bool shape_ok(const kv_config *c, std::string &why)
     if (c->n_head_kv / ns > kvb::kMaxLocalHeads) { why = "more than 64 KV heads per shard"; return false; }
     if (ns > 1 && (c->shard < 0 || c->shard >= ns)) { why = "shard out of range"; return false; }
     if (c->n_batch_max < 0) { why = "n_batch_max must be >= 0"; return false; }
+    if (c->ring_cells < 0) { why = "ring_cells must be >= 0"; return false; }
+    if (c->ring_cells > 0 && c->n_ctx <= 0) { why = "a ring cache needs n_ctx (its positions) > 0"; return false; }
     return true;
 }
 
@@ -547,7 +549,9 @@ uint64_t kv_cache_bytes(const kv_config *cfg, int64_t n_ctx)
 {
     if (!cfg || n_ctx < 0) return 0;
     const uint64_t per_token = (uint64_t)cfg->n_layer * (uint64_t)cfg->head_dim * (uint64_t)cfg->n_head_kv * 2u * 2u;
-    return per_token * (uint64_t)n_ctx;
+    // a ring holds min(ring_cells, n_ctx) rows whatever the positions (dory_kv_cost, dory.c:373-389)
+    const int64_t rows = cfg->ring_cells > 0 ? std::min<int64_t>(cfg->ring_cells, n_ctx) : n_ctx;
+    return per_token * (uint64_t)rows;
 }
 
 int64_t kv_auto_n_ctx(const kv_config *cfg, int64_t free_bytes)

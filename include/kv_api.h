@@ -116,7 +116,8 @@ typedef struct kv_config {
 int kv_config_init(kv_config *cfg);
 
 /* Bytes of the whole K+V cache at n_ctx positions, all layers and all shards:
- * exactly kv_cache_bytes() of the reference (model.cpp:869-885). */
+ * exactly kv_cache_bytes() of the reference (model.cpp:869-885); a ring
+ * configuration holds min(ring_cells, n_ctx) rows. */
 uint64_t kv_cache_bytes(const kv_config *cfg, int64_t n_ctx);
 
 /* Context auto-sizing rule of auto_n_ctx() (model.cpp:1002-1059) applied to

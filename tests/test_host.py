@@ -129,6 +129,42 @@ def test_bad_shapes_rejected():
         assert e.value.code == K.KV_E_ARG
 
 
+def test_ring_and_head_dim_256_shape_rules():
+    """Ring caches need explicit positions; head_dim 256 and the nGPT norm rotate
+    whole heads; qk_norm is 0, 1 or 2.  (shape_ok runs before any CUDA call.)"""
+    sp = specs.get("llama3.2-3b")
+    bad = []
+    c = K.make_config(sp, n_ctx=0, ring_cells=1024)
+    bad.append(c)
+    c = K.make_config(sp, ring_cells=-1)
+    bad.append(c)
+    c = K.make_config(sp)
+    c.head_dim, c.n_rot = 256, 128
+    bad.append(c)
+    c = K.make_config(sp)
+    c.qk_norm, c.n_rot = 2, 64
+    bad.append(c)
+    c = K.make_config(sp)
+    c.qk_norm = 3
+    bad.append(c)
+    for cfg in bad:
+        with pytest.raises(K.KvError) as e:
+            K.rope_table_host(cfg, 0, 1)
+        assert e.value.code == K.KV_E_ARG
+    ok = K.make_config(sp)
+    ok.head_dim, ok.n_rot, ok.qk_norm = 256, 256, 2
+    K.rope_table_host(ok, 0, 1)
+
+
+def test_ring_cache_bytes():
+    """A ring holds min(ring_cells, n_ctx) rows (dory_kv_cost, dory.c:373-389)."""
+    sp = specs.get("llama3.2-3b")
+    lin = K.make_config(sp, n_ctx=8192)
+    ring = K.make_config(sp, n_ctx=8192, ring_cells=1024)
+    assert K.cache_bytes(ring, 8192) * 8 == K.cache_bytes(lin, 8192)
+    assert K.cache_bytes(ring, 512) == K.cache_bytes(lin, 512)
+
+
 def test_alloc_without_gpu_returns_error():
     import torch
     if torch.cuda.is_available():
