@@ -326,7 +326,7 @@ def run_ours(args, sp):
     L, hq, hkv, d = sp["n_layer"], sp["n_head"], sp["n_head_kv"], sp["head_dim"]
     W = (hq + 2 * hkv) * d
     cfg = K.make_config(sp, n_ctx=sp["n_ctx"], n_batch_max=max(16, n_new), device=local, n_shards=world,
-                        shard=rank, comm_id=comm_id)
+                        shard=rank, comm_id=comm_id, flash_attn=args.flash)
     ctx = K.Context(cfg)
     stream = torch.cuda.current_stream()
     t0 = time.time()
@@ -518,6 +518,7 @@ def run_ours(args, sp):
             "config": {"workload": sp["name"], "n_layer": L, "n_head": hq, "n_head_kv": hkv, "head_dim": d,
                        "n_ctx": sp["n_ctx"], "n_past": sp["n_past"], "n_new": n_new,
                        "positions": "n_past + (step mod %d)" % cyc, "global_batch": 1,
+                       "branch": "flash-attn (use_flash_attn)" if args.flash else "default (soft_max_ext + mul_mat)",
                        "parallelism": ("kv-head shards x%d + per-layer all-gather" % world) if world > 1
                        else "single GPU",
                        "l2": "no flush: each step reads %.2f GB of cache (> 126 MB L2)" % (
@@ -573,6 +574,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) pass")
+    ap.add_argument("--flash", action="store_true",
+                    help="the reference's flash-attn branch (use_flash_attn) instead of its default one")
     ap.add_argument("--lead", type=int, default=100,
                     help="untimed steps between warm-up and the timed region (clock sampler start-up)")
     ap.add_argument("--layers", type=int, default=None,

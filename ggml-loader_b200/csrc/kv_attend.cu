@@ -232,9 +232,10 @@ struct Smem {
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-// EXT: the instance for kv_attend_mask (the caller's mask and/or the flash
-// branch); the plain causal instance is compiled without that code
-template <int D, bool EXT>
+// MASKED: the instance for the caller's mask or a ring's single token (every
+// key visible); FLASH: the flash-attn branch.  The plain causal default-branch
+// instance is compiled without either.
+template <int D, bool MASKED, bool FLASH>
 __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                     const __grid_constant__ CUtensorMap vmap,
                                                                     const AttnParams p)
@@ -334,9 +335,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     const int row_a = 2 * cq, row_b = 2 * cq + 1;
     const int tok_a = (p.row0 + min(row_a, R - 1)) / p.r, tok_b = (p.row0 + min(row_b, R - 1)) / p.r;
     // the last visible key of each row: the causal bound, or every key with a mask
-    const bool masked = EXT && p.mask;
-    const bool flash = EXT && p.flash;
-    const bool all = masked || (EXT && p.all_keys);
+    const bool masked = MASKED && p.mask;
+    const bool flash = FLASH;
+    const bool all = masked || (MASKED && p.all_keys);
     const int64_t lim_a = all ? p.n_kv : p.n_past + tok_a;
     const int64_t lim_b = all ? p.n_kv : p.n_past + tok_b;
     float *const Scta = p.S + (int64_t)c * p.S_tiles * kTileScores;
@@ -848,11 +849,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
 template <int D>
 cudaError_t prep()
 {
-    const cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)Smem<D>::bytes);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(attn_decode_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)Smem<D>::bytes);
+    const int b = (int)Smem<D>::bytes;
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_decode_kernel<D, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_decode_kernel<D, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_decode_kernel<D, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+    return e;
 }
 
 template <int D>
@@ -868,8 +873,11 @@ cudaError_t launch(const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnP
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (p.mask || p.flash || p.all_keys) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true>, kmap, vmap, p);
-    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, false>, kmap, vmap, p);
+    const bool m = p.mask || p.all_keys;
+    if (m && p.flash) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true, true>, kmap, vmap, p);
+    if (m) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true, false>, kmap, vmap, p);
+    if (p.flash) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, false, true>, kmap, vmap, p);
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, false, false>, kmap, vmap, p);
 }
 
 }  // namespace

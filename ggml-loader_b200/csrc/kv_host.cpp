@@ -1115,7 +1115,10 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
 
 int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *out, void *stream)
 {
-    return attend_impl(ctx, layer, n_past, n_new, MaskArg{}, out, stream);
+    if (!ctx) return fail(KV_E_ARG, "NULL context");
+    MaskArg mk;
+    mk.flash = ctx->cfg.flash_attn != 0;   // the session's branch (use_flash_attn)
+    return attend_impl(ctx, layer, n_past, n_new, mk, out, stream);
 }
 
 int kv_attend_mask(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, const void *mask, int32_t mask_type,
@@ -1128,7 +1131,7 @@ int kv_attend_mask(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, co
     mk.ptr = mask;
     mk.stride = mask ? mask_stride : 0;
     mk.f16 = mask_type == KV_MASK_F16;
-    mk.flash = (flags & KV_ATTN_FLASH) != 0;
+    mk.flash = (flags & KV_ATTN_FLASH) != 0 || (ctx && ctx->cfg.flash_attn != 0);
     return attend_impl(ctx, layer, n_past, n_new, mk, out, stream);
 }
 

@@ -48,6 +48,7 @@ class KvConfig(ctypes.Structure):
         ("n_shards", _i32), ("shard", _i32),
         ("comm_id", _vp),
         ("ring_cells", _i64),
+        ("flash_attn", _i32),
     ]
 
 
@@ -146,7 +147,8 @@ def _stream(s):
     return s.cuda_stream
 
 
-def make_config(spec, n_ctx=None, n_batch_max=None, device=-1, n_shards=1, shard=0, comm_id=None, ring_cells=0):
+def make_config(spec, n_ctx=None, n_batch_max=None, device=-1, n_shards=1, shard=0, comm_id=None, ring_cells=0,
+                flash_attn=False):
     """A KvConfig from a specs.py dict.  Keeps referenced buffers alive on the
     returned object (freq factors, comm id).  ring_cells > 0 makes a ring cache
     (positions bounded by n_ctx, rows = ring_cells)."""
@@ -179,6 +181,7 @@ def make_config(spec, n_ctx=None, n_batch_max=None, device=-1, n_shards=1, shard
     c.n_shards = n_shards
     c.shard = shard
     c.ring_cells = ring_cells
+    c.flash_attn = 1 if flash_attn else 0
     if comm_id is not None:
         c._id = ctypes.create_string_buffer(bytes(comm_id), 128)
         c.comm_id = ctypes.cast(c._id, _vp)

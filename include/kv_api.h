@@ -99,6 +99,10 @@ typedef struct kv_config {
                                    ring of ring_cells rows (dory.c:391-522), the
                                    token at position p in row p % ring_cells;
                                    n_ctx then bounds the positions (RoPE table)  */
+    int32_t flash_attn;         /* 1: kv_attend (and kv_forward) take the flash-attn
+                                   branch, as decode_session::use_flash_attn
+                                   selects it (model.h:381-384); see
+                                   KV_ATTN_FLASH at kv_attend_mask              */
 } kv_config;
 
 /* Defaults: NEOX RoPE, base 10000, scale 1, attn factor 1, no YaRN, eps 1e-6,

@@ -172,3 +172,32 @@ def test_mask_arguments_are_checked(cuda):
     run.ctx.append(0, 100, 1, base, w, base + 4 * sp["n_head"] * hd, w,
                    base + 4 * (sp["n_head"] + sp["n_head_kv"]) * hd, w)
     assert lib.kv_attend_mask(run.ctx.h, 0, 100, 1, m.data_ptr(), 0, 50, 0, out.data_ptr(), None) == K.KV_E_ARG
+
+
+def test_session_flash_flag_routes_kv_attend(cuda):
+    """kv_config.flash_attn (decode_session::use_flash_attn, model.h:381-384):
+    kv_attend then takes the flash branch, fused decode and chunk alike."""
+    import torch
+    for name, n_past, n_new in (("llama3.2-3b", 3000, 1), ("qwen3-8b-prefill", 1000, 100)):
+        sp, case = _case(name, n_past, n_new)
+        cfg = K.make_config(sp, n_ctx=case["n_ctx"], n_batch_max=max(16, n_new), flash_attn=True)
+        ctx = K.Context(cfg)
+        st = torch.cuda.current_stream()
+        ctx.fill_synthetic(sp["seed"], 0, n_past, stream=st)
+        kc, vc = _oracle_layer(sp, case["n_ctx"], n_past)
+        rows = synth.qkv_rows(sp, 3, 0, n_new)
+        t_rows = torch.from_numpy(np.ascontiguousarray(rows, np.float32)).to(cuda)
+        base, w = t_rows.data_ptr(), rows.shape[1]
+        hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+        qn, kn = synth.norm_weights(sp, 0) if sp["qk_norm"] else (None, None)
+        tq = None if qn is None else torch.from_numpy(qn).to(cuda)
+        tk = None if kn is None else torch.from_numpy(kn).to(cuda)
+        ctx.append(0, n_past, n_new, base, w, base + 4 * hq * d, w, base + 4 * (hq + hkv) * d, w, tq, tk, stream=st)
+        out = torch.full((n_new, hq * d), float("nan"), device=cuda)
+        ctx.attend(0, n_past, n_new, out, stream=st)
+        torch.cuda.synchronize()
+        q, k, v = _split(sp, rows)
+        orc = O.Oracle(sp)
+        qr = orc.append(kc, vc, n_past, q, k, v, qn, kn)
+        assert_close(out.cpu().numpy(), orc.attend_ex(kc, vc, n_past, qr, flash=True))
+        ctx.close()
