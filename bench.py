@@ -173,8 +173,9 @@ class CpuPath:
     workload: the first few layers of the model with their cache rows
     generated on the host, decode steps at the configuration's positions."""
 
-    def __init__(self, sp, max_steps, n_threads=0):
+    def __init__(self, sp, max_steps, n_threads=0, flash=False):
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        self.flash = flash
         import numpy as np
         import kv_oracle as O
         from kv_b200 import synth
@@ -212,7 +213,10 @@ class CpuPath:
             kc, vc = self.caches[l]
             t0 = time.perf_counter()
             qr = self.orc.append(kc, vc, n_past, q, k, v, self.norms[l][0], self.norms[l][1])
-            self.orc.attend(kc, vc, n_past, qr, n_threads=self.threads)
+            if self.flash:   # the flash-attn branch's restatement (oracle A6)
+                self.orc.attend_ex(kc, vc, n_past, qr, flash=True, n_threads=self.threads)
+            else:
+                self.orc.attend(kc, vc, n_past, qr, n_threads=self.threads)
             t += time.perf_counter() - t0
         return (t, self.n_lay * layer_bytes(sp, n_past + self.n_new, self.n_new), self.n_lay,
                 self.n_lay * layer_flops(sp, n_past, self.n_new))
@@ -225,9 +229,9 @@ class CpuPath:
                                                        self.threads))
 
 
-def cpu_sample(sp, seconds, max_steps):
+def cpu_sample(sp, seconds, max_steps, flash=False):
     """(GB/s, us per token, description, threads) of the CPU path over about `seconds`."""
-    cp = CpuPath(sp, max_steps)
+    cp = CpuPath(sp, max_steps, flash=flash)
     t_total, nbytes, nls, s, fl = 0.0, 0, 0, 0, 0
     while s < cp.max_steps and (t_total < seconds or s == 0):
         t, b, n, f = cp.step(s)
@@ -244,7 +248,7 @@ def run_reference(args, sp):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    cp = CpuPath(sp, args.warmup + args.steps)
+    cp = CpuPath(sp, args.warmup + args.steps, flash=args.flash)
     t_total, nbytes, nls, fl = 0.0, 0, 0, 0
     for i in range(args.warmup + args.steps):
         t, b, n, f = cp.step(i)
@@ -279,7 +283,8 @@ def run_reference(args, sp):
         "dtype": "f16 cache, f32 math", "data": "synthetic (seeded generator, configuration shapes)",
         "config": {"workload": sp["name"], "n_layer": sp["n_layer"], "n_head": sp["n_head"],
                    "n_head_kv": sp["n_head_kv"], "head_dim": sp["head_dim"], "n_ctx": sp["n_ctx"],
-                   "n_past": sp["n_past"], "parallelism": "host threads"},
+                   "n_past": sp["n_past"], "parallelism": "host threads",
+                   "branch": "flash-attn (use_flash_attn)" if args.flash else "default (soft_max_ext + mul_mat)"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": "each step: " + desc},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -493,7 +498,7 @@ def run_ours(args, sp):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        gbs, us, desc, threads, tfs = cpu_sample(sp, args.cpu_seconds, 64)
+        gbs, us, desc, threads, tfs = cpu_sample(sp, args.cpu_seconds, 64, flash=args.flash)
         cpu = {"value": round(tfs, 5) if prefill else round(gbs, 4), "unit": "TFLOP/s" if prefill else "GB/s",
                "cores": threads, "kind": "port", "sample": desc, "us_per_token": round(us, 1)}
 
