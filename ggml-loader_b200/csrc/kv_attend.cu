@@ -227,6 +227,9 @@ struct Smem {
     static constexpr size_t bytes = o_flags + 16;
     static_assert(bytes <= 227 * 1024, "shared memory of the attention kernel");
     static_assert(kStage % 1024 == 0, "ring stages stay 1024-byte aligned");
+    // the staged new rows and the scratch blocks are read with 16-byte vector loads
+    static_assert(o_sS % 16 == 0 && o_kf % 16 == 0 && o_knew % 16 == 0 && o_vnew % 16 == 0 && o_redm % 16 == 0,
+                  "16-byte aligned shared regions");
 };
 
 // ---------------------------------------------------------------------------
