@@ -721,7 +721,8 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
         const size_t slots = (size_t)ctx->sm_count * kseg * 256u;   // segments x two 128-row tiles
         e = cudaMalloc(&ctx->pf_stat, slots * 2u * sizeof(float));
         if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_out, slots * (size_t)D * sizeof(float));
-        const size_t nblk = (size_t)(c.n_batch_max + 2 * ctx->pf_tb - 1) / (2 * ctx->pf_tb);
+        const int ntile = kvb::prefill_tiles(ctx->D);
+        const size_t nblk = (size_t)(c.n_batch_max + ntile * ctx->pf_tb - 1) / (ntile * ctx->pf_tb);
         if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_rstat, (size_t)ctx->hkv_loc * nblk * 256u * sizeof(float2));
         if (e != cudaSuccess) return bail(fail(KV_E_OOM, "prefill scratch: %s", cudaGetErrorString(e)));
         e = kvb::prefill_prepare(ctx->D);
@@ -876,11 +877,13 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     pp.n_past = n_past;
     pp.n_new = n_new;
     pp.tb = ctx->pf_tb;
-    pp.nblk = (n_new + 2 * pp.tb - 1) / (2 * pp.tb);
+    pp.nt = kvb::prefill_tiles(ctx->D);
+    pp.nblk = (n_new + pp.nt * pp.tb - 1) / (pp.nt * pp.tb);
     std::vector<int64_t> nt(pp.nblk);
     pp.s_all = 0;
     for (int b = 0; b < pp.nblk; b++) {
-        nt[b] = (n_past + (mk.ptr ? (int64_t)n_new : std::min<int64_t>(n_new, (int64_t)(2 * b + 2) * pp.tb)) + 127) / 128;
+        nt[b] = (n_past + (mk.ptr ? (int64_t)n_new : std::min<int64_t>(n_new, (int64_t)(pp.nt * (b + 1)) * pp.tb)) +
+                 127) / 128;
         pp.s_all += nt[b];
     }
     const int64_t W = (int64_t)pp.hkv * pp.s_all;

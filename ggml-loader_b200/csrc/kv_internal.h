@@ -175,7 +175,8 @@ struct PrefillParams {
     int64_t n_past;
     int32_t n_new;
     int32_t tb;        // tokens per 128-row query tile (tb * r <= 128)
-    int32_t nblk;      // blocks of two query tiles: ceil(n_new / (2 tb)); pair = kv head * nblk + block
+    int32_t nt;        // query tiles a CTA holds (prefill_tiles: 2, or 1 at head_dim 256)
+    int32_t nblk;      // blocks of nt query tiles: ceil(n_new / (nt tb)); pair = kv head * nblk + block
     int64_t s_all;     // key tiles of one KV head summed over its blocks
     int32_t n_cta, kseg;
     float scale;
@@ -196,6 +197,7 @@ struct PrefillParams {
 };
 
 bool prefill_supported(int D);
+int prefill_tiles(int D);
 int prefill_max_segments();
 cudaError_t prefill_prepare(int D);
 // which: 0 the one-pass attention kernel, 1 the fold of pairs split over CTAs;

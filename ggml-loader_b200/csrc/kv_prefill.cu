@@ -74,12 +74,15 @@ constexpr int kOnePass = 0, kStats = 1, kExact = 2;
 
 template <int D>
 struct PL {
+    // query tiles a CTA holds: two (A, B) up to head_dim 128; one at 256, where
+    // O takes 256 TMEM columns and a 128-key K or V tile 64 KB of shared memory
+    static constexpr int NT = D == 256 ? 1 : 2;
     static constexpr int NB = D / 64;                        // boxes per Q/K/V row
     static constexpr uint32_t kTile = (uint32_t)NB * kBox;   // 128 rows x D halves
-    static constexpr int KS = D == 128 ? 3 : 6;              // K ring
-    static constexpr int VS = D == 128 ? 2 : 5;              // V ring
-    static constexpr size_t o_q = 0;                         // Q tiles A, B
-    static constexpr size_t o_k = o_q + 2 * (size_t)kTile;
+    static constexpr int KS = D == 256 ? 1 : D == 128 ? 3 : 6;   // K ring
+    static constexpr int VS = D == 256 ? 1 : D == 128 ? 2 : 5;   // V ring
+    static constexpr size_t o_q = 0;                         // Q tiles A (, B)
+    static constexpr size_t o_k = o_q + NT * (size_t)kTile;
     static constexpr size_t o_v = o_k + (size_t)KS * kTile;
     static constexpr size_t o_bar = o_v + (size_t)VS * kTile;
     // q_full, q_empty, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
@@ -150,11 +153,12 @@ __device__ __forceinline__ float no_key_scale(const PrefillParams &p)
 }
 
 // ---- the work split ------------------------------------------------------------
-// key tiles of block b (tokens [2b*tb, 2b*tb + 2*tb))
+// key tiles of block b (tokens [nt*b*tb, nt*(b+1)*tb), nt the query tiles a CTA holds)
 __device__ __forceinline__ int nt_of(const PrefillParams &p, int b)
 {
     // keys [0, last): the causal bound of the block's last token, or all keys with a mask
-    const int64_t last = p.n_past + (p.mask ? (int64_t)p.n_new : min((int64_t)p.n_new, (int64_t)(2 * b + 2) * p.tb));
+    const int64_t last = p.n_past + (p.mask ? (int64_t)p.n_new
+                                            : min((int64_t)p.n_new, (int64_t)(p.nt * (b + 1)) * p.tb));
     return (int)((last + 127) / 128);
 }
 
@@ -282,6 +286,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
     using L = PL<D>;
     constexpr int NB = L::NB, KS = L::KS, VS = L::VS;
     constexpr uint32_t kTile = L::kTile;
+    constexpr int NT = L::NT;
     extern __shared__ __align__(1024) unsigned char smem[];
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::o_bar);
     uint64_t *q_full = bar, *q_empty = bar + 1;
@@ -303,7 +308,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
             // o_empty; both S issuers commit to k_empty and q_empty
             const uint64_t *bi = &bar[i];
             const bool two = bi == q_empty || (bi >= k_empty && bi < k_empty + KS);
-            mbar_init(&bar[i], (bi >= p_full && bi < p_full + 4) ? kGW : bi == o_empty ? 2 * kGW : two ? 2 : 1);
+            mbar_init(&bar[i], (bi >= p_full && bi < p_full + 4) ? kGW : bi == o_empty ? NT * kGW : two ? NT : 1);
         }
         flags[0] = 0;
         fence_mbar_init();
@@ -331,13 +336,13 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                     give_up(p, flags, 2u);
                     return false;
                 }
-                mbar_arrive_expect_tx(q_full, 2 * qbytes);
+                mbar_arrive_expect_tx(q_full, NT * qbytes);
 #pragma unroll
-                for (int g = 0; g < 2; g++)
+                for (int g = 0; g < NT; g++)
 #pragma unroll
                     for (int bx = 0; bx < NB; bx++)
                         tma_load_3d(smem + L::o_q + g * kTile + bx * kBox, &qmap, q_full, bx * 64, kvh * p.r,
-                                    (2 * b + g) * p.tb);
+                                    (NT * b + g) * p.tb);
                 issued_q++;
                 for (int t = sg.t0; t < sg.t1; t++) {
                     const int s = issued_k % KS;
@@ -391,7 +396,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                 return ok;
             };
             int i = 0;   // sub-tiles consumed
-            if (role < 2) {
+            if (role < NT) {
                 const int g = role;
                 for_segments(p, c, [&](int k, const Seg &sg) {
                     const int i1 = i + 2 * (sg.t1 - sg.t0);
@@ -419,13 +424,13 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                     }
                     return true;
                 });
-            } else if (MODE != kStats) {
+            } else if (role == 2 && MODE != kStats) {
                 for_segments(p, c, [&](int k, const Seg &sg) {
                     const int i0 = i, i1 = i + 2 * (sg.t1 - sg.t0);
                     for (; i < i1; i++) {
                         const int tile = i >> 1;
 #pragma unroll
-                        for (int g = 0; g < 2; g++) {
+                        for (int g = 0; g < NT; g++) {
                             if (!wt(&p_full[g * 2 + (i & 1)], (i >> 1) & 1)) return false;
                             if (g == 0 && !(i & 1) && !wt(&v_full[tile % VS], (tile / VS) & 1)) return false;
                             if (g == 0 && i == i0 && k > 0 && !wt(o_empty, (k - 1) & 1)) return false;
@@ -455,6 +460,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
         // group grp (0: tile A, 1: tile B) of kGW warps; warp w reaches TMEM
         // lanes 32*(w%4) .. +31, one query row per thread, 64 keys a sub-tile
         const int grp = (warp - 2) / kGW;
+        if (grp < NT) {   // (one query tile at head_dim 256: group B is idle)
         const int q4 = warp & 3;
         const int row = q4 * 32 + lane;           // query row of the tile = token*r + head
         const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
@@ -466,7 +472,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
         int i = 0;
         for_segments(p, c, [&](int k, const Seg &sg) {
             const int b = sg.pair % p.nblk, kvh = sg.pair / p.nblk;
-            const int tok = (2 * b + grp) * p.tb + tok_in;
+            const int tok = (NT * b + grp) * p.tb + tok_in;
             const bool valid = row_ok && tok < p.n_new;
             const int64_t lim = !valid ? -1 : p.mask ? p.n_past + p.n_new - 1 : p.n_past + tok;   // last visible key
             const float mscl = p.mask ? __fdiv_rn(1.0f, p.scale) : 0.0f;   // mask / scale adds to the raw dot
@@ -650,6 +656,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
             if (lane == 0) mbar_arrive(o_empty);
             return true;
         });
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -701,8 +708,8 @@ __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
     const int grp = rr >> 7, row = rr & 127;
     const int tok_in = row / p.r, hd = row - tok_in * p.r;
     const int b = pair % p.nblk, kvh = pair / p.nblk;
-    const int tok = (2 * b + grp) * p.tb + tok_in;
-    if (tok_in >= p.tb || tok >= p.n_new) return;
+    const int tok = (p.nt * b + grp) * p.tb + tok_in;
+    if (grp >= p.nt || tok_in >= p.tb || tok >= p.n_new) return;
     auto slot = [&](int cc) { return (((int64_t)cc * p.kseg + (cc == ca ? seg_a : 0)) * 2 + grp) * 128 + row; };
     float4 *dst = reinterpret_cast<float4 *>(p.out + (int64_t)tok * p.out_stride +
                                              (int64_t)(p.out_head0 + kvh * p.r + hd) * D) + part * F4;
@@ -859,7 +866,7 @@ cudaError_t launch_pf(int which, const CUtensorMap &qmap, const CUtensorMap &kma
 
 }  // namespace
 
-bool prefill_supported(int D) { return D == 64 || D == 128; }
+bool prefill_supported(int D) { return D == 64 || D == 128 || D == 256; }
 int prefill_max_segments() { return 4; }
 
 cudaError_t prefill_prepare(int D)
@@ -867,9 +874,12 @@ cudaError_t prefill_prepare(int D)
     switch (D) {
     case 64: return prep_pf<64>();
     case 128: return prep_pf<128>();
+    case 256: return prep_pf<256>();
     default: return cudaSuccess;
     }
 }
+
+int prefill_tiles(int D) { return D == 256 ? PL<256>::NT : 2; }
 
 cudaError_t launch_prefill(int D, int which, const CUtensorMap &qmap, const CUtensorMap &kmap,
                            const CUtensorMap &vmap, const PrefillParams &p, cudaStream_t st)
@@ -877,6 +887,7 @@ cudaError_t launch_prefill(int D, int which, const CUtensorMap &qmap, const CUte
     switch (D) {
     case 64: return launch_pf<64>(which, qmap, kmap, vmap, p, st);
     case 128: return launch_pf<128>(which, qmap, kmap, vmap, p, st);
+    case 256: return launch_pf<256>(which, qmap, kmap, vmap, p, st);
     default: return cudaErrorInvalidValue;
     }
 }

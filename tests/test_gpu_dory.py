@@ -115,3 +115,59 @@ def test_head_dim_256_linear_decode(qk_norm, rope_mode, cuda):
         assert np.array_equal(ctx.export_rows(0, 0, n_past, 1), kc[n_past:n_past + 1])
         assert_close(out.cpu().numpy(), orc.attend(kc, vc, n_past, qr))
         n_past += 1
+
+
+@pytest.mark.parametrize("qk_norm,n_past,n_new", [(0, 3000, 100), (1, 1000, 256), (0, 40000, 40)])
+def test_head_dim_256_chunk_on_tensor_cores(qk_norm, n_past, n_new, cuda):
+    """head_dim 256 chunks on the tcgen05 kernel's one-tile form (one 128-row
+    query tile a CTA, O in TMEM columns 256-511, N = 256 P.V MMAs): the one-pass
+    mode, and past 32k keys the exact two passes."""
+    import torch
+    sp = _dory_spec(qk_norm=qk_norm, base=5e5, rope_mode=2)
+    n_ctx = n_past + n_new + 64
+    cfg = K.make_config(sp, n_ctx=n_ctx, n_batch_max=max(64, n_new))
+    ctx = K.Context(cfg)
+    st = torch.cuda.current_stream()
+    ctx.fill_synthetic(sp["seed"], 0, n_past, stream=st)
+    kc, vc = _oracle_layer(sp, n_ctx, n_past)
+    qn = kn = None
+    if qk_norm:
+        qn, kn = synth.norm_weights(sp, 0)
+    hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+    rows = synth.qkv_rows(sp, 7, 0, n_new)
+    t_rows = torch.from_numpy(np.ascontiguousarray(rows, np.float32)).to(cuda)
+    base, w = t_rows.data_ptr(), rows.shape[1]
+    tq = None if qn is None else torch.from_numpy(qn).to(cuda)
+    tk = None if kn is None else torch.from_numpy(kn).to(cuda)
+    ctx.profile(True)
+    ctx.append(0, n_past, n_new, base, w, base + 4 * hq * d, w, base + 4 * (hq + hkv) * d, w, tq, tk, stream=st)
+    out = torch.full((n_new, hq * d), float("nan"), device=cuda)
+    ctx.attend(0, n_past, n_new, out, stream=st)
+    torch.cuda.synchronize()
+    assert ctx.profile_read("prefill")[0] == (1 if n_past + n_new <= 32768 else 2)
+    q, k, v = _split(sp, rows)
+    orc = O.Oracle(sp)
+    qr = orc.append(kc, vc, n_past, q, k, v, qn, kn)
+    assert np.array_equal(ctx.export_rows(0, 0, n_past, n_new), kc[n_past:n_past + n_new])
+    assert_close(out.cpu().numpy(), orc.attend(kc, vc, n_past, qr))
+
+
+@pytest.mark.parametrize("flash", [False, True])
+def test_dory_ring_chunk_on_tensor_cores(flash, cuda):
+    """A 64-token dory batch across the ring's wrap: 256 query rows on the
+    tensor-core kernel with dory's mask (built on the device, or the caller's
+    F16 mask in the flash branch)."""
+    r = DoryRing(256, 4096, cuda)
+    p = 0
+    while p < 400:
+        r.step(p, 50, 5000 + p, check=False)
+        p += 50
+    mask = None
+    if flash:
+        n_used = min(256, p + 64)
+        mask = np.ascontiguousarray(O.ring_mask(256, p, 64)[:, :n_used].astype(np.float16))
+    r.ctx.profile(True)
+    got, want = r.step(p, 64, 21, mask=mask, flash=flash)
+    assert r.ctx.profile_read("prefill")[0] >= 1
+    assert_close(got, want)
+    assert np.array_equal(r.cells(0), r.kc)
