@@ -20,7 +20,8 @@
 // Work: query rows are packed GQA-group-major: a 128-row tile holds tb =
 // floor(128 / r) tokens x the r query heads of one KV head (row = token*r +
 // head), and a CTA holds two such tiles, A and B (2*tb consecutive tokens), so
-// a K/V tile staged once feeds four MMAs.  A "pair" is (KV head, block of 2*tb
+// a K/V tile staged once feeds four MMAs.  At head_dim 256 a CTA holds one
+// tile (PL<256>::NT): O takes 256 TMEM columns and a K or V tile 64 KB.  A "pair" is (KV head, block of 2*tb
 // tokens); its keys are the tiles of 128 keys up to the block's last visible
 // key.  The pairs' tiles, laid end to end, are cut into C equal ranges (one CTA
 // each, C <= SMs); a range holds one or more "segments" (the part of one pair
