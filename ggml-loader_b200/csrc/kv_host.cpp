@@ -227,6 +227,8 @@ struct kv_ctx {
     int last_n_new = 0;
     // chunked prefill on the tensor cores (head_dim 64/128, chunks of >= 32 query rows)
     bool pf = false;
+    int pf_D = 0;                           // the chunk kernel's head_dim (128 for a 96-wide head)
+    std::vector<CUtensorMap> pf_kmaps, pf_vmaps;   // head_dim 96: 64-wide boxes, columns 96-127 zero-filled
     int pf_tb = 0;                          // tokens per 128-row query tile
     CUtensorMap qmap{};                     // qbuf [n_batch_max][hq_loc][D], box 64 x r x tb
     float *pf_stat = nullptr;               // [sm_count][kseg][2 tiles][128][2]
@@ -709,7 +711,11 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
     }
 
     // chunked prefill: the tensor-core path, when chunks can hold 32+ query rows
-    if (kvb::prefill_supported(ctx->D) && ctx->r <= 128 && (int64_t)c.n_batch_max * ctx->r >= 32) {
+    // (head_dim 96 runs the 128 kernel: its 64-wide boxes read columns 96-127
+    // past the row's end, which TMA fills with zeros)
+    const int pfD = kvb::prefill_kernel_dim(ctx->D);
+    if (kvb::prefill_supported(pfD) && ctx->r <= 128 && (int64_t)c.n_batch_max * ctx->r >= 32) {
+        ctx->pf_D = pfD;
         ctx->pf_tb = std::min(128 / ctx->r, (int)c.n_batch_max);   // the Q box's tokens
         const cuuint64_t qdims[3] = {(cuuint64_t)D, (cuuint64_t)ctx->hq_loc, (cuuint64_t)c.n_batch_max};
         const cuuint64_t qstr[2] = {(cuuint64_t)D * 2, (cuuint64_t)ctx->hq_loc * D * 2};
@@ -720,13 +726,28 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
         const int kseg = kvb::prefill_max_segments();
         const size_t slots = (size_t)ctx->sm_count * kseg * 256u;   // segments x two 128-row tiles
         e = cudaMalloc(&ctx->pf_stat, slots * 2u * sizeof(float));
-        if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_out, slots * (size_t)D * sizeof(float));
-        const int ntile = kvb::prefill_tiles(ctx->D);
+        if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_out, slots * (size_t)pfD * sizeof(float));
+        const int ntile = kvb::prefill_tiles(pfD);
         const size_t nblk = (size_t)(c.n_batch_max + ntile * ctx->pf_tb - 1) / (ntile * ctx->pf_tb);
         if (e == cudaSuccess) e = cudaMalloc(&ctx->pf_rstat, (size_t)ctx->hkv_loc * nblk * 256u * sizeof(float2));
         if (e != cudaSuccess) return bail(fail(KV_E_OOM, "prefill scratch: %s", cudaGetErrorString(e)));
-        e = kvb::prefill_prepare(ctx->D);
+        e = kvb::prefill_prepare(pfD);
         if (e != cudaSuccess) return bail(cuda_fail(e, "prefill_prepare"));
+        if (pfD != ctx->D) {
+            ctx->pf_kmaps.resize(c.n_layer);
+            ctx->pf_vmaps.resize(c.n_layer);
+            const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)ctx->hkv_loc, (cuuint64_t)ctx->rows};
+            const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)ctx->hkv_loc * D * 2};
+            const cuuint32_t box[3] = {64, 1, (cuuint32_t)kvb::attn_tile_keys()};
+            for (int l = 0; l < c.n_layer; l++) {
+                int rc2 = encode_map(&ctx->pf_kmaps[l], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ctx->k_layer(l), dims,
+                                     strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+                if (rc2 == KV_OK)
+                    rc2 = encode_map(&ctx->pf_vmaps[l], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ctx->v_layer(l), dims,
+                                     strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+                if (rc2 != KV_OK) return bail(rc2);
+            }
+        }
         ctx->pf = true;
     }
 
@@ -877,7 +898,8 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     pp.n_past = n_past;
     pp.n_new = n_new;
     pp.tb = ctx->pf_tb;
-    pp.nt = kvb::prefill_tiles(ctx->D);
+    pp.nt = kvb::prefill_tiles(ctx->pf_D);
+    pp.dv = ctx->D;
     pp.nblk = (n_new + pp.nt * pp.tb - 1) / (pp.nt * pp.tb);
     std::vector<int64_t> nt(pp.nblk);
     pp.s_all = 0;
@@ -930,7 +952,7 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     for (int n = 0; n < nseq; n++) {
         const int which = seq[n];
         const int rc = launch(ctx, (which == 1 || which == 3) ? KV_K_PFOLD : KV_K_PREFILL, st, what[which],
-                              [&] { return kvb::launch_prefill(ctx->D, which, ctx->qmap, km, vm, pp, st); });
+                              [&] { return kvb::launch_prefill(ctx->pf_D, which, ctx->qmap, km, vm, pp, st); });
         if (rc) return rc;
     }
     return KV_OK;
@@ -1074,7 +1096,9 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
     const int rows_per = kvb::attn_rows();
     const CUtensorMap &km = ctx->kmaps[layer], &vm = ctx->vmaps[layer];
     if (!fused && ctx->pf && rows >= 32) {
-        rc = prefill(ctx, km, vm, kpast, n_new, dst, dst_stride, dst_head0, mk, st);
+        const bool padded = !ctx->pf_kmaps.empty();   // head_dim 96 on the 128 kernel
+        rc = prefill(ctx, padded ? ctx->pf_kmaps[layer] : km, padded ? ctx->pf_vmaps[layer] : vm, kpast, n_new, dst,
+                     dst_stride, dst_head0, mk, st);
         if (rc) return rc;
     }
     for (int row0 = 0; row0 < rows && !(!fused && ctx->pf && rows >= 32); row0 += rows_per) {

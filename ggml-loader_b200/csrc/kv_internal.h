@@ -176,6 +176,7 @@ struct PrefillParams {
     int32_t n_new;
     int32_t tb;        // tokens per 128-row query tile (tb * r <= 128)
     int32_t nt;        // query tiles a CTA holds (prefill_tiles: 2, or 1 at head_dim 256)
+    int32_t dv;        // the heads' real width in the output rows (the kernel's D, or 96 run as 128)
     int32_t nblk;      // blocks of nt query tiles: ceil(n_new / (nt tb)); pair = kv head * nblk + block
     int64_t s_all;     // key tiles of one KV head summed over its blocks
     int32_t n_cta, kseg;
@@ -198,6 +199,7 @@ struct PrefillParams {
 
 bool prefill_supported(int D);
 int prefill_tiles(int D);
+int prefill_kernel_dim(int D);   // the kernel instance a head_dim runs on
 int prefill_max_segments();
 cudaError_t prefill_prepare(int D);
 // which: 0 the one-pass attention kernel, 1 the fold of pairs split over CTAs;

@@ -626,7 +626,9 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                 return false;
             }
             tc_fence_after();
-            float *dst = p.out + (int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * D;
+            // (the caller's rows hold dv-wide heads; head_dim 96 runs here as 128
+            // with zero-filled columns 96-127, which are not written out)
+            float *dst = p.out + (int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * p.dv;
             float scl = 1.0f;   // the exact pass's O is final (p carries 1/Z)
             if (whole) {
                 if (MODE == kOnePass) scl = l > 0.0f ? __fdiv_rn(1.0f, l) : no_key_scale(p);
@@ -638,7 +640,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
             // K/V tiles other CTAs stream meanwhile
             const uint64_t pol = policy_evict_last();
 #pragma unroll 1
-            for (int ch = 0; ch < D / 32; ch++) {
+            for (int ch = 0; ch < p.dv / 32; ch++) {
                 uint32_t o[32];
                 tmem_ld32(tO + ch * 32, o);
                 tmem_wait_ld();
@@ -712,8 +714,9 @@ __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
     const int tok = (p.nt * b + grp) * p.tb + tok_in;
     if (grp >= p.nt || tok_in >= p.tb || tok >= p.n_new) return;
     auto slot = [&](int cc) { return (((int64_t)cc * p.kseg + (cc == ca ? seg_a : 0)) * 2 + grp) * 128 + row; };
+    if (part * F4 * 4 >= p.dv) return;   // the zero-filled columns past a 96-wide head
     float4 *dst = reinterpret_cast<float4 *>(p.out + (int64_t)tok * p.out_stride +
-                                             (int64_t)(p.out_head0 + kvh * p.r + hd) * D) + part * F4;
+                                             (int64_t)(p.out_head0 + kvh * p.r + hd) * p.dv) + part * F4;
     const bool exact = p.mode == kExact;   // the segments' rows are final: their sum, CTAs in order
     const float2 *ps = reinterpret_cast<const float2 *>(p.pstat);
     const uint64_t pol = policy_evict_first();
@@ -868,6 +871,7 @@ cudaError_t launch_pf(int which, const CUtensorMap &qmap, const CUtensorMap &kma
 }  // namespace
 
 bool prefill_supported(int D) { return D == 64 || D == 128 || D == 256; }
+int prefill_kernel_dim(int D) { return D == 96 ? 128 : D; }   // 96: the 128 kernel on zero-filled columns
 int prefill_max_segments() { return 4; }
 
 cudaError_t prefill_prepare(int D)

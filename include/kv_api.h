@@ -64,8 +64,7 @@ typedef struct kv_config {
     int32_t n_head;             /* hparams::n_head (query heads, whole model)     */
     int32_t n_head_kv;          /* hparams::n_head_kv                             */
     int32_t head_dim;           /* hparams::n_embd_head; 64, 96, 128 or 256 (256:
-                                   whole-head RoPE; 96: chunks on the decode
-                                   kernel, the others on the tensor cores)      */
+                                   whole-head RoPE)                             */
     int32_t n_rot;              /* hparams::n_rot (even, <= head_dim)             */
     int32_t rope_mode;          /* KV_ROPE_NORMAL (llama) / KV_ROPE_NEOX (others) */
     float   rope_base;          /* hparams::rope_freq_base                        */

@@ -112,6 +112,7 @@ def test_decode_window_mask_matches_oracle(name, n_past, n_new, flash, cuda):
     ("qwen3-8b-prefill", 2000, 512, 3, np.float16),     # odd row stride: element loads
     ("llama3.2-3b", 1000, 40, 0, np.float32),           # F32 mask, r = 3
     ("qwen2-0.5b", 150, 64, 0, np.float32),             # head_dim 64
+    ("phi3-mini", 1000, 100, 0, np.float16),            # head_dim 96 on the 128 kernel
 ])
 @pytest.mark.parametrize("flash", [False, True])
 def test_prefill_window_mask_matches_oracle(name, n_past, n_new, stride_pad, dtype, flash, cuda):

@@ -211,6 +211,8 @@ def test_mid_size_matches_oracle(name, n_past, n_new, cuda):
     ("qwen3-8b-prefill", 16384, 512),  # the benchmark chunk
     ("qwen3-8b-prefill", 40000, 40),   # past 32k keys: the exact two passes
     ("llama3.1-8b-128k", 120000, 33),  # 128k-class context, exact passes, pairs over many CTAs
+    ("phi3-mini", 3000, 64),           # head_dim 96 on the 128 kernel (zero-filled columns), MHA
+    ("phi3-mini", 500, 300),           # head_dim 96, pairs split over CTAs (fold writes 96 columns)
 ])
 def test_prefill_chunk_matches_oracle(name, n_past, n_new, cuda):
     """The tensor-core chunk path against the oracle's ggml softmax, within the
