@@ -174,3 +174,25 @@ def test_alloc_without_gpu_returns_error():
     rc = K.lib().kv_alloc(ctypes.byref(cfg), ctypes.byref(h))
     assert rc == K.KV_E_CUDA and not h.value
     assert "cuda" in K.last_error().lower()
+
+
+def test_bench_reference_arm_prints_one_contract_line():
+    """bench.py --impl reference (the CPU restatement on the host cores) prints
+    exactly one JSON line with the contract's keys, in both branches."""
+    import json
+    import subprocess
+    import sys as _sys
+    for extra in ([], ["--flash"]):
+        r = subprocess.run([_sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                            "--warmup", "1", "--config", "qwen2-0.5b"] + extra,
+                           capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        lines = [l for l in r.stdout.splitlines() if l.strip()]
+        assert len(lines) == 1, r.stdout
+        d = json.loads(lines[0])
+        for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                    "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+            assert key in d, key
+        assert d["impl"] == "reference" and d["value"] > 0 and d["cpu_baseline"]["kind"] == "port"
+        assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+        assert d["config"]["branch"].startswith("flash" if extra else "default")
