@@ -346,6 +346,14 @@ int decode_ctas(const kv_ctx *ctx, int64_t n_kv)
 {
     const int64_t T = (int64_t)ctx->hkv_loc * n_kv;
     int64_t c = std::min<int64_t>(std::min(ctx->sm_count, kvb::attn_max_ctas()), (T + 255) / 256);
+    // a multiple of the heads when that idles at most 5 % of the CTAs: every CTA
+    // then covers one head, one statistics poll and one output flush instead
+    // of two for the CTAs that straddle heads (8 heads: 144 of 148 SMs;
+    // llama-3.2-3B 32k 28.7 -> 27.1 us a layer, llama-3.1-8B 128k 91.1 -> 87.6)
+    if (c >= ctx->hkv_loc) {
+        const int64_t a = c / ctx->hkv_loc * ctx->hkv_loc;
+        if (a * 20 >= c * 19) c = a;
+    }
     c = std::max<int64_t>(c, ctx->hkv_loc);
     c = std::min<int64_t>(c, T);
     return (int)c;
