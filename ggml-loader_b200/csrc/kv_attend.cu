@@ -12,7 +12,8 @@
 // Work split: the layer's Hkv*n_kv (head, key) rows, head-major, are cut into C
 // equal contiguous ranges, one CTA each (hkv <= C <= SMs, one CTA per SM, so
 // all CTAs are resident together), every SM streams the same number of bytes
-// and a CTA spans at most two heads (two "segments").
+// and a CTA spans at most two heads (two "segments"); C is a multiple of the
+// heads, so that no CTA straddles two, when that idles at most 5 % of the SMs.
 //
 // attn_decode_kernel
 //   * warp 8 streams the range's K tiles (128 keys; 64-wide boxes with 128-byte
