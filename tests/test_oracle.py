@@ -441,6 +441,23 @@ def test_ngpt_append_rotates_then_normalises():
     assert np.allclose(np.linalg.norm(qr.astype(np.float64), axis=-1), 3.0, atol=1e-4)
 
 
+def test_masked_and_flash_attention_thread_count_invariant():
+    """The masked and flash restatements do not depend on the thread count either."""
+    case = G.CASES[6]
+    sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
+    orc = O.Oracle(sp)
+    n_past = case["n_past"]
+    q_roped = orc.append(kc, vc, n_past, q, k, v, qn, kn)
+    n_new = q_roped.shape[0]
+    mask = np.full((n_new, n_past + n_new), -np.inf, np.float16)
+    for t in range(n_new):
+        mask[t, max(0, n_past + t - 30): n_past + t + 1] = 0
+    for flash in (False, True):
+        a = orc.attend_ex(kc, vc, n_past, q_roped, mask=mask, flash=flash, n_threads=1)
+        b = orc.attend_ex(kc, vc, n_past, q_roped, mask=mask, flash=flash, n_threads=7)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
 def test_attention_thread_count_invariant():
     case = G.CASES[6]
     sp, kc, vc, rows, q, k, v, qn, kn = G.case_inputs(case)
