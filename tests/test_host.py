@@ -196,3 +196,19 @@ def test_bench_reference_arm_prints_one_contract_line():
         assert d["impl"] == "reference" and d["value"] > 0 and d["cpu_baseline"]["kind"] == "port"
         assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
         assert d["config"]["branch"].startswith("flash" if extra else "default")
+
+
+def test_headers_compile_as_c_and_cpp(tmp_path):
+    """include/*.h are a C ABI: they compile in a C99 and a C++17 translation unit."""
+    import shutil
+    import subprocess
+    src = ("#include \"kv_api.h\"\n#include \"kv_bench.h\"\n"
+           "int f(void) { kv_config c; kv_config_init(&c); return (int)c.n_layer + KV_ATTN_FLASH + KV_MASK_F16; }\n")
+    for compiler, ext, std in (("gcc", "c", "-std=c99"), ("g++", "cpp", "-std=c++17")):
+        if not shutil.which(compiler):
+            pytest.skip(compiler + " missing")
+        p = tmp_path / ("abi." + ext)
+        p.write_text(src)
+        r = subprocess.run([compiler, std, "-Wall", "-Werror", "-fsyntax-only", "-I", os.path.join(ROOT, "include"),
+                            str(p)], capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
