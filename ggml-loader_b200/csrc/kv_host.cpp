@@ -342,21 +342,26 @@ int launch(kv_ctx *ctx, int kernel_id, cudaStream_t st, const char *what, F &&fn
 // the statistics exchange and the output combine have fewer parties
 // (qwen2-0.5B at 2k keys: 12.5 -> 11.6 us a layer; 512 or more rows a CTA is
 // slower).
-int decode_ctas(const kv_ctx *ctx, int64_t n_kv)
+int decode_ctas_for(int sm_count, int hkv_loc, int64_t n_kv)
 {
-    const int64_t T = (int64_t)ctx->hkv_loc * n_kv;
-    int64_t c = std::min<int64_t>(std::min(ctx->sm_count, kvb::attn_max_ctas()), (T + 255) / 256);
+    const int64_t T = (int64_t)hkv_loc * n_kv;
+    int64_t c = std::min<int64_t>(std::min(sm_count, kvb::attn_max_ctas()), (T + 255) / 256);
     // a multiple of the heads when that idles at most 5 % of the CTAs: every CTA
     // then covers one head, one statistics poll and one output flush instead
     // of two for the CTAs that straddle heads (8 heads: 144 of 148 SMs;
     // llama-3.2-3B 32k 28.7 -> 27.1 us a layer, llama-3.1-8B 128k 91.1 -> 87.6)
-    if (c >= ctx->hkv_loc) {
-        const int64_t a = c / ctx->hkv_loc * ctx->hkv_loc;
+    if (c >= hkv_loc) {
+        const int64_t a = c / hkv_loc * hkv_loc;
         if (a * 20 >= c * 19) c = a;
     }
-    c = std::max<int64_t>(c, ctx->hkv_loc);
+    c = std::max<int64_t>(c, hkv_loc);
     c = std::min<int64_t>(c, T);
     return (int)c;
+}
+
+int decode_ctas(const kv_ctx *ctx, int64_t n_kv)
+{
+    return decode_ctas_for(ctx->sm_count, ctx->hkv_loc, n_kv);
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
@@ -1364,6 +1369,13 @@ int kv_rope_table_host(const kv_config *cfg, int64_t pos0, int64_t npos, float *
     RopeSpec rs{cfg->n_rot, cfg->rope_base, cfg->rope_freq_scale, cfg->rope_attn_factor, cfg->rope_ext_factor,
                 cfg->rope_beta_fast, cfg->rope_beta_slow, cfg->n_ctx_orig, cfg->rope_freq_factors};
     rope_rows(rs, pos0, pos0 + npos, out);
+    return KV_OK;
+}
+
+int kv_decode_ctas(int32_t sm_count, int32_t n_kv_heads_local, int64_t n_kv, int32_t *n_cta)
+{
+    if (!n_cta || sm_count <= 0 || n_kv_heads_local <= 0 || n_kv <= 0) return fail(KV_E_ARG, "bad argument");
+    *n_cta = decode_ctas_for(sm_count, n_kv_heads_local, n_kv);
     return KV_OK;
 }
 

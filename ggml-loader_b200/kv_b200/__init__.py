@@ -103,6 +103,7 @@ def lib():
         "kv_debug_inject": (ctypes.c_int, [_vp, _i32, _u64]),
         "kv_rope_table_host": (ctypes.c_int, [cfgp, _i64, _i64, _vp]),
         "kv_shard_geometry": (ctypes.c_int, [cfgp, _i32] + [ctypes.POINTER(_i32)] * 4),
+        "kv_decode_ctas": (ctypes.c_int, [_i32, _i32, _i64, ctypes.POINTER(_i32)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -60,6 +60,12 @@ int kv_rope_table_host(const kv_config *cfg, int64_t pos0, int64_t npos, float *
 int kv_shard_geometry(const kv_config *cfg, int32_t shard, int32_t *q_head0, int32_t *n_q_heads,
                       int32_t *kv_head0, int32_t *n_kv_heads);
 
+/* The decode split's CTA count for a layer of n_kv keys over n_kv_heads_local
+ * KV heads on a GPU with sm_count SMs (host arithmetic only): one CTA per SM
+ * at most, at least 256 (head, key) rows a CTA, at least one per head, and a
+ * multiple of the heads when that idles at most 5 % of them. */
+int kv_decode_ctas(int32_t sm_count, int32_t n_kv_heads_local, int64_t n_kv, int32_t *n_cta);
+
 #ifdef __cplusplus
 }
 #endif

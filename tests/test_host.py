@@ -212,3 +212,28 @@ def test_headers_compile_as_c_and_cpp(tmp_path):
         r = subprocess.run([compiler, std, "-Wall", "-Werror", "-fsyntax-only", "-I", os.path.join(ROOT, "include"),
                             str(p)], capture_output=True, text=True)
         assert r.returncode == 0, r.stderr
+
+
+def test_decode_split_cta_counts():
+    """kv_decode_ctas (the decode kernel's split, host arithmetic): a multiple of
+    the KV heads when that idles at most 5 % of the SMs, one CTA per SM at most,
+    >= 256 (head, key) rows a CTA, >= one CTA a head."""
+    def n_cta(sm, hkv, n_kv):
+        out = ctypes.c_int32()
+        assert K.lib().kv_decode_ctas(sm, hkv, n_kv, ctypes.byref(out)) == K.KV_OK
+        return out.value
+    assert n_cta(148, 8, 32001) == 144            # llama-3.2-3B / 3.1-8B: 18 CTAs a head
+    assert n_cta(148, 4, 131001) == 148           # 4 divides 148
+    assert n_cta(148, 1, 131001) == 148           # one-head shard
+    assert n_cta(148, 32, 3969) == 148            # phi3: 128 would idle 13.5 %
+    assert n_cta(148, 2, 2049) == 17              # qwen2-0.5B: ceil(4098 rows / 256); 16 would idle 6 %
+    assert n_cta(148, 8, 1) == 8                  # never fewer than the heads
+    assert n_cta(148, 3, 100000) == 147
+    for hkv in (1, 2, 3, 4, 6, 8, 12, 16, 24, 32, 40, 64):
+        for n_kv in (1, 7, 300, 4096, 32768, 131072):
+            c = n_cta(148, hkv, n_kv)
+            assert hkv <= c <= max(hkv, 148) and c <= hkv * n_kv
+            # a CTA's range covers at most one head's keys: it spans at most two heads
+            assert (hkv * n_kv + c - 1) // c <= n_kv
+    out = ctypes.c_int32()
+    assert K.lib().kv_decode_ctas(0, 8, 100, ctypes.byref(out)) == K.KV_E_ARG
