@@ -229,9 +229,13 @@ class CpuPath:
                                                        self.threads))
 
 
-def cpu_sample(sp, seconds, max_steps, flash=False):
-    """(GB/s, us per token, description, threads) of the CPU path over about `seconds`."""
-    cp = CpuPath(sp, max_steps, flash=flash)
+def cpu_sample(sp, seconds, max_steps, flash=False, n_threads=0, cp=None):
+    """(GB/s, us per token, description, threads, TFLOP/s, path) of the CPU path
+    over about `seconds` on `n_threads` host threads (0: every online core).
+    Passing the `cp` of an earlier sample reuses its generated cache rows."""
+    if cp is None:
+        cp = CpuPath(sp, max_steps, flash=flash)
+    cp.threads = n_threads if n_threads > 0 else cp.O.online_cores()
     t_total, nbytes, nls, s, fl = 0.0, 0, 0, 0, 0
     while s < cp.max_steps and (t_total < seconds or s == 0):
         t, b, n, f = cp.step(s)
@@ -241,7 +245,7 @@ def cpu_sample(sp, seconds, max_steps, flash=False):
         fl += f
         s += 1
     return (nbytes / t_total / 1e9, t_total / nls * sp["n_layer"] * 1e6, cp.describe(s), cp.threads,
-            fl / t_total / 1e12)
+            fl / t_total / 1e12, cp)
 
 
 def run_reference(args, sp):
@@ -498,9 +502,14 @@ def run_ours(args, sp):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        gbs, us, desc, threads, tfs = cpu_sample(sp, args.cpu_seconds, 64, flash=args.flash)
+        gbs, us, desc, threads, tfs, cp = cpu_sample(sp, args.cpu_seconds, 64, flash=args.flash)
         cpu = {"value": round(tfs, 5) if prefill else round(gbs, 4), "unit": "TFLOP/s" if prefill else "GB/s",
                "cores": threads, "kind": "port", "sample": desc, "us_per_token": round(us, 1)}
+        if threads != 8:
+            # the reference's own thread count: init_backend(..., 8) (cmd_bench.cpp:107)
+            g8, u8, d8, _, t8, _ = cpu_sample(sp, args.cpu_seconds, 64, n_threads=8, cp=cp)
+            cpu["threads_8"] = {"value": round(t8, 5) if prefill else round(g8, 4), "cores": 8,
+                                "sample": d8, "us_per_token": round(u8, 1)}
 
     clocks = sampler.summary() if rank == 0 else None
     barrier()

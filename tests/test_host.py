@@ -198,6 +198,22 @@ def test_bench_reference_arm_prints_one_contract_line():
         assert d["config"]["branch"].startswith("flash" if extra else "default")
 
 
+def test_cpu_baseline_sample_at_two_thread_counts():
+    """The GPU arm's cpu_baseline samples the CPU path on every core and on the
+    reference's own 8 threads, reusing one set of generated cache rows."""
+    import importlib
+    import sys as _sys
+    _sys.path.insert(0, ROOT)
+    bench = importlib.import_module("bench")
+    sp = specs.get("qwen2-0.5b")
+    g_all, us_all, desc, th_all, _, cp = bench.cpu_sample(sp, 0.2, 4)
+    g8, us8, desc8, th8, _, cp8 = bench.cpu_sample(sp, 0.2, 4, n_threads=8, cp=cp)
+    assert cp8 is cp and th8 == 8 and "8 threads" in desc8
+    assert th_all == cp.O.online_cores() >= 1
+    assert g_all > 0 and g8 > 0 and us_all > 0 and us8 > 0
+    assert "%d threads" % th_all in desc
+
+
 def test_headers_compile_as_c_and_cpp(tmp_path):
     """include/*.h are a C ABI: they compile in a C99 and a C++17 translation unit."""
     import shutil
