@@ -16,7 +16,10 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <exception>
+#include <new>
 #include <string>
+#include <system_error>
 #include <thread>
 #include <vector>
 
@@ -26,22 +29,40 @@
 
 namespace {
 
-thread_local std::string g_last_error;
+// a fixed buffer: recording an error never allocates, so it also works while
+// reporting a failed host allocation
+thread_local char g_last_error[512];
 
 int fail(int code, const char *fmt, ...)
 {
-    char buf[512];
     va_list ap;
     va_start(ap, fmt);
-    vsnprintf(buf, sizeof(buf), fmt, ap);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
     va_end(ap);
-    g_last_error = buf;
     return code;
 }
 
 int cuda_fail(cudaError_t e, const char *what)
 {
     return fail(KV_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// C callers cannot catch a C++ exception: the entry points that allocate host
+// memory (the RoPE table, TMA descriptor and segment-table vectors, error
+// strings) run their body through this and return KV_E_OOM instead of letting
+// std::bad_alloc (or a failed thread start) end the caller's process.
+template <class F>
+int guarded(const char *what, F &&fn) noexcept
+{
+    try {
+        return fn();
+    } catch (const std::bad_alloc &) {
+        return fail(KV_E_OOM, "%s: host memory allocation failed", what);
+    } catch (const std::exception &ex) {
+        return fail(KV_E_OOM, "%s: host resources exhausted (%s)", what, ex.what());
+    } catch (...) {
+        return fail(KV_E_OOM, "%s: host resources exhausted", what);
+    }
 }
 
 #define KV_CUDA(call)                                     \
@@ -152,11 +173,19 @@ void build_rope_table(const RopeSpec &r, int64_t n_pos, float *out)
     if (n_pos < 4096) nt = 1;
     const int64_t chunk = (n_pos + nt - 1) / nt;
     std::vector<std::thread> th;
+    th.reserve(nt);
+    int64_t handed = 0;   // rows [0, handed) belong to started threads
     for (unsigned w = 0; w < nt; w++) {
         const int64_t a = (int64_t)w * chunk, b = std::min(n_pos, a + chunk);
         if (a >= b) break;
-        th.emplace_back([&r, a, b, out, half] { rope_rows(r, a, b, out + (size_t)a * (size_t)half * 2u); });
+        try {
+            th.emplace_back([&r, a, b, out, half] { rope_rows(r, a, b, out + (size_t)a * (size_t)half * 2u); });
+        } catch (const std::system_error &) {
+            break;   // no thread to be had: this thread computes the rest
+        }
+        handed = b;
     }
+    if (handed < n_pos) rope_rows(r, handed, n_pos, out + (size_t)handed * (size_t)half * 2u);
     for (auto &t : th) t.join();
 }
 
@@ -164,7 +193,7 @@ void build_rope_table(const RopeSpec &r, int64_t n_pos, float *out)
 
 int kvb::set_last_error(int code, const char *msg)
 {
-    g_last_error = msg ? msg : "";
+    snprintf(g_last_error, sizeof(g_last_error), "%s", msg ? msg : "");
     return code;
 }
 
@@ -331,7 +360,11 @@ int launch(kv_ctx *ctx, int kernel_id, cudaStream_t st, const char *what, F &&fn
     ctx->launches.fetch_add(1, std::memory_order_relaxed);
     if (ctx->prof_on) {
         cudaEventRecord(b, st);
-        ctx->recs.push_back({kernel_id, a, b});
+        try {
+            ctx->recs.push_back({kernel_id, a, b});
+        } catch (const std::bad_alloc &) {
+            return fail(KV_E_OOM, "%s: no host memory for its profiling record", what);
+        }
     }
     return KV_OK;
 }
@@ -587,14 +620,23 @@ int64_t kv_auto_n_ctx(const kv_config *cfg, int64_t free_bytes)
     return n_ctx;
 }
 
-int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
+static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
 {
-    if (!cfg_in || !out) return fail(KV_E_ARG, "NULL argument");
-    *out = nullptr;
     std::string why;
     if (!shape_ok(cfg_in, why)) return fail(KV_E_ARG, "kv_alloc: %s", why.c_str());
 
-    kv_ctx *ctx = new kv_ctx();
+    // every early return, and an exception, frees what was set up so far
+    struct Owner {
+        kv_ctx *p;
+        ~Owner()
+        {
+            if (p) {
+                free_all(p);
+                delete p;
+            }
+        }
+    } own{new kv_ctx()};
+    kv_ctx *ctx = own.p;
     ctx->cfg = *cfg_in;
     kv_config &c = ctx->cfg;
     if (c.n_shards <= 1) { c.n_shards = 1; c.shard = 0; }
@@ -607,11 +649,7 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
     }
     c.comm_id = nullptr;
 
-    auto bail = [&](int code) {
-        free_all(ctx);
-        delete ctx;
-        return code;
-    };
+    auto bail = [](int code) { return code; };
     cudaError_t e;
     if (c.device >= 0) {
         e = cudaSetDevice(c.device);
@@ -784,8 +822,16 @@ int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
     }
     e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return bail(cuda_fail(e, "kv_alloc sync"));
+    own.p = nullptr;
     *out = ctx;
     return KV_OK;
+}
+
+int kv_alloc(const kv_config *cfg_in, kv_ctx **out)
+{
+    if (!cfg_in || !out) return fail(KV_E_ARG, "NULL argument");
+    *out = nullptr;
+    return guarded("kv_alloc", [&] { return alloc_impl(cfg_in, out); });
 }
 
 int kv_free(kv_ctx *ctx)
@@ -838,7 +884,7 @@ int kv_append_bias(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new,
     if (layer < 0 || layer >= c.n_layer) return fail(KV_E_ARG, "layer %d out of range", layer);
     if (n_new <= 0 || n_past < 0) return fail(KV_E_ARG, "n_new must be > 0 and n_past >= 0");
     if (n_new > c.n_batch_max) return fail(KV_E_RANGE, "n_new %d exceeds n_batch_max %d", n_new, c.n_batch_max);
-    if (n_past + n_new > ctx->n_ctx)
+    if (n_past > ctx->n_ctx - n_new)   // (n_past + n_new could overflow)
         return fail(KV_E_RANGE, "positions [%lld, %lld) exceed n_ctx %lld", (long long)n_past,
                     (long long)(n_past + n_new), (long long)ctx->n_ctx);
     if (ctx->ring && n_new > ctx->ring)   // a batch longer than the ring would overwrite its own rows
@@ -1158,7 +1204,7 @@ int kv_attend(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, float *
     if (!ctx) return fail(KV_E_ARG, "NULL context");
     MaskArg mk;
     mk.flash = ctx->cfg.flash_attn != 0;   // the session's branch (use_flash_attn)
-    return attend_impl(ctx, layer, n_past, n_new, mk, out, stream);
+    return guarded("kv_attend", [&] { return attend_impl(ctx, layer, n_past, n_new, mk, out, stream); });
 }
 
 int kv_attend_mask(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, const void *mask, int32_t mask_type,
@@ -1172,7 +1218,7 @@ int kv_attend_mask(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new, co
     mk.stride = mask ? mask_stride : 0;
     mk.f16 = mask_type == KV_MASK_F16;
     mk.flash = (flags & KV_ATTN_FLASH) != 0 || (ctx && ctx->cfg.flash_attn != 0);
-    return attend_impl(ctx, layer, n_past, n_new, mk, out, stream);
+    return guarded("kv_attend_mask", [&] { return attend_impl(ctx, layer, n_past, n_new, mk, out, stream); });
 }
 
 int kv_forward(kv_ctx *ctx, int64_t n_past, int32_t n_new,
@@ -1199,7 +1245,8 @@ static int rows_io(kv_ctx *ctx, int32_t layer, int32_t which, int64_t row0, int6
     if (!ctx || !host) return fail(KV_E_ARG, "NULL argument");
     if (layer < 0 || layer >= ctx->cfg.n_layer || (which != 0 && which != 1))
         return fail(KV_E_ARG, "bad layer or which");
-    if (row0 < 0 || nrows < 0 || row0 + nrows > ctx->rows) return fail(KV_E_RANGE, "rows outside the cache");
+    if (row0 < 0 || nrows < 0 || row0 > ctx->rows || nrows > ctx->rows - row0)
+        return fail(KV_E_RANGE, "rows outside the cache");
     int rc = ensure_device(ctx);
     if (rc) return rc;
     rc = flush_pending(ctx);
@@ -1251,7 +1298,7 @@ const char *kv_strerror(int code)
     }
 }
 
-const char *kv_last_error(void) { return g_last_error.c_str(); }
+const char *kv_last_error(void) { return g_last_error; }
 
 int kv_status(kv_ctx *ctx, void *stream)
 {
@@ -1287,7 +1334,8 @@ int kv_debug_inject(kv_ctx *ctx, int32_t what, uint64_t limit_ns)
 int kv_fill_synthetic(kv_ctx *ctx, uint64_t seed, uint64_t stream_base, int64_t row0, int64_t nrows, void *stream)
 {
     if (!ctx) return fail(KV_E_ARG, "NULL context");
-    if (row0 < 0 || nrows < 0 || row0 + nrows > ctx->rows) return fail(KV_E_RANGE, "rows outside the cache");
+    if (row0 < 0 || nrows < 0 || row0 > ctx->rows || nrows > ctx->rows - row0)
+        return fail(KV_E_RANGE, "rows outside the cache");
     int rc = ensure_device(ctx);
     if (rc) return rc;
     rc = flush_pending(ctx);
@@ -1325,10 +1373,18 @@ int kv_profile_enable(kv_ctx *ctx, int on)
 int kv_profile_reset(kv_ctx *ctx)
 {
     if (!ctx) return fail(KV_E_ARG, "NULL context");
-    for (auto &r : ctx->recs) {
-        cudaEventSynchronize(r.b);
-        ctx->ev_pool.push_back(r.a);
-        ctx->ev_pool.push_back(r.b);
+    for (auto &r : ctx->recs) cudaEventSynchronize(r.b);
+    try {
+        ctx->ev_pool.reserve(ctx->ev_pool.size() + 2 * ctx->recs.size());
+        for (auto &r : ctx->recs) {
+            ctx->ev_pool.push_back(r.a);
+            ctx->ev_pool.push_back(r.b);
+        }
+    } catch (const std::bad_alloc &) {   // no room to pool them: release the events instead
+        for (auto &r : ctx->recs) {
+            cudaEventDestroy(r.a);
+            cudaEventDestroy(r.b);
+        }
     }
     ctx->recs.clear();
     return KV_OK;
@@ -1363,13 +1419,15 @@ int64_t kv_launch_count(const kv_ctx *ctx) { return ctx ? ctx->launches.load() :
 int kv_rope_table_host(const kv_config *cfg, int64_t pos0, int64_t npos, float *out)
 {
     if (!cfg || !out || pos0 < 0 || npos < 0) return fail(KV_E_ARG, "bad argument");
-    std::string why;
-    if (!shape_ok(cfg, why)) return fail(KV_E_ARG, "%s", why.c_str());
-    if (cfg->n_rot == 0 || npos == 0) return KV_OK;
-    RopeSpec rs{cfg->n_rot, cfg->rope_base, cfg->rope_freq_scale, cfg->rope_attn_factor, cfg->rope_ext_factor,
-                cfg->rope_beta_fast, cfg->rope_beta_slow, cfg->n_ctx_orig, cfg->rope_freq_factors};
-    rope_rows(rs, pos0, pos0 + npos, out);
-    return KV_OK;
+    return guarded("kv_rope_table_host", [&] {
+        std::string why;
+        if (!shape_ok(cfg, why)) return fail(KV_E_ARG, "%s", why.c_str());
+        if (cfg->n_rot == 0 || npos == 0) return KV_OK;
+        RopeSpec rs{cfg->n_rot, cfg->rope_base, cfg->rope_freq_scale, cfg->rope_attn_factor, cfg->rope_ext_factor,
+                    cfg->rope_beta_fast, cfg->rope_beta_slow, cfg->n_ctx_orig, cfg->rope_freq_factors};
+        rope_rows(rs, pos0, pos0 + npos, out);
+        return KV_OK;
+    });
 }
 
 int kv_decode_ctas(int32_t sm_count, int32_t n_kv_heads_local, int64_t n_kv, int32_t *n_cta)

@@ -41,7 +41,7 @@ extern "C" {
 /* ---- return codes -------------------------------------------------------- */
 #define KV_OK              0
 #define KV_E_ARG          -1  /* bad argument or unsupported shape          */
-#define KV_E_OOM          -2  /* device allocation failed                   */
+#define KV_E_OOM          -2  /* device or host allocation failed           */
 #define KV_E_RANGE        -3  /* row range outside [0, n_ctx) / batch limit */
 #define KV_E_CUDA         -4  /* CUDA runtime error                         */
 #define KV_E_COMM         -5  /* collective (NCCL) error                    */
