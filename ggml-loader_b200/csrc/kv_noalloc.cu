@@ -86,6 +86,12 @@ extern "C" int kv_attend_decode_noalloc(const uint16_t *k_cache, const uint16_t 
         return kvb::set_last_error(KV_E_ARG, "kv_attend_decode_noalloc: bad head counts or n_kv < 1");
     if ((((uintptr_t)k_cache) | ((uintptr_t)v_cache)) & 15u)
         return kvb::set_last_error(KV_E_ARG, "kv_attend_decode_noalloc: cache pointers must be 16-byte aligned");
+    // shapes whose Q copy or one row of scores alone exceed the static array:
+    // refused before the sizing arithmetic below, which they could overflow
+    if ((uint64_t)n_head * (uint64_t)head_dim * sizeof(__half) > kScratchBytes ||
+        (uint64_t)n_kv > kScratchBytes / sizeof(float))
+        return kvb::set_last_error(KV_E_RANGE, "kv_attend_decode_noalloc: the shape needs more scratch than the "
+                                               "static array holds (fewer keys or heads per call)");
 
     const int D = head_dim, hkv = n_head_kv, r = n_head / n_head_kv;
     const int rmax = kvb::decode_rmax(D), split_max = kvb::decode_split_max(D);

@@ -198,6 +198,23 @@ def test_bench_reference_arm_prints_one_contract_line():
         assert d["config"]["branch"].startswith("flash" if extra else "default")
 
 
+def test_noalloc_refuses_oversized_shapes_before_any_device_work():
+    """kv_attend_decode_noalloc: key counts or head counts whose sizing would
+    overflow are refused with KV_E_RANGE by the argument checks, which run
+    before the device is touched (the placeholder addresses are never used)."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    lib = K.lib()
+    kc, vc, q, out = 0x10000, 0x20000, 0x30000, 0x40000
+    for n_head, n_kv_heads, n_kv in ((32, 8, 1 << 40), (32, 8, (1 << 62) + 1), (1 << 20, 1 << 20, 100)):
+        rc = lib.kv_attend_decode_noalloc(kc, vc, n_head, n_kv_heads, 128, n_kv, q, out, None)
+        assert rc == K.KV_E_RANGE, (n_head, n_kv_heads, n_kv, rc)
+        assert "scratch" in K.last_error()
+    # a shape within the bounds reaches the device query, which fails here
+    assert lib.kv_attend_decode_noalloc(kc, vc, 32, 8, 128, 4096, q, out, None) == K.KV_E_CUDA
+
+
 def test_cpu_baseline_sample_at_two_thread_counts():
     """The GPU arm's cpu_baseline samples the CPU path on every core and on the
     reference's own 8 threads, reusing one set of generated cache rows."""
