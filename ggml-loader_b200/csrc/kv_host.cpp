@@ -286,6 +286,8 @@ struct kv_ctx {
 
 namespace {
 
+constexpr int64_t kMaxPositions = (int64_t)1 << 31;
+
 bool shape_ok(const kv_config *c, std::string &why)
 {
     char buf[256];
@@ -312,6 +314,10 @@ bool shape_ok(const kv_config *c, std::string &why)
     if (c->n_batch_max < 0) { why = "n_batch_max must be >= 0"; return false; }
     if (c->ring_cells < 0) { why = "ring_cells must be >= 0"; return false; }
     if (c->ring_cells > 0 && c->n_ctx <= 0) { why = "a ring cache needs n_ctx (its positions) > 0"; return false; }
+    // TMA descriptors address at most 2^32 rows; 2^31 positions already exceed
+    // any device's memory at every supported shape, and keep the sizing
+    // arithmetic far from overflow
+    if (c->n_ctx > kMaxPositions) { why = "n_ctx above 2^31 positions"; return false; }
     return true;
 }
 
@@ -599,6 +605,7 @@ uint64_t kv_cache_bytes(const kv_config *cfg, int64_t n_ctx)
     const uint64_t per_token = (uint64_t)cfg->n_layer * (uint64_t)cfg->head_dim * (uint64_t)cfg->n_head_kv * 2u * 2u;
     // a ring holds min(ring_cells, n_ctx) rows whatever the positions (dory_kv_cost, dory.c:373-389)
     const int64_t rows = cfg->ring_cells > 0 ? std::min<int64_t>(cfg->ring_cells, n_ctx) : n_ctx;
+    if (per_token > 0 && (uint64_t)rows > UINT64_MAX / per_token) return UINT64_MAX;   // saturate
     return per_token * (uint64_t)rows;
 }
 
@@ -676,7 +683,7 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
     if (c.n_ctx <= 0) {
         size_t fr = 0, tot = 0;
         e = cudaMemGetInfo(&fr, &tot);
-        ctx->n_ctx = kv_auto_n_ctx(&c, e == cudaSuccess ? (int64_t)fr : -1);
+        ctx->n_ctx = std::min(kv_auto_n_ctx(&c, e == cudaSuccess ? (int64_t)fr : -1), kMaxPositions);
         fprintf(stderr,
                 "n_ctx=auto: free HBM %.0f MiB, reserve 384 MiB, %.1f KiB per position -> n_ctx=%lld\n",
                 (double)fr / (1024.0 * 1024.0), (double)per_position_bytes(&c) / 1024.0, (long long)ctx->n_ctx);
@@ -690,7 +697,10 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
     if (c.n_batch_max > ctx->rows) c.n_batch_max = (int32_t)ctx->rows;
 
     const int64_t D = ctx->D;
-    ctx->layer_elems = ctx->rows * ctx->hkv_loc * D;
+    ctx->layer_elems = ctx->rows * ctx->hkv_loc * D;   // <= 2^31 x 64 x 256
+    if ((double)c.n_layer * 4.0 * (double)ctx->layer_elems > 0x1p60)   // beyond any device, and near size_t's range
+        return bail(fail(KV_E_OOM, "a cache of %lld rows x %d layers is beyond any device's memory",
+                         (long long)ctx->rows, c.n_layer));
     const size_t cache_bytes = (size_t)c.n_layer * 2u * (size_t)ctx->layer_elems * sizeof(__half);
     e = cudaMalloc(&ctx->cache, cache_bytes);
     if (e != cudaSuccess) {

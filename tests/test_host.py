@@ -156,6 +156,25 @@ def test_ring_and_head_dim_256_shape_rules():
     K.rope_table_host(ok, 0, 1)
 
 
+def test_oversized_contexts_are_refused_and_sizes_saturate():
+    """n_ctx above 2^31 positions is a shape error (checked before any CUDA
+    call, so kv_alloc's sizing never overflows); kv_cache_bytes saturates
+    instead of wrapping."""
+    import ctypes
+    sp = specs.get("llama3.1-8b-128k")
+    for n_ctx in ((1 << 31) + 64, 1 << 40, (1 << 62) + 64):
+        cfg = K.make_config(sp, n_ctx=n_ctx)
+        with pytest.raises(K.KvError) as e:
+            K.rope_table_host(cfg, 0, 1)
+        assert e.value.code == K.KV_E_ARG and "2^31" in str(e.value)
+        h = ctypes.c_void_p()
+        assert K.lib().kv_alloc(ctypes.byref(cfg), ctypes.byref(h)) == K.KV_E_ARG and not h.value
+    cfg = K.make_config(sp, n_ctx=1 << 31)
+    K.rope_table_host(cfg, 0, 1)
+    assert K.cache_bytes(cfg, 1 << 31) == 32 * 8 * 128 * 4 * (1 << 31)
+    assert K.cache_bytes(cfg, 1 << 62) == 2 ** 64 - 1
+
+
 def test_ring_cache_bytes():
     """A ring holds min(ring_cells, n_ctx) rows (dory_kv_cost, dory.c:373-389)."""
     sp = specs.get("llama3.2-3b")
