@@ -84,7 +84,7 @@ typedef struct kv_config {
                                    Q then times q_norm_w [n_head][head_dim] (the
                                    squared learned scale); k_norm_w unused     */
     float   rms_eps;            /* hparams::rms_eps                               */
-    int64_t n_ctx;              /* cache positions; 0 = auto from free HBM         */
+    int64_t n_ctx;              /* cache positions (<= 2^31); 0 = auto from free HBM */
     int64_t n_ctx_train;        /* auto-sizing clamp; 0 = 262144 cap              */
     int32_t longrope_clamp;     /* 1: auto-sizing also clamps to n_ctx_orig
                                    (phi3 with LongRoPE, model.cpp:1037-1039)     */
@@ -120,7 +120,8 @@ int kv_config_init(kv_config *cfg);
 
 /* Bytes of the whole K+V cache at n_ctx positions, all layers and all shards:
  * exactly kv_cache_bytes() of the reference (model.cpp:869-885); a ring
- * configuration holds min(ring_cells, n_ctx) rows. */
+ * configuration holds min(ring_cells, n_ctx) rows.  UINT64_MAX when the product
+ * does not fit 64 bits. */
 uint64_t kv_cache_bytes(const kv_config *cfg, int64_t n_ctx);
 
 /* Context auto-sizing rule of auto_n_ctx() (model.cpp:1002-1059) applied to
