@@ -36,7 +36,7 @@
  *   A3 cpy F32->F16 rounds to nearest even (IEEE).
  *   A4 mul_mat with an F16 src0 converts the F32 src1 to F16 (RNE) and
  *      accumulates products in F32 (summation order is implementation-defined;
- *      parity on attention outputs is therefore judged within a tolerance).
+ *      parity on attention outputs is therefore checked within a tolerance).
  *   A5 soft_max_ext: w = s*scale + mask, m = max w, e = expf(w - m) in float,
  *      sum accumulated in double, p = e * (float)(1.0/sum); a row whose w are
  *      all -inf gives NaN (expf(-inf - -inf)).

@@ -2,7 +2,7 @@
 
 Bar: appended cache bytes bit-exact against the CPU oracle; attention outputs
 within max-abs 2e-3 and relative L2 1e-3 (F32) of the oracle -- the tolerance
-the reference's numerics are judged by.  Covers the golden fixtures of every
+set for the path's floating-point outputs.  Covers the golden fixtures of every
 benchmark shape, the full-size decode of the 32k and 128k shapes, and the
 edge cases of the reference's cache contract (first token, rewind by
 overwrite, multi-pass query rows, separate/fused/unaligned input rows).
