@@ -234,6 +234,38 @@ def test_noalloc_refuses_oversized_shapes_before_any_device_work():
     assert lib.kv_attend_decode_noalloc(kc, vc, 32, 8, 128, 4096, q, out, None) == K.KV_E_CUDA
 
 
+@pytest.mark.parametrize("name,unit,want", [
+    ("qwen2-0.5b", "GB", 0.0254),        # 24 layers, 2049 keys
+    ("llama3.2-3b", "GB", 3.686),        # 28 layers, 32001..32256 keys, mean of 256 steps
+    ("phi3-mini", "GB", 1.588),          # 32 MHA layers, 3969..4096 keys, mean of 128 steps
+    ("llama3.1-8b-128k", "GB", 17.18),   # 32 layers, 131001..131064 keys, mean of 64 steps
+    ("qwen3-8b-prefill", "TFLOP", 5.025),  # 512 causal queries after 16384 rows
+])
+def test_bench_algorithmic_work_per_token(name, unit, want):
+    """The roofline's numerator: bytes per decode token (K and V read once in
+    F16, the new rows written, k/v read and q/o in F32; split partials and
+    re-reads not counted) and causal FLOPs per chunk (4*d*Hq per visible
+    query-key pair), averaged over the configuration's steps."""
+    import importlib
+    import statistics
+    import sys as _sys
+    _sys.path.insert(0, ROOT)
+    bench = importlib.import_module("bench")
+    sp = specs.get(name)
+    pos = bench.positions(sp, 0, sp["steps"])
+    L, hq, hkv, d = sp["n_layer"], sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+    if unit == "TFLOP":
+        got = statistics.mean(bench.step_flops(sp, p, sp["n_new"]) for p in pos) / 1e12
+        n = sp["n_new"]
+        keys = sum(sp["n_past"] + i + 1 for i in range(n))
+        assert bench.step_flops(sp, sp["n_past"], n) == 4 * d * keys * hq * L
+    else:
+        got = statistics.mean(bench.step_bytes(sp, p) for p in pos) / 1e9
+        p0 = sp["n_past"]
+        assert bench.step_bytes(sp, p0) == L * ((p0 + 1) * hkv * d * 4 + hkv * d * 4 + hkv * d * 8 + hq * d * 8)
+    assert abs(got - want) / want < 2e-3, (got, want)
+
+
 def test_cpu_baseline_sample_at_two_thread_counts():
     """The GPU arm's cpu_baseline samples the CPU path on every core and on the
     reference's own 8 threads, reusing one set of generated cache rows."""
