@@ -3,7 +3,7 @@
  * TEST INFRASTRUCTURE ONLY (see kv_oracle.h for scope, sources and the
  * assumptions A1-A6 under which it restates ggml's op semantics).
  *
- * Build: oracle/build.sh (gcc -O3 -ffp-contract=off -pthread).  Contraction
+ * Build: oracle/build.py (gcc -O3 -ffp-contract=off -pthread).  Contraction
  * must stay off: RoPE and RMSNorm are compared bit-for-bit and their reference
  * form has separately rounded products and sums.
  */

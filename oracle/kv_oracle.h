@@ -46,11 +46,24 @@
  *      precision are not restated -- the oracle takes the exact weights
  *      exp(w - m) / sum in double, rounded once to float, with F32 accumulation
  *      of P . V, and a row whose w are all -inf gives 0 (its sum is 0).
- * The NEOX pairing, the RMSNorm formula and the softmax formula are also
- * cross-checked against the reference's own scalar backend
- * (src/moe_stream/compute_backend.c:42-86), compiled from its sources by
- * oracle/build_ref.sh; that backend sums in float, so the check is within a
- * tolerance and pins semantics, not bits.
+ * What reference code pins (the reference's MoE engine, src/moe_stream, which
+ * computes the same decode attention without ggml on an F32 cache; compiled
+ * from its sources by oracle/build.py):
+ *   - its scalar backend (compute_backend.c:42-86): the NEOX rotation bit for
+ *     bit given the same table; RMSNorm and softmax within 2e-6 (it sums in
+ *     float);
+ *   - its attention_block (qwen_model.c:456-524, driven by ref_attention.c):
+ *     the GQA mapping h / (n_head / n_head_kv), the scale 1/sqrtf(hd), the
+ *     causal range 0..pos, softmax and P.V, per-head Q/K RMSNorm -- outputs
+ *     within max-abs 2e-3 / rel-L2 1e-3 at the benchmark shapes (2k-32k keys);
+ *     its stored K row equals the oracle's rotation with its table entries bit
+ *     for bit, its V row the oracle's F16 row after RNE;
+ *   - its RoPE table (qwen_model.c:346-353, angles in double): every entry
+ *     within (pos + 2) * 2^-22 of the oracle's (NEOX, no freq factors).
+ * Still unpinned at the bit level (the MoE engine does not perform them):
+ * A1's double sum, A2's iterated float angles, A4's F16 rounding of Q and of
+ * the normalised P, A5's double sum, all of A6, and the NORMAL pairing, freq
+ * factors and YaRN of A2.
  */
 #ifndef KV_ORACLE_H
 #define KV_ORACLE_H

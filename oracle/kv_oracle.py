@@ -302,3 +302,60 @@ def reference_scalar_backend():
     L = ctypes.CDLL(_REF_PATH)
     L.compute_backend_scalar.restype = ctypes.POINTER(_RefBackend)
     return L.compute_backend_scalar().contents
+
+
+# -- the reference's own single-token attention (oracle/_ref/libref_attention.so) -
+
+_REF_ATTN_PATH = os.path.join(HERE, "_ref", "libref_attention.so")
+
+
+class ReferenceAttention:
+    """The reference MoE engine's attention_block (qwen_model.c:456-524) and
+    RoPE table (qwen_model.c:346-353), driven through oracle/ref_attention.c
+    on a model file written by oracle/ref_gguf.py.  F32 cache, NEOX RoPE over
+    the whole head, no freq factors: it pins the semantics the oracle shares
+    with it (GQA head mapping, scale, causal range, softmax, P.V, NEOX pairing,
+    the angle schedule), not ggml's F16 roundings."""
+
+    def __init__(self, path):
+        L = ctypes.CDLL(path)
+        L.ref_attention_step.restype = ctypes.c_int
+        L.ref_attention_step.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, _f32p, _f32p, _f32p, _f32p,
+                                         _f32p, ctypes.c_int, _f32p, _f32p, _f32p, _f32p, _f32p]
+        L.ref_model_geometry.restype = ctypes.c_int
+        L.ref_model_geometry.argtypes = [ctypes.c_char_p, ctypes.c_int] + [ctypes.POINTER(ctypes.c_int)] * 3 + \
+            [ctypes.POINTER(ctypes.c_float)] * 2
+        self._lib = L
+
+    def geometry(self, gguf, max_seq):
+        v = [ctypes.c_int() for _ in range(3)] + [ctypes.c_float() for _ in range(2)]
+        rc = self._lib.ref_model_geometry(gguf.encode(), max_seq, *[ctypes.byref(x) for x in v])
+        assert rc == 0, rc
+        return tuple(x.value for x in v)
+
+    def step(self, gguf, max_seq, pos, k_rows, v_rows, q, k, v, use_norm, n_head, n_head_kv, head_dim):
+        """One decode step at `pos` over cache rows [pos][n_head_kv*head_dim] F32.
+        Returns (attention output, stored K row, stored V row, cos table, sin table)."""
+        nkvd = n_head_kv * head_dim
+        kr = np.ascontiguousarray(np.asarray(k_rows, np.float32).reshape(pos, nkvd))
+        vr = np.ascontiguousarray(np.asarray(v_rows, np.float32).reshape(pos, nkvd))
+        q = np.ascontiguousarray(q, np.float32).reshape(-1)
+        k = np.ascontiguousarray(k, np.float32).reshape(-1)
+        v = np.ascontiguousarray(v, np.float32).reshape(-1)
+        out = np.zeros(n_head * head_dim, np.float32)
+        ko = np.zeros(nkvd, np.float32)
+        vo = np.zeros(nkvd, np.float32)
+        cs = np.zeros((max_seq, head_dim // 2), np.float32)
+        sn = np.zeros((max_seq, head_dim // 2), np.float32)
+        rc = self._lib.ref_attention_step(gguf.encode(), max_seq, pos, _p(kr), _p(vr), _p(q), _p(k), _p(v),
+                                          int(use_norm), _p(out), _p(ko), _p(vo), _p(cs), _p(sn))
+        assert rc == 0, rc
+        return out, ko, vo, cs, sn
+
+
+def reference_attention():
+    """ReferenceAttention over oracle/_ref/libref_attention.so, or None when it
+    was not built (no reference checkout on this host)."""
+    if not os.path.exists(_REF_ATTN_PATH):
+        return None
+    return ReferenceAttention(_REF_ATTN_PATH)

@@ -3,9 +3,11 @@ compared against.  The reference ships no fixtures for this path (ggml is not
 vendored), so the oracle is pinned by: (1) exhaustive/numpy checks of its F16
 rounding, (2) the reference's own scalar math backend
 (src/moe_stream/compute_backend.c, built by oracle/build.py into oracle/_ref)
-for the NEOX rotation, RMSNorm and softmax formulas, (3) an independent
-float64 numpy restatement of the attention, and (4) the committed golden
-fixtures (regression pin).
+for the NEOX rotation, RMSNorm and softmax formulas, (3) the reference's own
+decode attention and RoPE table (src/moe_stream/qwen_model.c:456-524 and
+:346-353, driven by oracle/ref_attention.c into oracle/_ref) at the benchmark
+shapes, (4) an independent float64 numpy restatement of the attention, and
+(5) the committed golden fixtures (regression pin).
 """
 import ctypes
 import math
@@ -261,6 +263,106 @@ def test_softmax_semantics_against_reference_scalar_backend():
         ref.softmax(None, _fp(s), n_kv)   # compute_backend.c:68-86
         o = s.astype(np.float16).astype(np.float32) @ V[:, kvh]
         assert np.allclose(o, got[0, h * d:(h + 1) * d], rtol=0, atol=2e-5)
+
+
+# ---------------------------------------------------------------------------
+# the reference's own decode attention (moe_stream/qwen_model.c:456-524) and
+# RoPE table (:346-353), compiled into oracle/_ref/libref_attention.so
+# ---------------------------------------------------------------------------
+
+def _ref_attention_case(tmp_path, name, pos, use_norm=False, **overrides):
+    """One decode step at `pos` through the reference's attention_block and the
+    oracle, on the same F16-representable cache and the same Q/K/V rows."""
+    ra = O.reference_attention()
+    if ra is None:
+        pytest.skip("oracle/_ref/libref_attention.so not built (no reference checkout on this host)")
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle"))
+    import ref_gguf
+    sp = specs.get(name)
+    sp.update(overrides)
+    hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+    qn, kn = synth.norm_weights(sp, 0) if use_norm else (None, None)
+    gguf = ref_gguf.write(str(tmp_path / "model.gguf"), hq, hkv, d, sp["rope_base"], sp["rms_eps"], qn, kn)
+    assert ra.geometry(gguf, pos + 1)[:3] == (hq, hkv, d)
+    kc = np.zeros((pos + 1, hkv, d), np.uint16)
+    vc = np.zeros_like(kc)
+    kc[:pos] = O.gen_cache_rows(sp["seed"], synth.STREAM_CACHE, 0, pos, hkv, d)
+    vc[:pos] = O.gen_cache_rows(sp["seed"], synth.STREAM_CACHE + 1, 0, pos, hkv, d)
+    rows = synth.qkv_rows(sp, 0, 0, 1)
+    q, k, v = rows[:, :hq * d], rows[:, hq * d:(hq + hkv) * d], rows[:, (hq + hkv) * d:]
+    ref = ra.step(gguf, pos + 1, pos, kc[:pos].view(np.float16).astype(np.float32),
+                  vc[:pos].view(np.float16).astype(np.float32), q, k, v, use_norm, hq, hkv, d)
+    orc = O.Oracle(sp)
+    q_roped = orc.append(kc, vc, pos, q, k, v, qn, kn)
+    ours = orc.attend(kc, vc, pos, q_roped)[0]
+    return sp, orc, kc, vc, rows, ref, ours
+
+
+# The reference's MoE engine keeps an F32 cache and F32 weights: the oracle's
+# ggml roundings (F16 Q and P in mul_mat, A4) and angle schedule (A2) are not
+# its; the outputs agree within the north-star tolerance, which an error in
+# the shared semantics (GQA mapping h / (Hq/Hkv), scale 1/sqrt(hd), the causal
+# range 0..pos, softmax, P.V, NEOX pairs) would exceed by orders of magnitude.
+@pytest.mark.parametrize("name,pos,use_norm,over", [
+    ("qwen2-0.5b", 2048, False, {}),                                     # config 1
+    ("llama3.2-3b", 4096, False, {"rope_mode": 2, "rope_freq_factors": None}),   # config 2's heads
+    ("llama3.2-3b", 32000, False, {"rope_mode": 2, "rope_freq_factors": None}),  # ... at its context
+    ("phi3-mini", 3968, False, {}),                                      # config 3 (MHA, head_dim 96)
+    ("qwen3-8b-prefill", 2000, True, {}),                                # config 4's heads, QK-Norm
+])
+def test_attention_matches_reference_attention_block(tmp_path, name, pos, use_norm, over):
+    sp, orc, kc, vc, rows, ref, ours = _ref_attention_case(tmp_path, name, pos, use_norm, **over)
+    out = ref[0].astype(np.float64)
+    d = ours - out
+    assert np.abs(d).max() <= 2e-3
+    assert np.linalg.norm(d) / np.linalg.norm(out) <= 1e-3
+    # the stored V row: the reference keeps the F32 input, the oracle its RNE F16
+    assert np.array_equal(ref[2].astype(np.float16).view(np.uint16), vc[pos].reshape(-1))
+
+
+@pytest.mark.parametrize("name,pos,over", [
+    ("qwen2-0.5b", 2048, {}),
+    ("llama3.2-3b", 32000, {"rope_mode": 2, "rope_freq_factors": None}),
+    ("phi3-mini", 3968, {}),
+])
+def test_rotation_matches_reference_given_its_table(tmp_path, name, pos, over):
+    """The reference's stored K row (NEOX RoPE by its scalar backend with its
+    own table) equals, bit for bit, the oracle's rotation of the same row with
+    the reference's table entries at pos: the pairing and the separately
+    rounded products and sums are the same; only the angles differ (A2)."""
+    sp, orc, kc, vc, rows, ref, ours = _ref_attention_case(tmp_path, name, pos, **over)
+    hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+    cs = np.stack([ref[3][pos], ref[4][pos]], axis=1)
+    k = rows[0, hq * d:(hq + hkv) * d].reshape(hkv, d)
+    got = np.concatenate([orc.rope_row(cs, k[h]) for h in range(hkv)])
+    assert np.array_equal(got.view(np.uint32), ref[1].view(np.uint32))
+
+
+@pytest.mark.parametrize("name,n_pos", [("qwen2-0.5b", 4096), ("llama3.2-3b", 32768), ("phi3-mini", 4096)])
+def test_rope_table_against_reference_table(tmp_path, name, n_pos):
+    """The oracle's angle table (ggml's schedule: theta_i by iterated float
+    products, angle pos * theta_i in float, A2) against the reference MoE
+    engine's (pos * base^(-2i/hd) in double, qwen_model.c:346-353) for NEOX
+    without freq factors: every entry within (pos + 1) * 2^-22 + 2^-22 -- the
+    float angle's relative error is a few 2^-24, times an angle of up to pos
+    radians."""
+    ra = O.reference_attention()
+    if ra is None:
+        pytest.skip("oracle/_ref/libref_attention.so not built (no reference checkout on this host)")
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle"))
+    import ref_gguf
+    sp = specs.get(name)
+    sp.update(rope_mode=2, rope_freq_factors=None)
+    hq, hkv, d = sp["n_head"], sp["n_head_kv"], sp["head_dim"]
+    gguf = ref_gguf.write(str(tmp_path / "model.gguf"), hq, hkv, d, sp["rope_base"])
+    z = np.zeros((1, hkv * d), np.float32)
+    ref = ra.step(gguf, n_pos, 0, z[:0], z[:0], np.zeros(hq * d, np.float32), z, z, False, hq, hkv, d)
+    tab = O.Oracle(sp).rope_table(0, n_pos)
+    bound = (np.arange(n_pos, dtype=np.float64)[:, None] + 2.0) * 2.0 ** -22
+    assert np.all(np.abs(tab[:, :, 0] - ref[3]) <= bound)
+    assert np.all(np.abs(tab[:, :, 1] - ref[4]) <= bound)
+    # position 0 exactly: cos 1, sin 0
+    assert np.all(tab[0, :, 0] == 1.0) and np.all(ref[3][0] == 1.0)
 
 
 def _causal_mask(n_past, n_new, stride, dtype):
