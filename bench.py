@@ -184,15 +184,27 @@ class CpuPath:
         self.max_steps = max(1, min(max_steps, sp["steps"]))
         n_ctx = sp["n_past"] + self.max_steps + sp["n_new"]
         per_layer_cache = 2 * n_ctx * hkv * d * 2
-        self.n_lay = max(1, min(sp["n_layer"], 4, int(2e9 // per_layer_cache)))
-        self.caches = []
-        for l in range(self.n_lay):
+        if sp["n_new"] == 1:
+            # decode: every layer whose cache fits in 8 GB of host memory (all
+            # of them up to the 32k configuration), so the per-token time is
+            # measured over the whole model where it can be
+            self.n_lay = max(1, min(sp["n_layer"], int(8e9 // per_layer_cache)))
+        else:
+            # a prefill chunk costs the CPU about a second per layer: 4 layers
+            self.n_lay = max(1, min(sp["n_layer"], 4, int(2e9 // per_layer_cache)))
+        self.caches = [None] * self.n_lay
+
+        def fill(l):
             kc = np.zeros((n_ctx, hkv, d), np.uint16)
             vc = np.zeros((n_ctx, hkv, d), np.uint16)
             kc[:sp["n_past"]] = O.gen_cache_rows(sp["seed"], synth.STREAM_CACHE + 2 * l, 0, sp["n_past"], hkv, d)
             vc[:sp["n_past"]] = O.gen_cache_rows(sp["seed"], synth.STREAM_CACHE + 2 * l + 1, 0, sp["n_past"],
                                                  hkv, d)
-            self.caches.append((kc, vc))
+            self.caches[l] = (kc, vc)
+
+        import concurrent.futures as cf   # the generator releases the GIL
+        with cf.ThreadPoolExecutor(max_workers=max(1, min(8, O.online_cores()))) as ex:
+            list(ex.map(fill, range(self.n_lay)))
         self.orc = O.Oracle(sp)
         self.threads = n_threads if n_threads > 0 else O.online_cores()
         self.norms = [synth.norm_weights(sp, l) if sp["qk_norm"] else (None, None) for l in range(self.n_lay)]
@@ -224,9 +236,12 @@ class CpuPath:
     def describe(self, steps):
         sp = self.sp
         what = "decode step(s)" if self.n_new == 1 else "%d-token chunk(s)" % self.n_new
-        return ("%d %s x first %d of %d layers at n_past %d, %d threads; per-step time "
-                "extrapolated linearly to all layers" % (steps, what, self.n_lay, sp["n_layer"], sp["n_past"],
-                                                       self.threads))
+        if self.n_lay == sp["n_layer"]:
+            return "%d %s x all %d layers at n_past %d, %d threads; measured, not extrapolated" % (
+                steps, what, sp["n_layer"], sp["n_past"], self.threads)
+        return ("%d %s x first %d of %d layers at n_past %d, %d threads; per-step time extrapolated x%.2f "
+                "from %d of %d layers" % (steps, what, self.n_lay, sp["n_layer"], sp["n_past"], self.threads,
+                                          sp["n_layer"] / self.n_lay, self.n_lay, sp["n_layer"]))
 
 
 def cpu_sample(sp, seconds, max_steps, flash=False, n_threads=0, cp=None):

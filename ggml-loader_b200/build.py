@@ -39,11 +39,11 @@ def _stale(target, deps):
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def _compile(src, verbose):
-    obj = os.path.join(OBJ, os.path.basename(src) + ".o")
+def _compile(src, verbose, obj_dir=OBJ, defines=()):
+    obj = os.path.join(obj_dir, os.path.basename(src) + ".o")
     if not _stale(obj, [src] + _headers()):
         return obj
-    cmd = [NVCC] + ARCH + COMMON + ["-c", src, "-o", obj]
+    cmd = [NVCC] + ARCH + COMMON + ["-D" + d for d in defines] + ["-c", src, "-o", obj]
     if verbose and src.endswith(".cu"):
         cmd += ["-Xptxas", "-v"]
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -54,18 +54,21 @@ def _compile(src, verbose):
     return obj
 
 
-def build(verbose=False):
-    os.makedirs(OBJ, exist_ok=True)
-    os.makedirs(os.path.dirname(LIB), exist_ok=True)
+def build(verbose=False, lib=LIB, obj_dir=OBJ, defines=()):
+    """Compile and link the library.  `defines` builds a variant (e.g.
+    KV_PHASE_STAMPS, the per-CTA phase stamps of the decode kernel, for
+    measurement) into its own `lib` and `obj_dir`."""
+    os.makedirs(obj_dir, exist_ok=True)
+    os.makedirs(os.path.dirname(lib), exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
-    if _stale(LIB, objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-ldl", "-lpthread"]
+        objs = list(ex.map(lambda s: _compile(s, verbose, obj_dir, defines), srcs))
+    if _stale(lib, objs):
+        cmd = [NVCC] + ARCH + ["-shared", "-o", lib] + objs + ["-ldl", "-lpthread"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n%s\n%s" % (" ".join(cmd), r.stderr))
-    return LIB
+    return lib
 
 
 if __name__ == "__main__":

@@ -51,6 +51,17 @@ namespace {
 
 using namespace sm100;
 
+// Phase stamps for measurement builds (-DKV_PHASE_STAMPS): one %globaltimer
+// value per (CTA, phase) into AttnParams::stamps; nothing in other builds.
+#ifdef KV_PHASE_STAMPS
+#define KV_STAMP(cond, i)                                                                  \
+    do {                                                                                   \
+        if (p.stamps && (cond)) p.stamps[(int64_t)blockIdx.x * kStampSlots + (i)] = globaltimer(); \
+    } while (0)
+#else
+#define KV_STAMP(cond, i) do { } while (0)
+#endif
+
 constexpr int kTK = 128;         // keys per tile (8 warps x 16)
 constexpr int kConsumers = 256;  // warps 0-7
 constexpr int kThreads = 288;    // + producer warp 8
@@ -285,6 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         fence_mbar_init();
     }
     __syncthreads();
+    KV_STAMP(tid == 0, 0);   // entry
 
     // ---- producer: K tiles 0..nt-1, then V tiles 0..nt-1, one ring ----
     if (warp == 8) {
@@ -319,6 +331,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                     waited = true;
                 }
                 mbar_arrive_expect_tx(&full[s], kStage);
+                if (j == 0) KV_STAMP(true, 10);   // first tile issued
+                if (j == NS) KV_STAMP(true, 11);  // first tile past the ring depth issued
 #pragma unroll
                 for (int b = 0; b < NB; b++)
                     tma_load_3d_hint(smem + s * kStage + b * kSub, isv ? &vmap : &kmap, &full[s], b * BW, h, (int)k0,
@@ -365,6 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     }
     pdl_wait();   // inputs, qbuf and the rows below may come from the previous kernel
     pdl_launch_dependents();   // only now: the next kernel may rely on every kernel before this one
+    KV_STAMP(tid == 0, 1);   // griddepcontrol.wait returned
 
     // decode: rotate the query rows of both heads and the new K row, one item per warp
     if (p.fused) {
@@ -392,6 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         }
         named_sync(1, kConsumers);
     }
+    KV_STAMP(tid == 0, 2);   // query rows rotated
 
     // B fragments (Q^T): column n = query row gq, k = dims
     uint32_t bq[KC][2];
@@ -512,6 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
 
     // ======================= statistics =======================
     // (max, sum) per (segment, row): the 8 lanes of a row pair, then the 8 warps
+    KV_STAMP(tid == 0, 3);   // warp 0's K loop done
     {
         const float m_s[2][2] = {{two ? ma0 : ma, two ? mb0 : mb}, {ma, mb}};
         const float z_s[2][2] = {{two ? za0 : za, two ? zb0 : zb}, {za, zb}};
@@ -559,6 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                        tag | __float_as_uint(aborted ? -INFINITY : M),
                        tag | __float_as_uint(aborted ? 0.0f : (float)Z));
     }
+    KV_STAMP(tid == 0, 4);   // statistics published
     // decode: the new V row of head h0 goes to the cache now, while others finish
     if (owns_new && warp == 7) {
         const float *src = p.v + (int64_t)(p.hkv0 + g.h0) * D;
@@ -651,6 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         }
     }
     aborted = named_sync_or(1, kConsumers, aborted || late);
+    KV_STAMP(tid == 0, 5);   // global statistics known
 
     // ======================= V phase =======================
     float oacc[DT][4];
@@ -707,6 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         if (tid == 0)
             flags[1 + sl] = atom_add_acq_rel_gpu(&p.counters[h], 1u) == (unsigned)(p.span_b[h] - p.span_a[h]);
         named_sync(1, kConsumers);
+        KV_STAMP(tid == 0, 7);   // partial added, ticket taken
         if (flags[1 + sl]) {
             const unsigned nan_rows = __ldcg(&p.nonfin[h]);
             const int par = (int)(p.epoch & 1u);
@@ -736,6 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 if (tid == 0) flags[3] = atomicAdd(p.xticket, 1u) == (unsigned)(p.hkv - 1);
                 named_sync(1, kConsumers);
                 if (flags[3]) {
+                    KV_STAMP(tid == 0, 8);   // collector starts polling the peers' words
                     // every column outside this shard's, once its word carries
                     // this launch's tag; a thread keeps up to 8 words' loads in
                     // flight per poll
@@ -770,6 +791,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                         }
                     }
                     if (named_sync_or(1, kConsumers, late) && tid == 0) atomicOr(p.err, 8u);
+                    KV_STAMP(tid == 0, 9);   // collector done
                     if (tid == 0) *p.xticket = 0u;
                 }
             }
@@ -842,12 +864,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         if (lane == 0) mbar_arrive(&empty[s]);
     }
     cp_async_wait<0>();
+    KV_STAMP(tid == 0, 6);   // warp 0's V loop done
     flush_out(two ? 1 : 0);
     // every consumer has read its scores (flush_out opens with a barrier): the
     // scratch is dead until the next launch rewrites it, so it leaves L2
     // without a write-back
     for (int ln = tid; ln < g.nt * (kTileScores / 32); ln += kConsumers) l2_discard(Scta + ln * 32);
     named_sync(2, kThreads);
+    KV_STAMP(tid == 0, 12);   // exit
 }
 
 // ---------------------------------------------------------------------------

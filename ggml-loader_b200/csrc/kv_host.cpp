@@ -272,6 +272,12 @@ struct kv_ctx {
     ncclComm_t comm = nullptr;
 
     std::atomic<int64_t> launches{0};
+#ifdef KV_PHASE_STAMPS
+    // measurement builds: phase stamps of the last kStampRing attention launches
+    static constexpr int kStampRing = 256;
+    unsigned long long *stamps = nullptr;   // [kStampRing][max_cta][kStampSlots]
+    int64_t stamp_next = 0;
+#endif
     bool prof_on = false;
     struct Rec {
         int k;
@@ -465,6 +471,9 @@ void free_all(kv_ctx *ctx)
                     ctx->local_out, ctx->gathered, ctx->pf_stat, ctx->pf_out, ctx->pf_rstat, ctx->ring_mask};
     for (void *p : ptrs)
         if (p) cudaFree(p);
+#ifdef KV_PHASE_STAMPS
+    if (ctx->stamps) cudaFree(ctx->stamps);
+#endif
 }
 
 
@@ -749,6 +758,14 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
     if (e != cudaSuccess) return bail(cuda_fail(e, "cudaMemset"));
     e = kvb::attn_prepare(ctx->D);
     if (e != cudaSuccess) return bail(cuda_fail(e, "attn_prepare"));
+#ifdef KV_PHASE_STAMPS
+    {
+        const size_t sb = (size_t)kv_ctx::kStampRing * ctx->max_cta * kvb::kStampSlots * sizeof(unsigned long long);
+        e = cudaMalloc(&ctx->stamps, sb);
+        if (e == cudaSuccess) e = cudaMemset(ctx->stamps, 0, sb);
+        if (e != cudaSuccess) return bail(fail(KV_E_OOM, "stamp buffer"));
+    }
+#endif
 
     // TMA descriptors: each layer's K and V as [n_ctx][hkv_loc][D] F16, box =
     // one head x 128 keys x a 64-wide column block with 128-byte swizzle (32
@@ -1179,6 +1196,9 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
             ctx->epoch = 1;
         }
         ap.epoch = ctx->epoch;
+#ifdef KV_PHASE_STAMPS
+        ap.stamps = ctx->stamps + (size_t)(ctx->stamp_next++ % kv_ctx::kStampRing) * ctx->max_cta * kvb::kStampSlots;
+#endif
         rc = launch(ctx, KV_K_ATTN, st, "attention kernel",
                     [&] { return kvb::launch_attn(ctx->D, km, vm, ap, st, true); });
         if (rc) return rc;
@@ -1425,6 +1445,23 @@ const char *kv_kernel_name(int32_t kernel)
 }
 
 int64_t kv_launch_count(const kv_ctx *ctx) { return ctx ? ctx->launches.load() : 0; }
+
+#ifdef KV_PHASE_STAMPS
+// Measurement builds only: copies the stamp ring ([ring][max_cta][slots]
+// globaltimer values) to host_dst and returns the number of launches stamped
+// so far (launch i sits in ring slot i % ring); *ring and *max_cta describe it.
+int64_t kv_debug_stamps(kv_ctx *ctx, unsigned long long *host_dst, int32_t *ring, int32_t *max_cta)
+{
+    if (!ctx || !host_dst) return -1;
+    if (ensure_device(ctx)) return -1;
+    cudaDeviceSynchronize();
+    *ring = kv_ctx::kStampRing;
+    *max_cta = ctx->max_cta;
+    cudaMemcpy(host_dst, ctx->stamps, (size_t)kv_ctx::kStampRing * ctx->max_cta * kvb::kStampSlots * 8u,
+               cudaMemcpyDeviceToHost);
+    return ctx->stamp_next;
+}
+#endif
 
 int kv_rope_table_host(const kv_config *cfg, int64_t pos0, int64_t npos, float *out)
 {

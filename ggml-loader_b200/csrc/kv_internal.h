@@ -152,7 +152,11 @@ struct AttnParams {
     // segment index head h has in CTA span_a[h] (1 when that CTA starts in head h-1)
     int16_t span_a[kMaxLocalHeads], span_b[kMaxLocalHeads];
     int8_t span_slot[kMaxLocalHeads];
+    // builds with KV_PHASE_STAMPS only (measurement): [n_cta][kStampSlots]
+    // %globaltimer stamps of this launch's phases, nullptr otherwise
+    unsigned long long *stamps;
 };
+constexpr int kStampSlots = 16;
 
 // query rows per launch (8), keys per tile (128), the column-box width of the
 // K/V tensor maps (64 halves, 128-byte swizzle; 32, 64-byte swizzle at 96), and

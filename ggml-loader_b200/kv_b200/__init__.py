@@ -12,7 +12,9 @@ from . import specs, synth  # noqa: F401
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
-LIB_PATH = os.path.join(PKG, "lib", "libkv_b200.so")
+# KV_B200_LIBRARY names another build of the same library to load instead
+# (a measurement variant such as the phase-stamp build)
+LIB_PATH = os.environ.get("KV_B200_LIBRARY") or os.path.join(PKG, "lib", "libkv_b200.so")
 
 KV_OK = 0
 KV_E_ARG = -1
