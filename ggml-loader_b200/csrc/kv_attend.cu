@@ -43,6 +43,8 @@
 // kv_status, and the CTA drains its own tile loads before leaving.
 #include <math.h>
 
+#include <algorithm>
+
 #include "kv_internal.h"
 #include "kv_sm100.cuh"
 
@@ -892,18 +894,42 @@ cudaError_t prep()
 }
 
 template <int D>
-cudaError_t launch(const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnParams &p, cudaStream_t st, bool pdl)
+cudaError_t occupancy(int *blocks)
+{
+    // the fewest resident CTAs an SM takes among the four instances
+    int b[4] = {0, 0, 0, 0};
+    const size_t sm = Smem<D>::bytes;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b[0], attn_decode_kernel<D, false, false>, kThreads, sm);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b[1], attn_decode_kernel<D, false, true>, kThreads, sm);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b[2], attn_decode_kernel<D, true, false>, kThreads, sm);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b[3], attn_decode_kernel<D, true, true>, kThreads, sm);
+    *blocks = std::min(std::min(b[0], b[1]), std::min(b[2], b[3]));
+    return e;
+}
+
+template <int D>
+cudaError_t launch(const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnParams &p, cudaStream_t st, bool pdl,
+                   bool coop)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)p.n_cta);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = Smem<D>::bytes;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (coop) {
+        attr[na].id = cudaLaunchAttributeCooperative;
+        attr[na].val.cooperative = 1;
+        na++;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = na;
     const bool m = p.mask || p.all_keys;
     if (m && p.flash) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true, true>, kmap, vmap, p);
     if (m) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true, false>, kmap, vmap, p);
@@ -930,15 +956,26 @@ cudaError_t attn_prepare(int D)
     }
 }
 
+cudaError_t attn_occupancy(int D, int *blocks_per_sm)
+{
+    switch (D) {
+    case 64: return occupancy<64>(blocks_per_sm);
+    case 96: return occupancy<96>(blocks_per_sm);
+    case 128: return occupancy<128>(blocks_per_sm);
+    case 256: return occupancy<256>(blocks_per_sm);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
 cudaError_t launch_attn(int D, const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnParams &p,
-                        cudaStream_t st, bool pdl)
+                        cudaStream_t st, bool pdl, bool coop)
 {
     if (p.nrows < 1 || p.nrows > kRows) return cudaErrorInvalidValue;
     switch (D) {
-    case 64: return launch<64>(kmap, vmap, p, st, pdl);
-    case 96: return launch<96>(kmap, vmap, p, st, pdl);
-    case 128: return launch<128>(kmap, vmap, p, st, pdl);
-    case 256: return launch<256>(kmap, vmap, p, st, pdl);
+    case 64: return launch<64>(kmap, vmap, p, st, pdl, coop);
+    case 96: return launch<96>(kmap, vmap, p, st, pdl, coop);
+    case 128: return launch<128>(kmap, vmap, p, st, pdl, coop);
+    case 256: return launch<256>(kmap, vmap, p, st, pdl, coop);
     default: return cudaErrorInvalidValue;
     }
 }

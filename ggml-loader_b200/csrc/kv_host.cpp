@@ -248,6 +248,7 @@ struct kv_ctx {
     std::vector<CUtensorMap> kmaps, vmaps;  // per layer: [n_ctx][hkv_loc][D] F16, swizzled column boxes
     uint64_t limit_ns = 1000000000ull;      // bound of every device-side wait (1 s)
     int inject = 0;                         // test hook, applies to the next decode launch
+    bool coop = false;                      // attention kernels as cooperative launches
 
     Pending pend;  // a deferred single-token kv_append
     // state of the last kv_append (kv_attend must follow it)
@@ -402,6 +403,12 @@ int decode_ctas_for(int sm_count, int hkv_loc, int64_t n_kv)
     c = std::max<int64_t>(c, hkv_loc);
     c = std::min<int64_t>(c, T);
     return (int)c;
+}
+
+// whether a grid of n_cta CTAs is resident at once with blocks_per_sm on each SM
+bool decode_grid_fits(int sm_count, int blocks_per_sm, int n_cta)
+{
+    return sm_count > 0 && blocks_per_sm > 0 && n_cta > 0 && (int64_t)sm_count * blocks_per_sm >= n_cta;
 }
 
 int decode_ctas(const kv_ctx *ctx, int64_t n_kv)
@@ -758,6 +765,19 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
     if (e != cudaSuccess) return bail(cuda_fail(e, "cudaMemset"));
     e = kvb::attn_prepare(ctx->D);
     if (e != cudaSuccess) return bail(cuda_fail(e, "attn_prepare"));
+    {
+        // the attention kernel's CTAs wait on one another: its largest grid
+        // must be resident at once on this device
+        int bps = 0;
+        e = kvb::attn_occupancy(ctx->D, &bps);
+        if (e != cudaSuccess) return bail(cuda_fail(e, "attention kernel occupancy"));
+        if (!decode_grid_fits(ctx->sm_count, bps, ctx->max_cta))
+            return bail(fail(KV_E_UNSUPPORTED,
+                             "the attention kernel's %d CTAs cannot be resident at once (%d SMs x %d CTAs an SM)",
+                             ctx->max_cta, ctx->sm_count, bps));
+        const char *cv = getenv("KV_B200_COOPERATIVE");
+        ctx->coop = cv && cv[0] == '1';
+    }
 #ifdef KV_PHASE_STAMPS
     {
         const size_t sb = (size_t)kv_ctx::kStampRing * ctx->max_cta * kvb::kStampSlots * sizeof(unsigned long long);
@@ -1200,7 +1220,7 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
         ap.stamps = ctx->stamps + (size_t)(ctx->stamp_next++ % kv_ctx::kStampRing) * ctx->max_cta * kvb::kStampSlots;
 #endif
         rc = launch(ctx, KV_K_ATTN, st, "attention kernel",
-                    [&] { return kvb::launch_attn(ctx->D, km, vm, ap, st, true); });
+                    [&] { return kvb::launch_attn(ctx->D, km, vm, ap, st, true, ctx->coop); });
         if (rc) return rc;
         ap.hz_row = -1;   // row groups after the first do not write the cache
     }
@@ -1475,6 +1495,11 @@ int kv_rope_table_host(const kv_config *cfg, int64_t pos0, int64_t npos, float *
         rope_rows(rs, pos0, pos0 + npos, out);
         return KV_OK;
     });
+}
+
+int kv_decode_grid_fits(int32_t sm_count, int32_t blocks_per_sm, int32_t n_cta)
+{
+    return decode_grid_fits(sm_count, blocks_per_sm, n_cta) ? 1 : 0;
 }
 
 int kv_decode_ctas(int32_t sm_count, int32_t n_kv_heads_local, int64_t n_kv, int32_t *n_cta)

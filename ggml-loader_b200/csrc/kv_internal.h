@@ -167,9 +167,12 @@ int attn_box_width(int D);
 int attn_tile_scores();
 int attn_max_ctas();   // CTAs one launch may have (a head's span is read in one sweep)
 cudaError_t attn_prepare(int D);
-// pdl: launch as a programmatic dependent of the previous kernel in the stream
+// CTAs of the attention kernel one SM holds at once (the fewest over its instances)
+cudaError_t attn_occupancy(int D, int *blocks_per_sm);
+// pdl: launch as a programmatic dependent of the previous kernel in the stream;
+// coop: as a cooperative launch (the driver starts the grid only with every CTA resident)
 cudaError_t launch_attn(int D, const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnParams &p,
-                        cudaStream_t st, bool pdl);
+                        cudaStream_t st, bool pdl, bool coop);
 
 // ---------------------------------------------------------------------------
 // chunked-prefill attention (kv_prefill.cu): tcgen05 tensor cores, two passes

@@ -106,6 +106,7 @@ def lib():
         "kv_rope_table_host": (ctypes.c_int, [cfgp, _i64, _i64, _vp]),
         "kv_shard_geometry": (ctypes.c_int, [cfgp, _i32] + [ctypes.POINTER(_i32)] * 4),
         "kv_decode_ctas": (ctypes.c_int, [_i32, _i32, _i64, ctypes.POINTER(_i32)]),
+        "kv_decode_grid_fits": (ctypes.c_int, [_i32, _i32, _i32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -66,6 +66,12 @@ int kv_shard_geometry(const kv_config *cfg, int32_t shard, int32_t *q_head0, int
  * multiple of the heads when that idles at most 5 % of them. */
 int kv_decode_ctas(int32_t sm_count, int32_t n_kv_heads_local, int64_t n_kv, int32_t *n_cta);
 
+/* 1 when a decode grid of n_cta CTAs is resident at once on sm_count SMs
+ * holding blocks_per_sm CTAs each, else 0 (host arithmetic only).  The decode
+ * kernel's CTAs wait on one another, so kv_alloc refuses a device where its
+ * largest grid does not fit (blocks_per_sm from the CUDA occupancy query). */
+int kv_decode_grid_fits(int32_t sm_count, int32_t blocks_per_sm, int32_t n_cta);
+
 #ifdef __cplusplus
 }
 #endif

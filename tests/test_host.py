@@ -321,3 +321,25 @@ def test_decode_split_cta_counts():
             assert (hkv * n_kv + c - 1) // c <= n_kv
     out = ctypes.c_int32()
     assert K.lib().kv_decode_ctas(0, 8, 100, ctypes.byref(out)) == K.KV_E_ARG
+
+
+def test_decode_grid_residency_check():
+    """kv_decode_grid_fits: the decode kernel's CTAs wait on one another, so
+    kv_alloc accepts a device only if its largest grid is resident at once
+    (SMs x resident CTAs an SM >= CTAs)."""
+    fits = K.lib().kv_decode_grid_fits
+    assert fits(148, 1, 148) == 1                 # one CTA per SM, the whole grid
+    assert fits(148, 1, 149) == 0                 # one CTA more than the SMs
+    assert fits(148, 0, 1) == 0                   # the kernel does not fit on an SM at all
+    assert fits(74, 2, 148) == 1                  # two CTAs an SM
+    assert fits(100, 1, 144) == 0                 # a device (or partition) with fewer SMs
+    assert fits(0, 1, 1) == 0 and fits(148, 1, 0) == 0
+    # every grid kv_decode_ctas produces fits one CTA per SM on that SM count
+    out = ctypes.c_int32()
+    for sm in (16, 74, 132, 148):
+        for hkv in (1, 2, 8, 32):
+            for n_kv in (1, 2049, 32001, 131001):
+                if hkv > sm:
+                    continue
+                assert K.lib().kv_decode_ctas(sm, hkv, n_kv, ctypes.byref(out)) == K.KV_OK
+                assert fits(sm, 1, out.value) == 1
