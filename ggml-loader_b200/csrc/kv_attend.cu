@@ -76,7 +76,7 @@ constexpr float kUnfix = 1.0f / 1099511627776.0f;
 
 template <int D> struct G4;
 template <> struct G4<64>  { static constexpr int BW = 64, NS = 11; };
-template <> struct G4<96>  { static constexpr int BW = 32, NS = 7; };
+template <> struct G4<96>  { static constexpr int BW = 32, NS = 6; };
 // (4 stages: 128 KB in flight an SM keeps HBM busy; a fifth only lengthens the
 // queue the statistics poll and the query loads wait behind -- 128k: 92.7 ->
 // 90.7 us a layer, 32k: 28.9 -> 28.8)
@@ -241,8 +241,16 @@ struct Smem {
     static constexpr size_t o_knew = o_kf + (size_t)D * 4;                 // [D] f16
     static constexpr size_t o_vnew = o_knew + (size_t)D * 2;               // [D] f16
     static constexpr size_t o_flags = o_vnew + (size_t)D * 2;              // abort, last(seg 0), last(seg 1), collector
-    static constexpr size_t bytes = o_flags + 16;
+    // cluster exchange (kMaxQ > 1): the cluster's (max, sum) per (rank, row),
+    // two transaction barriers (statistics, partial outputs) and the leader's
+    // receive buffer for the other ranks' partial outputs [kMaxQ-1][8 rows][D]
+    static constexpr int kMaxQ = D <= 128 ? 8 : 1;
+    static constexpr size_t o_cst = o_flags + 16;                          // [kMaxQ][8] float2
+    static constexpr size_t o_cbar = o_cst + (size_t)kMaxQ * kRows * 8;   // [2] u64
+    static constexpr size_t o_crecv = (o_cbar + 16 + 15) / 16 * 16;
+    static constexpr size_t bytes = o_crecv + (size_t)(kMaxQ - 1) * kRows * D * 4;
     static_assert(bytes <= 227 * 1024, "shared memory of the attention kernel");
+    static_assert(o_cst % 16 == 0 && o_cbar % 8 == 0 && o_crecv % 16 == 0, "aligned cluster regions");
     static_assert(kStage % 1024 == 0, "ring stages stay 1024-byte aligned");
     // the staged new rows and the scratch blocks are read with 16-byte vector loads
     static_assert(o_sS % 16 == 0 && o_kf % 16 == 0 && o_knew % 16 == 0 && o_vnew % 16 == 0 && o_redm % 16 == 0,
@@ -279,10 +287,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     __half *knew = reinterpret_cast<__half *>(smem + L::o_knew);
     __half *vnew = reinterpret_cast<__half *>(smem + L::o_vnew);
     volatile int *flags = reinterpret_cast<volatile int *>(smem + L::o_flags);
+    float2 *cst = reinterpret_cast<float2 *>(smem + L::o_cst);
+    uint64_t *cbar = reinterpret_cast<uint64_t *>(smem + L::o_cbar);
+    float *crecv = reinterpret_cast<float *>(smem + L::o_crecv);
+    // cluster mode (p.cq > 1): CTAs c of one cluster cover one head; rank 0 leads
+    const bool clus = L::kMaxQ > 1 && p.cq > 1;
+    const uint32_t crank = clus ? cluster_rank() : 0u;
 
     const int c = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const Range g = cta_range(c, p.n_kv, p.hkv, p.n_cta);
     const bool two = g.nt > g.nt0;
+    const bool s_local = g.nt <= kSD;   // the range's scores fit the V phase's staging ring
     // decode: this CTA owns head h0's new row when its first segment ends the head
     const bool owns_new = p.fused && g.e0 == p.n_kv;
     const int it_new = owns_new ? (int)((p.n_past - g.s0) / kTK) : -1;
@@ -295,9 +310,19 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         flags[0] = 0;
         flags[1] = 0;
         flags[2] = 0;
+        if (clus) {
+            // statistics: every rank's 8 rows; partial outputs: the other
+            // ranks' rows (leader only) -- counted as transaction bytes
+            mbar_init(&cbar[0], 1);
+            mbar_init(&cbar[1], 1);
+            mbar_arrive_expect_tx(&cbar[0], (uint32_t)((p.cq - 1) * kRows * 8));
+            if (crank == 0) mbar_arrive_expect_tx(&cbar[1], (uint32_t)((p.cq - 1) * p.nrows * D * 4));
+        }
         fence_mbar_init();
     }
     __syncthreads();
+    // no rank may store into another before its barriers are initialised
+    if (clus) cluster_sync_all();
     KV_STAMP(tid == 0, 0);   // entry
 
     // ---- producer: K tiles 0..nt-1, then V tiles 0..nt-1, one ring ----
@@ -312,6 +337,18 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             for (int j = 0; j < total; j++) {
                 if (p.inject == 1 && j == 1) break;   // test hook: withhold tile 1
                 const int s = j % NS;
+                // the two waits for a free stage that last longest -- behind the
+                // previous kernel's tail and behind the statistics exchange --
+                // keep HBM busy: the next l2pf tiles go to L2 first
+                if ((j == NS || j == g.nt + NS) && p.l2pf > 0)
+                    for (int t = j; t < total && t < j + p.l2pf; t++) {
+                        const bool tv = t >= g.nt;
+                        int h2;
+                        int64_t k2, e2;
+                        tile_of(g, tv ? t - g.nt : t, h2, k2, e2);
+#pragma unroll
+                        for (int b = 0; b < NB; b++) tma_prefetch_3d(tv ? &vmap : &kmap, b * BW, h2, (int)k2);
+                    }
                 if (j >= NS && !mbar_wait(&empty[s], ((j / NS) - 1) & 1, p.limit_ns)) {
                     atomicOr(p.err, 2u);
                     flags[0] = 1;
@@ -349,6 +386,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         if (lane == 0 && flags[0])
             for (int j = issued > NS ? issued - NS : 0; j < issued; j++)
                 mbar_wait(&full[j % NS], (j / NS) & 1, p.limit_ns);
+        __syncwarp();
+        if (clus) {   // every thread of the cluster takes part in its exit barrier
+            cluster_arrive();
+            cluster_wait();
+        }
         return;
     }
 
@@ -514,7 +556,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             const float sb0 = score(acc0[1] + acc1[1], v0 && key0 <= lim_b, mk[1]);
             const float sa1 = score(acc0[2] + acc1[2], v1 && key1 <= lim_a, mk[2]);
             const float sb1 = score(acc0[3] + acc1[3], v1 && key1 <= lim_b, mk[3]);
-            float *Sw = Scta + (int64_t)i * kTileScores + warp * 128;
+            // a range of at most kSD tiles keeps its scores in the V phase's
+            // staging ring (the same layout per tile): no global round trip
+            float *Sw = (s_local ? sS + (i % kSD) * (kConsumers * 4) : Scta + (int64_t)i * kTileScores) + warp * 128;
             if (row_a < R) {
                 if (v0) Sw[so_a] = sa0;
                 if (v1) Sw[so_a + 2] = sa1;
@@ -573,10 +617,31 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         for (int w = 0; w < 8; w++)
             if (mw[w] != -INFINITY) Z = fmaf(zw[w], __expf(mw[w] - M), Z);
         // an aborted CTA publishes empty statistics, so no other CTA waits for it
-        const unsigned long long tag = (unsigned long long)p.epoch << 32;
-        st_volatile_v2(p.stats + 2 * (((int64_t)c * 2 + sl) * kRows + row),
-                       tag | __float_as_uint(aborted ? -INFINITY : M),
-                       tag | __float_as_uint(aborted ? 0.0f : (float)Z));
+        const float Mp = aborted ? -INFINITY : M, Zp = aborted ? 0.0f : (float)Z;
+        if (clus) {
+            // row `row` of rank crank: here with a plain store, into every
+            // other rank counted on its statistics barrier
+            if (sl == 0) {
+                cst[crank * kRows + row] = make_float2(Mp, Zp);
+                const uint32_t la = smem_addr(cst + crank * kRows + row), lb = smem_addr(&cbar[0]);
+                for (int q = 0; q < p.cq; q++)
+                    if (q != (int)crank) st_async_v2(mapa(la, (uint32_t)q), Mp, Zp, mapa(lb, (uint32_t)q));
+            }
+        } else {
+            const unsigned long long tag = (unsigned long long)p.epoch << 32;
+            st_volatile_v2(p.stats + 2 * (((int64_t)c * 2 + sl) * kRows + row), tag | __float_as_uint(Mp),
+                           tag | __float_as_uint(Zp));
+        }
+    }
+    // the leader's last store into another rank's shared memory is behind it;
+    // this rank's own row is seen by the warps that combine the rows
+    bool c_arrived = false;
+    if (clus) {
+        named_sync(1, kConsumers);
+        if (crank == 0) {
+            cluster_arrive();
+            c_arrived = true;
+        }
     }
     KV_STAMP(tid == 0, 4);   // statistics published
     // decode: the new V row of head h0 goes to the cache now, while others finish
@@ -595,7 +660,42 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     // of row w of every CTA of its heads (all loads in flight at once; spans of
     // up to kPU*32 CTAs) until every tag shows this launch, bounded by limit_ns
     bool late = false;
-    if (!aborted) {
+    // cluster mode: the cluster's (max, sum) of row `warp` from its ranks' rows
+    bool cdone = false;   // the cluster covers the whole head: statistics known
+    if (clus && !aborted && warp < R) {
+        const bool ok = mbar_wait(&cbar[0], 0, p.limit_ns);
+        float mq = -INFINITY, zq = 0.0f;
+        if (ok && lane < p.cq) {
+            const float2 v = cst[lane * kRows + warp];
+            mq = v.x;
+            zq = v.y;
+        }
+        float M = mq;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float Z = mq == -INFINITY ? 0.0f : zq * __expf(mq - M);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) Z += __shfl_xor_sync(0xffffffffu, Z, o);
+        if (!__all_sync(0xffffffffu, ok)) {
+            late = true;
+            if (lane == 0) {
+                atomicOr(p.err, 4u);
+                flags[0] = 1;
+            }
+        } else if (p.ncl == 1) {
+            if (lane == 0) {
+                rowM[warp] = M;
+                rowInv[warp] = Z > 0.0f ? __fdiv_rn(1.0f, Z) : 0.0f;
+            }
+            cdone = true;
+        } else if (crank == 0 && lane == 0) {
+            // one slot per (cluster, row), tagged as the CTA slots
+            const unsigned long long tag = (unsigned long long)p.epoch << 32;
+            st_volatile_v2(p.stats + 2 * (((int64_t)(c / p.cq) * 2) * kRows + warp), tag | __float_as_uint(M),
+                           tag | __float_as_uint(Z));
+        }
+    }
+    if (!aborted && !late && !cdone) {
         constexpr int kPU = kMaxSpan / 32;
         float mm[2][kPU], zz[2][kPU];
         unsigned pend = 0u;
@@ -604,8 +704,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         for (int sl = 0; sl < 2; sl++) {
             const int h = g.h0 + sl;
             const bool act = warp < R && (sl == 0 || two);
-            ca[sl] = act ? p.span_a[h] : 0;
-            cb[sl] = act ? p.span_b[h] : -1;
+            // the parties: the head's CTAs, or its clusters in cluster mode
+            ca[sl] = act ? (clus ? h * p.ncl : p.span_a[h]) : 0;
+            cb[sl] = act ? (clus ? h * p.ncl + p.ncl - 1 : p.span_b[h]) : -1;
 #pragma unroll
             for (int u = 0; u < kPU; u++) {
                 mm[sl][u] = -INFINITY;
@@ -624,9 +725,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
 #pragma unroll
                 for (int u = 0; u < kPU; u++) {
                     w0[sl][u] = w1[sl][u] = 0ull;
-                    if (pend & (1u << (sl * kPU + u)))
-                        ld_volatile_v2(p.stats + 2 * (part_slot(p, g.h0 + sl, ca[sl] + lane + 32 * u) * kRows + warp),
-                                       w0[sl][u], w1[sl][u]);
+                    if (pend & (1u << (sl * kPU + u))) {
+                        const int cc = ca[sl] + lane + 32 * u;
+                        const int64_t slot = clus ? (int64_t)cc * 2 : part_slot(p, g.h0 + sl, cc);
+                        ld_volatile_v2(p.stats + 2 * (slot * kRows + warp), w0[sl][u], w1[sl][u]);
+                    }
                 }
 #pragma unroll
             for (int sl = 0; sl < 2; sl++)
@@ -683,14 +786,88 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     const float *Sl = Scta + warp * 128 + (gq * 4 + cq) * 4;
     float *stg = sS + tid * 4;
     auto stage_s = [&](int i) {
+        if (s_local) {   // already in place; an empty group keeps the wait counts
+            cp_async_commit();
+            return;
+        }
         if (i < g.nt && gq < R) cp_async_16(stg + (i % kSD) * (kConsumers * 4), Sl + (int64_t)i * kTileScores);
         cp_async_commit();
     };
     if (!aborted)
         for (int i = 0; i < kSD - 1; i++) stage_s(i);
 
-    // this CTA's partial output of segment sl into the head's fixed-point
-    // accumulator; the head's last CTA converts and writes the output
+    // the head's final values into out and, with KV-head shards, into every
+    // peer's receive buffer; the CTA that writes the shard's last local head
+    // then collects the peers' heads.  value_of(idx, row, dd) gives element
+    // idx = row * D + dd; each thread takes the idx it took in the sums before.
+    auto emit_head = [&](int h, auto &&value_of) {
+        const int par = (int)(p.epoch & 1u);
+        for (int idx = tid; idx < R * D; idx += kConsumers) {
+            const int row = idx / D, dd = idx - row * D;
+            const float val = value_of(idx, row, dd);
+            const int qrow = p.row0 + row;
+            const int64_t o = (int64_t)(qrow / p.r) * p.out_stride + (int64_t)(p.out_head0 + h * p.r + qrow % p.r) * D + dd;
+            p.out[o] = val;
+            // KV-head shards: the same value, tagged with this launch, into
+            // every peer's receive buffer (NVLink stores; no fence or flag:
+            // the reader checks each word's tag)
+            const unsigned long long word = ((unsigned long long)p.epoch << 32) | __float_as_uint(val);
+            for (int gg = 0; gg < p.n_peers; gg++)
+                if (gg != p.shard) p.rx[gg][par * p.rx_stride + o] = word;
+        }
+        if (p.n_peers > 1) {
+            named_sync(1, kConsumers);
+            // count the head in; the CTA that converts the last local head
+            // collects the peers' heads
+            if (tid == 0) flags[3] = atomicAdd(p.xticket, 1u) == (unsigned)(p.hkv - 1);
+            named_sync(1, kConsumers);
+            if (flags[3]) {
+                KV_STAMP(tid == 0, 8);   // collector starts polling the peers' words
+                // every column outside this shard's, once its word carries
+                // this launch's tag; a thread keeps up to 8 words' loads in
+                // flight per poll
+                const unsigned long long *src = p.rx[p.shard] + par * p.rx_stride;
+                const int cols = p.hkv * p.r * D;   // this shard's columns
+                const int lo = p.out_head0 * D, all = p.n_peers * cols;
+                const unsigned ep = p.epoch;
+                bool xlate = false;
+                const uint64_t t0 = globaltimer();
+                for (int base = 0; base < all && !xlate; base += 8 * kConsumers) {
+                    unsigned pend = 0u;
+#pragma unroll
+                    for (int u = 0; u < 8; u++) {
+                        const int o = base + u * kConsumers + tid;
+                        if (o < all && (o < lo || o >= lo + cols)) pend |= 1u << u;
+                    }
+                    while (pend) {
+                        unsigned long long w[8];
+#pragma unroll
+                        for (int u = 0; u < 8; u++)   // all loads out before any is used
+                            w[u] = (pend & (1u << u)) ? ld_volatile_u64(src + base + u * kConsumers + tid) : 0ull;
+#pragma unroll
+                        for (int u = 0; u < 8; u++)
+                            if ((pend & (1u << u)) && (unsigned)(w[u] >> 32) == ep) {
+                                p.out[base + u * kConsumers + tid] = __uint_as_float((unsigned)w[u]);
+                                pend &= ~(1u << u);
+                            }
+                        if (pend && globaltimer() - t0 > p.limit_ns) {
+                            xlate = true;
+                            break;
+                        }
+                    }
+                }
+                if (named_sync_or(1, kConsumers, xlate) && tid == 0) atomicOr(p.err, 8u);
+                KV_STAMP(tid == 0, 9);   // collector done
+                if (tid == 0) *p.xticket = 0u;
+            }
+        }
+    };
+
+    // this CTA's partial output of segment sl: into the head's fixed-point
+    // accumulator, whose last CTA converts and writes the output; in cluster
+    // mode first into the cluster leader's shared memory, and the leader adds
+    // the ranks' rows in rank order (the head's output when its one cluster
+    // covers it, else the cluster's rows go to the accumulator)
     auto flush_out = [&](int sl) {
         if (named_sync_or(1, kConsumers, aborted)) {
             aborted = true;
@@ -707,14 +884,79 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             oacc[dt][0] = oacc[dt][1] = oacc[dt][2] = oacc[dt][3] = 0.0f;
         }
         named_sync(1, kConsumers);
+        if (clus) {
+            if (crank != 0) {
+                // the rank's rows (the 8 warps' sum; flash: normalised) into
+                // the leader, counted on its output barrier
+                const uint32_t lb = mapa(smem_addr(&cbar[1]), 0u);
+                for (int i4 = tid; i4 < R * D / 4; i4 += kConsumers) {
+                    const int idx = i4 * 4, row = idx / D, dd = idx - row * D;
+                    float4 v = *reinterpret_cast<const float4 *>(red + row * RED_LD + dd);
+#pragma unroll
+                    for (int w = 1; w < 8; w++) {
+                        const float4 x = *reinterpret_cast<const float4 *>(red + (w * kRows + row) * RED_LD + dd);
+                        v.x += x.x;
+                        v.y += x.y;
+                        v.z += x.z;
+                        v.w += x.w;
+                    }
+                    if (flash) {
+                        const float iz = rowInv[row];
+                        v.x = __fmul_rn(v.x, iz);
+                        v.y = __fmul_rn(v.y, iz);
+                        v.z = __fmul_rn(v.z, iz);
+                        v.w = __fmul_rn(v.w, iz);
+                    }
+                    st_async_v4(mapa(smem_addr(crecv + ((crank - 1) * kRows + row) * D + dd), 0u), v, lb);
+                }
+                // its last store into another rank is behind it
+                __syncwarp();
+                cluster_arrive();
+                c_arrived = true;
+                return;
+            }
+            const bool got = mbar_wait(&cbar[1], 0, p.limit_ns);
+            if (named_sync_or(1, kConsumers, !got)) {
+                if (tid == 0) {
+                    atomicOr(p.err, 16u);
+                    flags[0] = 1;
+                }
+                aborted = true;
+                return;
+            }
+            // the cluster's rows, kept in warp 0's slot of each element (the
+            // thread that sums an element is the one that reads it later)
+            for (int idx = tid; idx < R * D; idx += kConsumers) {
+                const int row = idx / D, dd = idx - row * D;
+                float sum = 0.0f;
+#pragma unroll
+                for (int w = 0; w < 8; w++) sum += red[(w * kRows + row) * RED_LD + dd];
+                if (flash) sum = __fmul_rn(sum, rowInv[row]);
+                for (int q = 1; q < p.cq; q++) sum += crecv[((q - 1) * kRows + row) * D + dd];
+                red[row * RED_LD + dd] = sum;
+            }
+            if (p.ncl == 1) {
+                KV_STAMP(tid == 0, 7);   // the cluster's rows summed
+                emit_head(h, [&](int, int row, int dd) {
+                    const float v = red[row * RED_LD + dd];
+                    return isfinite(v) ? v : __int_as_float(0x7fc00000);
+                });
+                return;
+            }
+        }
         long long *acc = p.acc + (int64_t)h * kRows * D;
         unsigned bad = 0u;   // rows with a non-finite partial
         for (int idx = tid; idx < R * D; idx += kConsumers) {
             const int row = idx / D, dd = idx - row * D;
-            float sum = 0.0f;
+            float sum;
+            if (clus) {
+                sum = red[row * RED_LD + dd];
+            } else {
+                sum = 0.0f;
 #pragma unroll
-            for (int w = 0; w < 8; w++) sum += red[(w * kRows + row) * RED_LD + dd];
-            if (flash) sum = __fmul_rn(sum, rowInv[sl * kRows + row]);   // flash: normalised here
+                for (int w = 0; w < 8; w++) sum += red[(w * kRows + row) * RED_LD + dd];
+                if (flash) sum = __fmul_rn(sum, rowInv[sl * kRows + row]);   // flash: normalised here
+            }
             if (isfinite(sum))
                 atomicAdd(reinterpret_cast<unsigned long long *>(acc + idx),
                           (unsigned long long)__float2ll_rn(__fmul_rn(sum, kFix)));
@@ -725,77 +967,22 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         // the CTA's atomics, ordered by the barrier, are released by the ticket
         // (cumulativity); the last CTA's ticket acquires every other CTA's
         named_sync(1, kConsumers);
-        if (tid == 0)
-            flags[1 + sl] = atom_add_acq_rel_gpu(&p.counters[h], 1u) == (unsigned)(p.span_b[h] - p.span_a[h]);
+        if (tid == 0) {
+            const unsigned parties = clus ? (unsigned)p.ncl : (unsigned)(p.span_b[h] - p.span_a[h] + 1);
+            flags[1 + sl] = atom_add_acq_rel_gpu(&p.counters[h], 1u) == parties - 1u;
+        }
         named_sync(1, kConsumers);
         KV_STAMP(tid == 0, 7);   // partial added, ticket taken
         if (flags[1 + sl]) {
             const unsigned nan_rows = __ldcg(&p.nonfin[h]);
-            const int par = (int)(p.epoch & 1u);
-            for (int idx = tid; idx < R * D; idx += kConsumers) {
-                const int row = idx / D, dd = idx - row * D;
+            emit_head(h, [&](int idx, int row, int) {
                 const long long v = __ldcg(acc + idx);
                 acc[idx] = 0;
-                const int qrow = p.row0 + row;
-                const int64_t o = (int64_t)(qrow / p.r) * p.out_stride + (int64_t)(p.out_head0 + h * p.r + qrow % p.r) * D + dd;
-                const float val = (nan_rows >> row) & 1u ? __int_as_float(0x7fc00000) : __fmul_rn(__ll2float_rn(v), kUnfix);
-                p.out[o] = val;
-                // KV-head shards: the same value, tagged with this launch, into
-                // every peer's receive buffer (NVLink stores; no fence or flag:
-                // the reader checks each word's tag)
-                const unsigned long long word = ((unsigned long long)p.epoch << 32) | __float_as_uint(val);
-                for (int g = 0; g < p.n_peers; g++)
-                    if (g != p.shard) p.rx[g][par * p.rx_stride + o] = word;
-            }
+                return (nan_rows >> row) & 1u ? __int_as_float(0x7fc00000) : __fmul_rn(__ll2float_rn(v), kUnfix);
+            });
             if (tid == 0) {
                 p.counters[h] = 0u;
                 p.nonfin[h] = 0u;
-            }
-            if (p.n_peers > 1) {
-                named_sync(1, kConsumers);
-                // count the head in; the CTA that converts the last local head
-                // collects the peers' heads
-                if (tid == 0) flags[3] = atomicAdd(p.xticket, 1u) == (unsigned)(p.hkv - 1);
-                named_sync(1, kConsumers);
-                if (flags[3]) {
-                    KV_STAMP(tid == 0, 8);   // collector starts polling the peers' words
-                    // every column outside this shard's, once its word carries
-                    // this launch's tag; a thread keeps up to 8 words' loads in
-                    // flight per poll
-                    const unsigned long long *src = p.rx[p.shard] + par * p.rx_stride;
-                    const int cols = p.hkv * p.r * D;   // this shard's columns
-                    const int lo = p.out_head0 * D, all = p.n_peers * cols;
-                    const unsigned ep = p.epoch;
-                    bool late = false;
-                    const uint64_t t0 = globaltimer();
-                    for (int base = 0; base < all && !late; base += 8 * kConsumers) {
-                        unsigned pend = 0u;
-#pragma unroll
-                        for (int u = 0; u < 8; u++) {
-                            const int o = base + u * kConsumers + tid;
-                            if (o < all && (o < lo || o >= lo + cols)) pend |= 1u << u;
-                        }
-                        while (pend) {
-                            unsigned long long w[8];
-#pragma unroll
-                            for (int u = 0; u < 8; u++)   // all loads out before any is used
-                                w[u] = (pend & (1u << u)) ? ld_volatile_u64(src + base + u * kConsumers + tid) : 0ull;
-#pragma unroll
-                            for (int u = 0; u < 8; u++)
-                                if ((pend & (1u << u)) && (unsigned)(w[u] >> 32) == ep) {
-                                    p.out[base + u * kConsumers + tid] = __uint_as_float((unsigned)w[u]);
-                                    pend &= ~(1u << u);
-                                }
-                            if (pend && globaltimer() - t0 > p.limit_ns) {
-                                late = true;
-                                break;
-                            }
-                        }
-                    }
-                    if (named_sync_or(1, kConsumers, late) && tid == 0) atomicOr(p.err, 8u);
-                    KV_STAMP(tid == 0, 9);   // collector done
-                    if (tid == 0) *p.xticket = 0u;
-                }
             }
         }
     };
@@ -871,9 +1058,23 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     // every consumer has read its scores (flush_out opens with a barrier): the
     // scratch is dead until the next launch rewrites it, so it leaves L2
     // without a write-back
-    for (int ln = tid; ln < g.nt * (kTileScores / 32); ln += kConsumers) l2_discard(Scta + ln * 32);
+    if (!s_local)
+        for (int ln = tid; ln < g.nt * (kTileScores / 32); ln += kConsumers) l2_discard(Scta + ln * 32);
     named_sync(2, kThreads);
     KV_STAMP(tid == 0, 12);   // exit
+    if (clus) {
+        // no rank leaves while another may still store into its shared
+        // memory: every transaction counted here has landed, and every thread
+        // of the cluster is past its last store into another rank
+        __syncwarp();
+        if (!c_arrived) cluster_arrive();
+        if (tid == 0) {
+            mbar_wait(&cbar[0], 0, p.limit_ns);
+            if (crank == 0) mbar_wait(&cbar[1], 0, p.limit_ns);
+        }
+        __syncwarp();
+        cluster_wait();
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -916,7 +1117,7 @@ cudaError_t launch(const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnP
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = Smem<D>::bytes;
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[3];
     int na = 0;
     if (pdl) {
         attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -926,6 +1127,14 @@ cudaError_t launch(const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnP
     if (coop) {
         attr[na].id = cudaLaunchAttributeCooperative;
         attr[na].val.cooperative = 1;
+        na++;
+    }
+    if (p.cq > 1) {
+        if (Smem<D>::kMaxQ < p.cq || p.n_cta % p.cq) return cudaErrorInvalidValue;
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = (unsigned)p.cq;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
         na++;
     }
     cfg.attrs = attr;
@@ -953,6 +1162,41 @@ cudaError_t attn_prepare(int D)
     case 128: return prep<128>();
     case 256: return prep<256>();
     default: return cudaErrorInvalidValue;
+    }
+}
+
+template <int D>
+cudaError_t cluster_occupancy(int q, int *clusters)
+{
+    *clusters = 0;
+    if (Smem<D>::kMaxQ < q) return cudaSuccess;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(q * 32));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Smem<D>::bytes;
+    cudaLaunchAttribute a[1];
+    a[0].id = cudaLaunchAttributeClusterDimension;
+    a[0].val.clusterDim.x = (unsigned)q;
+    a[0].val.clusterDim.y = 1;
+    a[0].val.clusterDim.z = 1;
+    cfg.attrs = a;
+    cfg.numAttrs = 1;
+    int n[4] = {0, 0, 0, 0};
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&n[0], attn_decode_kernel<D, false, false>, &cfg);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n[1], attn_decode_kernel<D, false, true>, &cfg);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n[2], attn_decode_kernel<D, true, false>, &cfg);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n[3], attn_decode_kernel<D, true, true>, &cfg);
+    if (e == cudaSuccess) *clusters = std::min(std::min(n[0], n[1]), std::min(n[2], n[3]));
+    return e;
+}
+
+cudaError_t attn_cluster_occupancy(int D, int q, int *clusters)
+{
+    switch (D) {
+    case 64: return cluster_occupancy<64>(q, clusters);
+    case 96: return cluster_occupancy<96>(q, clusters);
+    case 128: return cluster_occupancy<128>(q, clusters);
+    default: *clusters = 0; return cudaSuccess;
     }
 }
 

@@ -191,6 +191,30 @@ void build_rope_table(const RopeSpec &r, int64_t n_pos, float *out)
 
 }  // namespace
 
+// The decode split's per-launch tables for ap.n_cta CTAs over hkv heads of
+// n_kv keys: the score tiles a CTA owns and each head's CTA span.  CTA c
+// covers the flattened (head, key) rows [c*T/C, (c+1)*T/C), T = hkv * n_kv.
+void kvb::attn_split(AttnParams &ap, int hkv, int64_t n_kv)
+{
+    const int64_t T = (int64_t)hkv * n_kv, C = ap.n_cta, tk = attn_tile_keys();
+    // score tiles of the longest CTA range: ceil(ceil(T/C)/128) + 1 (a range
+    // that crosses a head boundary starts a second partial tile)
+    ap.S_tiles = ((T + C - 1) / C + tk - 1) / tk + 1;
+    auto lo = [&](int64_t cc) { return cc * T / C; };
+    auto cta_of = [&](int64_t x) {
+        int64_t cc = std::min<int64_t>(C - 1, x * C / T);
+        while (cc + 1 < C && lo(cc + 1) <= x) cc++;
+        while (cc > 0 && lo(cc) > x) cc--;
+        return cc;
+    };
+    for (int h = 0; h < hkv; h++) {
+        const int64_t a = cta_of((int64_t)h * n_kv), b = cta_of((int64_t)(h + 1) * n_kv - 1);
+        ap.span_a[h] = (int16_t)a;
+        ap.span_b[h] = (int16_t)b;
+        ap.span_slot[h] = (int8_t)(lo(a) < (int64_t)h * n_kv ? 1 : 0);
+    }
+}
+
 int kvb::set_last_error(int code, const char *msg)
 {
     snprintf(g_last_error, sizeof(g_last_error), "%s", msg ? msg : "");
@@ -222,7 +246,6 @@ struct kv_ctx {
     int64_t ring = 0;         // ring cells (0: linear cache)
     __half *ring_mask = nullptr;   // ring caches: [n_batch_max][rows] F16 visibility of a chunk
     int D = 0, hq_loc = 0, hkv_loc = 0, r = 1, hq0 = 0, hkv0 = 0;
-    int rmax = 0, split_max = 0, max_splits = 0;
     float scale = 1.0f;
 
     __half *cache = nullptr;  // [n_layer][2][rows][hkv_loc][D]
@@ -249,6 +272,9 @@ struct kv_ctx {
     uint64_t limit_ns = 1000000000ull;      // bound of every device-side wait (1 s)
     int inject = 0;                         // test hook, applies to the next decode launch
     bool coop = false;                      // attention kernels as cooperative launches
+    int max_clusters[kvb::kMaxClusterCtas + 1] = {};   // q-CTA clusters of the attention kernel held at once
+    int force_q = 0;                        // KV_B200_CLUSTER: 0 policy, < 0 none, q > 1 that size
+    int l2pf = 0;                           // KV_B200_L2PF: tiles prefetched to L2 at the long stage waits
 
     Pending pend;  // a deferred single-token kv_append
     // state of the last kv_append (kv_attend must follow it)
@@ -411,10 +437,56 @@ bool decode_grid_fits(int sm_count, int blocks_per_sm, int n_cta)
     return sm_count > 0 && blocks_per_sm > 0 && n_cta > 0 && (int64_t)sm_count * blocks_per_sm >= n_cta;
 }
 
+// The decode grid: n_cta CTAs in clusters of cq (cq = 1: no clusters), ncl
+// clusters per local head.  max_clusters[q] is the number of q-CTA clusters
+// the device holds at once (0: not possible); force_q > 0 asks for that
+// cluster size (several clusters per head where one does not cover it),
+// force_q < 0 for none.
+//  * One cluster per head, when the head's keys fit a cluster's CTAs (>= 256
+//    keys each) and the grid keeps at least 85 % of the CTAs of the split
+//    without clusters: the statistics and the partial outputs never leave the
+//    cluster's shared memory (short contexts, many heads; measured on B200:
+//    qwen2-0.5B 11.8 -> 10.1 us a layer, phi3-mini 18.4 -> 16.5).
+//  * Else no clusters.  Several clusters per head (a cluster-level exchange,
+//    then a global one among the clusters) measured slower than the plain
+//    split on one-head shards (11.3 -> 14.9 us a layer at 32k: the two levels
+//    add their latencies, and clusters of 8 fit only 120 of the 148 SMs), so
+//    the policy does not choose it.
+struct DecodeShape {
+    int n_cta, cq, ncl;
+};
+
+DecodeShape decode_shape_for(int sm_count, int hkv_loc, int64_t n_kv, const int *max_clusters, int force_q)
+{
+    const int c0 = decode_ctas_for(sm_count, hkv_loc, n_kv);
+    DecodeShape none{c0, 1, 1};
+    if (!max_clusters || force_q < 0) return none;
+    auto fits = [&](int q, int ncl) { return q <= kvb::kMaxClusterCtas && max_clusters[q] >= hkv_loc * ncl; };
+    if (force_q > 1) {
+        const int q = std::min(force_q, kvb::kMaxClusterCtas);
+        const int ncl = std::max(1, c0 / (hkv_loc * q));
+        return fits(q, ncl) && (int64_t)hkv_loc * ncl * q <= std::min(sm_count, kvb::attn_max_ctas()) ? DecodeShape{hkv_loc * ncl * q, q, ncl}
+                                                                                                   : none;
+    }
+    const int64_t per_head_keys = (n_kv + 255) / 256;
+    const int qa = (int)std::min<int64_t>({(int64_t)kvb::kMaxClusterCtas, sm_count / hkv_loc, per_head_keys});
+    if (qa >= 2 && (int64_t)hkv_loc * qa * 100 >= (int64_t)c0 * 85 && fits(qa, 1)) return DecodeShape{hkv_loc * qa, qa, 1};
+    return none;
+}
+
 int decode_ctas(const kv_ctx *ctx, int64_t n_kv)
 {
     return decode_ctas_for(ctx->sm_count, ctx->hkv_loc, n_kv);
 }
+
+}  // namespace
+
+int kvb::attn_plain_ctas(int sm_count, int hkv, int64_t n_kv)
+{
+    return decode_ctas_for(sm_count, hkv, n_kv);
+}
+
+namespace {
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -448,6 +520,23 @@ int encode_map(CUtensorMap *m, CUtensorMapDataType dt, int rank, void *base, con
     if (r != CUDA_SUCCESS) return fail(KV_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return KV_OK;
 }
+
+}  // namespace
+
+// One layer's K or V cache [rows][hkv][D] F16 as the attention kernel's
+// tensor map: boxes of one head x 128 keys x a 64-wide column block with
+// 128-byte swizzle (32 wide, 64-byte swizzle at head_dim 96).
+int kvb::encode_cache_map(CUtensorMap *m, const void *base, int64_t rows, int hkv, int D)
+{
+    const int bw = attn_box_width(D);
+    const CUtensorMapSwizzle sw = bw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)hkv, (cuuint64_t)rows};
+    const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)hkv * D * 2};
+    const cuuint32_t box[3] = {(cuuint32_t)bw, 1, (cuuint32_t)attn_tile_keys()};
+    return encode_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, sw);
+}
+
+namespace {
 
 void unmap_peers(kv_ctx *ctx);
 
@@ -692,8 +781,6 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
     if (ctx->hkv_loc > ctx->sm_count)   // the attention kernel keeps one CTA per SM, all resident
         return bail(fail(KV_E_UNSUPPORTED, "%d local KV heads exceed the device's %d SMs", ctx->hkv_loc,
                          ctx->sm_count));
-    ctx->rmax = kvb::decode_rmax(ctx->D);
-    ctx->split_max = kvb::decode_split_max(ctx->D);
     ctx->scale = 1.0f / sqrtf((float)ctx->D);
 
     if (c.n_ctx <= 0) {
@@ -777,6 +864,17 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
                              ctx->max_cta, ctx->sm_count, bps));
         const char *cv = getenv("KV_B200_COOPERATIVE");
         ctx->coop = cv && cv[0] == '1';
+        for (int q = 2; q <= kvb::kMaxClusterCtas; q++) {
+            e = kvb::attn_cluster_occupancy(ctx->D, q, &ctx->max_clusters[q]);
+            if (e != cudaSuccess) {   // no cluster mode on this device
+                cudaGetLastError();
+                ctx->max_clusters[q] = 0;
+            }
+        }
+        const char *cl = getenv("KV_B200_CLUSTER");
+        if (cl && *cl) ctx->force_q = atoi(cl) <= 1 ? -1 : atoi(cl);
+        const char *pf = getenv("KV_B200_L2PF");
+        if (pf && *pf) ctx->l2pf = std::max(0, std::min(16, atoi(pf)));
     }
 #ifdef KV_PHASE_STAMPS
     {
@@ -792,20 +890,10 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
     // wide, 64-byte swizzle at head_dim 96)
     ctx->kmaps.resize(c.n_layer);
     ctx->vmaps.resize(c.n_layer);
-    {
-        const int bw = kvb::attn_box_width(ctx->D);
-        const CUtensorMapSwizzle sw = bw == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-        const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)ctx->hkv_loc, (cuuint64_t)ctx->rows};
-        const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)ctx->hkv_loc * D * 2};
-        const cuuint32_t box[3] = {(cuuint32_t)bw, 1, (cuuint32_t)kvb::attn_tile_keys()};
-        for (int l = 0; l < c.n_layer; l++) {
-            int rc = encode_map(&ctx->kmaps[l], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ctx->k_layer(l), dims, strides,
-                                box, sw);
-            if (rc == KV_OK)
-                rc = encode_map(&ctx->vmaps[l], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ctx->v_layer(l), dims, strides,
-                                box, sw);
-            if (rc != KV_OK) return bail(rc);
-        }
+    for (int l = 0; l < c.n_layer; l++) {
+        int rc = kvb::encode_cache_map(&ctx->kmaps[l], ctx->k_layer(l), ctx->rows, ctx->hkv_loc, ctx->D);
+        if (rc == KV_OK) rc = kvb::encode_cache_map(&ctx->vmaps[l], ctx->v_layer(l), ctx->rows, ctx->hkv_loc, ctx->D);
+        if (rc != KV_OK) return bail(rc);
     }
 
     // chunked prefill: the tensor-core path, when chunks can hold 32+ query rows
@@ -1122,7 +1210,16 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
     ap.hkv0 = ctx->hkv0;
     ap.n_kv = n_kv;
     ap.n_past = kpast;
-    ap.n_cta = decode_ctas(ctx, n_kv);
+    {
+        // clusters need the CTAs resident together with the cooperative
+        // launch's guarantee off: the cooperative attribute keeps the plain grid
+        const DecodeShape ds = decode_shape_for(ctx->sm_count, ctx->hkv_loc, n_kv,
+                                                ctx->coop ? nullptr : ctx->max_clusters, ctx->force_q);
+        ap.n_cta = ds.n_cta;
+        ap.cq = ds.cq;
+        ap.ncl = ds.ncl;
+    }
+    ap.l2pf = ctx->l2pf;
     ap.scale = ctx->scale;
     ap.fused = fused ? 1 : 0;
     ap.q = pd.q;
@@ -1171,32 +1268,10 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
         ap.rx[g] = via_peers ? ctx->peer_rx[g] : nullptr;
     }
     if (ap.n_cta > ctx->max_cta) return fail(KV_E_RANGE, "internal: %d CTAs > %d", ap.n_cta, ctx->max_cta);
-    {
-        // score tiles of the longest CTA range: ceil(ceil(T/C)/128) + 1 (a range
-        // that crosses a head boundary starts a second partial tile)
-        const int64_t T = (int64_t)ctx->hkv_loc * n_kv, C = ap.n_cta, tk = kvb::attn_tile_keys();
-        ap.S_tiles = ((T + C - 1) / C + tk - 1) / tk + 1;
-        if (C * ap.S_tiles * kvb::attn_tile_scores() > ctx->S_floats)
-            return fail(KV_E_RANGE, "internal: score scratch too small for %lld CTAs x %lld tiles", (long long)C,
-                        (long long)ap.S_tiles);
-    }
-    {
-        // CTA c covers flattened rows [c*T/C, (c+1)*T/C) (the kernels' split)
-        const int64_t T = (int64_t)ctx->hkv_loc * n_kv, C = ap.n_cta;
-        auto lo = [&](int64_t cc) { return cc * T / C; };
-        auto cta_of = [&](int64_t x) {
-            int64_t cc = std::min<int64_t>(C - 1, x * C / T);
-            while (cc + 1 < C && lo(cc + 1) <= x) cc++;
-            while (cc > 0 && lo(cc) > x) cc--;
-            return cc;
-        };
-        for (int h = 0; h < ctx->hkv_loc; h++) {
-            const int64_t a = cta_of((int64_t)h * n_kv), b = cta_of((int64_t)(h + 1) * n_kv - 1);
-            ap.span_a[h] = (int16_t)a;
-            ap.span_b[h] = (int16_t)b;
-            ap.span_slot[h] = (int8_t)(lo(a) < (int64_t)h * n_kv ? 1 : 0);
-        }
-    }
+    kvb::attn_split(ap, ctx->hkv_loc, n_kv);
+    if ((int64_t)ap.n_cta * ap.S_tiles * kvb::attn_tile_scores() > ctx->S_floats)
+        return fail(KV_E_RANGE, "internal: score scratch too small for %d CTAs x %lld tiles", ap.n_cta,
+                    (long long)ap.S_tiles);
 
     const int rows = n_new * ctx->r;
     const int rows_per = kvb::attn_rows();
@@ -1495,6 +1570,21 @@ int kv_rope_table_host(const kv_config *cfg, int64_t pos0, int64_t npos, float *
         rope_rows(rs, pos0, pos0 + npos, out);
         return KV_OK;
     });
+}
+
+int kv_decode_shape(int32_t sm_count, int32_t n_kv_heads_local, int64_t n_kv, const int32_t *max_clusters,
+                    int32_t *n_cta, int32_t *cluster_ctas, int32_t *clusters_per_head)
+{
+    if (!n_cta || !cluster_ctas || !clusters_per_head || sm_count <= 0 || n_kv_heads_local <= 0 || n_kv <= 0)
+        return fail(KV_E_ARG, "bad argument");
+    int mc[kvb::kMaxClusterCtas + 1] = {};
+    if (max_clusters)
+        for (int q = 2; q <= kvb::kMaxClusterCtas; q++) mc[q] = max_clusters[q];
+    const DecodeShape d = decode_shape_for(sm_count, n_kv_heads_local, n_kv, max_clusters ? mc : nullptr, 0);
+    *n_cta = d.n_cta;
+    *cluster_ctas = d.cq;
+    *clusters_per_head = d.ncl;
+    return KV_OK;
 }
 
 int kv_decode_grid_fits(int32_t sm_count, int32_t blocks_per_sm, int32_t n_cta)

@@ -37,51 +37,6 @@ cudaError_t launch_ring_mask(__half *dst, int64_t stride, int64_t n_cells, int64
                              cudaStream_t st);
 
 // ---------------------------------------------------------------------------
-// decode attention (CUDA cores, two passes): scores, then P.V + combine
-// ---------------------------------------------------------------------------
-// "Query rows" of a KV head: row i = t*r + j is token t, query head j of the
-// GQA group.  One launch handles rows [row0, row0+nrows), nrows <= rmax(D).
-struct ScoresParams {
-    const __half *kc;                // layer K cache
-    int32_t row_elems;               // hkv_loc * D
-    const __half *qbuf;              // [n_new][hq_loc][D]
-    int32_t hq_loc, r;
-    int32_t row0, nrows;
-    int64_t n_past, n_kv;
-    int32_t split_len, n_splits;
-    float scale;
-    float *S;                        // [hkv_loc][RMAX][S_stride]
-    int64_t S_stride;
-    float *part_m;                   // [hkv_loc][n_splits][RMAX]
-    double *part_z;
-};
-
-struct PVParams {
-    const __half *vc;
-    int32_t row_elems;
-    const float *S;
-    int64_t S_stride;
-    const float *part_m;
-    const double *part_z;
-    float *part_o;                   // [hkv_loc][n_splits][RMAX][D]
-    unsigned *counters;              // [hkv_loc], zero between calls
-    int32_t r, row0, nrows;
-    int64_t n_past, n_kv;
-    int32_t split_len, n_splits;
-    float *out;                      // row t at out + t*out_stride
-    int64_t out_stride;
-    int32_t out_head0;               // column head of local query head 0
-};
-
-int decode_rmax(int D);
-size_t scores_smem(int D, int split_len);
-size_t pv_smem(int D, int split_len);
-int decode_split_max(int D);
-cudaError_t decode_prepare(int D);   // raises dynamic smem limits once
-cudaError_t launch_scores(int D, const ScoresParams &p, int hkv_loc, cudaStream_t st);
-cudaError_t launch_pv(int D, const PVParams &p, int hkv_loc, cudaStream_t st);
-
-// ---------------------------------------------------------------------------
 // attention of kv_attend (kv_attend.cu): one TMA-fed, tensor-core kernel per
 // layer and group of <= 8 query rows, chained with programmatic dependent launch
 // ---------------------------------------------------------------------------
@@ -94,6 +49,12 @@ struct AttnParams {
     int64_t n_kv, n_past;
     int32_t row0, nrows;             // query rows of this launch (row = t*r + j), nrows <= attn_rows()
     int32_t n_cta;                   // CTAs; hkv <= n_cta <= min(SMs, attn_max_ctas(), hkv*n_kv), all resident
+    // cluster mode (cq > 1, head_dim <= 128): clusters of cq CTAs, ncl of them
+    // per local head (n_cta = hkv * ncl * cq); a cluster's CTAs exchange the
+    // statistics and partial outputs through distributed shared memory
+    int32_t cq, ncl;
+    // tiles sent to L2 ahead of the ring where the producer waits longest (0: none)
+    int32_t l2pf;
     float scale;
     // single-token append done inside the kernel (decode): fused = 1
     int32_t fused;
@@ -169,6 +130,16 @@ int attn_max_ctas();   // CTAs one launch may have (a head's span is read in one
 cudaError_t attn_prepare(int D);
 // CTAs of the attention kernel one SM holds at once (the fewest over its instances)
 cudaError_t attn_occupancy(int D, int *blocks_per_sm);
+// clusters of q CTAs of the attention kernel the device holds at once (0: no
+// cluster mode at this head_dim)
+cudaError_t attn_cluster_occupancy(int D, int q, int *clusters);
+constexpr int kMaxClusterCtas = 8;
+// the split's per-launch tables (score tiles per CTA, each head's CTA span) for ap.n_cta CTAs
+void attn_split(AttnParams &ap, int hkv, int64_t n_kv);
+// CTAs of the plain (cluster-less) decode split
+int attn_plain_ctas(int sm_count, int hkv, int64_t n_kv);
+// one layer's K or V cache [rows][hkv][D] F16 as the attention kernel's tensor map (KV_OK or an error code)
+int encode_cache_map(CUtensorMap *m, const void *base, int64_t rows, int hkv, int D);
 // pdl: launch as a programmatic dependent of the previous kernel in the stream;
 // coop: as a cooperative launch (the driver starts the grid only with every CTA resident)
 cudaError_t launch_attn(int D, const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnParams &p,

@@ -1,15 +1,15 @@
 // kv_noalloc.cu -- decode attention for callers that must not allocate device memory.
 //
-// kv_attend() works inside a kv_ctx whose scratch (rotated Q, scores, split
-// partials, completion counters) kv_alloc() obtained with cudaMalloc.  Some
+// kv_attend() works inside a kv_ctx whose scratch (scores, statistics slots,
+// output accumulators, tickets) kv_alloc() obtained with cudaMalloc.  Some
 // callers cannot do that: a host framework that plans and owns every device
 // buffer up front (ggml's graph allocator, a serving engine that reserves all
 // of HBM for its own pool) and runs this op as a callback in the middle of its
 // compute, where a cudaMalloc would either fail for lack of free memory or
 // stall the device with the allocator's implicit synchronisation.  For them,
-// kv_attend_decode_noalloc() runs the same two decode kernels (scores, then
-// F16-rounded P.V with the deterministic combine) on one token, with the
-// caller's cache, query and output buffers, and with all scratch taken from a
+// kv_attend_decode_noalloc() runs kv_attend's decode attention kernel on one
+// token -- the default (not the flash-attn) branch, plain grid -- over the
+// caller's cache, query and output buffers, with all scratch taken from a
 // fixed array compiled into this library.
 //
 // The array is a file-scope `static __device__` object of kScratchBytes: every
@@ -17,14 +17,20 @@
 // cannot use the array's name as a device address (on the host it names a
 // stand-in object), so the first call on each device, with that device
 // current, asks the runtime for its device address once (cudaGetSymbolAddress)
-// and keeps it.  Because of that one-time set-up, the first call on a device
-// should be made before any stream capture begins.
+// and keeps it, together with the kernel's shared-memory set-up.  Because of
+// that one-time set-up, the first call on a device should be made before any
+// stream capture begins; and because it is kept for the life of the process,
+// a cudaDeviceReset() invalidates it (restart the process after one).
 //
 // All calls share the one array and it keeps whatever the last call left
-// there; this file clears the part that must start at zero (the per-head
-// completion counters) at the start of every call.  Two calls whose work
-// overlaps on the GPU (different streams, or different host threads) race on
-// the array: serialise them.
+// there; each call clears the part that must start at zero (the per-head
+// output accumulators and tickets) before its kernels run.  Two calls whose
+// work overlaps on the GPU (different streams, or different host threads)
+// race on the array: serialise them.
+//
+// The kernel's CTAs wait on one another; this entry launches it cooperatively,
+// so the driver starts it only with the whole grid resident, even when the
+// caller's other work shares the GPU.
 #include <cstdio>
 #include <mutex>
 
@@ -33,13 +39,15 @@
 
 namespace {
 
-constexpr size_t kScratchBytes = (size_t)8 << 20;   // 8 MiB per device
+constexpr size_t kScratchBytes = (size_t)16 << 20;   // 16 MiB per device
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 struct DeviceSlot {
     unsigned char *base = nullptr;  // device address of g_noalloc_scratch
     int sm_count = 0;
+    unsigned prepared = 0;          // head dims whose kernel attributes are set (bit per 64/96/128)
+    uint32_t epoch = 0;             // tag of the last launch's statistics slots
 };
 DeviceSlot g_slots[kMaxDevices];
 std::mutex g_slot_mu;
@@ -54,7 +62,12 @@ __global__ void q_to_f16_kernel(const float *q, __half *dst, int n)
     if (i < n) dst[i] = __float2half_rn(q[i]);
 }
 
-int setup_device(int dev, DeviceSlot **out, const char **why)
+unsigned dim_bit(int D) { return D == 64 ? 1u : D == 96 ? 2u : 4u; }
+
+// Per-device set-up, once: the array's device address and the kernel's
+// shared-memory limit for this head_dim.  Returns the slot with the epochs of
+// `launches` launches reserved (first one in *epoch0), under the lock.
+int setup_device(int dev, int D, int launches, DeviceSlot *out, uint32_t *epoch0, bool *wrapped, const char **why)
 {
     std::lock_guard<std::mutex> lk(g_slot_mu);
     DeviceSlot &s = g_slots[dev];
@@ -68,7 +81,21 @@ int setup_device(int dev, DeviceSlot **out, const char **why)
         s.base = static_cast<unsigned char *>(p);
         s.sm_count = sms;
     }
-    *out = &s;
+    if (!(s.prepared & dim_bit(D))) {
+        cudaError_t e = kvb::attn_prepare(D);
+        if (e != cudaSuccess) { *why = cudaGetErrorString(e); return KV_E_CUDA; }
+        s.prepared |= dim_bit(D);
+    }
+    // epochs tag the statistics slots; the array starts zeroed, so 0 is never
+    // a launch's tag, and a wrap clears the slots (by the caller, on its stream)
+    *wrapped = false;
+    if (s.epoch > 0xffffffffu - (uint32_t)launches) {
+        s.epoch = 0;
+        *wrapped = true;
+    }
+    *epoch0 = s.epoch + 1;
+    s.epoch += (uint32_t)launches;
+    *out = s;
     return KV_OK;
 }
 
@@ -86,42 +113,44 @@ extern "C" int kv_attend_decode_noalloc(const uint16_t *k_cache, const uint16_t 
         return kvb::set_last_error(KV_E_ARG, "kv_attend_decode_noalloc: bad head counts or n_kv < 1");
     if ((((uintptr_t)k_cache) | ((uintptr_t)v_cache)) & 15u)
         return kvb::set_last_error(KV_E_ARG, "kv_attend_decode_noalloc: cache pointers must be 16-byte aligned");
-    // shapes whose Q copy or one row of scores alone exceed the static array:
+    // shapes whose query copy or scores alone exceed the static array:
     // refused before the sizing arithmetic below, which they could overflow
+    const uint64_t tile_bytes = (uint64_t)kvb::attn_tile_scores() * sizeof(float);
     if ((uint64_t)n_head * (uint64_t)head_dim * sizeof(__half) > kScratchBytes ||
-        (uint64_t)n_kv > kScratchBytes / sizeof(float))
+        (uint64_t)n_kv > (uint64_t)(kScratchBytes / tile_bytes) * kvb::attn_tile_keys() / (uint64_t)n_head_kv)
         return kvb::set_last_error(KV_E_RANGE, "kv_attend_decode_noalloc: the shape needs more scratch than the "
-                                               "static array holds (fewer keys or heads per call)");
+                                               "static array holds (fewer keys or KV heads per call)");
+    if (n_head_kv > kvb::kMaxLocalHeads)
+        return kvb::set_last_error(KV_E_RANGE, "kv_attend_decode_noalloc: more KV heads than a launch covers (64)");
 
     const int D = head_dim, hkv = n_head_kv, r = n_head / n_head_kv;
-    const int rmax = kvb::decode_rmax(D), split_max = kvb::decode_split_max(D);
+    const int rows_per = kvb::attn_rows();
+    const int launches = (r + rows_per - 1) / rows_per;
 
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
         return kvb::set_last_error(KV_E_CUDA, "kv_attend_decode_noalloc: no usable current device");
-    DeviceSlot *slot = nullptr;
+    DeviceSlot slot;
+    uint32_t epoch0 = 0;
+    bool wrapped = false;
     const char *why = "";
-    int rc = setup_device(dev, &slot, &why);
+    int rc = setup_device(dev, D, launches, &slot, &epoch0, &wrapped, &why);
     if (rc != KV_OK) return kvb::set_last_error(rc, why);
 
-    // the split choice of kv_attend: ~2 CTAs per SM, splits of 64..split_max keys
-    const int target = (2 * slot->sm_count + hkv - 1) / hkv > 1 ? (2 * slot->sm_count + hkv - 1) / hkv : 1;
-    int64_t split_len = (n_kv + target - 1) / target;
-    split_len = ((split_len + 63) / 64) * 64;
-    if (split_len < 64) split_len = 64;
-    if (split_len > split_max) split_len = split_max;
-    const int n_splits = (int)((n_kv + split_len - 1) / split_len);
+    // the plain split of kv_attend (one CTA per SM at most, >= 256 keys a CTA)
+    kvb::AttnParams ap{};
+    ap.n_cta = std::min(kvb::attn_plain_ctas(slot.sm_count, hkv, n_kv), kvb::attn_max_ctas());
+    kvb::attn_split(ap, hkv, n_kv);
 
-    // carve the static array: Q (F16), scores, partial max / sum / output, counters
-    const int64_t S_stride = ((n_kv + 3) / 4) * 4;
-    const size_t n_part = (size_t)hkv * (size_t)n_splits * (size_t)rmax;
+    // carve the static array: query (F16), scores, statistics slots, then the
+    // zeroed block: output accumulators, tickets + non-finite flags, error word
     const size_t off_q = 0;
     const size_t off_s = off_q + align256((size_t)n_head * D * sizeof(__half));
-    const size_t off_m = off_s + align256((size_t)hkv * rmax * (size_t)S_stride * sizeof(float));
-    const size_t off_z = off_m + align256(n_part * sizeof(float));
-    const size_t off_o = off_z + align256(n_part * sizeof(double));
-    const size_t off_c = off_o + align256(n_part * (size_t)D * sizeof(float));
-    const size_t need = off_c + align256((size_t)hkv * sizeof(unsigned));
+    const size_t off_st = off_s + align256((size_t)ap.n_cta * ap.S_tiles * tile_bytes);
+    const size_t off_acc = off_st + align256((size_t)ap.n_cta * 2u * 8u * 2u * sizeof(unsigned long long));
+    const size_t off_ctl = off_acc + (size_t)hkv * 8u * (size_t)D * sizeof(long long);
+    const size_t zero_bytes = (off_ctl - off_acc) + (2u * (size_t)hkv + 2u) * sizeof(unsigned);
+    const size_t need = off_acc + zero_bytes;
     if (need > kScratchBytes) {
         char msg[200];
         snprintf(msg, sizeof(msg), "kv_attend_decode_noalloc: needs %zu bytes of scratch, the static array holds %zu "
@@ -129,64 +158,50 @@ extern "C" int kv_attend_decode_noalloc(const uint16_t *k_cache, const uint16_t 
         return kvb::set_last_error(KV_E_RANGE, msg);
     }
 
-    unsigned char *base = slot->base;
+    CUtensorMap km, vm;
+    rc = kvb::encode_cache_map(&km, k_cache, n_kv, hkv, D);
+    if (rc == KV_OK) rc = kvb::encode_cache_map(&vm, v_cache, n_kv, hkv, D);
+    if (rc != KV_OK) return rc;
+
+    unsigned char *base = slot.base;
     __half *qbuf = reinterpret_cast<__half *>(base + off_q);
-    float *S = reinterpret_cast<float *>(base + off_s);
-    float *part_m = reinterpret_cast<float *>(base + off_m);
-    double *part_z = reinterpret_cast<double *>(base + off_z);
-    float *part_o = reinterpret_cast<float *>(base + off_o);
-    unsigned *counters = reinterpret_cast<unsigned *>(base + off_c);
+    unsigned *ctl = reinterpret_cast<unsigned *>(base + off_ctl);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 
-    if (kvb::decode_prepare(D) != cudaSuccess) return kvb::set_last_error(KV_E_CUDA, "kv_attend_decode_noalloc: kernel attribute set-up failed");
-    if (cudaMemsetAsync(counters, 0, (size_t)hkv * sizeof(unsigned), st) != cudaSuccess)
-        return kvb::set_last_error(KV_E_CUDA, "kv_attend_decode_noalloc: clearing the counters failed");
+    if (wrapped && cudaMemsetAsync(base + off_st, 0, off_acc - off_st, st) != cudaSuccess)
+        return kvb::set_last_error(KV_E_CUDA, "kv_attend_decode_noalloc: clearing the statistics slots failed");
+    if (cudaMemsetAsync(base + off_acc, 0, zero_bytes, st) != cudaSuccess)
+        return kvb::set_last_error(KV_E_CUDA, "kv_attend_decode_noalloc: clearing the accumulators failed");
     const int nq = n_head * D;
     q_to_f16_kernel<<<(nq + 255) / 256, 256, 0, st>>>(q, qbuf, nq);
     if (cudaGetLastError() != cudaSuccess) return kvb::set_last_error(KV_E_CUDA, "kv_attend_decode_noalloc: launch failed");
 
-    for (int row0 = 0; row0 < r; row0 += rmax) {
-        const int nrows = r - row0 < rmax ? r - row0 : rmax;
-        kvb::ScoresParams sp;
-        sp.kc = reinterpret_cast<const __half *>(k_cache);
-        sp.row_elems = hkv * D;
-        sp.qbuf = qbuf;
-        sp.hq_loc = n_head;
-        sp.r = r;
-        sp.row0 = row0;
-        sp.nrows = nrows;
-        sp.n_past = n_kv - 1;
-        sp.n_kv = n_kv;
-        sp.split_len = (int)split_len;
-        sp.n_splits = n_splits;
-        sp.scale = 1.0f / sqrtf((float)D);
-        sp.S = S;
-        sp.S_stride = S_stride;
-        sp.part_m = part_m;
-        sp.part_z = part_z;
-        if (kvb::launch_scores(D, sp, hkv, st) != cudaSuccess)
-            return kvb::set_last_error(KV_E_CUDA, "kv_attend_decode_noalloc: scores launch failed");
-        kvb::PVParams pp;
-        pp.vc = reinterpret_cast<const __half *>(v_cache);
-        pp.row_elems = sp.row_elems;
-        pp.S = S;
-        pp.S_stride = S_stride;
-        pp.part_m = part_m;
-        pp.part_z = part_z;
-        pp.part_o = part_o;
-        pp.counters = counters;
-        pp.r = r;
-        pp.row0 = row0;
-        pp.nrows = nrows;
-        pp.n_past = n_kv - 1;
-        pp.n_kv = n_kv;
-        pp.split_len = (int)split_len;
-        pp.n_splits = n_splits;
-        pp.out = out;
-        pp.out_stride = (int64_t)n_head * D;
-        pp.out_head0 = 0;
-        if (kvb::launch_pv(D, pp, hkv, st) != cudaSuccess)
-            return kvb::set_last_error(KV_E_CUDA, "kv_attend_decode_noalloc: P.V launch failed");
+    ap.hkv = hkv;
+    ap.r = r;
+    ap.hq_loc = n_head;
+    ap.n_kv = n_kv;
+    ap.n_past = n_kv - 1;
+    ap.scale = 1.0f / sqrtf((float)D);
+    ap.qbuf = qbuf;
+    ap.hz_row = -1;
+    ap.S = reinterpret_cast<float *>(base + off_s);
+    ap.stats = reinterpret_cast<unsigned long long *>(base + off_st);
+    ap.acc = reinterpret_cast<long long *>(base + off_acc);
+    ap.counters = ctl;
+    ap.nonfin = ctl + hkv;
+    ap.xticket = ctl + 2 * hkv;
+    ap.err = ctl + 2 * hkv + 1;
+    ap.limit_ns = 1000000000ull;
+    ap.out = out;
+    ap.out_stride = (int64_t)n_head * D;
+    ap.cq = 1;
+    ap.ncl = 1;
+    for (int i = 0; i < launches; i++) {
+        ap.row0 = i * rows_per;
+        ap.nrows = std::min(rows_per, r - ap.row0);
+        ap.epoch = epoch0 + (uint32_t)i;
+        if (kvb::launch_attn(D, km, vm, ap, st, false, true) != cudaSuccess)
+            return kvb::set_last_error(KV_E_CUDA, "kv_attend_decode_noalloc: attention launch failed");
     }
     kvb::set_last_error(KV_OK, "");
     return KV_OK;

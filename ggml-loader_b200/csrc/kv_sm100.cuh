@@ -145,6 +145,16 @@ __device__ __forceinline__ void tma_load_3d_hint(void *dst, const CUtensorMap *m
         : "memory");
 }
 
+// 3-D tile of a tensor map into L2 only (no shared memory, no barrier); the
+// innermost coordinate x follows tma_load_3d's alignment rule
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap *m, int x, int y, int z)
+{
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                     reinterpret_cast<uint64_t>(m)),
+                 "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+
 // drop a dead 128-byte line from L2 without writing it back (scratch that is
 // rewritten before it is read again)
 __device__ __forceinline__ void l2_discard(const void *p)
@@ -278,6 +288,104 @@ __device__ __forceinline__ void ld_volatile_v2(const unsigned long long *p, unsi
                                                unsigned long long &b)
 {
     asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// ---- thread-block clusters: distributed shared memory ------------------------------
+// A cluster's CTAs are resident together on one GPC; each can address the
+// others' shared memory through the shared::cluster window (mapa).  Only this
+// GPU's own shared memory is reached this way.
+__device__ __forceinline__ uint32_t cluster_rank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// every thread of every CTA in the cluster: arrive (release) and wait (acquire)
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// the shared::cluster address of the same offset in CTA `rank`'s shared memory
+__device__ __forceinline__ uint32_t mapa(uint32_t local_addr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void st_cluster_v2(uint32_t addr, float a, float b)
+{
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float4 v)
+{
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w)
+                 : "memory");
+}
+
+// asynchronous stores into another CTA's shared memory (addresses from mapa):
+// each completes `bytes` of the transaction count of the mbarrier `remote_bar`
+// in that CTA, whose wait then sees the data
+__device__ __forceinline__ void st_async_v2(uint32_t addr, float a, float b, uint32_t remote_bar)
+{
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+                 "f"(a), "f"(b), "r"(remote_bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void st_async_v4(uint32_t addr, float4 v, uint32_t remote_bar)
+{
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     addr),
+                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar)
+                 : "memory");
+}
+
+// the two halves of a cluster barrier phase: every thread of every CTA arrives
+// once (release) and later waits once (acquire)
+__device__ __forceinline__ void cluster_arrive()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait()
+{
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// arrive on an mbarrier in another CTA of the cluster (address from mapa),
+// releasing at cluster scope what this thread -- and, through a preceding CTA
+// barrier, its CTA -- wrote before
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits (acquiring at cluster scope) for the phase with the given parity; false after limit_ns.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, uint64_t limit_ns)
+{
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t n = 1;; n++) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((n & 15u) == 0 && globaltimer() - t0 > limit_ns) return false;
+    }
 }
 
 // ---- 5th-generation tensor cores: TMEM and tcgen05.mma ----------------------------

@@ -107,6 +107,8 @@ def lib():
         "kv_shard_geometry": (ctypes.c_int, [cfgp, _i32] + [ctypes.POINTER(_i32)] * 4),
         "kv_decode_ctas": (ctypes.c_int, [_i32, _i32, _i64, ctypes.POINTER(_i32)]),
         "kv_decode_grid_fits": (ctypes.c_int, [_i32, _i32, _i32]),
+        "kv_decode_shape": (ctypes.c_int, [_i32, _i32, _i64, ctypes.POINTER(_i32), ctypes.POINTER(_i32),
+                                           ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

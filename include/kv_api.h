@@ -253,15 +253,17 @@ int kv_forward(kv_ctx *ctx, int64_t n_past, int32_t n_new,
  *                     token's K/V already written at row n_kv-1;
  *   q:   the new token's rotated query, [n_head][head_dim] F32 (device);
  *   out: [n_head*head_dim] F32 (device), the layout kv_attend writes.
- * Same math as kv_attend for one token.  Its scratch is a fixed 8 MiB array
- * built into the library (held by every GPU that loads it until exit); a call
- * needs about n_head_kv*rows_per_pass*n_kv*4 bytes of it for scores (rows per
- * pass: 4 at head_dim 96/128, 8 at 64 -- about 60k keys with 8 KV heads at
- * head_dim 128, 15k with 32 at 96) and returns KV_E_RANGE, with
- * kv_last_error() saying so,
- * when the shape does not fit.  The first call on a device looks up the
- * array's device address, so make it before any stream capture.  Calls share
- * the array: calls that overlap on the GPU race and must be serialised.
+ * It runs kv_attend's decode attention kernel (its default branch -- not the
+ * flash-attn one -- over a plain grid, launched cooperatively so the driver
+ * starts it only with all its CTAs resident).  Its scratch is a fixed 16 MiB
+ * array built into the library (held by every GPU that loads it until exit);
+ * a call needs about 32 bytes of it per (KV head, key) for scores -- about
+ * 56k keys with 8 KV heads, 14k with 32 -- and returns KV_E_RANGE, with
+ * kv_last_error() saying so, when the shape does not fit.  The first call on
+ * a device looks up the array's device address and sets up the kernel, so
+ * make it before any stream capture; a cudaDeviceReset() invalidates that
+ * set-up for the rest of the process.  Calls share the array: calls that
+ * overlap on the GPU race and must be serialised.
  */
 int kv_attend_decode_noalloc(const uint16_t *k_cache, const uint16_t *v_cache,
                              int32_t n_head, int32_t n_head_kv, int32_t head_dim, int64_t n_kv,

@@ -66,6 +66,15 @@ int kv_shard_geometry(const kv_config *cfg, int32_t shard, int32_t *q_head0, int
  * multiple of the heads when that idles at most 5 % of them. */
 int kv_decode_ctas(int32_t sm_count, int32_t n_kv_heads_local, int64_t n_kv, int32_t *n_cta);
 
+/* The decode grid for a layer (host arithmetic only): n_cta CTAs in clusters
+ * of cluster_ctas CTAs (1: no clusters), clusters_per_head per local KV head.
+ * max_clusters[q] (q = 2..8; NULL: none) is the number of q-CTA clusters the
+ * device holds at once.  One cluster per head when the head's keys fit its
+ * CTAs (>= 256 keys each) at >= 85 % of kv_decode_ctas' CTA count; else no
+ * clusters. */
+int kv_decode_shape(int32_t sm_count, int32_t n_kv_heads_local, int64_t n_kv, const int32_t *max_clusters,
+                    int32_t *n_cta, int32_t *cluster_ctas, int32_t *clusters_per_head);
+
 /* 1 when a decode grid of n_cta CTAs is resident at once on sm_count SMs
  * holding blocks_per_sm CTAs each, else 0 (host arithmetic only).  The decode
  * kernel's CTAs wait on one another, so kv_alloc refuses a device where its

@@ -343,3 +343,31 @@ def test_decode_grid_residency_check():
                     continue
                 assert K.lib().kv_decode_ctas(sm, hkv, n_kv, ctypes.byref(out)) == K.KV_OK
                 assert fits(sm, 1, out.value) == 1
+
+
+def test_decode_cluster_shapes():
+    """kv_decode_shape (host arithmetic): one cluster of <= 8 CTAs per head when
+    the head's keys fit it (>= 256 keys a CTA) at >= 85 % of the plain split's
+    CTAs; otherwise no clusters; never a cluster size the device cannot hold."""
+    def shape(sm, hkv, n_kv, mc):
+        arr = None
+        if mc is not None:
+            arr = (ctypes.c_int32 * 9)(*[mc.get(q, 0) for q in range(9)])
+        out = [ctypes.c_int32() for _ in range(3)]
+        assert K.lib().kv_decode_shape(sm, hkv, n_kv, arr, *[ctypes.byref(o) for o in out]) == K.KV_OK
+        return tuple(o.value for o in out)
+    roomy = {q: 148 // q for q in range(2, 9)}
+    b200 = {2: 74, 3: 45, 4: 33, 5: 0, 6: 22, 7: 0, 8: 15}   # measured at 216 KB of shared memory a CTA
+    assert shape(148, 2, 2049, b200) == (16, 8, 1)         # qwen2-0.5B: a cluster of 8 per head
+    assert shape(148, 32, 3969, b200) == (128, 4, 1)       # phi3-mini: a cluster of 4 per head
+    assert shape(148, 1, 32001, b200) == (126, 1, 1)       # one-head shard: the plain split
+    assert shape(148, 8, 32001, b200) == (144, 1, 1)       # llama-3.2-3B: the plain split
+    assert shape(148, 8, 32001, None) == (144, 1, 1)       # no cluster support: the plain split
+    assert shape(148, 32, 3969, {4: 31}) == (148, 1, 1)    # 32 clusters of 4 do not fit
+    assert shape(148, 2, 2049, {8: 1, 4: 4}) == (17, 1, 1)  # 2 clusters of 8 do not fit; 4s keep too few CTAs
+    for hkv in (1, 2, 4, 8, 32):
+        for n_kv in (1, 300, 2049, 4096, 32001, 131001):
+            c, q, ncl = shape(148, hkv, n_kv, roomy)
+            assert c <= 148 and q <= 8 and ncl == 1
+            if q > 1:                                     # one cluster a head, within the device's capacity
+                assert c == hkv * q and roomy[q] >= hkv and (n_kv + 255) // 256 >= q
