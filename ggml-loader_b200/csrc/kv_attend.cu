@@ -340,8 +340,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 // the two waits for a free stage that last longest -- behind the
                 // previous kernel's tail and behind the statistics exchange --
                 // keep HBM busy: the next l2pf tiles go to L2 first
-                if ((j == NS || j == g.nt + NS) && p.l2pf > 0)
-                    for (int t = j; t < total && t < j + p.l2pf; t++) {
+                if (((j == NS && (p.l2pf & 0x100)) || (j == g.nt + NS && (p.l2pf & 0x200))) && (p.l2pf & 0xff))
+                    for (int t = j; t < total && t < j + (p.l2pf & 0xff); t++) {
                         const bool tv = t >= g.nt;
                         int h2;
                         int64_t k2, e2;

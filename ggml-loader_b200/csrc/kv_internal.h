@@ -53,7 +53,10 @@ struct AttnParams {
     // per local head (n_cta = hkv * ncl * cq); a cluster's CTAs exchange the
     // statistics and partial outputs through distributed shared memory
     int32_t cq, ncl;
-    // tiles sent to L2 ahead of the ring where the producer waits longest (0: none)
+    // tiles sent to L2 ahead of the ring where the producer waits longest: the
+    // count in bits 0-7 (0: none); bit 8: at its first wait (behind the previous
+    // kernel's tail), bit 9: at its first wait among the V tiles (behind the
+    // statistics exchange)
     int32_t l2pf;
     float scale;
     // single-token append done inside the kernel (decode): fused = 1
