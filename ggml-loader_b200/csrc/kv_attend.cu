@@ -261,9 +261,10 @@ struct Smem {
 // the kernel
 // ---------------------------------------------------------------------------
 // MASKED: the instance for the caller's mask or a ring's single token (every
-// key visible); FLASH: the flash-attn branch.  The plain causal default-branch
-// instance is compiled without either.
-template <int D, bool MASKED, bool FLASH>
+// key visible); FLASH: the flash-attn branch; CL: cluster mode (launched with
+// clusters of p.cq CTAs).  The plain causal default-branch instance is
+// compiled without any of them.
+template <int D, bool MASKED, bool FLASH, bool CL>
 __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                                                                     const __grid_constant__ CUtensorMap vmap,
                                                                     const AttnParams p)
@@ -291,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     uint64_t *cbar = reinterpret_cast<uint64_t *>(smem + L::o_cbar);
     float *crecv = reinterpret_cast<float *>(smem + L::o_crecv);
     // cluster mode (p.cq > 1): CTAs c of one cluster cover one head; rank 0 leads
-    const bool clus = L::kMaxQ > 1 && p.cq > 1;
+    constexpr bool clus = CL && L::kMaxQ > 1;   // the plain instances carry no cluster code
     const uint32_t crank = clus ? cluster_rank() : 0u;
 
     const int c = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1080,17 +1081,25 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
+template <int D, bool CL>
+cudaError_t prep_cl()
+{
+    const int b = (int)Smem<D>::bytes;
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, false, false, CL>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_decode_kernel<D, false, true, CL>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_decode_kernel<D, true, false, CL>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_decode_kernel<D, true, true, CL>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+    return e;
+}
+
 template <int D>
 cudaError_t prep()
 {
-    const int b = (int)Smem<D>::bytes;
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(attn_decode_kernel<D, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(attn_decode_kernel<D, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(attn_decode_kernel<D, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, b);
+    cudaError_t e = prep_cl<D, false>();
+    if (e == cudaSuccess && Smem<D>::kMaxQ > 1) e = prep_cl<D, Smem<D>::kMaxQ != 1>();
     return e;
 }
 
@@ -1100,10 +1109,10 @@ cudaError_t occupancy(int *blocks)
     // the fewest resident CTAs an SM takes among the four instances
     int b[4] = {0, 0, 0, 0};
     const size_t sm = Smem<D>::bytes;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b[0], attn_decode_kernel<D, false, false>, kThreads, sm);
-    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b[1], attn_decode_kernel<D, false, true>, kThreads, sm);
-    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b[2], attn_decode_kernel<D, true, false>, kThreads, sm);
-    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b[3], attn_decode_kernel<D, true, true>, kThreads, sm);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b[0], attn_decode_kernel<D, false, false, false>, kThreads, sm);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b[1], attn_decode_kernel<D, false, true, false>, kThreads, sm);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b[2], attn_decode_kernel<D, true, false, false>, kThreads, sm);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b[3], attn_decode_kernel<D, true, true, false>, kThreads, sm);
     *blocks = std::min(std::min(b[0], b[1]), std::min(b[2], b[3]));
     return e;
 }
@@ -1140,10 +1149,17 @@ cudaError_t launch(const CUtensorMap &kmap, const CUtensorMap &vmap, const AttnP
     cfg.attrs = attr;
     cfg.numAttrs = na;
     const bool m = p.mask || p.all_keys;
-    if (m && p.flash) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true, true>, kmap, vmap, p);
-    if (m) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true, false>, kmap, vmap, p);
-    if (p.flash) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, false, true>, kmap, vmap, p);
-    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, false, false>, kmap, vmap, p);
+    if (p.cq > 1) {
+        constexpr bool C = Smem<D>::kMaxQ > 1;   // (the launch was refused above otherwise)
+        if (m && p.flash) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true, true, C>, kmap, vmap, p);
+        if (m) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true, false, C>, kmap, vmap, p);
+        if (p.flash) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, false, true, C>, kmap, vmap, p);
+        return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, false, false, C>, kmap, vmap, p);
+    }
+    if (m && p.flash) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true, true, false>, kmap, vmap, p);
+    if (m) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, true, false, false>, kmap, vmap, p);
+    if (p.flash) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, false, true, false>, kmap, vmap, p);
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, false, false, false>, kmap, vmap, p);
 }
 
 }  // namespace
@@ -1182,10 +1198,10 @@ cudaError_t cluster_occupancy(int q, int *clusters)
     cfg.attrs = a;
     cfg.numAttrs = 1;
     int n[4] = {0, 0, 0, 0};
-    cudaError_t e = cudaOccupancyMaxActiveClusters(&n[0], attn_decode_kernel<D, false, false>, &cfg);
-    if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n[1], attn_decode_kernel<D, false, true>, &cfg);
-    if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n[2], attn_decode_kernel<D, true, false>, &cfg);
-    if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n[3], attn_decode_kernel<D, true, true>, &cfg);
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&n[0], attn_decode_kernel<D, false, false, true>, &cfg);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n[1], attn_decode_kernel<D, false, true, true>, &cfg);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n[2], attn_decode_kernel<D, true, false, true>, &cfg);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n[3], attn_decode_kernel<D, true, true, true>, &cfg);
     if (e == cudaSuccess) *clusters = std::min(std::min(n[0], n[1]), std::min(n[2], n[3]));
     return e;
 }
