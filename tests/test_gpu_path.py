@@ -203,6 +203,36 @@ def test_mid_size_matches_oracle(name, n_past, n_new, cuda):
     assert_close(out, orc.attend(kc, vc, n_past, qr))
 
 
+@pytest.mark.parametrize("n_new", [1, 24])
+def test_no_rope_layers_match_oracle(n_new, cuda):
+    """Attention layers without positional encoding (nemotron_h: model.cpp:1389
+    skips ggml_rope_ext when hp.no_rope) are a context with n_rot = 0: the
+    append stores the raw (normalised) K rows, decode and chunk alike."""
+    sp = specs.get("llama3.2-3b")
+    sp.update(n_layer=1, n_rot=0, rope_freq_factors=None)
+    n_past = 3000
+    n_ctx = n_past + 64
+    case = dict(name="no-rope", spec="llama3.2-3b", n_ctx=n_ctx, n_past=n_past, n_new=n_new)
+    run = Run(case, cuda, n_batch_max=64)
+    run.sp = sp
+    run.ctx.close()
+    run.cfg = K.make_config(sp, n_ctx=n_ctx, n_batch_max=64)
+    run.ctx = K.Context(run.cfg)
+    run.ctx.fill_synthetic(sp["seed"], 0, n_past, stream=run.stream)
+    kc, vc = _oracle_layer(sp, n_ctx, n_past)
+    rows = synth.qkv_rows(sp, 4, 0, n_new)
+    out = run.step(rows, n_past)
+    q, k, v = _split(sp, rows)
+    orc = O.Oracle(sp)
+    qr = orc.append(kc, vc, n_past, q, k, v)
+    hkv, d = sp["n_head_kv"], sp["head_dim"]
+    # the stored K rows are the inputs rounded to F16, unrotated
+    assert np.array_equal(kc[n_past:n_past + n_new], O.f32_to_f16_bits(k.reshape(n_new, hkv, d)))
+    assert np.array_equal(run.rows(0, n_past, n_new), kc[n_past:n_past + n_new])
+    assert np.array_equal(run.rows(1, n_past, n_new), vc[n_past:n_past + n_new])
+    assert_close(out, orc.attend(kc, vc, n_past, qr))
+
+
 @pytest.mark.parametrize("name,n_past,n_new", [
     ("qwen3-8b-prefill", 64, 8),       # one key tile per pair: every pair written by its own CTA
     ("qwen3-8b-prefill", 300, 200),    # pairs split over CTAs (fold), a last block with an empty tile B
