@@ -945,7 +945,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 return;
             }
         }
-        long long *acc = p.acc + (int64_t)h * kRows * D * p.acc_stride;
+        long long *acc = p.acc + (int64_t)h * kRows * D;
         unsigned bad = 0u;   // rows with a non-finite partial
         for (int idx = tid; idx < R * D; idx += kConsumers) {
             const int row = idx / D, dd = idx - row * D;
@@ -959,7 +959,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 if (flash) sum = __fmul_rn(sum, rowInv[sl * kRows + row]);   // flash: normalised here
             }
             if (isfinite(sum))
-                atomicAdd(reinterpret_cast<unsigned long long *>(acc + (int64_t)idx * p.acc_stride),
+                atomicAdd(reinterpret_cast<unsigned long long *>(acc + idx),
                           (unsigned long long)__float2ll_rn(__fmul_rn(sum, kFix)));
             else
                 bad |= 1u << row;
@@ -977,8 +977,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         if (flags[1 + sl]) {
             const unsigned nan_rows = __ldcg(&p.nonfin[h]);
             emit_head(h, [&](int idx, int row, int) {
-                const long long v = __ldcg(acc + (int64_t)idx * p.acc_stride);
-                acc[(int64_t)idx * p.acc_stride] = 0;
+                const long long v = __ldcg(acc + idx);
+                acc[idx] = 0;
                 return (nan_rows >> row) & 1u ? __int_as_float(0x7fc00000) : __fmul_rn(__ll2float_rn(v), kUnfix);
             });
             if (tid == 0) {

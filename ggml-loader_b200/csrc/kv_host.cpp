@@ -321,10 +321,6 @@ struct kv_ctx {
 namespace {
 
 constexpr int64_t kMaxPositions = (int64_t)1 << 31;
-// u64 words between consecutive output accumulators: one element per 128-byte
-// line, so the fixed-point additions of many CTAs to one head (a one-head
-// shard has ~126) are spread over as many lines as elements
-constexpr size_t kAccStride = 16;
 
 bool shape_ok(const kv_config *c, std::string &why)
 {
@@ -855,7 +851,7 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
         {(void **)&ctx->qbuf, (size_t)c.n_batch_max * ctx->hq_loc * D * sizeof(__half)},
         {(void **)&ctx->S, (size_t)ctx->S_floats * sizeof(float)},
         {(void **)&ctx->stats, n_part * 2u * sizeof(unsigned long long)},
-        {(void **)&ctx->acc, (size_t)ctx->hkv_loc * 8u * (size_t)D * kAccStride * sizeof(long long)},
+        {(void **)&ctx->acc, (size_t)ctx->hkv_loc * 8u * (size_t)D * sizeof(long long)},
         {(void **)&ctx->ctl, (2u * (size_t)ctx->hkv_loc + 1u) * sizeof(unsigned)},
         {(void **)&ctx->err, sizeof(unsigned)},
         {(void **)&ctx->ring_mask, ctx->ring ? (size_t)c.n_batch_max * (size_t)ctx->rows * sizeof(__half) : 0},
@@ -867,7 +863,7 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
     }
     e = cudaMemset(ctx->ctl, 0, (2u * (size_t)ctx->hkv_loc + 1u) * sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(ctx->stats, 0, n_part * 2u * sizeof(unsigned long long));
-    if (e == cudaSuccess) e = cudaMemset(ctx->acc, 0, (size_t)ctx->hkv_loc * 8u * (size_t)D * kAccStride * sizeof(long long));
+    if (e == cudaSuccess) e = cudaMemset(ctx->acc, 0, (size_t)ctx->hkv_loc * 8u * (size_t)D * sizeof(long long));
     if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, sizeof(unsigned));
     if (e != cudaSuccess) return bail(cuda_fail(e, "cudaMemset"));
     e = kvb::attn_prepare(ctx->D);
@@ -1267,7 +1263,6 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
     ap.S = ctx->S;
     ap.stats = ctx->stats;
     ap.acc = ctx->acc;
-    ap.acc_stride = (int32_t)kAccStride;
     ap.counters = ctx->ctl;
     ap.nonfin = ctx->ctl + ctx->hkv_loc;
     ap.hz_row = (ctx->hz_stream == st && ctx->hz_layer == layer) ? ctx->hz_row : -1;
@@ -1465,7 +1460,7 @@ int kv_status(kv_ctx *ctx, void *stream)
     // a CTA that left early never counted itself in: restart the per-head
     // tickets and clear the output accumulators
     KV_CUDA(cudaMemset(ctx->ctl, 0, (2u * (size_t)ctx->hkv_loc + 1u) * sizeof(unsigned)));
-    KV_CUDA(cudaMemset(ctx->acc, 0, (size_t)ctx->hkv_loc * 8u * (size_t)ctx->D * kAccStride * sizeof(long long)));
+    KV_CUDA(cudaMemset(ctx->acc, 0, (size_t)ctx->hkv_loc * 8u * (size_t)ctx->D * sizeof(long long)));
     KV_CUDA(cudaMemset(ctx->err, 0, sizeof(unsigned)));
     return fail(KV_E_TIMEOUT, "a device-side wait expired (error word 0x%x); the outputs of that call are invalid",
                 word);

@@ -80,10 +80,7 @@ struct AttnParams {
     unsigned long long *stats;       // [n_cta][2][8][2] (max, sum of exp) per (CTA, segment, row),
                                      // each word = epoch << 32 | float bits
     uint32_t epoch;                  // tag of this launch's statistics (never 0)
-    long long *acc;                  // [hkv][8][D] output accumulators, fixed point 2^-40, zero between calls,
-                                     // element i at acc + i * acc_stride (one per 128-byte line: the
-                                     // CTAs' additions to one element do not queue behind other elements')
-    int32_t acc_stride;
+    long long *acc;                  // [hkv][8][D] output accumulators, fixed point 2^-40, zero between calls
     unsigned *counters;              // [hkv] output tickets, zero between calls
     unsigned *nonfin;                // [hkv] rows (bit per row) with a non-finite partial output, zero between calls
     unsigned *err;                   // error word (1: consumer tile wait, 2: producer, 4: statistics wait)
