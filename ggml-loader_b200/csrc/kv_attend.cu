@@ -813,8 +813,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             // every peer's receive buffer (NVLink stores; no fence or flag:
             // the reader checks each word's tag)
             const unsigned long long word = ((unsigned long long)p.epoch << 32) | __float_as_uint(val);
-            for (int gg = 0; gg < p.n_peers; gg++)
-                if (gg != p.shard) p.rx[gg][par * p.rx_stride + o] = word;
+            if (p.xpull) {
+                if (p.n_peers > 1) p.rx[p.shard][par * p.rx_stride + o] = word;
+            } else {
+                for (int gg = 0; gg < p.n_peers; gg++)
+                    if (gg != p.shard) p.rx[gg][par * p.rx_stride + o] = word;
+            }
         }
         if (p.n_peers > 1) {
             named_sync(1, kConsumers);
@@ -825,28 +829,35 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             if (flags[3]) {
                 KV_STAMP(tid == 0, 8);   // collector starts polling the peers' words
                 // every column outside this shard's, once its word carries
-                // this launch's tag; a thread keeps up to 8 words' loads in
+                // this launch's tag; a thread keeps up to kXW words' loads in
                 // flight per poll
-                const unsigned long long *src = p.rx[p.shard] + par * p.rx_stride;
-                const int cols = p.hkv * p.r * D;   // this shard's columns
+                const int cols = p.hkv * p.r * D;   // this shard's columns (every shard has as many)
+                // push: the peers' words sit in this shard's buffer; pull: in
+                // the buffer of the shard that owns the column
+                auto word_at = [&](int o) -> const unsigned long long * {
+                    return (p.xpull ? p.rx[o / cols] : p.rx[p.shard]) + par * p.rx_stride + o;
+                };
                 const int lo = p.out_head0 * D, all = p.n_peers * cols;
                 const unsigned ep = p.epoch;
                 bool xlate = false;
                 const uint64_t t0 = globaltimer();
-                for (int base = 0; base < all && !xlate; base += 8 * kConsumers) {
+                // up to kXW words a thread in one batch: at 8 shards every peer
+                // column of a 4-head group (3584 words) in one poll round trip
+                constexpr int kXW = 16;
+                for (int base = 0; base < all && !xlate; base += kXW * kConsumers) {
                     unsigned pend = 0u;
 #pragma unroll
-                    for (int u = 0; u < 8; u++) {
+                    for (int u = 0; u < kXW; u++) {
                         const int o = base + u * kConsumers + tid;
                         if (o < all && (o < lo || o >= lo + cols)) pend |= 1u << u;
                     }
                     while (pend) {
-                        unsigned long long w[8];
+                        unsigned long long w[kXW];
 #pragma unroll
-                        for (int u = 0; u < 8; u++)   // all loads out before any is used
-                            w[u] = (pend & (1u << u)) ? ld_volatile_u64(src + base + u * kConsumers + tid) : 0ull;
+                        for (int u = 0; u < kXW; u++)   // all loads out before any is used
+                            w[u] = (pend & (1u << u)) ? ld_volatile_u64(word_at(base + u * kConsumers + tid)) : 0ull;
 #pragma unroll
-                        for (int u = 0; u < 8; u++)
+                        for (int u = 0; u < kXW; u++)
                             if ((pend & (1u << u)) && (unsigned)(w[u] >> 32) == ep) {
                                 p.out[base + u * kConsumers + tid] = __uint_as_float((unsigned)w[u]);
                                 pend &= ~(1u << u);
@@ -869,11 +880,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     // mode first into the cluster leader's shared memory, and the leader adds
     // the ranks' rows in rank order (the head's output when its one cluster
     // covers it, else the cluster's rows go to the accumulator)
-    auto flush_out = [&](int sl) {
+    auto flush_out = [&](int sl, bool last) {
         if (named_sync_or(1, kConsumers, aborted)) {
             aborted = true;
             return;
         }
+        // after the last V tile every consumer has read its scores (the
+        // barrier above): the scratch is dead until the next launch rewrites
+        // it, so it leaves L2 without a write-back -- dropped here, so the
+        // drops complete while the output is added, not at the kernel's end
+        if (last && !s_local)
+            for (int ln = tid; ln < g.nt * (kTileScores / 32); ln += kConsumers) l2_discard(Scta + ln * 32);
         const int h = g.h0 + sl;
 #pragma unroll
         for (int dt = 0; dt < DT; dt++) {
@@ -989,7 +1006,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     };
 
     for (int i = 0; i < g.nt; i++) {
-        if (i == g.nt0 && i > 0) flush_out(0);
+        if (i == g.nt0 && i > 0) flush_out(0, false);
         if (aborted) continue;   // keep step with the other warps' barriers
         const int j = g.nt + i, s = j % NS;
         stage_s(i + kSD - 1);
@@ -1055,12 +1072,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
     }
     cp_async_wait<0>();
     KV_STAMP(tid == 0, 6);   // warp 0's V loop done
-    flush_out(two ? 1 : 0);
-    // every consumer has read its scores (flush_out opens with a barrier): the
-    // scratch is dead until the next launch rewrites it, so it leaves L2
-    // without a write-back
-    if (!s_local)
-        for (int ln = tid; ln < g.nt * (kTileScores / 32); ln += kConsumers) l2_discard(Scta + ln * 32);
+    flush_out(two ? 1 : 0, true);
     named_sync(2, kThreads);
     KV_STAMP(tid == 0, 12);   // exit
     if (clus) {

@@ -272,6 +272,7 @@ struct kv_ctx {
     uint64_t limit_ns = 1000000000ull;      // bound of every device-side wait (1 s)
     int inject = 0;                         // test hook, applies to the next decode launch
     bool coop = false;                      // attention kernels as cooperative launches
+    bool xpull = false;                     // KV_B200_XPULL=1: sharded decode collects by remote loads
     int max_clusters[kvb::kMaxClusterCtas + 1] = {};   // q-CTA clusters of the attention kernel held at once
     int force_q = 0;                        // KV_B200_CLUSTER: 0 policy, < 0 none, q > 1 that size
     int l2pf = -1;                          // KV_B200_L2PF: tiles prefetched to L2 at the long stage waits
@@ -880,6 +881,8 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
                              ctx->max_cta, ctx->sm_count, bps));
         const char *cv = getenv("KV_B200_COOPERATIVE");
         ctx->coop = cv && cv[0] == '1';
+        const char *xp = getenv("KV_B200_XPULL");
+        ctx->xpull = xp && xp[0] == '1';
         for (int q = 2; q <= kvb::kMaxClusterCtas; q++) {
             e = kvb::attn_cluster_occupancy(ctx->D, q, &ctx->max_clusters[q]);
             if (e != cudaSuccess) {   // no cluster mode on this device
@@ -1282,6 +1285,7 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
     const bool via_peers = sharded && ctx->peers && n_new == 1 && ctx->r <= kvb::attn_rows() &&
                            !(!fused && ctx->pf && n_new * ctx->r >= 32);
     ap.n_peers = via_peers ? c.n_shards : 0;
+    ap.xpull = ctx->xpull ? 1 : 0;
     ap.shard = c.shard;
     ap.rx_stride = ctx->rx_stride;
     ap.xticket = ctx->ctl + 2 * ctx->hkv_loc;

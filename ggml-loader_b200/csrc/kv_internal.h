@@ -109,6 +109,10 @@ struct AttnParams {
     // head) = epoch << 32 | float bits, so a word is valid once its tag shows
     // the launch; xticket counts this launch's converted local heads
     int32_t n_peers, shard;
+    // 0: push -- a head's words go into every peer's buffer, the collector
+    // polls its own; 1: pull -- a head's words stay in this shard's buffer,
+    // the collector polls each peer's buffer over NVLink (no remote stores)
+    int32_t xpull;
     unsigned long long *rx[kMaxShards];
     int64_t rx_stride;
     unsigned *xticket;
