@@ -1,11 +1,13 @@
-"""KV-head sharded path on two GPUs: one process per GPU, the library's own NCCL
-all-gather of the head outputs (decode in place; chunks through the gather
-buffer and the unshard kernel), checked against the unsharded oracle.
+"""KV-head sharded path on two, four and eight GPUs: one process per GPU,
+checked against the unsharded oracle.  Decode exchanges the head outputs
+inside the attention kernel over NVLink (every shard writes its heads into
+every peer's receive buffer); chunks use the library's NCCL all-gather into
+the gather buffer and the unshard kernel.
 
-Skipped unless two GPUs are visible.  Each rank fills only its shard of the
-cache (kv_fill_synthetic generates rows from the global head index) and reads
-only its heads out of the replicated input rows; both ranks must return the
-full [n_new][Hq*d] output.
+Each case is skipped unless enough GPUs are visible.  Each rank fills only its
+shard of the cache (kv_fill_synthetic generates rows from the global head
+index) and reads only its heads out of the replicated input rows; every rank
+must return the same full [n_new][Hq*d] output.
 """
 import os
 import sys
@@ -65,13 +67,9 @@ def _rank(rank, world, name, n_past, n_new, idq, outq):
         outq.put((rank, "error", repr(e)))
 
 
-@pytest.mark.gpu
-@pytest.mark.parametrize("name,n_past,n_new", [("llama3.1-8b-128k", 3000, 1), ("qwen3-8b-prefill", 2000, 40),
-                                               ("llama3.2-3b", 1500, 3)])
-def test_two_gpu_shards_match_oracle(name, n_past, n_new):
-    import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def _run_shards(world, name, n_past, n_new):
+    """Run `world` shards of one layer, one process per GPU; check every shard
+    returns the same bits and that they match the unsharded oracle."""
     import torch.multiprocessing as mp
     _paths()
     import kv_oracle as O
@@ -79,11 +77,11 @@ def test_two_gpu_shards_match_oracle(name, n_past, n_new):
     from test_gpu_path import _oracle_layer, _split, assert_close
     ctxm = mp.get_context("spawn")
     idq, outq = ctxm.Queue(), ctxm.Queue()
-    procs = [ctxm.Process(target=_rank, args=(r, 2, name, n_past, n_new, idq, outq)) for r in range(2)]
+    procs = [ctxm.Process(target=_rank, args=(r, world, name, n_past, n_new, idq, outq)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
-    for _ in range(2):
+    for _ in range(world):
         try:
             r, status, val = outq.get(timeout=300)
         except Exception:
@@ -93,7 +91,7 @@ def test_two_gpu_shards_match_oracle(name, n_past, n_new):
         p.join(timeout=60)
         if p.is_alive():
             p.kill()
-    assert len(res) == 2 and all(v[0] == "ok" for v in res.values()), res
+    assert len(res) == world and all(v[0] == "ok" for v in res.values()), res
     sp = specs.get(name)
     sp["n_layer"] = 1
     n_ctx = n_past + n_new + 64
@@ -104,5 +102,28 @@ def test_two_gpu_shards_match_oracle(name, n_past, n_new):
     orc = O.Oracle(sp)
     qr = orc.append(kc, vc, n_past, q, k, v, qn, kn)
     want = orc.attend(kc, vc, n_past, qr)
-    assert np.array_equal(res[0][1].view(np.uint32), res[1][1].view(np.uint32))
+    for r in range(1, world):
+        assert np.array_equal(res[0][1].view(np.uint32), res[r][1].view(np.uint32)), r
     assert_close(res[0][1], want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,n_past,n_new", [("llama3.1-8b-128k", 3000, 1), ("qwen3-8b-prefill", 2000, 40),
+                                               ("llama3.2-3b", 1500, 3)])
+def test_two_gpu_shards_match_oracle(name, n_past, n_new):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    _run_shards(2, name, n_past, n_new)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [4, 8])
+@pytest.mark.parametrize("name,n_past,n_new", [("llama3.1-8b-128k", 5000, 1), ("llama3.2-3b", 1500, 3)])
+def test_wider_shards_match_oracle(name, n_past, n_new, world):
+    """Four and eight shards (two and one KV heads each on these shapes): the
+    decode exchange reaches every peer, the chunk goes through NCCL."""
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
+    _run_shards(world, name, n_past, n_new)
