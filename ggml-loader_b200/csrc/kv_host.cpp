@@ -29,6 +29,10 @@
 
 namespace {
 
+// the fewest keys a decode CTA streams (two 128-key tiles): more CTAs than
+// that would spend more time in the statistics exchange than they save
+constexpr int kDecodeMinKeys = 256;
+
 // a fixed buffer: recording an error never allocates, so it also works while
 // reporting a failed host allocation
 thread_local char g_last_error[512];
@@ -275,6 +279,7 @@ struct kv_ctx {
     bool xpull = false;                     // KV_B200_XPULL=1: sharded decode collects by remote loads
     int max_clusters[kvb::kMaxClusterCtas + 1] = {};   // q-CTA clusters of the attention kernel held at once
     int force_q = 0;                        // KV_B200_CLUSTER: 0 policy, < 0 none, q > 1 that size
+    int min_keys = kDecodeMinKeys;          // KV_B200_MIN_KEYS: fewest keys a decode CTA streams
     int l2pf = -1;                          // KV_B200_L2PF: tiles prefetched to L2 at the long stage waits
                                             // (-1: the default rule of l2pf_default)
 
@@ -416,10 +421,11 @@ int launch(kv_ctx *ctx, int kernel_id, cudaStream_t st, const char *what, F &&fn
 // the statistics exchange and the output combine have fewer parties
 // (qwen2-0.5B at 2k keys: 12.5 -> 11.6 us a layer; 512 or more rows a CTA is
 // slower).
-int decode_ctas_for(int sm_count, int hkv_loc, int64_t n_kv)
+int decode_ctas_for(int sm_count, int hkv_loc, int64_t n_kv, int min_keys = kDecodeMinKeys)
 {
     const int64_t T = (int64_t)hkv_loc * n_kv;
-    int64_t c = std::min<int64_t>(std::min(sm_count, kvb::attn_max_ctas()), (T + 255) / 256);
+    const int64_t mk = std::max(128, min_keys);
+    int64_t c = std::min<int64_t>(std::min(sm_count, kvb::attn_max_ctas()), (T + mk - 1) / mk);
     // a multiple of the heads when that idles at most 5 % of the CTAs: every CTA
     // then covers one head, one statistics poll and one output flush instead
     // of two for the CTAs that straddle heads (8 heads: 144 of 148 SMs;
@@ -458,9 +464,10 @@ struct DecodeShape {
     int n_cta, cq, ncl;
 };
 
-DecodeShape decode_shape_for(int sm_count, int hkv_loc, int64_t n_kv, const int *max_clusters, int force_q)
+DecodeShape decode_shape_for(int sm_count, int hkv_loc, int64_t n_kv, const int *max_clusters, int force_q,
+                             int min_keys = kDecodeMinKeys)
 {
-    const int c0 = decode_ctas_for(sm_count, hkv_loc, n_kv);
+    const int c0 = decode_ctas_for(sm_count, hkv_loc, n_kv, min_keys);
     DecodeShape none{c0, 1, 1};
     if (!max_clusters || force_q < 0) return none;
     auto fits = [&](int q, int ncl) { return q <= kvb::kMaxClusterCtas && max_clusters[q] >= hkv_loc * ncl; };
@@ -474,11 +481,6 @@ DecodeShape decode_shape_for(int sm_count, int hkv_loc, int64_t n_kv, const int 
     const int qa = (int)std::min<int64_t>({(int64_t)kvb::kMaxClusterCtas, sm_count / hkv_loc, per_head_keys});
     if (qa >= 2 && (int64_t)hkv_loc * qa * 100 >= (int64_t)c0 * 85 && fits(qa, 1)) return DecodeShape{hkv_loc * qa, qa, 1};
     return none;
-}
-
-int decode_ctas(const kv_ctx *ctx, int64_t n_kv)
-{
-    return decode_ctas_for(ctx->sm_count, ctx->hkv_loc, n_kv);
 }
 
 // The decode kernel's L2 prefetch (AttnParams::l2pf) by the tiles a CTA
@@ -890,6 +892,8 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
                 ctx->max_clusters[q] = 0;
             }
         }
+        const char *mk = getenv("KV_B200_MIN_KEYS");
+        if (mk && *mk) ctx->min_keys = std::max(128, std::min(1 << 20, atoi(mk)));
         const char *cl = getenv("KV_B200_CLUSTER");
         if (cl && *cl) ctx->force_q = atoi(cl) <= 1 ? -1 : atoi(cl);
         const char *pf = getenv("KV_B200_L2PF");
@@ -1238,7 +1242,8 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
         // clusters need the CTAs resident together with the cooperative
         // launch's guarantee off: the cooperative attribute keeps the plain grid
         const DecodeShape ds = decode_shape_for(ctx->sm_count, ctx->hkv_loc, n_kv,
-                                                ctx->coop ? nullptr : ctx->max_clusters, ctx->force_q);
+                                                ctx->coop ? nullptr : ctx->max_clusters, ctx->force_q,
+                                                ctx->min_keys);
         ap.n_cta = ds.n_cta;
         ap.cq = ds.cq;
         ap.ncl = ds.ncl;
