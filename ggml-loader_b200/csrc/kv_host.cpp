@@ -280,6 +280,7 @@ struct kv_ctx {
     int max_clusters[kvb::kMaxClusterCtas + 1] = {};   // q-CTA clusters of the attention kernel held at once
     int force_q = 0;                        // KV_B200_CLUSTER: 0 policy, < 0 none, q > 1 that size
     int min_keys = kDecodeMinKeys;          // KV_B200_MIN_KEYS: fewest keys a decode CTA streams
+    int dec_sms = 0;                        // SMs the decode split uses (KV_B200_DECODE_SMS, <= sm_count)
     int l2pf = -1;                          // KV_B200_L2PF: tiles prefetched to L2 at the long stage waits
                                             // (-1: the default rule of l2pf_default)
 
@@ -892,6 +893,9 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
                 ctx->max_clusters[q] = 0;
             }
         }
+        ctx->dec_sms = ctx->sm_count;
+        const char *ds = getenv("KV_B200_DECODE_SMS");
+        if (ds && *ds) ctx->dec_sms = std::max(1, std::min(ctx->sm_count, atoi(ds)));
         const char *mk = getenv("KV_B200_MIN_KEYS");
         if (mk && *mk) ctx->min_keys = std::max(128, std::min(1 << 20, atoi(mk)));
         const char *cl = getenv("KV_B200_CLUSTER");
@@ -1241,7 +1245,7 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
     {
         // clusters need the CTAs resident together with the cooperative
         // launch's guarantee off: the cooperative attribute keeps the plain grid
-        const DecodeShape ds = decode_shape_for(ctx->sm_count, ctx->hkv_loc, n_kv,
+        const DecodeShape ds = decode_shape_for(ctx->dec_sms, ctx->hkv_loc, n_kv,
                                                 ctx->coop ? nullptr : ctx->max_clusters, ctx->force_q,
                                                 ctx->min_keys);
         ap.n_cta = ds.n_cta;
