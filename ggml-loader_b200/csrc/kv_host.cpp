@@ -276,7 +276,7 @@ struct kv_ctx {
     uint64_t limit_ns = 1000000000ull;      // bound of every device-side wait (1 s)
     int inject = 0;                         // test hook, applies to the next decode launch
     bool coop = false;                      // attention kernels as cooperative launches
-    bool xpull = false;                     // KV_B200_XPULL=1: sharded decode collects by remote loads
+    bool xpull = false;                     // sharded decode collects the peers' heads by remote loads
     int max_clusters[kvb::kMaxClusterCtas + 1] = {};   // q-CTA clusters of the attention kernel held at once
     int force_q = 0;                        // KV_B200_CLUSTER: 0 policy, < 0 none, q > 1 that size
     int min_keys = kDecodeMinKeys;          // KV_B200_MIN_KEYS: fewest keys a decode CTA streams
@@ -656,9 +656,13 @@ int map_peers(kv_ctx *ctx)
     }
     ctx->peers = true;
     for (int g = 0; g < G; g++) ctx->peers = ctx->peers && flags[g] == 1;
-    // KV_B200_EXCHANGE=nccl keeps the NCCL all-gather for decode as well
+    // KV_B200_EXCHANGE: "push" (every shard stores its heads into every
+    // peer's buffer), "pull" (the collector loads them from the peers'
+    // buffers), "nccl" (the NCCL all-gather after the kernel, for decode too)
     const char *env = getenv("KV_B200_EXCHANGE");
     if (env && strcmp(env, "nccl") == 0) ctx->peers = false;
+    if (env && strcmp(env, "pull") == 0) ctx->xpull = true;
+    if (env && strcmp(env, "push") == 0) ctx->xpull = false;
     return KV_OK;
 }
 
@@ -884,8 +888,6 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
                              ctx->max_cta, ctx->sm_count, bps));
         const char *cv = getenv("KV_B200_COOPERATIVE");
         ctx->coop = cv && cv[0] == '1';
-        const char *xp = getenv("KV_B200_XPULL");
-        ctx->xpull = xp && xp[0] == '1';
         for (int q = 2; q <= kvb::kMaxClusterCtas; q++) {
             e = kvb::attn_cluster_occupancy(ctx->D, q, &ctx->max_clusters[q]);
             if (e != cudaSuccess) {   // no cluster mode on this device
