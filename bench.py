@@ -13,8 +13,10 @@ positions n_past, n_past+1, ... (cycling over the configuration's step count).
 n_kv*Hkv*d*2*2 (read K and V) + Hkv*d*2*2 (append) + Hkv*d*4*2 (read k, v) +
 Hq*d*4*2 (read q, write o), summed over layers and steps, divided by the max
 over ranks of the device-timed region.  Inputs are synthetic (seeded
-generator) with the configuration's shapes; the cache (GiBs) exceeds L2 every
-step, so no flush is needed.
+generator) with the configuration's shapes.  Where a step's cache reads exceed
+twice the L2 (GiBs on the 3B/8B/phi3 caches) the steps run back to back in
+one timed span; where they fit (qwen2-0.5B, 25 MB) each step is timed alone,
+with a write of four times L2's size between the spans.
 
 Default workload: llama-3.2-3B shape, 32k context (the single-GPU decode
 configuration); `--config llama3.1-8b-128k` runs the 128k configuration.
@@ -37,6 +39,7 @@ METRIC = "decode KV-append+attention µs/token and HBM GB/s (% of roofline) at 1
 METRIC_PREFILL = "chunked-prefill KV-append+attention TFLOP/s (% of tensor roofline) on B200"
 DEFAULT_CONFIG = "llama3.2-3b"
 NOMINAL_HBM_GBS = 8000.0
+L2_BYTES = 126 * 2 ** 20      # B200 L2
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
@@ -397,6 +400,12 @@ def run_ours(args, sp):
     sampler = ClockSampler(smi_index)
     if rank == 0:
         sampler.start()
+    # a step whose cache reads fit in L2 (qwen2-0.5B: 25 MB) would find them
+    # there on the next step: such steps are timed one by one, with a write of
+    # a buffer four times L2's size between them, outside the timed spans
+    per_gpu_bytes = statistics.mean(step_bytes(sp, sp["n_past"] + i, n_new) for i in range(cyc)) / world
+    flush = per_gpu_bytes < 2 * L2_BYTES
+    scrub = torch.empty(4 * L2_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
     lead = args.lead   # untimed steps on every rank while the sampler starts
     for s in range(args.warmup, args.warmup + lead):
         step(s)
@@ -406,16 +415,27 @@ def run_ours(args, sp):
     launches0 = ctx.launch_count()
     barrier()
     sampler.mark("start")
-    e0.record(stream)
     h0 = time.perf_counter()
-    for i in range(args.steps):
-        step(first + i)
-    host_ms = (time.perf_counter() - h0) * 1e3   # host submission time of the timed steps
-    e1.record(stream)
-    e1.synchronize()
+    if flush:
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for i in range(args.steps):
+            scrub.fill_(float(i))
+            ev[i][0].record(stream)
+            step(first + i)
+            ev[i][1].record(stream)
+        host_ms = (time.perf_counter() - h0) * 1e3
+        ev[-1][1].synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in ev)
+    else:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(first + i)
+        host_ms = (time.perf_counter() - h0) * 1e3   # host submission time of the timed steps
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
     sampler.mark("end")
     launches = ctx.launch_count() - launches0
-    ms = e0.elapsed_time(e1)
     barrier()
     if rank == 0:
         sampler.stop()
@@ -497,16 +517,26 @@ def run_ours(args, sp):
         efirst = pfirst + prof_steps
         barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2e_ms = 0.0
         f0.record(stream)
         for i in range(e2e_steps):
             s = efirst + i
+            if flush:   # (the flush between the steps' timed spans, as above)
+                scrub.fill_(float(i))
+                f0.record(stream)
             staging.copy_(host_in[s % cyc], non_blocking=True)
             step(s, src=staging)
             host_out.copy_(out, non_blocking=True)
+            if flush:
+                f1.record(stream)
             stream.synchronize()
-        f1.record(stream)
-        f1.synchronize()
-        e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+            if flush:
+                e2e_ms += f0.elapsed_time(f1)
+        if not flush:
+            f1.record(stream)
+            f1.synchronize()
+            e2e_ms = f0.elapsed_time(f1)
+        e2e_ms = max_over_ranks(e2e_ms)
         epos = positions(sp, efirst, e2e_steps)
         e2e_value = sum(step_bytes(sp, p, n_new) for p in epos) / (e2e_ms / 1e3) / 1e9
         if prefill:
@@ -550,8 +580,11 @@ def run_ours(args, sp):
                        "branch": "flash-attn (use_flash_attn)" if args.flash else "default (soft_max_ext + mul_mat)",
                        "parallelism": ("kv-head shards x%d + per-layer all-gather" % world) if world > 1
                        else "single GPU",
-                       "l2": "no flush: each step reads %.2f GB of cache (> 126 MB L2)" % (
-                           statistics.mean(step_bytes(sp, p, n_new) for p in pos) / 1e9)},
+                       "l2": ("flushed: each step reads %.1f MB of cache a GPU (< 2 x 126 MB L2), so the "
+                              "steps are timed one by one with a %d MB write between them" % (
+                                  per_gpu_bytes / 1e6, 4 * L2_BYTES // 10 ** 6)) if flush else
+                             ("no flush: each step reads %.2f GB of cache a GPU (> 2 x 126 MB L2)" % (
+                                 per_gpu_bytes / 1e9))},
             "roofline": {"bound": "tensor" if prefill else "hbm", "kernel": "kv_" + dom,
                          "achieved": round(achieved, 1) if achieved else None,
                          "peak": peak, "unit": "TFLOP/s" if prefill else "GB/s",
