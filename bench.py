@@ -457,7 +457,7 @@ def run_ours(args, sp):
         step(pfirst + i)
     torch.cuda.synchronize()
     kern = {}
-    for name in ("append", "attn", "prefill", "pfold", "gather"):
+    for name in ("append", "attn", "prefill", "prefill2", "pfold", "gather"):
         n, tms = ctx.profile_read(name)
         kern[name] = (n, tms)
     ctx.profile(False)
@@ -493,7 +493,8 @@ def run_ours(args, sp):
     if prefill:
         # the tensor-core kernel carries the layer's algorithmic FLOPs (one
         # launch per layer; the fold is timed apart)
-        dom = "prefill"
+        # (the chunk kernel on CTA pairs at head_dim 128, else the one-CTA kernel)
+        dom = "prefill2" if kern["prefill2"][0] else "prefill"
         peak, peak_kind = measured_peak("bf16_tflops")
         lf = statistics.mean(layer_flops(sp, p, n_new, world) for p in ppos)
         dom_us = in_region_us(dom)

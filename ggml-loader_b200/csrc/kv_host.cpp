@@ -297,6 +297,10 @@ struct kv_ctx {
     bool pf = false;
     int pf_D = 0;                           // the chunk kernel's head_dim (128 for a 96-wide head)
     std::vector<CUtensorMap> pf_kmaps, pf_vmaps;   // head_dim 96: 64-wide boxes, columns 96-127 zero-filled
+    // the CTA-pair chunk kernel (head_dim 128): each layer's K with 32-key
+    // boxes; empty when the device cannot run its clusters (or
+    // KV_B200_PREFILL_PAIR=0)
+    std::vector<CUtensorMap> pf2_kmaps;
     int pf_tb = 0;                          // tokens per 128-row query tile
     CUtensorMap qmap{};                     // qbuf [n_batch_max][hq_loc][D], box 64 x r x tb
     float *pf_stat = nullptr;               // [sm_count][kseg][2 tiles][128][2]
@@ -973,6 +977,26 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
                 if (rc2 != KV_OK) return bail(rc2);
             }
         }
+        if (pfD == 128 && ctx->D == 128) {
+            const char *pe = getenv("KV_B200_PREFILL_PAIR");
+            int clusters = 0;
+            e = (pe && pe[0] == '0') ? cudaSuccess : kvb::prefill_pair_prepare(&clusters);
+            if (e != cudaSuccess) {   // no pair kernel on this device: the one-CTA kernel runs
+                cudaGetLastError();
+                clusters = 0;
+            }
+            if (clusters > 0) {
+                ctx->pf2_kmaps.resize(c.n_layer);
+                const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)ctx->hkv_loc, (cuuint64_t)ctx->rows};
+                const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)ctx->hkv_loc * D * 2};
+                const cuuint32_t box[3] = {64, 1, 32};
+                for (int l = 0; l < c.n_layer; l++) {
+                    const int rc2 = encode_map(&ctx->pf2_kmaps[l], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ctx->k_layer(l),
+                                               dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+                    if (rc2 != KV_OK) return bail(rc2);
+                }
+            }
+        }
         ctx->pf = true;
     }
 
@@ -1111,7 +1135,9 @@ constexpr int64_t kOnePassKeys = 32768;
 // (kv_prefill.cu).  A pair is (KV head,
 // block of two 128-row query tiles); the pairs' key tiles, laid end to end, are
 // cut into C equal ranges; C is the SM count, lowered until no range holds more
-// than prefill_max_segments() pairs.
+// than prefill_max_segments() pairs.  The one pass at head_dim 128 runs on CTA
+// pairs (2-CTA clusters, tcgen05 cta_group::2): a block holds four tiles and a
+// range goes to a CTA pair, C at most half the SM count.
 // the caller's mask of kv_attend_mask (ptr nullptr: the implicit causal mask)
 struct MaskArg {
     const void *ptr = nullptr;
@@ -1120,10 +1146,15 @@ struct MaskArg {
     bool flash = false;
 };
 
-int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n_past, int32_t n_new, float *dst,
-            int64_t dst_stride, int dst_head0, const MaskArg &mk, cudaStream_t st)
+int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, const CUtensorMap *km32, int64_t n_past,
+            int32_t n_new, float *dst, int64_t dst_stride, int dst_head0, const MaskArg &mk, cudaStream_t st)
 {
     kvb::PrefillParams pp{};
+    // the exact two passes reproduce the default branch's rounding at long
+    // contexts; the flash-attn branch is one online softmax at any length
+    pp.mode = !mk.flash && n_past + n_new > kOnePassKeys ? 2 : 0;
+    // the one pass runs on CTA pairs where the layer has that kernel's K map
+    const bool cta2 = km32 && pp.mode == 0;
     pp.hkv = ctx->hkv_loc;
     pp.r = ctx->r;
     pp.hq_loc = ctx->hq_loc;
@@ -1131,7 +1162,7 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     pp.n_past = n_past;
     pp.n_new = n_new;
     pp.tb = ctx->pf_tb;
-    pp.nt = kvb::prefill_tiles(ctx->pf_D);
+    pp.nt = cta2 ? 4 : kvb::prefill_tiles(ctx->pf_D);
     pp.dv = ctx->D;
     pp.nblk = (n_new + pp.nt * pp.tb - 1) / (pp.nt * pp.tb);
     std::vector<int64_t> nt(pp.nblk);
@@ -1146,7 +1177,8 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     // the pairs' starts, to count the segments of each range
     std::vector<int64_t> start((size_t)pp.hkv * pp.nblk + 1, 0);
     for (int pr = 0; pr < pp.hkv * pp.nblk; pr++) start[pr + 1] = start[pr] + nt[pr % pp.nblk];
-    int C = (int)std::min<int64_t>(ctx->sm_count, W);
+    // work ranges: one a CTA, or one a CTA pair
+    int C = (int)std::min<int64_t>(cta2 ? ctx->sm_count / 2 : ctx->sm_count, W);
     for (;; C = std::max(1, C * 3 / 4)) {
         int worst = 0;
         for (int cc = 0; cc < C; cc++) {
@@ -1160,9 +1192,6 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     pp.n_cta = C;
     pp.kseg = kseg;
     pp.scale = ctx->scale;
-    // the exact two passes reproduce the default branch's rounding at long
-    // contexts; the flash-attn branch is one online softmax at any length
-    pp.mode = !mk.flash && n_past + n_new > kOnePassKeys ? 2 : 0;
     pp.mask = mk.ptr;
     pp.mask_stride = mk.stride;
     pp.mask_f16 = mk.f16 ? 1 : 0;
@@ -1184,8 +1213,11 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, int64_t n
     const int nseq = pp.mode ? 4 : 2;
     for (int n = 0; n < nseq; n++) {
         const int which = seq[n];
-        const int rc = launch(ctx, (which == 1 || which == 3) ? KV_K_PFOLD : KV_K_PREFILL, st, what[which],
-                              [&] { return kvb::launch_prefill(ctx->pf_D, which, ctx->qmap, km, vm, pp, st); });
+        const int kid = (which == 1 || which == 3) ? KV_K_PFOLD : (which == 0 && cta2) ? KV_K_PREFILL2 : KV_K_PREFILL;
+        const int rc = launch(ctx, kid, st, what[which], [&] {
+            return which == 0 && cta2 ? kvb::launch_prefill_pair(ctx->qmap, *km32, vm, pp, st)
+                                      : kvb::launch_prefill(ctx->pf_D, which, ctx->qmap, km, vm, pp, st);
+        });
         if (rc) return rc;
     }
     return KV_OK;
@@ -1319,8 +1351,9 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
     const CUtensorMap &km = ctx->kmaps[layer], &vm = ctx->vmaps[layer];
     if (!fused && ctx->pf && rows >= 32) {
         const bool padded = !ctx->pf_kmaps.empty();   // head_dim 96 on the 128 kernel
-        rc = prefill(ctx, padded ? ctx->pf_kmaps[layer] : km, padded ? ctx->pf_vmaps[layer] : vm, kpast, n_new, dst,
-                     dst_stride, dst_head0, mk, st);
+        rc = prefill(ctx, padded ? ctx->pf_kmaps[layer] : km, padded ? ctx->pf_vmaps[layer] : vm,
+                     ctx->pf2_kmaps.empty() ? nullptr : &ctx->pf2_kmaps[layer], kpast, n_new, dst, dst_stride,
+                     dst_head0, mk, st);
         if (rc) return rc;
     }
     for (int row0 = 0; row0 < rows && !(!fused && ctx->pf && rows >= 32); row0 += rows_per) {
@@ -1576,7 +1609,8 @@ int kv_profile_read(kv_ctx *ctx, int32_t kernel, int64_t *launches, double *tota
 
 const char *kv_kernel_name(int32_t kernel)
 {
-    static const char *names[KV_K_COUNT] = {"kv_append", "kv_attn", "kv_prefill", "kv_prefill_fold", "kv_unshard"};
+    static const char *names[KV_K_COUNT] = {"kv_append", "kv_attn", "kv_prefill", "kv_prefill_fold", "kv_unshard",
+                                            "kv_prefill_pair"};
     return (kernel >= 0 && kernel < KV_K_COUNT) ? names[kernel] : "?";
 }
 

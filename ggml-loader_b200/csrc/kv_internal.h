@@ -160,15 +160,15 @@ struct PrefillParams {
     int64_t n_past;
     int32_t n_new;
     int32_t tb;        // tokens per 128-row query tile (tb * r <= 128)
-    int32_t nt;        // query tiles a CTA holds (prefill_tiles: 2, or 1 at head_dim 256)
+    int32_t nt;        // query tiles a CTA holds (prefill_tiles: 2, or 1 at head_dim 256; 4 a CTA pair)
     int32_t dv;        // the heads' real width in the output rows (the kernel's D, or 96 run as 128)
     int32_t nblk;      // blocks of nt query tiles: ceil(n_new / (nt tb)); pair = kv head * nblk + block
     int64_t s_all;     // key tiles of one KV head summed over its blocks
     int32_t n_cta, kseg;
     float scale;
     int32_t mode;      // 0 one pass (online softmax), 2 the exact two passes (long contexts)
-    float *pstat;      // [n_cta][kseg][2 tiles][128] (m, l) per segment and row
-    float *pout;       // [n_cta][kseg][2 tiles][128][D] partial outputs of split pairs
+    float *pstat;      // [n_cta][kseg][nt tiles][128] (m, l) per segment and row
+    float *pout;       // [n_cta][kseg][nt tiles][128][D] partial outputs of split pairs
     float2 *rstat;     // [hkv * nblk][256] (M, 1/Z) per pair and row (exact passes)
     float *out;        // row t at out + t*out_stride, head h at (out_head0 + h)*D
     int64_t out_stride;
@@ -191,6 +191,13 @@ cudaError_t prefill_prepare(int D);
 // the exact two passes: 2 statistics kernel, 3 statistics fold, 4 output kernel
 cudaError_t launch_prefill(int D, int which, const CUtensorMap &qmap, const CUtensorMap &kmap,
                            const CUtensorMap &vmap, const PrefillParams &p, cudaStream_t st);
+// The CTA-pair (tcgen05 cta_group::2) form of the one-pass kernel at head_dim
+// 128: p.nt = 4 query tiles a 2-CTA cluster, p.n_cta clusters (2 * n_cta
+// CTAs); kmap32 is the layer's K map with 32-key boxes.  prepare returns the
+// number of its clusters the device holds at once (0: not available).
+cudaError_t prefill_pair_prepare(int *clusters);
+cudaError_t launch_prefill_pair(const CUtensorMap &qmap, const CUtensorMap &kmap32, const CUtensorMap &vmap,
+                                const PrefillParams &p, cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // gather / layout helpers

@@ -613,7 +613,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
                 if (lane == 0) mbar_arrive(&p_full[grp * 2 + bf]);
             }
             const bool whole = sg.t0 == 0 && sg.t1 == nt_of(p, b);   // no other CTA holds this pair
-            const int64_t slot = (((int64_t)c * p.kseg + k) * 2 + grp) * 128 + row;
+            const int64_t slot = (((int64_t)c * p.kseg + k) * p.nt + grp) * 128 + row;
             if constexpr (MODE == kStats) {
                 // (max in scaled units, sum) of every segment, split or not
                 reinterpret_cast<float2 *>(p.pstat)[slot] =
@@ -679,6 +679,377 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------------------
+// the CTA-pair form (tcgen05 cta_group::2) of the one-pass kernel, head_dim 128
+// ---------------------------------------------------------------------------
+// A 2-CTA cluster holds four query tiles of one KV head (a block of 4 tb
+// tokens): the even CTA tiles 0 and 1 (A, B), the odd CTA tiles 2 and 3.  The
+// even CTA's three MMA-issuing warps drive both SMs' tensor cores with M = 256
+// instructions -- rows 0-127 from the even CTA's tile, 128-255 from the odd
+// CTA's -- so one instruction does what two did in prefill_kernel, whose
+// sub-tile rate the MMA issue bounds.  Each CTA stages half of every K and V
+// tile: K's keys 32*rank .. +31 of both 64-key sub-tiles (B's N = 64 keys split
+// 32/32), V's dims 64*rank .. +63 (N = 128 split 64/64).  Both CTAs' TMA loads
+// complete on the even CTA's full barriers; the issuers' commits arrive on
+// both CTAs' barriers (empty slots, S ready, P . V done); both CTAs' softmax
+// warps report P and the free O on the even CTA's barriers.  Each CTA's
+// softmax and epilogue handle its own 256 rows, as in prefill_kernel.
+struct PL2 {
+    static constexpr int NT = 2;                          // query tiles a CTA holds (4 a pair)
+    static constexpr int KS = 6, VS = 4;                  // half-tile rings
+    static constexpr uint32_t kQTile = 2 * kBox;          // 128 rows x 128 halves
+    static constexpr uint32_t kKBox = 32 * 128;           // [32 keys][64 halves]
+    static constexpr uint32_t kKHalf = 4 * kKBox;         // [2 sub-tiles][2 dim boxes][32 keys][64 halves]
+    static constexpr uint32_t kVHalf = kBox;              // [128 keys][this CTA's 64 dims]
+    static constexpr size_t o_q = 0;
+    static constexpr size_t o_k = o_q + NT * (size_t)kQTile;
+    static constexpr size_t o_v = o_k + (size_t)KS * kKHalf;
+    static constexpr size_t o_bar = o_v + (size_t)VS * kVHalf;
+    // as PL: q_full, q_empty, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
+    // s_full[2][2], p_full[2][2], o_ready[2][2], o_full, o_empty, drain[3]
+    static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 12 + 5;
+    static constexpr size_t o_tm = o_bar + (size_t)NBAR * 8;
+    static constexpr size_t o_flags = o_tm + 16;
+    static constexpr size_t bytes = o_flags + 16;
+    static_assert(bytes <= 227 * 1024, "shared memory of the pair kernel");
+    static_assert(o_k % 1024 == 0 && o_v % 1024 == 0 && kKBox % 1024 == 0, "swizzled boxes 1024-byte aligned");
+};
+
+template <bool MASKED>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
+    prefill2_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap32,
+                    const __grid_constant__ CUtensorMap vmap, const PrefillParams p)
+{
+    constexpr int D = 128;
+    using L = PL2;
+    constexpr int KS = L::KS, VS = L::VS, NT = L::NT;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::o_bar);
+    uint64_t *q_full = bar, *q_empty = bar + 1;
+    uint64_t *k_full = bar + 2, *k_empty = k_full + KS;
+    uint64_t *v_full = k_empty + KS, *v_empty = v_full + VS;
+    uint64_t *s_full = v_empty + VS;
+    uint64_t *p_full = s_full + 4;
+    uint64_t *o_ready = p_full + 4;
+    uint64_t *o_full = o_ready + 4, *o_empty = o_full + 1;
+    uint64_t *drain = o_empty + 1;
+    uint32_t *tm_slot = reinterpret_cast<uint32_t *>(smem + L::o_tm);
+    volatile int *flags = reinterpret_cast<volatile int *>(smem + L::o_flags);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rank = (int)cluster_rank(), c = blockIdx.x >> 1;   // c: the pair's work range
+    // the even CTA's barrier at the offset of `b` (shared::cluster address)
+    auto lead = [&](uint64_t *b) { return mapa(smem_addr(b), 0); };
+    int issued_q = 0, issued_k = 0, issued_v = 0;
+
+    if (tid == 0) {
+        for (int i = 0; i < L::NBAR; i++) {
+            // the even CTA's full barriers count its own expect_tx arrival; its
+            // p_full the softmax warps of a tile group of both CTAs, its o_empty
+            // every epilogue warp of both; k_empty and q_empty get the commits of
+            // both S issuers
+            const uint64_t *bi = &bar[i];
+            const bool two = bi == q_empty || (bi >= k_empty && bi < k_empty + KS);
+            mbar_init(&bar[i], (bi >= p_full && bi < p_full + 4) ? 2 * kGW : bi == o_empty ? 2 * NT * kGW : two ? 2 : 1);
+        }
+        flags[0] = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc2(tm_slot, 512);
+        tmem_relinquish2();
+    }
+    tc_fence_before();
+    __syncthreads();
+    // neither CTA signals the other's barriers before both are initialised
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem = *tm_slot;
+    pdl_launch_dependents();
+
+    if (warp == 0) {
+        // ================= TMA (both CTAs: this CTA's halves) =================
+        if (lane == 0) {
+            prefetch_tmap(&qmap);
+            prefetch_tmap(&kmap32);
+            prefetch_tmap(&vmap);
+            const uint32_t qbytes = (uint32_t)(p.r * p.tb) * 128u * 2u;   // one Q tile (zero fill counts)
+            for_segments(p, c, [&](int k, const Seg &sg) {
+                const int kvh = sg.pair / p.nblk, b = sg.pair % p.nblk;
+                if (k > 0 && !mbar_wait_ab(q_empty, (k - 1) & 1, p.limit_ns, flags)) {
+                    give_up(p, flags, 2u);
+                    return false;
+                }
+                if (rank == 0) mbar_arrive_expect_tx(q_full, 2 * NT * qbytes);
+#pragma unroll
+                for (int g = 0; g < NT; g++)
+#pragma unroll
+                    for (int bx = 0; bx < 2; bx++)
+                        tma_load_3d_pair(smem + L::o_q + g * L::kQTile + bx * kBox, &qmap, lead(q_full), bx * 64,
+                                         kvh * p.r, (4 * b + 2 * rank + g) * p.tb);
+                issued_q++;
+                for (int t = sg.t0; t < sg.t1; t++) {
+                    const int s = issued_k % KS;
+                    if (issued_k >= KS && !mbar_wait_ab(&k_empty[s], ((issued_k / KS) - 1) & 1, p.limit_ns, flags)) {
+                        give_up(p, flags, 2u);
+                        return false;
+                    }
+                    if (rank == 0) mbar_arrive_expect_tx(&k_full[s], 2 * L::kKHalf);
+#pragma unroll
+                    for (int sub = 0; sub < 2; sub++)
+#pragma unroll
+                        for (int bx = 0; bx < 2; bx++)
+                            tma_load_3d_pair(smem + L::o_k + s * L::kKHalf + (2 * sub + bx) * L::kKBox, &kmap32,
+                                             lead(&k_full[s]), bx * 64, kvh, t * 128 + sub * 64 + rank * 32);
+                    issued_k++;
+                    const int sv = issued_v % VS;
+                    if (issued_v >= VS && !mbar_wait_ab(&v_empty[sv], ((issued_v / VS) - 1) & 1, p.limit_ns, flags)) {
+                        give_up(p, flags, 2u);
+                        return false;
+                    }
+                    if (rank == 0) mbar_arrive_expect_tx(&v_full[sv], 2 * L::kVHalf);
+                    tma_load_3d_pair(smem + L::o_v + sv * L::kVHalf, &vmap, lead(&v_full[sv]), rank * 64, kvh,
+                                     t * 128);
+                    issued_v++;
+                }
+                return true;
+            });
+        }
+    } else if (warp == 1 || warp >= 2 + 2 * kGW) {
+        // ================= MMA issue (even CTA) =================
+        const int role = warp == 1 ? 0 : warp - (1 + 2 * kGW);   // 0: S_A, 1: S_B, 2: PV
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idS = idesc_f16_f32(256, 64, false);
+            constexpr uint32_t idO = idesc_f16_f32(256, D, true);
+            const uint32_t sq = smem_addr(smem + L::o_q), sk = smem_addr(smem + L::o_k);
+            const uint32_t sv = smem_addr(smem + L::o_v);
+            bool ok = true;
+            auto wt = [&](uint64_t *b, uint32_t par) {   // a barrier only this CTA's agents signal
+                if (ok && !mbar_wait_ab(b, par, p.limit_ns, flags)) {
+                    give_up(p, flags, 1u);
+                    ok = false;
+                }
+                return ok;
+            };
+            auto wt_cl = [&](uint64_t *b, uint32_t par) {   // one the odd CTA's threads arrive on too
+                if (ok && !mbar_wait_cluster_ab(b, par, p.limit_ns, flags)) {
+                    give_up(p, flags, 1u);
+                    ok = false;
+                }
+                return ok;
+            };
+            int i = 0;
+            if (role < NT) {
+                const int g = role;
+                for_segments(p, c, [&](int k, const Seg &sg) {
+                    const int i1 = i + 2 * (sg.t1 - sg.t0);
+                    if (!wt(q_full, k & 1)) return false;
+                    for (; i < i1; i++) {
+                        const int tile = i >> 1;
+                        if (!(i & 1) && !wt(&k_full[tile % KS], (tile / KS) & 1)) return false;
+                        if (i >= 2 && !wt(&o_ready[g * 2 + (i & 1)], ((i - 2) >> 1) & 1)) return false;
+                        tc_fence_after();
+                        // S_g(i) (both CTAs' rows) = Q_g . K(sub-tile i&1: 32 keys in each CTA)^T
+                        const uint32_t kt = sk + (tile % KS) * L::kKHalf + (i & 1) * 2 * L::kKBox;
+#pragma unroll
+                        for (int kk = 0; kk < D / 16; kk++) {
+                            umma_ss2(tmem + g * 128 + (i & 1) * 64,
+                                     sdesc_k_sw128(sq + g * L::kQTile + (kk >> 2) * kBox + (kk & 3) * 32),
+                                     sdesc_k_sw128(kt + (kk >> 2) * L::kKBox + (kk & 3) * 32), idS, kk > 0);
+                        }
+                        umma_commit2_mc(&s_full[g * 2 + (i & 1)], 3);
+                        if (i & 1) umma_commit2_mc(&k_empty[tile % KS], 3);
+                        if (i == i1 - 1) umma_commit2_mc(q_empty, 3);
+                    }
+                    return true;
+                });
+            } else if (role == 2) {
+                for_segments(p, c, [&](int k, const Seg &sg) {
+                    const int i0 = i, i1 = i + 2 * (sg.t1 - sg.t0);
+                    for (; i < i1; i++) {
+                        const int tile = i >> 1;
+#pragma unroll
+                        for (int g = 0; g < NT; g++) {
+                            if (!wt_cl(&p_full[g * 2 + (i & 1)], (i >> 1) & 1)) return false;
+                            if (g == 0 && !(i & 1) && !wt(&v_full[tile % VS], (tile / VS) & 1)) return false;
+                            if (g == 0 && i == i0 && k > 0 && !wt_cl(o_empty, (k - 1) & 1)) return false;
+                            tc_fence_after();
+                            // O_g (+)= P_g(i) . V(64 keys; 64 of the dims in each CTA)
+                            const uint32_t vt = sv + (tile % VS) * L::kVHalf + (i & 1) * 8192;
+#pragma unroll
+                            for (int kk = 0; kk < 4; kk++)
+                                umma_ts2(tmem + kTmO + g * D, tmem + g * 128 + (i & 1) * 64 + kk * 8,
+                                         sdesc_mn_sw128(vt + kk * 2048, kBox), idO, !(i == i0 && kk == 0));
+                            umma_commit2_mc(&o_ready[g * 2 + (i & 1)], 3);
+                        }
+                        if (i & 1) umma_commit2_mc(&v_empty[tile % VS], 3);
+                        if (i == i1 - 1) umma_commit2_mc(o_full, 3);
+                    }
+                    return true;
+                });
+            }
+            umma_commit2(&drain[role]);
+            mbar_wait(&drain[role], 0, p.limit_ns);
+        }
+    } else {
+        // ================= softmax / epilogue (both CTAs, their own rows) =================
+        const int grp = (warp - 2) / kGW;
+        const int gt = 2 * rank + grp;            // the tile of the pair's block
+        const int q4 = warp & 3;
+        const int row = q4 * 32 + lane;
+        const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+        const uint32_t tS = trow + grp * 128, tO = trow + kTmO + grp * D;
+        const int tok_in = row / p.r, hd = row - tok_in * p.r;
+        const bool row_ok = tok_in < p.tb;
+        const float cs = p.scale * kLog2e;
+        const uint64_t cs2 = pk2(cs, cs);
+        const uint32_t pf_lead = lead(&p_full[grp * 2]), oe_lead = lead(o_empty);
+        int i = 0;
+        for_segments(p, c, [&](int k, const Seg &sg) {
+            const int b = sg.pair % p.nblk, kvh = sg.pair / p.nblk;
+            const int tok = (4 * b + gt) * p.tb + tok_in;
+            const bool valid = row_ok && tok < p.n_new;
+            const int64_t lim = !valid ? -1 : p.mask ? p.n_past + p.n_new - 1 : p.n_past + tok;
+            const float mscl = p.mask ? __fdiv_rn(1.0f, p.scale) : 0.0f;
+            const int i0 = i, i1 = i + 2 * (sg.t1 - sg.t0);
+            float m = -INFINITY, l = 0.0f;
+            for (; i < i1; i++) {
+                const int bf = i & 1;
+                if (!mbar_wait_ab(&s_full[grp * 2 + bf], (i >> 1) & 1, p.limit_ns, flags)) {
+                    give_up(p, flags, 1u);
+                    return false;
+                }
+                tc_fence_after();
+                uint32_t v[64];
+                tmem_ld32(tS + bf * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
+                tmem_ld32(tS + bf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+                tmem_wait_ld();
+                const int64_t kb = (int64_t)(2 * sg.t0 + (i - i0)) * 64;
+                const int nvis = (int)max((int64_t)0, min((int64_t)64, lim - kb + 1));
+                const bool full = __all_sync(0xffffffffu, nvis == 64);
+                if (!full) {
+#pragma unroll
+                    for (int e = 0; e < 64; e++)
+                        if (e >= nvis) v[e] = __float_as_uint(-INFINITY);
+                }
+                if constexpr (MASKED)
+                    if (valid) add_mask(p, tok, kb, nvis, mscl, v);
+                float m4[4];
+#pragma unroll
+                for (int a = 0; a < 4; a++) m4[a] = fmaxf(__uint_as_float(v[a]), __uint_as_float(v[4 + a]));
+#pragma unroll
+                for (int e = 8; e < 64; e += 8)
+#pragma unroll
+                    for (int a = 0; a < 4; a++)
+                        m4[a] = max3(m4[a], __uint_as_float(v[e + a]), __uint_as_float(v[e + 4 + a]));
+                const float mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+                float f = 1.0f;
+                bool resc = false;
+                const float xm = mx * cs;
+                if (xm > m + kLazy) {
+                    f = ex2_approx(m - xm);
+                    resc = m != -INFINITY;
+                    l *= f;
+                    m = xm;
+                }
+                const float nm = m == -INFINITY ? 0.0f : -m;
+                const uint64_t nm2 = pk2(nm, nm);
+                uint64_t s2[2] = {0ull, 0ull};
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    uint32_t pkd[16];
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        const float2 xy = up2(fma2(pk2(__uint_as_float(v[u * 32 + 2 * e]),
+                                                       __uint_as_float(v[u * 32 + 2 * e + 1])), cs2, nm2));
+                        const float x0 = ex2_approx(xy.x), x1 = ex2_approx(xy.y);
+                        s2[e & 1] = add2(s2[e & 1], pk2(x0, x1));
+                        const __half2 h2 = __floats2half2_rn(x0, x1);
+                        pkd[e] = *reinterpret_cast<const uint32_t *>(&h2);
+                    }
+                    tmem_st16(tS + bf * 64 + u * 16, pkd);
+                }
+                const float2 sa = up2(add2(s2[0], s2[1]));
+                l += sa.x + sa.y;
+                if (i > i0 && __any_sync(0xffffffffu, resc)) {
+                    if (!mbar_wait_ab(&o_ready[grp * 2 + ((i - 1) & 1)], ((i - 1) >> 1) & 1, p.limit_ns, flags)) {
+                        give_up(p, flags, 1u);
+                        return false;
+                    }
+                    tc_fence_after();
+                    const float fo = resc ? f : 1.0f;
+#pragma unroll 1
+                    for (int ch = 0; ch < D / 16; ch++) {
+                        uint32_t o[16];
+                        tmem_ld16(tO + ch * 16, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * fo);
+                        tmem_st16(tO + ch * 16, o);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(pf_lead + (uint32_t)(bf * 8));
+            }
+            const bool whole = sg.t0 == 0 && sg.t1 == nt_of(p, b);
+            const int64_t slot = (((int64_t)c * p.kseg + k) * 4 + gt) * 128 + row;
+            if (!mbar_wait_ab(o_full, k & 1, p.limit_ns, flags)) {
+                give_up(p, flags, 1u);
+                return false;
+            }
+            tc_fence_after();
+            float *dst = p.out + (int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * p.dv;
+            float scl = 1.0f;
+            if (whole) {
+                scl = l > 0.0f ? __fdiv_rn(1.0f, l) : no_key_scale(p);
+            } else {
+                reinterpret_cast<float2 *>(p.pstat)[slot] = make_float2(m, l);
+                dst = p.pout + slot * D;
+            }
+            const uint64_t pol = policy_evict_last();
+#pragma unroll 1
+            for (int ch = 0; ch < p.dv / 32; ch++) {
+                uint32_t o[32];
+                tmem_ld32(tO + ch * 32, o);
+                tmem_wait_ld();
+                if (valid)
+#pragma unroll
+                    for (int q = 0; q < 8; q++) {
+                        const float4 val = make_float4(__uint_as_float(o[4 * q]) * scl, __uint_as_float(o[4 * q + 1]) * scl,
+                                                       __uint_as_float(o[4 * q + 2]) * scl,
+                                                       __uint_as_float(o[4 * q + 3]) * scl);
+                        if (whole) *reinterpret_cast<float4 *>(dst + ch * 32 + 4 * q) = val;
+                        else st_v4_hint(dst + ch * 32 + 4 * q, val, pol);
+                    }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(oe_lead);
+            return true;
+        });
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0 && lane == 0 && rank == 0 && flags[0]) {
+        // the CTA gave up: loads of either CTA nobody waited for may still be
+        // landing (both CTAs' complete on these barriers)
+        for (int j = issued_k > KS ? issued_k - KS : 0; j < issued_k; j++)
+            mbar_wait(&k_full[j % KS], (j / KS) & 1, p.limit_ns);
+        for (int j = issued_v > VS ? issued_v - VS : 0; j < issued_v; j++)
+            mbar_wait(&v_full[j % VS], (j / VS) & 1, p.limit_ns);
+        if (issued_q > 0) mbar_wait(q_full, (issued_q - 1) & 1, p.limit_ns);
+    }
+    // every MMA of the pair has completed (the issuers' drains) and every load
+    // has landed before either CTA frees its tensor memory or leaves
+    __syncthreads();
+    cluster_sync_all();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc2(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // the fold of split pairs
 // ---------------------------------------------------------------------------
 // out = sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i over the pair's segments
@@ -694,7 +1065,8 @@ template <int D>
 __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
 {
     constexpr int F4 = D / 64;   // float4s of a thread
-    const int pair = blockIdx.x >> 4, row0 = (blockIdx.x & 15) * 16;
+    const int bpp = 8 * p.nt;    // blocks of 16 rows a pair
+    const int pair = blockIdx.x / bpp, row0 = (blockIdx.x % bpp) * 16;
     __shared__ int info[3];
     if (threadIdx.x == 0) {
         int ca, cb;
@@ -713,7 +1085,7 @@ __global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
     const int b = pair % p.nblk, kvh = pair / p.nblk;
     const int tok = (p.nt * b + grp) * p.tb + tok_in;
     if (grp >= p.nt || tok_in >= p.tb || tok >= p.n_new) return;
-    auto slot = [&](int cc) { return (((int64_t)cc * p.kseg + (cc == ca ? seg_a : 0)) * 2 + grp) * 128 + row; };
+    auto slot = [&](int cc) { return (((int64_t)cc * p.kseg + (cc == ca ? seg_a : 0)) * p.nt + grp) * 128 + row; };
     if (part * F4 * 4 >= p.dv) return;   // the zero-filled columns past a 96-wide head
     float4 *dst = reinterpret_cast<float4 *>(p.out + (int64_t)tok * p.out_stride +
                                              (int64_t)(p.out_head0 + kvh * p.r + hd) * p.dv) + part * F4;
@@ -797,7 +1169,8 @@ __global__ void __launch_bounds__(256) prefill_stats_fold(const PrefillParams p)
     }
     __syncthreads();
     const int ca = info[0], cb = info[1], seg_a = info[2];
-    auto slot = [&](int cc) { return (((int64_t)cc * p.kseg + (cc == ca ? seg_a : 0)) * 2 + grp) * 128 + row; };
+    if (grp >= p.nt) return;   // (one query tile a CTA at head_dim 256)
+    auto slot = [&](int cc) { return (((int64_t)cc * p.kseg + (cc == ca ? seg_a : 0)) * p.nt + grp) * 128 + row; };
     const float2 *ps = reinterpret_cast<const float2 *>(p.pstat);
     float M = -INFINITY;
     for (int cc = ca; cc <= cb; cc++) M = fmaxf(M, __ldcg(ps + slot(cc)).x);
@@ -854,7 +1227,7 @@ cudaError_t launch_pf(int which, const CUtensorMap &qmap, const CUtensorMap &kma
     default: {
         // the fold may be scheduled once every attention CTA has started
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)(p.hkv * p.nblk * 16));
+        cfg.gridDim = dim3((unsigned)(p.hkv * p.nblk * 8 * p.nt));
         cfg.blockDim = dim3(256);
         cfg.stream = st;
         cudaLaunchAttribute attr[1];
@@ -885,6 +1258,30 @@ cudaError_t prefill_prepare(int D)
 }
 
 int prefill_tiles(int D) { return D == 256 ? PL<256>::NT : 2; }
+
+cudaError_t prefill_pair_prepare(int *clusters)
+{
+    *clusters = 0;
+    cudaError_t e = cudaFuncSetAttribute(prefill2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)PL2::bytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PL2::bytes);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = PL2::bytes;
+    return cudaOccupancyMaxActiveClusters(clusters, prefill2_kernel<false>, &cfg);
+}
+
+cudaError_t launch_prefill_pair(const CUtensorMap &qmap, const CUtensorMap &kmap32, const CUtensorMap &vmap,
+                                const PrefillParams &p, cudaStream_t st)
+{
+    // (the kernel's cluster shape is compiled in: 2 x 1 x 1)
+    if (p.mask) prefill2_kernel<true><<<2 * p.n_cta, kPThreads, PL2::bytes, st>>>(qmap, kmap32, vmap, p);
+    else prefill2_kernel<false><<<2 * p.n_cta, kPThreads, PL2::bytes, st>>>(qmap, kmap32, vmap, p);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_prefill(int D, int which, const CUtensorMap &qmap, const CUtensorMap &kmap,
                            const CUtensorMap &vmap, const PrefillParams &p, cudaStream_t st)

@@ -103,6 +103,19 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *m, uin
         : "memory");
 }
 
+// The CTA-pair form: the tile lands in this CTA's shared memory and its bytes
+// complete on `bar_cluster`, an mbarrier of either CTA of the pair (a
+// shared::cluster address from mapa).
+__device__ __forceinline__ void tma_load_3d_pair(void *dst, const CUtensorMap *m, uint32_t bar_cluster, int x, int y,
+                                                 int z)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+        "%5}], [%2];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
 // L2 policy for data read once (streamed K/V tiles): evicted before other lines
 __device__ __forceinline__ uint64_t policy_evict_first()
 {
@@ -388,6 +401,18 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
     }
 }
 
+// As mbar_wait_cluster, but also gives up (false) as soon as *abort is non-zero.
+__device__ __forceinline__ bool mbar_wait_cluster_ab(uint64_t *bar, uint32_t parity, uint64_t limit_ns,
+                                                     const volatile int *abort)
+{
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t n = 1;; n++) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((n & 15u) == 0 && (*abort || globaltimer() - t0 > limit_ns)) return false;
+    }
+}
+
 // ---- 5th-generation tensor cores: TMEM and tcgen05.mma ----------------------------
 // Tensor memory: 128 lanes x up to 512 columns of 32-bit cells per SM.  An
 // address is (lane << 16) | column.  Allocation, relinquish and deallocation
@@ -407,6 +432,27 @@ __device__ __forceinline__ void tmem_relinquish()
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
 {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// The CTA-pair forms (cta_group::2): one warp of each CTA of a 2-CTA cluster
+// (the same warp in both) allocates, relinquishes and frees; the pair's
+// columns have the same address in both CTAs.  A kernel uses one cta_group
+// in all its tcgen05 instructions.
+__device__ __forceinline__ void tmem_alloc2(uint32_t *dst_smem, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish2()
+{
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
 // Order tcgen05 operations against thread synchronisation (mbarrier, bar.sync).
@@ -461,6 +507,47 @@ __device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t adesc, uint64_
 __device__ __forceinline__ void umma_commit(uint64_t *bar)
 {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// The CTA pair's MMA, issued by one thread of the even CTA: M = 256 rows, the
+// first 128 from the even CTA's A (shared memory or TMEM) into its TMEM, the
+// others from the odd CTA's, at the same addresses; B's N columns are split,
+// the first N/2 in the even CTA's shared memory, the rest in the odd one's.
+__device__ __forceinline__ void umma_ss2(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         bool accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_ts2(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                         bool accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+}
+
+// One arrival on `bar` in this CTA once the pair MMAs this thread issued have
+// completed; the second form arrives on `bar` in every CTA of `cta_mask`
+// (bar's offset in each).
+__device__ __forceinline__ void umma_commit2(uint64_t *bar)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void umma_commit2_mc(uint64_t *bar, uint16_t cta_mask)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::
+                     "r"(smem_addr(bar)),
+                 "h"(cta_mask)
                  : "memory");
 }
 

@@ -26,7 +26,7 @@ KV_E_TIMEOUT = -6
 KV_E_STATE = -7
 KV_E_UNSUPPORTED = -8
 
-KERNELS = {"append": 0, "attn": 1, "prefill": 2, "pfold": 3, "gather": 4}
+KERNELS = {"append": 0, "attn": 1, "prefill": 2, "pfold": 3, "gather": 4, "prefill2": 5}
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32

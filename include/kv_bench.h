@@ -35,7 +35,8 @@ int kv_gen_normal_device(float *dst, uint64_t seed, uint64_t stream,
 #define KV_K_PREFILL  2   /* both tensor-core passes */
 #define KV_K_PFOLD    3   /* the prefill statistics / output folds */
 #define KV_K_GATHER   4
-#define KV_K_COUNT    5
+#define KV_K_PREFILL2 5   /* the one-pass chunk kernel on CTA pairs (head_dim 128) */
+#define KV_K_COUNT    6
 int kv_profile_enable(kv_ctx *ctx, int on);
 int kv_profile_reset(kv_ctx *ctx);
 /* Synchronizes the recorded events; returns launches and summed milliseconds. */

@@ -259,13 +259,51 @@ def test_prefill_chunk_matches_oracle(name, n_past, n_new, cuda):
     rows = synth.qkv_rows(sp, 3, 0, n_new)
     run.ctx.profile(True)
     out = run.step(rows, n_past)
-    assert run.ctx.profile_read("prefill")[0] == (1 if n_past + n_new <= 32768 else 2)   # the tensor-core path ran
+    # the tensor-core path ran: one pass (on CTA pairs at head_dim 128), or the exact two
+    one_pass = n_past + n_new <= 32768
+    pair = one_pass and sp["head_dim"] == 128
+    assert run.ctx.profile_read("prefill2")[0] == (1 if pair else 0)
+    assert run.ctx.profile_read("prefill")[0] == (0 if pair else 1 if one_pass else 2)
     q, k, v = _split(sp, rows)
     qn, kn = synth.norm_weights(sp, 0) if sp["qk_norm"] else (None, None)
     orc = O.Oracle(sp)
     qr = orc.append(kc, vc, n_past, q, k, v, qn, kn)
     assert np.array_equal(run.rows(0, n_past, n_new), kc[n_past:n_past + n_new])
     assert_close(out, orc.attend(kc, vc, n_past, qr))
+
+
+@pytest.mark.parametrize("pair", ["1", "0"])
+@pytest.mark.parametrize("name,n_past,n_new", [
+    ("qwen3-8b-prefill", 16384, 512),  # the benchmark chunk: 4 blocks of 128 tokens a KV head
+    ("qwen3-8b-prefill", 300, 200),    # a last block with two tiles past the chunk's end, pairs split (fold)
+    ("qwen3-8b-prefill", 64, 40),      # one block: the odd CTA's tiles lie past the query buffer's rows
+    ("llama3.2-3b", 5000, 90),         # r = 3 (42 tokens a tile, 126 rows), three of the four tiles in use
+])
+def test_prefill_on_cta_pairs_matches_oracle(name, n_past, n_new, pair, cuda, monkeypatch):
+    """The one-pass chunk kernel on CTA pairs (2-CTA clusters, tcgen05
+    cta_group::2: M = 256 MMAs over both SMs, each CTA staging half of every K
+    and V tile) and the one-CTA kernel (KV_B200_PREFILL_PAIR=0) on the same
+    chunks, both within the attention tolerance of the oracle."""
+    monkeypatch.setenv("KV_B200_PREFILL_PAIR", pair)
+    sp = specs.get(name)
+    sp["n_layer"] = 1
+    n_ctx = n_past + n_new + 64
+    case = dict(name=name, spec=name, n_ctx=n_ctx, n_past=n_past, n_new=n_new)
+    run = Run(case, cuda, n_batch_max=n_new)
+    run.sp = sp
+    kc, vc = _oracle_layer(sp, n_ctx, n_past)
+    rows = synth.qkv_rows(sp, 4, 0, n_new)
+    run.ctx.profile(True)
+    out = run.step(rows, n_past)
+    assert run.ctx.profile_read("prefill2")[0] == (1 if pair == "1" else 0)
+    assert run.ctx.profile_read("prefill")[0] == (0 if pair == "1" else 1)
+    q, k, v = _split(sp, rows)
+    qn, kn = synth.norm_weights(sp, 0) if sp["qk_norm"] else (None, None)
+    orc = O.Oracle(sp)
+    qr = orc.append(kc, vc, n_past, q, k, v, qn, kn)
+    assert np.array_equal(run.rows(0, n_past, n_new), kc[n_past:n_past + n_new])
+    assert_close(out, orc.attend(kc, vc, n_past, qr))
+    run.ctx.status()
 
 
 @pytest.mark.parametrize("n_new", [1, 40])
