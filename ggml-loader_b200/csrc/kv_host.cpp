@@ -278,9 +278,11 @@ struct kv_ctx {
     bool coop = false;                      // attention kernels as cooperative launches
     // sharded decode: the collector loads the peers' heads from their buffers
     // (pull) instead of every shard storing its heads into every peer's
-    // buffer (push); pull measured ahead on 2 B200s, same box: llama-3.2-3B
-    // 32k 644.0 -> 624.9 us/token, llama-3.1-8B 128k 1635.3 -> 1622.6
-    bool xpull = true;
+    // buffer (push) -- with two shards, where pull measured ahead (2 B200s,
+    // same box: llama-3.2-3B 32k 644.0 -> 624.9 us/token, llama-3.1-8B 128k
+    // 1635.3 -> 1622.6); with eight push did (llama-3.2-3B 32k 462.2 -> 423.3:
+    // the collector's polls stay local instead of crossing NVLink per peer)
+    bool xpull = false;
     int max_clusters[kvb::kMaxClusterCtas + 1] = {};   // q-CTA clusters of the attention kernel held at once
     int force_q = 0;                        // KV_B200_CLUSTER: 0 policy, < 0 none, q > 1 that size
     int min_keys = kDecodeMinKeys;          // KV_B200_MIN_KEYS: fewest keys a decode CTA streams
@@ -664,11 +666,12 @@ int map_peers(kv_ctx *ctx)
     }
     ctx->peers = true;
     for (int g = 0; g < G; g++) ctx->peers = ctx->peers && flags[g] == 1;
-    // KV_B200_EXCHANGE: "pull" (the default: the collector loads the peers'
-    // heads from their buffers), "push" (every shard stores its heads into
-    // every peer's buffer), "nccl" (the NCCL all-gather after the kernel, for
-    // decode too)
+    // KV_B200_EXCHANGE: "pull" (the collector loads the peers' heads from
+    // their buffers; the default with two shards), "push" (every shard stores
+    // its heads into every peer's buffer; the default with more), "nccl" (the
+    // NCCL all-gather after the kernel, for decode too)
     const char *env = getenv("KV_B200_EXCHANGE");
+    ctx->xpull = G == 2;
     if (env && strcmp(env, "nccl") == 0) ctx->peers = false;
     if (env && strcmp(env, "pull") == 0) ctx->xpull = true;
     if (env && strcmp(env, "push") == 0) ctx->xpull = false;
