@@ -822,15 +822,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             const uint32_t sq = smem_addr(smem + L::o_q), sk = smem_addr(smem + L::o_k);
             const uint32_t sv = smem_addr(smem + L::o_v);
             bool ok = true;
-            auto wt = [&](uint64_t *b, uint32_t par) {   // a barrier only this CTA's agents signal
+            auto wt = [&](uint64_t *b, uint32_t par) {
                 if (ok && !mbar_wait_ab(b, par, p.limit_ns, flags)) {
-                    give_up(p, flags, 1u);
-                    ok = false;
-                }
-                return ok;
-            };
-            auto wt_cl = [&](uint64_t *b, uint32_t par) {   // one the odd CTA's threads arrive on too
-                if (ok && !mbar_wait_cluster_ab(b, par, p.limit_ns, flags)) {
                     give_up(p, flags, 1u);
                     ok = false;
                 }
@@ -868,9 +861,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                         const int tile = i >> 1;
 #pragma unroll
                         for (int g = 0; g < NT; g++) {
-                            if (!wt_cl(&p_full[g * 2 + (i & 1)], (i >> 1) & 1)) return false;
+                            if (!wt(&p_full[g * 2 + (i & 1)], (i >> 1) & 1)) return false;
                             if (g == 0 && !(i & 1) && !wt(&v_full[tile % VS], (tile / VS) & 1)) return false;
-                            if (g == 0 && i == i0 && k > 0 && !wt_cl(o_empty, (k - 1) & 1)) return false;
+                            if (g == 0 && i == i0 && k > 0 && !wt(o_empty, (k - 1) & 1)) return false;
                             tc_fence_after();
                             // O_g (+)= P_g(i) . V(64 keys; 64 of the dims in each CTA)
                             const uint32_t vt = sv + (tile % VS) * L::kVHalf + (i & 1) * 8192;
@@ -989,7 +982,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(pf_lead + (uint32_t)(bf * 8));
+                if (lane == 0) mbar_arrive_remote(pf_lead + (uint32_t)(bf * 8));
             }
             const bool whole = sg.t0 == 0 && sg.t1 == nt_of(p, b);
             const int64_t slot = (((int64_t)c * p.kseg + k) * 4 + gt) * 128 + row;
@@ -1024,7 +1017,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(oe_lead);
+            if (lane == 0) mbar_arrive_remote(oe_lead);
             return true;
         });
     }

@@ -378,6 +378,16 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar)
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
 }
 
+// arrive on an mbarrier of either CTA of the cluster (address from mapa) with
+// the default semantics (release at CTA scope, no cluster-wide fence): for
+// hand-offs whose data the tensor cores read after tcgen05 fences (TMEM
+// written with tcgen05.st, then tcgen05.wait::st and
+// tcgen05.fence::before_thread_sync), as the CTA-pair pipelines do
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar)
+{
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity)
 {
     uint32_t ok;
@@ -398,18 +408,6 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
     for (uint32_t n = 1;; n++) {
         if (mbar_try_wait_cluster(bar, parity)) return true;
         if ((n & 15u) == 0 && globaltimer() - t0 > limit_ns) return false;
-    }
-}
-
-// As mbar_wait_cluster, but also gives up (false) as soon as *abort is non-zero.
-__device__ __forceinline__ bool mbar_wait_cluster_ab(uint64_t *bar, uint32_t parity, uint64_t limit_ns,
-                                                     const volatile int *abort)
-{
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    const uint64_t t0 = globaltimer();
-    for (uint32_t n = 1;; n++) {
-        if (mbar_try_wait_cluster(bar, parity)) return true;
-        if ((n & 15u) == 0 && (*abort || globaltimer() - t0 > limit_ns)) return false;
     }
 }
 

@@ -168,6 +168,6 @@ def test_dory_ring_chunk_on_tensor_cores(flash, cuda):
         mask = np.ascontiguousarray(O.ring_mask(256, p, 64)[:, :n_used].astype(np.float16))
     r.ctx.profile(True)
     got, want = r.step(p, 64, 21, mask=mask, flash=flash)
-    assert r.ctx.profile_read("prefill")[0] >= 1
+    assert r.ctx.profile_read("prefill")[0] + r.ctx.profile_read("prefill2")[0] >= 1
     assert_close(got, want)
     assert np.array_equal(r.cells(0), r.kc)

@@ -118,7 +118,7 @@ def test_decode_window_mask_matches_oracle(name, n_past, n_new, flash, cuda):
 def test_prefill_window_mask_matches_oracle(name, n_past, n_new, stride_pad, dtype, flash, cuda):
     mask = _window_mask(n_past, n_new, n_past + n_new + stride_pad, 256, dtype)
     got, want, run = _run_masked(name, n_past, n_new, mask, flash, cuda)
-    assert run.ctx.profile_read("prefill")[0] >= 1   # the tensor-core path ran
+    assert run.ctx.profile_read("prefill")[0] + run.ctx.profile_read("prefill2")[0] >= 1   # the tensor-core path ran
     assert_close(got, want)
 
 
@@ -129,7 +129,8 @@ def test_long_context_branches_match_oracle(flash, cuda):
     name, n_past, n_new = "qwen3-8b-prefill", 40000, 40
     mask = _window_mask(n_past, n_new, n_past + n_new, 1 << 30, np.float16)   # causal, explicit
     got, want, run = _run_masked(name, n_past, n_new, mask, flash, cuda)
-    assert run.ctx.profile_read("prefill")[0] == (1 if flash else 2)
+    # (the one pass runs on CTA pairs at head_dim 128)
+    assert run.ctx.profile_read("prefill")[0] + run.ctx.profile_read("prefill2")[0] == (1 if flash else 2)
     assert_close(got, want)
 
 
