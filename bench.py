@@ -650,7 +650,9 @@ def main():
         sp["n_layer"] = args.layers
         sp["name"] += "-%dlayers" % args.layers
     if args.steps is None:
-        args.steps = sp["steps"]
+        # the configuration's positions, and at least 16 steps (qwen2-0.5B's
+        # single position is timed 16 times, each step rewriting the same row)
+        args.steps = max(sp["steps"], 16)
     if args.warmup < 3:
         log("note: raising --warmup to 3")
         args.warmup = 3
