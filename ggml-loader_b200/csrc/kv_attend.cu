@@ -80,10 +80,7 @@ template <> struct G4<96>  { static constexpr int BW = 32, NS = 6; };
 // (4 stages: 128 KB in flight an SM keeps HBM busy; a fifth only lengthens the
 // queue the statistics poll and the query loads wait behind -- 128k: 92.7 ->
 // 90.7 us a layer, 32k: 28.9 -> 28.8)
-#ifndef KV_DECODE_NS128
-#define KV_DECODE_NS128 4
-#endif
-template <> struct G4<128> { static constexpr int BW = 64, NS = KV_DECODE_NS128; };
+template <> struct G4<128> { static constexpr int BW = 64, NS = 4; };
 template <> struct G4<256> { static constexpr int BW = 64, NS = 2; };   // 64 KB stages; the V-phase buffer takes 66 KB
 
 template <int BW>
@@ -344,20 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 // the two waits for a free stage that last longest -- behind the
                 // previous kernel's tail and behind the statistics exchange --
                 // keep HBM busy: the next l2pf tiles go to L2 first
-                // (0x400: a look-ahead window instead -- the l2pf tiles past the
-                // ring's go to L2 as each tile is issued)
-                const int la = p.l2pf & 0xff;
-                const bool ahead = (p.l2pf & 0x400) != 0;
-                int pf0 = 0, pf1 = 0;
-                if (ahead) {
-                    pf0 = j == 0 ? NS : j + NS + la - 1;
-                    pf1 = j + NS + la;
-                } else if (((j == NS && (p.l2pf & 0x100)) || (j == g.nt + NS && (p.l2pf & 0x200))) && la) {
-                    pf0 = j;
-                    pf1 = j + la;
-                }
-                if (pf0 < pf1)
-                    for (int t = pf0; t < total && t < pf1; t++) {
+                if (((j == NS && (p.l2pf & 0x100)) || (j == g.nt + NS && (p.l2pf & 0x200))) && (p.l2pf & 0xff))
+                    for (int t = j; t < total && t < j + (p.l2pf & 0xff); t++) {
                         const bool tv = t >= g.nt;
                         int h2;
                         int64_t k2, e2;

@@ -917,14 +917,9 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
         const char *pf = getenv("KV_B200_L2PF");
         if (pf && *pf) {
             ctx->l2pf = std::max(0, std::min(16, atoi(pf)));
-            // entry, exchange, both (default) or ahead (a window past the ring)
-            const char *at = getenv("KV_B200_L2PF_AT");
-            if (at && strcmp(at, "ahead") == 0) {
-                ctx->l2pf |= 0x400;
-            } else {
-                const bool entry = !at || strcmp(at, "exchange") != 0, exch = !at || strcmp(at, "entry") != 0;
-                ctx->l2pf |= (entry ? 0x100 : 0) | (exch ? 0x200 : 0);
-            }
+            const char *at = getenv("KV_B200_L2PF_AT");   // entry, exchange or both (default)
+            const bool entry = !at || strcmp(at, "exchange") != 0, exch = !at || strcmp(at, "entry") != 0;
+            ctx->l2pf |= (entry ? 0x100 : 0) | (exch ? 0x200 : 0);
         }
     }
 #ifdef KV_PHASE_STAMPS

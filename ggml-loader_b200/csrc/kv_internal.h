@@ -56,8 +56,7 @@ struct AttnParams {
     // tiles sent to L2 ahead of the ring where the producer waits longest: the
     // count in bits 0-7 (0: none); bit 8: at its first wait (behind the previous
     // kernel's tail), bit 9: at its first wait among the V tiles (behind the
-    // statistics exchange); bit 10: instead, a window of that many tiles past
-    // the ring's, kept as each tile is issued
+    // statistics exchange)
     int32_t l2pf;
     float scale;
     // single-token append done inside the kernel (decode): fused = 1
