@@ -643,12 +643,22 @@ def main():
                     help="untimed steps between warm-up and the timed region (clock sampler start-up)")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the layer count (small profiling cases only; the bench line is invalid)")
+    ap.add_argument("--shard-of", type=int, default=None,
+                    help="run one GPU's share of a G-way KV-head shard (n_head/G, n_head_kv/G) on one GPU, "
+                         "without the exchange (profiling cases only; the bench line is invalid)")
     args = ap.parse_args()
     from kv_b200 import specs
     sp = specs.get(args.config)
     if args.layers:
         sp["n_layer"] = args.layers
         sp["name"] += "-%dlayers" % args.layers
+    if args.shard_of:
+        g = args.shard_of
+        if g < 1 or sp["n_head_kv"] % g:
+            raise SystemExit("--shard-of %d does not divide %d KV heads" % (g, sp["n_head_kv"]))
+        sp["n_head"] //= g
+        sp["n_head_kv"] //= g
+        sp["name"] += "-shard1of%d" % g
     if args.steps is None:
         # the configuration's positions, and at least 16 steps (qwen2-0.5B's
         # single position is timed 16 times, each step rewriting the same row)

@@ -71,5 +71,17 @@ def build(verbose=False, lib=LIB, obj_dir=OBJ, defines=()):
     return lib
 
 
+# the phase-stamp measurement build (kv_debug_stamps; python -m kv_b200.stamps)
+STAMPS_LIB = os.path.join(HERE, "lib", "stamps", "libkv_b200.so")
+STAMPS_OBJ = os.path.join(HERE, "_build", "stamps")
+
+
+def build_stamps(verbose=False):
+    return build(verbose, STAMPS_LIB, STAMPS_OBJ, ("KV_PHASE_STAMPS",))
+
+
 if __name__ == "__main__":
-    print(build(verbose="-v" in sys.argv))
+    if "--stamps" in sys.argv:
+        print(build_stamps(verbose="-v" in sys.argv))
+    else:
+        print(build(verbose="-v" in sys.argv))

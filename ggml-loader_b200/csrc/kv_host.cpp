@@ -1625,14 +1625,25 @@ int64_t kv_launch_count(const kv_ctx *ctx) { return ctx ? ctx->launches.load() :
 // so far (launch i sits in ring slot i % ring); *ring and *max_cta describe it.
 int64_t kv_debug_stamps(kv_ctx *ctx, unsigned long long *host_dst, int32_t *ring, int32_t *max_cta)
 {
-    if (!ctx || !host_dst) return -1;
+    if (!ctx || !ring || !max_cta) return -1;
     if (ensure_device(ctx)) return -1;
-    cudaDeviceSynchronize();
     *ring = kv_ctx::kStampRing;
     *max_cta = ctx->max_cta;
-    cudaMemcpy(host_dst, ctx->stamps, (size_t)kv_ctx::kStampRing * ctx->max_cta * kvb::kStampSlots * 8u,
-               cudaMemcpyDeviceToHost);
+    if (host_dst) {   // (NULL: the sizes only)
+        cudaDeviceSynchronize();
+        cudaMemcpy(host_dst, ctx->stamps, (size_t)kv_ctx::kStampRing * ctx->max_cta * kvb::kStampSlots * 8u,
+                   cudaMemcpyDeviceToHost);
+    }
     return ctx->stamp_next;
+}
+#else
+int64_t kv_debug_stamps(kv_ctx *ctx, unsigned long long *host_dst, int32_t *ring, int32_t *max_cta)
+{
+    (void)ctx;
+    (void)host_dst;
+    (void)ring;
+    (void)max_cta;
+    return (int64_t)fail(KV_E_UNSUPPORTED, "this library was built without KV_PHASE_STAMPS (build.py --stamps)");
 }
 #endif
 

@@ -100,6 +100,7 @@ def lib():
         "kv_profile_read": (ctypes.c_int, [_vp, _i32, ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_double)]),
         "kv_kernel_name": (ctypes.c_char_p, [_i32]),
         "kv_launch_count": (_i64, [_vp]),
+        "kv_debug_stamps": (_i64, [_vp, _vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
         "kv_attend_decode_noalloc": (ctypes.c_int, [_vp, _vp, _i32, _i32, _i32, _i64, _vp, _vp, _vp]),
         "kv_status": (ctypes.c_int, [_vp, _vp]),
         "kv_debug_inject": (ctypes.c_int, [_vp, _i32, _u64]),
@@ -330,6 +331,18 @@ class Context:
 
     def launch_count(self):
         return int(lib().kv_launch_count(self.h))
+
+    def debug_stamps(self):
+        """The phase-stamp build's ring of decode launches: (array [ring][max_cta][16]
+        of %globaltimer values, launches stamped so far).  Other builds raise."""
+        import numpy as np
+        ring, mc = _i32(), _i32()
+        n = int(lib().kv_debug_stamps(self.h, None, ctypes.byref(ring), ctypes.byref(mc)))
+        if n < 0:
+            _check(KV_E_UNSUPPORTED, "kv_debug_stamps")
+        buf = np.zeros(ring.value * mc.value * 16, np.uint64)
+        n = int(lib().kv_debug_stamps(self.h, buf.ctypes.data, ctypes.byref(ring), ctypes.byref(mc)))
+        return buf.reshape(ring.value, mc.value, 16), n
 
     def status(self, stream=None):
         """KV_OK, or KV_E_TIMEOUT if a bounded device-side wait expired (raises)."""

@@ -82,6 +82,17 @@ int kv_decode_shape(int32_t sm_count, int32_t n_kv_heads_local, int64_t n_kv, co
  * largest grid does not fit (blocks_per_sm from the CUDA occupancy query). */
 int kv_decode_grid_fits(int32_t sm_count, int32_t blocks_per_sm, int32_t n_cta);
 
+/* Per-CTA phase stamps of the decode kernel, in the measurement build only
+ * (compiled with KV_PHASE_STAMPS: `python ggml-loader_b200/build.py --stamps`):
+ * each launch records %globaltimer at its phases (entry, first tile issued,
+ * griddepcontrol.wait returned, query rows rotated, K loop done, statistics
+ * published / known, V loop done, output ticket, collector start / done,
+ * exit) into a ring of launches.  Sets *ring and *max_cta, copies the ring
+ * ([ring][max_cta][16]) to host_dst unless it is NULL, and returns the number
+ * of launches stamped so far (launch i in slot i % ring); other builds return
+ * KV_E_UNSUPPORTED. */
+int64_t kv_debug_stamps(kv_ctx *ctx, unsigned long long *host_dst, int32_t *ring, int32_t *max_cta);
+
 #ifdef __cplusplus
 }
 #endif
