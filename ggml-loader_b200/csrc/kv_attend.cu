@@ -956,9 +956,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 return;
             }
         }
-        // this CTA's copy of the head's accumulators (cluster leaders: copy 0)
-        long long *const acc_h = p.acc + (int64_t)h * p.acc_copies * kRows * D;
-        long long *acc = acc_h + (int64_t)(clus ? 0 : (c - p.span_a[h]) & (p.acc_copies - 1)) * kRows * D;
+        long long *acc = p.acc + (int64_t)h * kRows * D;
         unsigned bad = 0u;   // rows with a non-finite partial
         for (int idx = tid; idx < R * D; idx += kConsumers) {
             const int row = idx / D, dd = idx - row * D;
@@ -990,17 +988,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
         if (flags[1 + sl]) {
             const unsigned nan_rows = __ldcg(&p.nonfin[h]);
             emit_head(h, [&](int idx, int row, int) {
-                long long cv[kAccCopies];
-#pragma unroll
-                for (int k = 0; k < kAccCopies; k++)
-                    cv[k] = k < p.acc_copies ? __ldcg(acc_h + (int64_t)k * kRows * D + idx) : 0ll;
-                long long v = 0;
-#pragma unroll
-                for (int k = 0; k < kAccCopies; k++)
-                    if (k < p.acc_copies) {
-                        v += cv[k];
-                        acc_h[(int64_t)k * kRows * D + idx] = 0;
-                    }
+                const long long v = __ldcg(acc + idx);
+                acc[idx] = 0;
                 return (nan_rows >> row) & 1u ? __int_as_float(0x7fc00000) : __fmul_rn(__ll2float_rn(v), kUnfix);
             });
             if (tid == 0) {

@@ -260,8 +260,7 @@ struct kv_ctx {
     int64_t S_floats = 0;
     unsigned long long *stats = nullptr;  // [max_cta][2][8][2] epoch-tagged (max, sum) slots
     uint32_t epoch = 0;                   // tag of the last attention launch
-    long long *acc = nullptr; // [hkv_loc][kAccCopies][8][D] fixed-point output accumulators
-    int acc_copies = 0;       // KV_B200_ACC_COPIES: 0 the rule of acc_copies_for, else 1, 2 or 4
+    long long *acc = nullptr; // [hkv_loc][8][D] fixed-point output accumulators
     unsigned *ctl = nullptr;  // [2][hkv_loc]: output tickets, non-finite flags; then the peer-exchange ticket
     unsigned *err = nullptr;  // device error word of the bounded waits
     float *local_out = nullptr;   // sharded prefill: [n_batch_max][hq_loc*D]
@@ -493,15 +492,6 @@ DecodeShape decode_shape_for(int sm_count, int hkv_loc, int64_t n_kv, const int 
     const int qa = (int)std::min<int64_t>({(int64_t)kvb::kMaxClusterCtas, sm_count / hkv_loc, per_head_keys});
     if (qa >= 2 && (int64_t)hkv_loc * qa * 100 >= (int64_t)c0 * 85 && fits(qa, 1)) return DecodeShape{hkv_loc * qa, qa, 1};
     return none;
-}
-
-// Copies of a head's output accumulators by the CTAs on it: with one or two
-// KV heads a shard (~60-150 CTAs a head) every accumulator word takes one
-// 64-bit atomic add per CTA, serialised in its L2 slice; four copies spread
-// them over four times the lines.  Few CTAs a head keep one copy.
-int acc_copies_for(int span)
-{
-    return span >= 64 ? 4 : span >= 32 ? 2 : 1;
 }
 
 // The decode kernel's L2 prefetch (AttnParams::l2pf) by the tiles a CTA
@@ -881,7 +871,7 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
         {(void **)&ctx->qbuf, (size_t)c.n_batch_max * ctx->hq_loc * D * sizeof(__half)},
         {(void **)&ctx->S, (size_t)ctx->S_floats * sizeof(float)},
         {(void **)&ctx->stats, n_part * 2u * sizeof(unsigned long long)},
-        {(void **)&ctx->acc, (size_t)ctx->hkv_loc * kvb::kAccCopies * 8u * (size_t)D * sizeof(long long)},
+        {(void **)&ctx->acc, (size_t)ctx->hkv_loc * 8u * (size_t)D * sizeof(long long)},
         {(void **)&ctx->ctl, (2u * (size_t)ctx->hkv_loc + 1u) * sizeof(unsigned)},
         {(void **)&ctx->err, sizeof(unsigned)},
         {(void **)&ctx->ring_mask, ctx->ring ? (size_t)c.n_batch_max * (size_t)ctx->rows * sizeof(__half) : 0},
@@ -893,8 +883,7 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
     }
     e = cudaMemset(ctx->ctl, 0, (2u * (size_t)ctx->hkv_loc + 1u) * sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(ctx->stats, 0, n_part * 2u * sizeof(unsigned long long));
-    if (e == cudaSuccess)
-        e = cudaMemset(ctx->acc, 0, (size_t)ctx->hkv_loc * kvb::kAccCopies * 8u * (size_t)D * sizeof(long long));
+    if (e == cudaSuccess) e = cudaMemset(ctx->acc, 0, (size_t)ctx->hkv_loc * 8u * (size_t)D * sizeof(long long));
     if (e == cudaSuccess) e = cudaMemset(ctx->err, 0, sizeof(unsigned));
     if (e != cudaSuccess) return bail(cuda_fail(e, "cudaMemset"));
     e = kvb::attn_prepare(ctx->D);
@@ -921,11 +910,6 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
         ctx->dec_sms = ctx->sm_count;
         const char *ds = getenv("KV_B200_DECODE_SMS");
         if (ds && *ds) ctx->dec_sms = std::max(1, std::min(ctx->sm_count, atoi(ds)));
-        const char *ac = getenv("KV_B200_ACC_COPIES");
-        if (ac && *ac) {
-            const int v = atoi(ac);
-            ctx->acc_copies = v >= 4 ? 4 : v >= 2 ? 2 : 1;
-        }
         const char *mk = getenv("KV_B200_MIN_KEYS");
         if (mk && *mk) ctx->min_keys = std::max(128, std::min(1 << 20, atoi(mk)));
         const char *cl = getenv("KV_B200_CLUSTER");
@@ -1361,11 +1345,6 @@ static int attend_impl(kv_ctx *ctx, int32_t layer, int64_t n_past, int32_t n_new
     }
     if (ap.n_cta > ctx->max_cta) return fail(KV_E_RANGE, "internal: %d CTAs > %d", ap.n_cta, ctx->max_cta);
     kvb::attn_split(ap, ctx->hkv_loc, n_kv);
-    {
-        int span = 1;
-        for (int h = 0; h < ctx->hkv_loc; h++) span = std::max(span, ap.span_b[h] - ap.span_a[h] + 1);
-        ap.acc_copies = ctx->acc_copies ? ctx->acc_copies : acc_copies_for(span);
-    }
     if ((int64_t)ap.n_cta * ap.S_tiles * kvb::attn_tile_scores() > ctx->S_floats)
         return fail(KV_E_RANGE, "internal: score scratch too small for %d CTAs x %lld tiles", ap.n_cta,
                     (long long)ap.S_tiles);
@@ -1537,7 +1516,7 @@ int kv_status(kv_ctx *ctx, void *stream)
     // a CTA that left early never counted itself in: restart the per-head
     // tickets and clear the output accumulators
     KV_CUDA(cudaMemset(ctx->ctl, 0, (2u * (size_t)ctx->hkv_loc + 1u) * sizeof(unsigned)));
-    KV_CUDA(cudaMemset(ctx->acc, 0, (size_t)ctx->hkv_loc * kvb::kAccCopies * 8u * (size_t)ctx->D * sizeof(long long)));
+    KV_CUDA(cudaMemset(ctx->acc, 0, (size_t)ctx->hkv_loc * 8u * (size_t)ctx->D * sizeof(long long)));
     KV_CUDA(cudaMemset(ctx->err, 0, sizeof(unsigned)));
     return fail(KV_E_TIMEOUT, "a device-side wait expired (error word 0x%x); the outputs of that call are invalid",
                 word);

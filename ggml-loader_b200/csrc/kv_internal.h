@@ -80,11 +80,7 @@ struct AttnParams {
     unsigned long long *stats;       // [n_cta][2][8][2] (max, sum of exp) per (CTA, segment, row),
                                      // each word = epoch << 32 | float bits
     uint32_t epoch;                  // tag of this launch's statistics (never 0)
-    long long *acc;                  // [hkv][acc_copies][8][D] output accumulators, fixed point 2^-40, zero between calls
-    // copies of each head's accumulators (1, 2 or kAccCopies): a head's CTAs
-    // add into copy (c - span_a) % acc_copies, its last CTA sums them (exact
-    // integer sums), so many CTAs on one head spread their atomics
-    int32_t acc_copies;
+    long long *acc;                  // [hkv][8][D] output accumulators, fixed point 2^-40, zero between calls
     unsigned *counters;              // [hkv] output tickets, zero between calls
     unsigned *nonfin;                // [hkv] rows (bit per row) with a non-finite partial output, zero between calls
     unsigned *err;                   // error word (1: consumer tile wait, 2: producer, 4: statistics wait)
@@ -144,7 +140,6 @@ cudaError_t attn_occupancy(int D, int *blocks_per_sm);
 // clusters of q CTAs of the attention kernel the device holds at once (0: no
 // cluster mode at this head_dim)
 cudaError_t attn_cluster_occupancy(int D, int q, int *clusters);
-constexpr int kAccCopies = 4;   // most copies of a head's output accumulators
 constexpr int kMaxClusterCtas = 8;
 // the split's per-launch tables (score tiles per CTA, each head's CTA span) for ap.n_cta CTAs
 void attn_split(AttnParams &ap, int hkv, int64_t n_kv);

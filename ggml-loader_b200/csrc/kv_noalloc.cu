@@ -187,7 +187,6 @@ extern "C" int kv_attend_decode_noalloc(const uint16_t *k_cache, const uint16_t 
     ap.S = reinterpret_cast<float *>(base + off_s);
     ap.stats = reinterpret_cast<unsigned long long *>(base + off_st);
     ap.acc = reinterpret_cast<long long *>(base + off_acc);
-    ap.acc_copies = 1;
     ap.counters = ctl;
     ap.nonfin = ctl + hkv;
     ap.xticket = ctl + 2 * hkv;
