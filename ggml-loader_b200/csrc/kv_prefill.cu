@@ -1043,6 +1043,376 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// the CTA-pair kernel with one query tile a CTA and 128-key S (head_dim 128)
+// ---------------------------------------------------------------------------
+// As prefill2_kernel, but each CTA of the pair holds one 128-row query tile (a
+// block is 2 tb tokens: tile 0 in the even CTA, tile 1 in the odd one) and S
+// covers a whole 128-key K tile: S = Q . K^T with M = 256, N = 128 (each CTA
+// stages K's keys 64*rank .. +63), double-buffered in TMEM (two 128-column
+// buffers, O in columns 256-383), so an S instruction carries twice the math
+// of prefill2's N = 64 ones for the same issue and front-end slot.  Eight
+// softmax warps share the tile: two per TMEM lane quarter, each on 64 of a
+// row's 128 keys; the pair exchanges the row's maximum through shared memory
+// (a 64-thread named barrier per quarter) so both halves use one running
+// maximum, and each keeps its half of the row sum (added at the segment's
+// end) and rescales its half of the row's O.  P (F16 pairs) overwrites S's
+// first 64 columns after both halves have read S.
+struct PL3 {
+    static constexpr int KS = 6, VS = 4;
+    static constexpr uint32_t kQTile = 2 * kBox;          // 128 rows x 128 halves
+    static constexpr uint32_t kKBox = 32 * 128;           // [32 keys][64 halves]
+    static constexpr uint32_t kKHalf = 4 * kKBox;         // [2 dim boxes][64 keys][64 halves]
+    static constexpr uint32_t kVHalf = kBox;              // [128 keys][this CTA's 64 dims]
+    static constexpr uint32_t kTmO = 256;                 // O's TMEM columns (S buffers at 0, 128)
+    static constexpr size_t o_q = 0;
+    static constexpr size_t o_k = o_q + kQTile;
+    static constexpr size_t o_v = o_k + (size_t)KS * kKHalf;
+    static constexpr size_t o_bar = o_v + (size_t)VS * kVHalf;
+    // q_full, q_empty, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
+    // s_full[2], p_full[2], o_ready[2], o_full, o_empty, drain[2]
+    static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 6 + 2 + 2;
+    static constexpr size_t o_tm = o_bar + (size_t)NBAR * 8;
+    static constexpr size_t o_red = (o_tm + 16 + 15) / 16 * 16;   // [2 tiles' parity][2 halves][128 rows] maxima
+    static constexpr size_t o_redl = o_red + 2 * 2 * 128 * 4;     // [2 halves][128 rows] row sums
+    static constexpr size_t o_flags = o_redl + 2 * 128 * 4;
+    static constexpr size_t bytes = o_flags + 16;
+    static_assert(bytes <= 227 * 1024, "shared memory of the one-tile pair kernel");
+    static_assert(o_k % 1024 == 0 && o_v % 1024 == 0, "swizzled boxes 1024-byte aligned");
+};
+
+template <bool MASKED>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
+    prefill3_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap32,
+                    const __grid_constant__ CUtensorMap vmap, const PrefillParams p)
+{
+    constexpr int D = 128;
+    using L = PL3;
+    constexpr int KS = L::KS, VS = L::VS;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::o_bar);
+    uint64_t *q_full = bar, *q_empty = bar + 1;
+    uint64_t *k_full = bar + 2, *k_empty = k_full + KS;
+    uint64_t *v_full = k_empty + KS, *v_empty = v_full + VS;
+    uint64_t *s_full = v_empty + VS;   // [buffer]
+    uint64_t *p_full = s_full + 2;     // [buffer] (the even CTA's: both CTAs' softmax warps)
+    uint64_t *o_ready = p_full + 2;    // [buffer]: the P . V that read the buffer's P has completed
+    uint64_t *o_full = o_ready + 2, *o_empty = o_full + 1;
+    uint64_t *drain = o_empty + 1;     // [issuer]
+    uint32_t *tm_slot = reinterpret_cast<uint32_t *>(smem + L::o_tm);
+    float *red = reinterpret_cast<float *>(smem + L::o_red);
+    float *redl = reinterpret_cast<float *>(smem + L::o_redl);
+    volatile int *flags = reinterpret_cast<volatile int *>(smem + L::o_flags);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rank = (int)cluster_rank(), c = blockIdx.x >> 1;
+    auto lead = [&](uint64_t *b) { return mapa(smem_addr(b), 0); };
+    int issued_q = 0, issued_k = 0, issued_v = 0;
+
+    if (tid == 0) {
+        for (int i = 0; i < L::NBAR; i++) {
+            const uint64_t *bi = &bar[i];
+            const bool arrivals = (bi >= p_full && bi < p_full + 2) || bi == o_empty;   // 8 warps x 2 CTAs
+            mbar_init(&bar[i], arrivals ? 16 : 1);
+        }
+        flags[0] = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc2(tm_slot, 512);
+        tmem_relinquish2();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem = *tm_slot;
+    pdl_launch_dependents();
+
+    if (warp == 0) {
+        // ================= TMA (both CTAs: their tile and halves) =================
+        if (lane == 0) {
+            prefetch_tmap(&qmap);
+            prefetch_tmap(&kmap32);
+            prefetch_tmap(&vmap);
+            const uint32_t qbytes = (uint32_t)(p.r * p.tb) * 128u * 2u;   // one Q tile (zero fill counts)
+            for_segments(p, c, [&](int k, const Seg &sg) {
+                const int kvh = sg.pair / p.nblk, b = sg.pair % p.nblk;
+                if (k > 0 && !mbar_wait_ab(q_empty, (k - 1) & 1, p.limit_ns, flags)) {
+                    give_up(p, flags, 2u);
+                    return false;
+                }
+                if (rank == 0) mbar_arrive_expect_tx(q_full, 2 * qbytes);
+#pragma unroll
+                for (int bx = 0; bx < 2; bx++)
+                    tma_load_3d_pair(smem + L::o_q + bx * kBox, &qmap, lead(q_full), bx * 64, kvh * p.r,
+                                     (2 * b + rank) * p.tb);
+                issued_q++;
+                for (int t = sg.t0; t < sg.t1; t++) {
+                    const int s = issued_k % KS;
+                    if (issued_k >= KS && !mbar_wait_ab(&k_empty[s], ((issued_k / KS) - 1) & 1, p.limit_ns, flags)) {
+                        give_up(p, flags, 2u);
+                        return false;
+                    }
+                    if (rank == 0) mbar_arrive_expect_tx(&k_full[s], 2 * L::kKHalf);
+                    // this CTA's 64 keys of the tile, [dim box][64 keys] (two 32-key boxes each)
+#pragma unroll
+                    for (int bx = 0; bx < 2; bx++)
+#pragma unroll
+                        for (int kh = 0; kh < 2; kh++)
+                            tma_load_3d_pair(smem + L::o_k + s * L::kKHalf + bx * 2 * L::kKBox + kh * L::kKBox,
+                                             &kmap32, lead(&k_full[s]), bx * 64, kvh, t * 128 + rank * 64 + kh * 32);
+                    issued_k++;
+                    const int sv = issued_v % VS;
+                    if (issued_v >= VS && !mbar_wait_ab(&v_empty[sv], ((issued_v / VS) - 1) & 1, p.limit_ns, flags)) {
+                        give_up(p, flags, 2u);
+                        return false;
+                    }
+                    if (rank == 0) mbar_arrive_expect_tx(&v_full[sv], 2 * L::kVHalf);
+                    tma_load_3d_pair(smem + L::o_v + sv * L::kVHalf, &vmap, lead(&v_full[sv]), rank * 64, kvh,
+                                     t * 128);
+                    issued_v++;
+                }
+                return true;
+            });
+        }
+    } else if (warp == 1 || warp == 10) {
+        // ================= MMA issue (even CTA): S (warp 1), P . V (warp 10) =================
+        const int role = warp == 1 ? 0 : 1;
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idS = idesc_f16_f32(256, 128, false);
+            constexpr uint32_t idO = idesc_f16_f32(256, D, true);
+            const uint32_t sq = smem_addr(smem + L::o_q), sk = smem_addr(smem + L::o_k);
+            const uint32_t sv = smem_addr(smem + L::o_v);
+            bool ok = true;
+            auto wt = [&](uint64_t *b, uint32_t par) {
+                if (ok && !mbar_wait_ab(b, par, p.limit_ns, flags)) {
+                    give_up(p, flags, 1u);
+                    ok = false;
+                }
+                return ok;
+            };
+            int i = 0;   // K/V tiles consumed
+            if (role == 0) {
+                for_segments(p, c, [&](int k, const Seg &sg) {
+                    const int i1 = i + (sg.t1 - sg.t0);
+                    if (!wt(q_full, k & 1)) return false;
+                    for (; i < i1; i++) {
+                        if (!wt(&k_full[i % KS], (i / KS) & 1)) return false;
+                        // the buffer is free once the P . V of tile i-2 has read its P
+                        if (i >= 2 && !wt(&o_ready[i & 1], ((i - 2) >> 1) & 1)) return false;
+                        tc_fence_after();
+                        const uint32_t kt = sk + (i % KS) * L::kKHalf;
+#pragma unroll
+                        for (int kk = 0; kk < D / 16; kk++)
+                            umma_ss2(tmem + (i & 1) * 128, sdesc_k_sw128(sq + (kk >> 2) * kBox + (kk & 3) * 32),
+                                     sdesc_k_sw128(kt + (kk >> 2) * 2 * L::kKBox + (kk & 3) * 32), idS, kk > 0);
+                        umma_commit2_mc(&s_full[i & 1], 3);
+                        umma_commit2_mc(&k_empty[i % KS], 3);
+                        if (i == i1 - 1) umma_commit2_mc(q_empty, 3);
+                    }
+                    return true;
+                });
+            } else {
+                for_segments(p, c, [&](int k, const Seg &sg) {
+                    const int i0 = i, i1 = i + (sg.t1 - sg.t0);
+                    for (; i < i1; i++) {
+                        if (!wt(&p_full[i & 1], (i >> 1) & 1)) return false;
+                        if (!wt(&v_full[i % VS], (i / VS) & 1)) return false;
+                        if (i == i0 && k > 0 && !wt(o_empty, (k - 1) & 1)) return false;
+                        tc_fence_after();
+                        // O (+)= P(i) . V(128 keys; 64 of the dims in each CTA)
+                        const uint32_t vt = sv + (i % VS) * L::kVHalf;
+#pragma unroll
+                        for (int kk = 0; kk < 8; kk++)
+                            umma_ts2(tmem + L::kTmO, tmem + (i & 1) * 128 + kk * 8, sdesc_mn_sw128(vt + kk * 2048, kBox),
+                                     idO, !(i == i0 && kk == 0));
+                        umma_commit2_mc(&o_ready[i & 1], 3);
+                        umma_commit2_mc(&v_empty[i % VS], 3);
+                        if (i == i1 - 1) umma_commit2_mc(o_full, 3);
+                    }
+                    return true;
+                });
+            }
+            umma_commit2(&drain[role]);
+            mbar_wait(&drain[role], 0, p.limit_ns);
+        }
+    } else if (warp >= 2 && warp < 10) {
+        // ================= softmax / epilogue (both CTAs, their own tile) =================
+        const int q4 = warp & 3, half = (warp - 2) >> 2;   // lane quarter; the row's keys / dims half
+        const int row = q4 * 32 + lane;
+        const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+        const uint32_t tO = trow + L::kTmO + half * 64;
+        const int tok_in = row / p.r, hd = row - tok_in * p.r;
+        const bool row_ok = tok_in < p.tb;
+        const float cs = p.scale * kLog2e;
+        const uint64_t cs2 = pk2(cs, cs);
+        const uint32_t pf_lead = lead(&p_full[0]), oe_lead = lead(o_empty);
+        // the two warps of this lane quarter meet on a named barrier; every
+        // decision to leave is taken there together (barrier.red.or), so
+        // neither is ever left waiting for a partner that gave up
+        const uint32_t pair_bar = 1 + q4;
+        bool bad = false;   // a bounded wait of this warp expired since the last meeting
+        auto leave = [&](bool mine) {
+            if (named_sync_or(pair_bar, 64, mine)) {
+                give_up(p, flags, 1u);
+                return true;
+            }
+            return false;
+        };
+        int i = 0;
+        for_segments(p, c, [&](int k, const Seg &sg) {
+            const int b = sg.pair % p.nblk, kvh = sg.pair / p.nblk;
+            const int tok = (2 * b + rank) * p.tb + tok_in;
+            const bool valid = row_ok && tok < p.n_new;
+            const int64_t lim = !valid ? -1 : p.mask ? p.n_past + p.n_new - 1 : p.n_past + tok;
+            const float mscl = p.mask ? __fdiv_rn(1.0f, p.scale) : 0.0f;
+            const int i0 = i, i1 = i + (sg.t1 - sg.t0);
+            float m = -INFINITY, l = 0.0f;   // running max (log2 units, shared by the halves); this half's sum
+            for (; i < i1; i++) {
+                const int bf = i & 1;
+                const bool got = !bad && mbar_wait_ab(&s_full[bf], (i >> 1) & 1, p.limit_ns, flags);
+                if (leave(!got)) return false;
+                tc_fence_after();
+                uint32_t v[64];
+                const uint32_t tS = trow + bf * 128;
+                tmem_ld32(tS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
+                tmem_ld32(tS + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+                tmem_wait_ld();
+                const int64_t kb = (int64_t)(sg.t0 + (i - i0)) * 128 + half * 64;   // this half's first key
+                const int nvis = (int)max((int64_t)0, min((int64_t)64, lim - kb + 1));
+                const bool full = __all_sync(0xffffffffu, nvis == 64);
+                if (!full) {
+#pragma unroll
+                    for (int e = 0; e < 64; e++)
+                        if (e >= nvis) v[e] = __float_as_uint(-INFINITY);
+                }
+                if constexpr (MASKED)
+                    if (valid) add_mask(p, tok, kb, nvis, mscl, v);
+                float m4[4];
+#pragma unroll
+                for (int a = 0; a < 4; a++) m4[a] = fmaxf(__uint_as_float(v[a]), __uint_as_float(v[4 + a]));
+#pragma unroll
+                for (int e = 8; e < 64; e += 8)
+#pragma unroll
+                    for (int a = 0; a < 4; a++)
+                        m4[a] = max3(m4[a], __uint_as_float(v[e + a]), __uint_as_float(v[e + 4 + a]));
+                // the row's maximum over both halves (buffers alternate with the
+                // tile: the next meeting orders a reuse after the partner's read);
+                // past this barrier S of the buffer is in both halves' registers,
+                // so P may overwrite its first 64 columns
+                float *rm = red + bf * 256;
+                rm[half * 128 + row] = max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+                named_sync(pair_bar, 64);
+                const float mx = fmaxf(rm[row], rm[128 + row]);
+                float f = 1.0f;
+                bool resc = false;
+                const float xm = mx * cs;
+                if (xm > m + kLazy) {
+                    f = ex2_approx(m - xm);
+                    resc = m != -INFINITY;
+                    l *= f;
+                    m = xm;
+                }
+                const float nm = m == -INFINITY ? 0.0f : -m;
+                const uint64_t nm2 = pk2(nm, nm);
+                uint64_t s2[2] = {0ull, 0ull};
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    uint32_t pkd[16];
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        const float2 xy = up2(fma2(pk2(__uint_as_float(v[u * 32 + 2 * e]),
+                                                       __uint_as_float(v[u * 32 + 2 * e + 1])), cs2, nm2));
+                        const float x0 = ex2_approx(xy.x), x1 = ex2_approx(xy.y);
+                        s2[e & 1] = add2(s2[e & 1], pk2(x0, x1));
+                        const __half2 h2 = __floats2half2_rn(x0, x1);
+                        pkd[e] = *reinterpret_cast<const uint32_t *>(&h2);
+                    }
+                    // keys half*64 + 32u .. +31 -> packed columns half*32 + 16u .. +15
+                    tmem_st16(tS + half * 32 + u * 16, pkd);
+                }
+                const float2 sa = up2(add2(s2[0], s2[1]));
+                l += sa.x + sa.y;
+                if (i > i0 && __any_sync(0xffffffffu, resc)) {
+                    // this half's 64 dims of O, once the last P . V into it has completed
+                    if (mbar_wait_ab(&o_ready[(i - 1) & 1], ((i - 1) >> 1) & 1, p.limit_ns, flags)) {
+                        tc_fence_after();
+                        const float fo = resc ? f : 1.0f;
+#pragma unroll 1
+                        for (int ch = 0; ch < 4; ch++) {
+                            uint32_t o[16];
+                            tmem_ld16(tO + ch * 16, o);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * fo);
+                            tmem_st16(tO + ch * 16, o);
+                        }
+                    } else {
+                        bad = true;   // reported at the next meeting
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(pf_lead + (uint32_t)(bf * 8));
+            }
+            // the row's sum: both halves; the output once the last P . V is in O
+            redl[half * 128 + row] = l;
+            if (leave(bad)) return false;
+            const float lt = redl[row] + redl[128 + row];
+            const bool got = mbar_wait_ab(o_full, k & 1, p.limit_ns, flags);
+            if (leave(!got)) return false;   // (also: both read redl before it is written again)
+            tc_fence_after();
+            const bool whole = sg.t0 == 0 && sg.t1 == nt_of(p, b);
+            const int64_t slot = (((int64_t)c * p.kseg + k) * 2 + rank) * 128 + row;
+            float *dst = p.out + (int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * p.dv;
+            float scl = 1.0f;
+            if (whole) {
+                scl = lt > 0.0f ? __fdiv_rn(1.0f, lt) : no_key_scale(p);
+            } else {
+                if (half == 0) reinterpret_cast<float2 *>(p.pstat)[slot] = make_float2(m, lt);
+                dst = p.pout + slot * D;
+            }
+            const uint64_t pol = policy_evict_last();
+#pragma unroll 1
+            for (int ch = 0; ch < 2; ch++) {   // this half's 64 dims
+                uint32_t o[32];
+                tmem_ld32(tO + ch * 32, o);
+                tmem_wait_ld();
+                if (valid)
+#pragma unroll
+                    for (int q = 0; q < 8; q++) {
+                        const float4 val = make_float4(__uint_as_float(o[4 * q]) * scl, __uint_as_float(o[4 * q + 1]) * scl,
+                                                       __uint_as_float(o[4 * q + 2]) * scl,
+                                                       __uint_as_float(o[4 * q + 3]) * scl);
+                        float *d4 = dst + half * 64 + ch * 32 + 4 * q;
+                        if (whole) *reinterpret_cast<float4 *>(d4) = val;
+                        else st_v4_hint(d4, val, pol);
+                    }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(oe_lead);
+            return true;
+        });
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0 && lane == 0 && rank == 0 && flags[0]) {
+        for (int j = issued_k > KS ? issued_k - KS : 0; j < issued_k; j++)
+            mbar_wait(&k_full[j % KS], (j / KS) & 1, p.limit_ns);
+        for (int j = issued_v > VS ? issued_v - VS : 0; j < issued_v; j++)
+            mbar_wait(&v_full[j % VS], (j / VS) & 1, p.limit_ns);
+        if (issued_q > 0) mbar_wait(q_full, (issued_q - 1) & 1, p.limit_ns);
+    }
+    __syncthreads();
+    cluster_sync_all();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc2(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // the fold of split pairs
 // ---------------------------------------------------------------------------
 // out = sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i over the pair's segments
@@ -1259,6 +1629,10 @@ cudaError_t prefill_pair_prepare(int *clusters)
                                          (int)PL2::bytes);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(prefill2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PL2::bytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill3_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PL3::bytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(prefill3_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PL3::bytes);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2);
@@ -1270,9 +1644,15 @@ cudaError_t prefill_pair_prepare(int *clusters)
 cudaError_t launch_prefill_pair(const CUtensorMap &qmap, const CUtensorMap &kmap32, const CUtensorMap &vmap,
                                 const PrefillParams &p, cudaStream_t st)
 {
-    // (the kernel's cluster shape is compiled in: 2 x 1 x 1)
-    if (p.mask) prefill2_kernel<true><<<2 * p.n_cta, kPThreads, PL2::bytes, st>>>(qmap, kmap32, vmap, p);
-    else prefill2_kernel<false><<<2 * p.n_cta, kPThreads, PL2::bytes, st>>>(qmap, kmap32, vmap, p);
+    // (the kernels' cluster shape is compiled in: 2 x 1 x 1); p.nt selects the
+    // form: 4 tiles a pair (prefill2_kernel) or 2 (prefill3_kernel)
+    if (p.nt == 2) {
+        if (p.mask) prefill3_kernel<true><<<2 * p.n_cta, kPThreads, PL3::bytes, st>>>(qmap, kmap32, vmap, p);
+        else prefill3_kernel<false><<<2 * p.n_cta, kPThreads, PL3::bytes, st>>>(qmap, kmap32, vmap, p);
+    } else {
+        if (p.mask) prefill2_kernel<true><<<2 * p.n_cta, kPThreads, PL2::bytes, st>>>(qmap, kmap32, vmap, p);
+        else prefill2_kernel<false><<<2 * p.n_cta, kPThreads, PL2::bytes, st>>>(qmap, kmap32, vmap, p);
+    }
     return cudaGetLastError();
 }
 
