@@ -1048,8 +1048,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 // As prefill2_kernel, but each CTA of the pair holds one 128-row query tile (a
 // block is 2 tb tokens: tile 0 in the even CTA, tile 1 in the odd one) and S
 // covers a whole 128-key K tile: S = Q . K^T with M = 256, N = 128 (each CTA
-// stages K's keys 64*rank .. +63), double-buffered in TMEM (two 128-column
-// buffers, O in columns 256-383), so an S instruction carries twice the math
+// stages K's keys 64*rank .. +63), in three 128-column TMEM buffers (O in
+// columns 384-511; S runs up to two tiles ahead of P . V), so an S
+// instruction carries twice the math
 // of prefill2's N = 64 ones for the same issue and front-end slot.  Eight
 // softmax warps share the tile: two per TMEM lane quarter, each on 64 of a
 // row's 128 keys; the pair exchanges the row's maximum through shared memory
@@ -1063,14 +1064,15 @@ struct PL3 {
     static constexpr uint32_t kKBox = 32 * 128;           // [32 keys][64 halves]
     static constexpr uint32_t kKHalf = 4 * kKBox;         // [2 dim boxes][64 keys][64 halves]
     static constexpr uint32_t kVHalf = kBox;              // [128 keys][this CTA's 64 dims]
-    static constexpr uint32_t kTmO = 256;                 // O's TMEM columns (S buffers at 0, 128)
+    static constexpr int NBUF = 3;                        // S buffers of 128 TMEM columns
+    static constexpr uint32_t kTmO = NBUF * 128;          // O's TMEM columns (after the S buffers)
     static constexpr size_t o_q = 0;
     static constexpr size_t o_k = o_q + kQTile;
     static constexpr size_t o_v = o_k + (size_t)KS * kKHalf;
     static constexpr size_t o_bar = o_v + (size_t)VS * kVHalf;
     // q_full, q_empty, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
-    // s_full[2], p_full[2], o_ready[2], o_full, o_empty, drain[2]
-    static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 6 + 2 + 2;
+    // s_full[NBUF], p_full[NBUF], o_ready[NBUF], o_full, o_empty, drain[2]
+    static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 3 * NBUF + 2 + 2;
     static constexpr size_t o_tm = o_bar + (size_t)NBAR * 8;
     static constexpr size_t o_red = (o_tm + 16 + 15) / 16 * 16;   // [2 tiles' parity][2 halves][128 rows] maxima
     static constexpr size_t o_redl = o_red + 2 * 2 * 128 * 4;     // [2 halves][128 rows] row sums
@@ -1087,16 +1089,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 {
     constexpr int D = 128;
     using L = PL3;
-    constexpr int KS = L::KS, VS = L::VS;
+    constexpr int KS = L::KS, VS = L::VS, NBUF = L::NBUF;
     extern __shared__ __align__(1024) unsigned char smem[];
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::o_bar);
     uint64_t *q_full = bar, *q_empty = bar + 1;
     uint64_t *k_full = bar + 2, *k_empty = k_full + KS;
     uint64_t *v_full = k_empty + KS, *v_empty = v_full + VS;
     uint64_t *s_full = v_empty + VS;   // [buffer]
-    uint64_t *p_full = s_full + 2;     // [buffer] (the even CTA's: both CTAs' softmax warps)
-    uint64_t *o_ready = p_full + 2;    // [buffer]: the P . V that read the buffer's P has completed
-    uint64_t *o_full = o_ready + 2, *o_empty = o_full + 1;
+    uint64_t *p_full = s_full + NBUF;  // [buffer] (the even CTA's: both CTAs' softmax warps)
+    uint64_t *o_ready = p_full + NBUF; // [buffer]: the P . V that read the buffer's P has completed
+    uint64_t *o_full = o_ready + NBUF, *o_empty = o_full + 1;
     uint64_t *drain = o_empty + 1;     // [issuer]
     uint32_t *tm_slot = reinterpret_cast<uint32_t *>(smem + L::o_tm);
     float *red = reinterpret_cast<float *>(smem + L::o_red);
@@ -1110,7 +1112,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     if (tid == 0) {
         for (int i = 0; i < L::NBAR; i++) {
             const uint64_t *bi = &bar[i];
-            const bool arrivals = (bi >= p_full && bi < p_full + 2) || bi == o_empty;   // 8 warps x 2 CTAs
+            const bool arrivals = (bi >= p_full && bi < p_full + NBUF) || bi == o_empty;   // 8 warps x 2 CTAs
             mbar_init(&bar[i], arrivals ? 16 : 1);
         }
         flags[0] = 0;
@@ -1197,15 +1199,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                     if (!wt(q_full, k & 1)) return false;
                     for (; i < i1; i++) {
                         if (!wt(&k_full[i % KS], (i / KS) & 1)) return false;
-                        // the buffer is free once the P . V of tile i-2 has read its P
-                        if (i >= 2 && !wt(&o_ready[i & 1], ((i - 2) >> 1) & 1)) return false;
+                        // the buffer is free once the P . V of tile i-NBUF has read its P
+                        if (i >= NBUF && !wt(&o_ready[i % NBUF], ((i - NBUF) / NBUF) & 1)) return false;
                         tc_fence_after();
                         const uint32_t kt = sk + (i % KS) * L::kKHalf;
 #pragma unroll
                         for (int kk = 0; kk < D / 16; kk++)
-                            umma_ss2(tmem + (i & 1) * 128, sdesc_k_sw128(sq + (kk >> 2) * kBox + (kk & 3) * 32),
+                            umma_ss2(tmem + (i % NBUF) * 128, sdesc_k_sw128(sq + (kk >> 2) * kBox + (kk & 3) * 32),
                                      sdesc_k_sw128(kt + (kk >> 2) * 2 * L::kKBox + (kk & 3) * 32), idS, kk > 0);
-                        umma_commit2_mc(&s_full[i & 1], 3);
+                        umma_commit2_mc(&s_full[i % NBUF], 3);
                         umma_commit2_mc(&k_empty[i % KS], 3);
                         if (i == i1 - 1) umma_commit2_mc(q_empty, 3);
                     }
@@ -1215,7 +1217,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 for_segments(p, c, [&](int k, const Seg &sg) {
                     const int i0 = i, i1 = i + (sg.t1 - sg.t0);
                     for (; i < i1; i++) {
-                        if (!wt(&p_full[i & 1], (i >> 1) & 1)) return false;
+                        if (!wt(&p_full[i % NBUF], (i / NBUF) & 1)) return false;
                         if (!wt(&v_full[i % VS], (i / VS) & 1)) return false;
                         if (i == i0 && k > 0 && !wt(o_empty, (k - 1) & 1)) return false;
                         tc_fence_after();
@@ -1223,9 +1225,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                         const uint32_t vt = sv + (i % VS) * L::kVHalf;
 #pragma unroll
                         for (int kk = 0; kk < 8; kk++)
-                            umma_ts2(tmem + L::kTmO, tmem + (i & 1) * 128 + kk * 8, sdesc_mn_sw128(vt + kk * 2048, kBox),
+                            umma_ts2(tmem + L::kTmO, tmem + (i % NBUF) * 128 + kk * 8, sdesc_mn_sw128(vt + kk * 2048, kBox),
                                      idO, !(i == i0 && kk == 0));
-                        umma_commit2_mc(&o_ready[i & 1], 3);
+                        umma_commit2_mc(&o_ready[i % NBUF], 3);
                         umma_commit2_mc(&v_empty[i % VS], 3);
                         if (i == i1 - 1) umma_commit2_mc(o_full, 3);
                     }
@@ -1268,8 +1270,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             const int i0 = i, i1 = i + (sg.t1 - sg.t0);
             float m = -INFINITY, l = 0.0f;   // running max (log2 units, shared by the halves); this half's sum
             for (; i < i1; i++) {
-                const int bf = i & 1;
-                const bool got = !bad && mbar_wait_ab(&s_full[bf], (i >> 1) & 1, p.limit_ns, flags);
+                const int bf = i % NBUF;
+                const bool got = !bad && mbar_wait_ab(&s_full[bf], (i / NBUF) & 1, p.limit_ns, flags);
                 if (leave(!got)) return false;
                 tc_fence_after();
                 uint32_t v[64];
@@ -1299,7 +1301,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 // tile: the next meeting orders a reuse after the partner's read);
                 // past this barrier S of the buffer is in both halves' registers,
                 // so P may overwrite its first 64 columns
-                float *rm = red + bf * 256;
+                float *rm = red + (i & 1) * 256;
                 rm[half * 128 + row] = max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
                 named_sync(pair_bar, 64);
                 const float mx = fmaxf(rm[row], rm[128 + row]);
@@ -1334,7 +1336,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 l += sa.x + sa.y;
                 if (i > i0 && __any_sync(0xffffffffu, resc)) {
                     // this half's 64 dims of O, once the last P . V into it has completed
-                    if (mbar_wait_ab(&o_ready[(i - 1) & 1], ((i - 1) >> 1) & 1, p.limit_ns, flags)) {
+                    if (mbar_wait_ab(&o_ready[(i - 1) % NBUF], ((i - 1) / NBUF) & 1, p.limit_ns, flags)) {
                         tc_fence_after();
                         const float fo = resc ? f : 1.0f;
 #pragma unroll 1
