@@ -1051,13 +1051,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 // stages K's keys 64*rank .. +63), in three 128-column TMEM buffers (O in
 // columns 384-511; S runs up to two tiles ahead of P . V), so an S
 // instruction carries twice the math
-// of prefill2's N = 64 ones for the same issue and front-end slot.  Eight
-// softmax warps share the tile: two per TMEM lane quarter, each on 64 of a
-// row's 128 keys; the pair exchanges the row's maximum through shared memory
-// (a 64-thread named barrier per quarter) so both halves use one running
-// maximum, and each keeps its half of the row sum (added at the segment's
-// end) and rescales its half of the row's O.  P (F16 pairs) overwrites S's
-// first 64 columns after both halves have read S.
+// of prefill2's N = 64 ones for the same issue and front-end slot.  The
+// softmax runs in two sets of four warps that take the tiles in turn (below),
+// a thread one row's 128 keys in two passes over S (the maximum, then P);
+// P (F16 pairs) overwrites S's first 64 columns.
 struct PL3 {
     static constexpr int KS = 6, VS = 4;
     static constexpr uint32_t kQTile = 2 * kBox;          // 128 rows x 128 halves
@@ -1074,9 +1071,14 @@ struct PL3 {
     // s_full[NBUF], p_full[NBUF], o_ready[NBUF], o_full, o_empty, drain[2]
     static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 3 * NBUF + 2 + 2;
     static constexpr size_t o_tm = o_bar + (size_t)NBAR * 8;
-    static constexpr size_t o_red = (o_tm + 16 + 15) / 16 * 16;   // [2 tiles' parity][2 halves][128 rows] maxima
-    static constexpr size_t o_redl = o_red + 2 * 2 * 128 * 4;     // [2 halves][128 rows] row sums
-    static constexpr size_t o_flags = o_redl + 2 * 128 * 4;
+    // the softmax sets' hand-offs: the running max after a tile [128 rows]
+    // (tile tag << 32 | max bits), and at a segment's end each set's (max,
+    // sum) [2 segment parities][2 sets][128 rows] (segment tag << 32 | max
+    // bits, the sum beside it)
+    static constexpr size_t o_hand = (o_tm + 16 + 15) / 16 * 16;
+    static constexpr size_t o_fin = o_hand + 128 * 8;
+    static constexpr size_t o_finl = o_fin + 2 * 2 * 128 * 8;
+    static constexpr size_t o_flags = o_finl + 2 * 2 * 128 * 4;
     static constexpr size_t bytes = o_flags + 16;
     static_assert(bytes <= 227 * 1024, "shared memory of the one-tile pair kernel");
     static_assert(o_k % 1024 == 0 && o_v % 1024 == 0, "swizzled boxes 1024-byte aligned");
@@ -1101,8 +1103,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     uint64_t *o_full = o_ready + NBUF, *o_empty = o_full + 1;
     uint64_t *drain = o_empty + 1;     // [issuer]
     uint32_t *tm_slot = reinterpret_cast<uint32_t *>(smem + L::o_tm);
-    float *red = reinterpret_cast<float *>(smem + L::o_red);
-    float *redl = reinterpret_cast<float *>(smem + L::o_redl);
+    volatile unsigned long long *hand = reinterpret_cast<volatile unsigned long long *>(smem + L::o_hand);
+    volatile unsigned long long *fin = reinterpret_cast<volatile unsigned long long *>(smem + L::o_fin);
+    volatile float *finl = reinterpret_cast<volatile float *>(smem + L::o_finl);
     volatile int *flags = reinterpret_cast<volatile int *>(smem + L::o_flags);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rank = (int)cluster_rank(), c = blockIdx.x >> 1;
@@ -1112,11 +1115,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     if (tid == 0) {
         for (int i = 0; i < L::NBAR; i++) {
             const uint64_t *bi = &bar[i];
-            const bool arrivals = (bi >= p_full && bi < p_full + NBUF) || bi == o_empty;   // 8 warps x 2 CTAs
-            mbar_init(&bar[i], arrivals ? 16 : 1);
+            // p_full: the 4 warps of a tile's softmax set in both CTAs; o_empty:
+            // all 8 softmax warps of both
+            mbar_init(&bar[i], (bi >= p_full && bi < p_full + NBUF) ? 8 : bi == o_empty ? 16 : 1);
         }
         flags[0] = 0;
         fence_mbar_init();
+    }
+    for (int x = tid; x < 128 + 2 * 2 * 128; x += kPThreads) {   // no tag matches 0
+        if (x < 128) hand[x] = 0ull;
+        else fin[x - 128] = 0ull;
     }
     if (warp == 1) {
         tmem_alloc2(tm_slot, 512);
@@ -1239,26 +1247,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
     } else if (warp >= 2 && warp < 10) {
         // ================= softmax / epilogue (both CTAs, their own tile) =================
-        const int q4 = warp & 3, half = (warp - 2) >> 2;   // lane quarter; the row's keys / dims half
+        // Two sets of four warps (warps 2-5, 6-9) take the tiles in turn (set
+        // = tile parity), a thread one row's 128 keys: the two warps of a lane
+        // quarter work on different tiles, so one's latency hides behind the
+        // other's work.  The running max goes from a tile's set to the next
+        // tile's through a tagged shared slot (bounded polls, no barrier a
+        // set could be left waiting on); each set keeps its own share of the
+        // row sum, relative to the max it last used; the tile that raises the
+        // max rescales the row of O (after the previous tile's P . V).
+        const int q4 = warp & 3, set = (warp - 2) >> 2;
         const int row = q4 * 32 + lane;
         const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-        const uint32_t tO = trow + L::kTmO + half * 64;
+        const uint32_t tO = trow + L::kTmO;
         const int tok_in = row / p.r, hd = row - tok_in * p.r;
         const bool row_ok = tok_in < p.tb;
         const float cs = p.scale * kLog2e;
         const uint64_t cs2 = pk2(cs, cs);
         const uint32_t pf_lead = lead(&p_full[0]), oe_lead = lead(o_empty);
-        // the two warps of this lane quarter meet on a named barrier; every
-        // decision to leave is taken there together (barrier.red.or), so
-        // neither is ever left waiting for a partner that gave up
-        const uint32_t pair_bar = 1 + q4;
-        bool bad = false;   // a bounded wait of this warp expired since the last meeting
-        auto leave = [&](bool mine) {
-            if (named_sync_or(pair_bar, 64, mine)) {
-                give_up(p, flags, 1u);
-                return true;
+        // a tagged slot's value once its tag reads `tag`; false when the wait
+        // expires or the CTA gave up
+        auto poll = [&](const volatile unsigned long long *slot, unsigned tag, unsigned long long &val) {
+            const uint64_t t0 = globaltimer();
+            for (uint32_t n = 0;; n++) {
+                val = *slot;
+                if ((unsigned)(val >> 32) == tag) return true;
+                if ((n & 15u) == 15u && (flags[0] || globaltimer() - t0 > p.limit_ns)) return false;
             }
-            return false;
+        };
+        // S (or the caller's mask added) of keys [64 hc, 64 hc + 64) of the
+        // tile's row in v, keys past the row's last visible one at -inf
+        auto load_s = [&](uint32_t tS, int hc, int64_t kb, int nvis, int tok, bool valid, float mscl,
+                          uint32_t (&v)[64]) {
+            tmem_ld32(tS + hc * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
+            tmem_ld32(tS + hc * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+            tmem_wait_ld();
+            const int nv = max(0, min(64, nvis - hc * 64));
+            if (!__all_sync(0xffffffffu, nv == 64)) {
+#pragma unroll
+                for (int e = 0; e < 64; e++)
+                    if (e >= nv) v[e] = __float_as_uint(-INFINITY);
+            }
+            if constexpr (MASKED)
+                if (valid) add_mask(p, tok, kb + hc * 64, nv, mscl, v);
         };
         int i = 0;
         for_segments(p, c, [&](int k, const Seg &sg) {
@@ -1268,88 +1298,94 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             const int64_t lim = !valid ? -1 : p.mask ? p.n_past + p.n_new - 1 : p.n_past + tok;
             const float mscl = p.mask ? __fdiv_rn(1.0f, p.scale) : 0.0f;
             const int i0 = i, i1 = i + (sg.t1 - sg.t0);
-            float m = -INFINITY, l = 0.0f;   // running max (log2 units, shared by the halves); this half's sum
+            float mX = -INFINITY, lX = 0.0f;   // this set's share of the row sum, relative to mX
             for (; i < i1; i++) {
+                if ((i & 1) != set) continue;
                 const int bf = i % NBUF;
-                const bool got = !bad && mbar_wait_ab(&s_full[bf], (i / NBUF) & 1, p.limit_ns, flags);
-                if (leave(!got)) return false;
+                if (!mbar_wait_ab(&s_full[bf], (i / NBUF) & 1, p.limit_ns, flags)) {
+                    give_up(p, flags, 1u);
+                    return false;
+                }
                 tc_fence_after();
-                uint32_t v[64];
                 const uint32_t tS = trow + bf * 128;
-                tmem_ld32(tS + half * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
-                tmem_ld32(tS + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-                tmem_wait_ld();
-                const int64_t kb = (int64_t)(sg.t0 + (i - i0)) * 128 + half * 64;   // this half's first key
-                const int nvis = (int)max((int64_t)0, min((int64_t)64, lim - kb + 1));
-                const bool full = __all_sync(0xffffffffu, nvis == 64);
-                if (!full) {
+                const int64_t kb = (int64_t)(sg.t0 + (i - i0)) * 128;   // the tile's first key
+                const int nvis = (int)max((int64_t)0, min((int64_t)128, lim - kb + 1));
+                uint32_t v[64];
+                float mx = -INFINITY;
+#pragma unroll 1
+                for (int hc = 0; hc < 2; hc++) {   // pass 1: the tile's row maximum
+                    load_s(tS, hc, kb, nvis, tok, valid, mscl, v);
+                    float m4[4];
 #pragma unroll
-                    for (int e = 0; e < 64; e++)
-                        if (e >= nvis) v[e] = __float_as_uint(-INFINITY);
+                    for (int a = 0; a < 4; a++) m4[a] = fmaxf(__uint_as_float(v[a]), __uint_as_float(v[4 + a]));
+#pragma unroll
+                    for (int e = 8; e < 64; e += 8)
+#pragma unroll
+                        for (int a = 0; a < 4; a++)
+                            m4[a] = max3(m4[a], __uint_as_float(v[e + a]), __uint_as_float(v[e + 4 + a]));
+                    mx = max3(mx, fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
                 }
-                if constexpr (MASKED)
-                    if (valid) add_mask(p, tok, kb, nvis, mscl, v);
-                float m4[4];
-#pragma unroll
-                for (int a = 0; a < 4; a++) m4[a] = fmaxf(__uint_as_float(v[a]), __uint_as_float(v[4 + a]));
-#pragma unroll
-                for (int e = 8; e < 64; e += 8)
-#pragma unroll
-                    for (int a = 0; a < 4; a++)
-                        m4[a] = max3(m4[a], __uint_as_float(v[e + a]), __uint_as_float(v[e + 4 + a]));
-                // the row's maximum over both halves (buffers alternate with the
-                // tile: the next meeting orders a reuse after the partner's read);
-                // past this barrier S of the buffer is in both halves' registers,
-                // so P may overwrite its first 64 columns
-                float *rm = red + (i & 1) * 256;
-                rm[half * 128 + row] = max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
-                named_sync(pair_bar, 64);
-                const float mx = fmaxf(rm[row], rm[128 + row]);
-                float f = 1.0f;
-                bool resc = false;
+                // the running max after the previous tile (the other set's), raised lazily
+                float mprev = -INFINITY;
+                if (i > i0) {
+                    unsigned long long hv;
+                    if (!poll(hand + row, (unsigned)i, hv)) {
+                        give_up(p, flags, 1u);
+                        return false;
+                    }
+                    mprev = __uint_as_float((unsigned)hv);
+                }
+                float m = mprev;
                 const float xm = mx * cs;
-                if (xm > m + kLazy) {
-                    f = ex2_approx(m - xm);
-                    resc = m != -INFINITY;
-                    l *= f;
-                    m = xm;
+                if (xm > m + kLazy) m = xm;
+                if (i + 1 < i1) hand[row] = ((unsigned long long)(i + 1) << 32) | __float_as_uint(m);
+                if (m != mX) {   // this set's share follows the max
+                    lX = mX == -INFINITY ? 0.0f : lX * ex2_approx(mX - m);
+                    mX = m;
                 }
+                const bool resc = i > i0 && m != mprev && mprev != -INFINITY;   // O holds earlier tiles at mprev
+                const float f = resc ? ex2_approx(mprev - m) : 1.0f;
                 const float nm = m == -INFINITY ? 0.0f : -m;
                 const uint64_t nm2 = pk2(nm, nm);
                 uint64_t s2[2] = {0ull, 0ull};
+#pragma unroll 1
+                for (int hc = 0; hc < 2; hc++) {   // pass 2: P = F16(2^(s*cs - m)) over S's first 64 columns
+                    load_s(tS, hc, kb, nvis, tok, valid, mscl, v);
 #pragma unroll
-                for (int u = 0; u < 2; u++) {
-                    uint32_t pkd[16];
+                    for (int u = 0; u < 2; u++) {
+                        uint32_t pkd[16];
 #pragma unroll
-                    for (int e = 0; e < 16; e++) {
-                        const float2 xy = up2(fma2(pk2(__uint_as_float(v[u * 32 + 2 * e]),
-                                                       __uint_as_float(v[u * 32 + 2 * e + 1])), cs2, nm2));
-                        const float x0 = ex2_approx(xy.x), x1 = ex2_approx(xy.y);
-                        s2[e & 1] = add2(s2[e & 1], pk2(x0, x1));
-                        const __half2 h2 = __floats2half2_rn(x0, x1);
-                        pkd[e] = *reinterpret_cast<const uint32_t *>(&h2);
+                        for (int e = 0; e < 16; e++) {
+                            const float2 xy = up2(fma2(pk2(__uint_as_float(v[u * 32 + 2 * e]),
+                                                           __uint_as_float(v[u * 32 + 2 * e + 1])), cs2, nm2));
+                            const float x0 = ex2_approx(xy.x), x1 = ex2_approx(xy.y);
+                            s2[e & 1] = add2(s2[e & 1], pk2(x0, x1));
+                            const __half2 h2 = __floats2half2_rn(x0, x1);
+                            pkd[e] = *reinterpret_cast<const uint32_t *>(&h2);
+                        }
+                        // keys 64 hc + 32 u .. +31 -> packed columns 32 hc + 16 u .. +15
+                        // (S columns this thread has already read)
+                        tmem_st16(tS + hc * 32 + u * 16, pkd);
                     }
-                    // keys half*64 + 32u .. +31 -> packed columns half*32 + 16u .. +15
-                    tmem_st16(tS + half * 32 + u * 16, pkd);
                 }
                 const float2 sa = up2(add2(s2[0], s2[1]));
-                l += sa.x + sa.y;
+                lX += sa.x + sa.y;
                 if (i > i0 && __any_sync(0xffffffffu, resc)) {
-                    // this half's 64 dims of O, once the last P . V into it has completed
-                    if (mbar_wait_ab(&o_ready[(i - 1) % NBUF], ((i - 1) / NBUF) & 1, p.limit_ns, flags)) {
-                        tc_fence_after();
-                        const float fo = resc ? f : 1.0f;
+                    // the row of O, once the previous tile's P . V has completed
+                    if (!mbar_wait_ab(&o_ready[(i - 1) % NBUF], ((i - 1) / NBUF) & 1, p.limit_ns, flags)) {
+                        give_up(p, flags, 1u);
+                        return false;
+                    }
+                    tc_fence_after();
+                    const float fo = resc ? f : 1.0f;
 #pragma unroll 1
-                        for (int ch = 0; ch < 4; ch++) {
-                            uint32_t o[16];
-                            tmem_ld16(tO + ch * 16, o);
-                            tmem_wait_ld();
+                    for (int ch = 0; ch < D / 16; ch++) {
+                        uint32_t o[16];
+                        tmem_ld16(tO + ch * 16, o);
+                        tmem_wait_ld();
 #pragma unroll
-                            for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * fo);
-                            tmem_st16(tO + ch * 16, o);
-                        }
-                    } else {
-                        bad = true;   // reported at the next meeting
+                        for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * fo);
+                        tmem_st16(tO + ch * 16, o);
                     }
                 }
                 tmem_wait_st();
@@ -1357,12 +1393,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive_remote(pf_lead + (uint32_t)(bf * 8));
             }
-            // the row's sum: both halves; the output once the last P . V is in O
-            redl[half * 128 + row] = l;
-            if (leave(bad)) return false;
-            const float lt = redl[row] + redl[128 + row];
-            const bool got = mbar_wait_ab(o_full, k & 1, p.limit_ns, flags);
-            if (leave(!got)) return false;   // (also: both read redl before it is written again)
+            // the row sum over both sets (segment parity keeps a slot from
+            // being rewritten before the other set has read it)
+            const int sp = k & 1;
+            finl[(sp * 2 + set) * 128 + row] = lX;
+            __threadfence_block();
+            fin[(sp * 2 + set) * 128 + row] = ((unsigned long long)(k + 1) << 32) | __float_as_uint(mX);
+            unsigned long long ov;
+            if (!poll(fin + (sp * 2 + (set ^ 1)) * 128 + row, (unsigned)(k + 1), ov)) {
+                give_up(p, flags, 1u);
+                return false;
+            }
+            __threadfence_block();
+            const float mo = __uint_as_float((unsigned)ov), lo = finl[(sp * 2 + (set ^ 1)) * 128 + row];
+            const float m = fmaxf(mX, mo);   // the running max after the segment's last tile
+            const float lt = (mX == -INFINITY ? 0.0f : lX * ex2_approx(mX - m)) +
+                             (mo == -INFINITY ? 0.0f : lo * ex2_approx(mo - m));
+            if (!mbar_wait_ab(o_full, k & 1, p.limit_ns, flags)) {
+                give_up(p, flags, 1u);
+                return false;
+            }
             tc_fence_after();
             const bool whole = sg.t0 == 0 && sg.t1 == nt_of(p, b);
             const int64_t slot = (((int64_t)c * p.kseg + k) * 2 + rank) * 128 + row;
@@ -1371,14 +1421,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             if (whole) {
                 scl = lt > 0.0f ? __fdiv_rn(1.0f, lt) : no_key_scale(p);
             } else {
-                if (half == 0) reinterpret_cast<float2 *>(p.pstat)[slot] = make_float2(m, lt);
+                if (set == 0) reinterpret_cast<float2 *>(p.pstat)[slot] = make_float2(m, lt);
                 dst = p.pout + slot * D;
             }
             const uint64_t pol = policy_evict_last();
 #pragma unroll 1
-            for (int ch = 0; ch < 2; ch++) {   // this half's 64 dims
+            for (int ch = 0; ch < 2; ch++) {   // this set's 64 dims of the row
                 uint32_t o[32];
-                tmem_ld32(tO + ch * 32, o);
+                tmem_ld32(tO + set * 64 + ch * 32, o);
                 tmem_wait_ld();
                 if (valid)
 #pragma unroll
@@ -1386,7 +1436,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
                         const float4 val = make_float4(__uint_as_float(o[4 * q]) * scl, __uint_as_float(o[4 * q + 1]) * scl,
                                                        __uint_as_float(o[4 * q + 2]) * scl,
                                                        __uint_as_float(o[4 * q + 3]) * scl);
-                        float *d4 = dst + half * 64 + ch * 32 + 4 * q;
+                        float *d4 = dst + set * 64 + ch * 32 + 4 * q;
                         if (whole) *reinterpret_cast<float4 *>(d4) = val;
                         else st_v4_hint(d4, val, pol);
                     }
