@@ -303,7 +303,6 @@ struct kv_ctx {
     // boxes; empty when the device cannot run its clusters (or
     // KV_B200_PREFILL_PAIR=0)
     std::vector<CUtensorMap> pf2_kmaps;
-    int pf_pair_tiles = 4;   // query tiles a CTA pair holds: 4 (two a CTA), or 2 (KV_B200_PREFILL_PAIR=2)
     int pf_tb = 0;                          // tokens per 128-row query tile
     CUtensorMap qmap{};                     // qbuf [n_batch_max][hq_loc][D], box 64 x r x tb
     float *pf_stat = nullptr;               // [sm_count][kseg][2 tiles][128][2]
@@ -983,7 +982,6 @@ static int alloc_impl(const kv_config *cfg_in, kv_ctx **out)
         }
         if (pfD == 128 && ctx->D == 128) {
             const char *pe = getenv("KV_B200_PREFILL_PAIR");
-            if (pe && pe[0] == '2') ctx->pf_pair_tiles = 2;
             int clusters = 0;
             e = (pe && pe[0] == '0') ? cudaSuccess : kvb::prefill_pair_prepare(&clusters);
             if (e != cudaSuccess) {   // no pair kernel on this device: the one-CTA kernel runs
@@ -1167,7 +1165,7 @@ int prefill(kv_ctx *ctx, const CUtensorMap &km, const CUtensorMap &vm, const CUt
     pp.n_past = n_past;
     pp.n_new = n_new;
     pp.tb = ctx->pf_tb;
-    pp.nt = cta2 ? ctx->pf_pair_tiles : kvb::prefill_tiles(ctx->pf_D);
+    pp.nt = cta2 ? 4 : kvb::prefill_tiles(ctx->pf_D);
     pp.dv = ctx->D;
     pp.nblk = (n_new + pp.nt * pp.tb - 1) / (pp.nt * pp.tb);
     std::vector<int64_t> nt(pp.nblk);

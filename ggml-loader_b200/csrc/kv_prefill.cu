@@ -1043,428 +1043,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// the CTA-pair kernel with one query tile a CTA and 128-key S (head_dim 128)
-// ---------------------------------------------------------------------------
-// As prefill2_kernel, but each CTA of the pair holds one 128-row query tile (a
-// block is 2 tb tokens: tile 0 in the even CTA, tile 1 in the odd one) and S
-// covers a whole 128-key K tile: S = Q . K^T with M = 256, N = 128 (each CTA
-// stages K's keys 64*rank .. +63), in three 128-column TMEM buffers (O in
-// columns 384-511; S runs up to two tiles ahead of P . V), so an S
-// instruction carries twice the math
-// of prefill2's N = 64 ones for the same issue and front-end slot.  The
-// softmax runs in two sets of four warps that take the tiles in turn (below),
-// a thread one row's 128 keys in two passes over S (the maximum, then P);
-// P (F16 pairs) overwrites S's first 64 columns.
-struct PL3 {
-    static constexpr int KS = 6, VS = 4;
-    static constexpr uint32_t kQTile = 2 * kBox;          // 128 rows x 128 halves
-    static constexpr uint32_t kKBox = 32 * 128;           // [32 keys][64 halves]
-    static constexpr uint32_t kKHalf = 4 * kKBox;         // [2 dim boxes][64 keys][64 halves]
-    static constexpr uint32_t kVHalf = kBox;              // [128 keys][this CTA's 64 dims]
-    static constexpr int NBUF = 3;                        // S buffers of 128 TMEM columns
-    static constexpr uint32_t kTmO = NBUF * 128;          // O's TMEM columns (after the S buffers)
-    static constexpr size_t o_q = 0;
-    static constexpr size_t o_k = o_q + kQTile;
-    static constexpr size_t o_v = o_k + (size_t)KS * kKHalf;
-    static constexpr size_t o_bar = o_v + (size_t)VS * kVHalf;
-    // q_full, q_empty, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS],
-    // s_full[NBUF], p_full[NBUF], o_ready[NBUF], o_full, o_empty, drain[2]
-    static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 3 * NBUF + 2 + 2;
-    static constexpr size_t o_tm = o_bar + (size_t)NBAR * 8;
-    // the softmax sets' hand-offs: the running max after a tile [128 rows]
-    // (tile tag << 32 | max bits), and at a segment's end each set's (max,
-    // sum) [2 segment parities][2 sets][128 rows] (segment tag << 32 | max
-    // bits, the sum beside it)
-    static constexpr size_t o_hand = (o_tm + 16 + 15) / 16 * 16;
-    static constexpr size_t o_fin = o_hand + 128 * 8;
-    static constexpr size_t o_finl = o_fin + 2 * 2 * 128 * 8;
-    static constexpr size_t o_flags = o_finl + 2 * 2 * 128 * 4;
-    static constexpr size_t bytes = o_flags + 16;
-    static_assert(bytes <= 227 * 1024, "shared memory of the one-tile pair kernel");
-    static_assert(o_k % 1024 == 0 && o_v % 1024 == 0, "swizzled boxes 1024-byte aligned");
-};
-
-template <bool MASKED>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
-    prefill3_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap32,
-                    const __grid_constant__ CUtensorMap vmap, const PrefillParams p)
-{
-    constexpr int D = 128;
-    using L = PL3;
-    constexpr int KS = L::KS, VS = L::VS, NBUF = L::NBUF;
-    extern __shared__ __align__(1024) unsigned char smem[];
-    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::o_bar);
-    uint64_t *q_full = bar, *q_empty = bar + 1;
-    uint64_t *k_full = bar + 2, *k_empty = k_full + KS;
-    uint64_t *v_full = k_empty + KS, *v_empty = v_full + VS;
-    uint64_t *s_full = v_empty + VS;   // [buffer]
-    uint64_t *p_full = s_full + NBUF;  // [buffer] (the even CTA's: both CTAs' softmax warps)
-    uint64_t *o_ready = p_full + NBUF; // [buffer]: the P . V that read the buffer's P has completed
-    uint64_t *o_full = o_ready + NBUF, *o_empty = o_full + 1;
-    uint64_t *drain = o_empty + 1;     // [issuer]
-    uint32_t *tm_slot = reinterpret_cast<uint32_t *>(smem + L::o_tm);
-    volatile unsigned long long *hand = reinterpret_cast<volatile unsigned long long *>(smem + L::o_hand);
-    volatile unsigned long long *fin = reinterpret_cast<volatile unsigned long long *>(smem + L::o_fin);
-    volatile float *finl = reinterpret_cast<volatile float *>(smem + L::o_finl);
-    volatile int *flags = reinterpret_cast<volatile int *>(smem + L::o_flags);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int rank = (int)cluster_rank(), c = blockIdx.x >> 1;
-    auto lead = [&](uint64_t *b) { return mapa(smem_addr(b), 0); };
-    int issued_q = 0, issued_k = 0, issued_v = 0;
-
-    if (tid == 0) {
-        for (int i = 0; i < L::NBAR; i++) {
-            const uint64_t *bi = &bar[i];
-            // p_full: the 4 warps of a tile's softmax set in both CTAs; o_empty:
-            // all 8 softmax warps of both
-            mbar_init(&bar[i], (bi >= p_full && bi < p_full + NBUF) ? 8 : bi == o_empty ? 16 : 1);
-        }
-        flags[0] = 0;
-        fence_mbar_init();
-    }
-    for (int x = tid; x < 128 + 2 * 2 * 128; x += kPThreads) {   // no tag matches 0
-        if (x < 128) hand[x] = 0ull;
-        else fin[x - 128] = 0ull;
-    }
-    if (warp == 1) {
-        tmem_alloc2(tm_slot, 512);
-        tmem_relinquish2();
-    }
-    tc_fence_before();
-    __syncthreads();
-    cluster_sync_all();
-    tc_fence_after();
-    const uint32_t tmem = *tm_slot;
-    pdl_launch_dependents();
-
-    if (warp == 0) {
-        // ================= TMA (both CTAs: their tile and halves) =================
-        if (lane == 0) {
-            prefetch_tmap(&qmap);
-            prefetch_tmap(&kmap32);
-            prefetch_tmap(&vmap);
-            const uint32_t qbytes = (uint32_t)(p.r * p.tb) * 128u * 2u;   // one Q tile (zero fill counts)
-            for_segments(p, c, [&](int k, const Seg &sg) {
-                const int kvh = sg.pair / p.nblk, b = sg.pair % p.nblk;
-                if (k > 0 && !mbar_wait_ab(q_empty, (k - 1) & 1, p.limit_ns, flags)) {
-                    give_up(p, flags, 2u);
-                    return false;
-                }
-                if (rank == 0) mbar_arrive_expect_tx(q_full, 2 * qbytes);
-#pragma unroll
-                for (int bx = 0; bx < 2; bx++)
-                    tma_load_3d_pair(smem + L::o_q + bx * kBox, &qmap, lead(q_full), bx * 64, kvh * p.r,
-                                     (2 * b + rank) * p.tb);
-                issued_q++;
-                for (int t = sg.t0; t < sg.t1; t++) {
-                    const int s = issued_k % KS;
-                    if (issued_k >= KS && !mbar_wait_ab(&k_empty[s], ((issued_k / KS) - 1) & 1, p.limit_ns, flags)) {
-                        give_up(p, flags, 2u);
-                        return false;
-                    }
-                    if (rank == 0) mbar_arrive_expect_tx(&k_full[s], 2 * L::kKHalf);
-                    // this CTA's 64 keys of the tile, [dim box][64 keys] (two 32-key boxes each)
-#pragma unroll
-                    for (int bx = 0; bx < 2; bx++)
-#pragma unroll
-                        for (int kh = 0; kh < 2; kh++)
-                            tma_load_3d_pair(smem + L::o_k + s * L::kKHalf + bx * 2 * L::kKBox + kh * L::kKBox,
-                                             &kmap32, lead(&k_full[s]), bx * 64, kvh, t * 128 + rank * 64 + kh * 32);
-                    issued_k++;
-                    const int sv = issued_v % VS;
-                    if (issued_v >= VS && !mbar_wait_ab(&v_empty[sv], ((issued_v / VS) - 1) & 1, p.limit_ns, flags)) {
-                        give_up(p, flags, 2u);
-                        return false;
-                    }
-                    if (rank == 0) mbar_arrive_expect_tx(&v_full[sv], 2 * L::kVHalf);
-                    tma_load_3d_pair(smem + L::o_v + sv * L::kVHalf, &vmap, lead(&v_full[sv]), rank * 64, kvh,
-                                     t * 128);
-                    issued_v++;
-                }
-                return true;
-            });
-        }
-    } else if (warp == 1 || warp == 10) {
-        // ================= MMA issue (even CTA): S (warp 1), P . V (warp 10) =================
-        const int role = warp == 1 ? 0 : 1;
-        if (lane == 0 && rank == 0) {
-            constexpr uint32_t idS = idesc_f16_f32(256, 128, false);
-            constexpr uint32_t idO = idesc_f16_f32(256, D, true);
-            const uint32_t sq = smem_addr(smem + L::o_q), sk = smem_addr(smem + L::o_k);
-            const uint32_t sv = smem_addr(smem + L::o_v);
-            bool ok = true;
-            auto wt = [&](uint64_t *b, uint32_t par) {
-                if (ok && !mbar_wait_ab(b, par, p.limit_ns, flags)) {
-                    give_up(p, flags, 1u);
-                    ok = false;
-                }
-                return ok;
-            };
-            int i = 0;   // K/V tiles consumed
-            if (role == 0) {
-                for_segments(p, c, [&](int k, const Seg &sg) {
-                    const int i1 = i + (sg.t1 - sg.t0);
-                    if (!wt(q_full, k & 1)) return false;
-                    for (; i < i1; i++) {
-                        if (!wt(&k_full[i % KS], (i / KS) & 1)) return false;
-                        // the buffer is free once the P . V of tile i-NBUF has read its P
-                        if (i >= NBUF && !wt(&o_ready[i % NBUF], ((i - NBUF) / NBUF) & 1)) return false;
-                        tc_fence_after();
-                        const uint32_t kt = sk + (i % KS) * L::kKHalf;
-#pragma unroll
-                        for (int kk = 0; kk < D / 16; kk++)
-                            umma_ss2(tmem + (i % NBUF) * 128, sdesc_k_sw128(sq + (kk >> 2) * kBox + (kk & 3) * 32),
-                                     sdesc_k_sw128(kt + (kk >> 2) * 2 * L::kKBox + (kk & 3) * 32), idS, kk > 0);
-                        umma_commit2_mc(&s_full[i % NBUF], 3);
-                        umma_commit2_mc(&k_empty[i % KS], 3);
-                        if (i == i1 - 1) umma_commit2_mc(q_empty, 3);
-                    }
-                    return true;
-                });
-            } else {
-                for_segments(p, c, [&](int k, const Seg &sg) {
-                    const int i0 = i, i1 = i + (sg.t1 - sg.t0);
-                    for (; i < i1; i++) {
-                        if (!wt(&p_full[i % NBUF], (i / NBUF) & 1)) return false;
-                        if (!wt(&v_full[i % VS], (i / VS) & 1)) return false;
-                        if (i == i0 && k > 0 && !wt(o_empty, (k - 1) & 1)) return false;
-                        tc_fence_after();
-                        // O (+)= P(i) . V(128 keys; 64 of the dims in each CTA)
-                        const uint32_t vt = sv + (i % VS) * L::kVHalf;
-#pragma unroll
-                        for (int kk = 0; kk < 8; kk++)
-                            umma_ts2(tmem + L::kTmO, tmem + (i % NBUF) * 128 + kk * 8, sdesc_mn_sw128(vt + kk * 2048, kBox),
-                                     idO, !(i == i0 && kk == 0));
-                        umma_commit2_mc(&o_ready[i % NBUF], 3);
-                        umma_commit2_mc(&v_empty[i % VS], 3);
-                        if (i == i1 - 1) umma_commit2_mc(o_full, 3);
-                    }
-                    return true;
-                });
-            }
-            umma_commit2(&drain[role]);
-            mbar_wait(&drain[role], 0, p.limit_ns);
-        }
-    } else if (warp >= 2 && warp < 10) {
-        // ================= softmax / epilogue (both CTAs, their own tile) =================
-        // Two sets of four warps (warps 2-5, 6-9) take the tiles in turn (set
-        // = tile parity), a thread one row's 128 keys: the two warps of a lane
-        // quarter work on different tiles, so one's latency hides behind the
-        // other's work.  The running max goes from a tile's set to the next
-        // tile's through a tagged shared slot (bounded polls, no barrier a
-        // set could be left waiting on); each set keeps its own share of the
-        // row sum, relative to the max it last used; the tile that raises the
-        // max rescales the row of O (after the previous tile's P . V).
-        const int q4 = warp & 3, set = (warp - 2) >> 2;
-        const int row = q4 * 32 + lane;
-        const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-        const uint32_t tO = trow + L::kTmO;
-        const int tok_in = row / p.r, hd = row - tok_in * p.r;
-        const bool row_ok = tok_in < p.tb;
-        const float cs = p.scale * kLog2e;
-        const uint64_t cs2 = pk2(cs, cs);
-        const uint32_t pf_lead = lead(&p_full[0]), oe_lead = lead(o_empty);
-        // a tagged slot's value once its tag reads `tag`; false when the wait
-        // expires or the CTA gave up
-        auto poll = [&](const volatile unsigned long long *slot, unsigned tag, unsigned long long &val) {
-            const uint64_t t0 = globaltimer();
-            for (uint32_t n = 0;; n++) {
-                val = *slot;
-                if ((unsigned)(val >> 32) == tag) return true;
-                if ((n & 15u) == 15u && (flags[0] || globaltimer() - t0 > p.limit_ns)) return false;
-            }
-        };
-        // S (or the caller's mask added) of keys [64 hc, 64 hc + 64) of the
-        // tile's row in v, keys past the row's last visible one at -inf
-        auto load_s = [&](uint32_t tS, int hc, int64_t kb, int nvis, int tok, bool valid, float mscl,
-                          uint32_t (&v)[64]) {
-            tmem_ld32(tS + hc * 64, *reinterpret_cast<uint32_t(*)[32]>(v));
-            tmem_ld32(tS + hc * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-            tmem_wait_ld();
-            const int nv = max(0, min(64, nvis - hc * 64));
-            if (!__all_sync(0xffffffffu, nv == 64)) {
-#pragma unroll
-                for (int e = 0; e < 64; e++)
-                    if (e >= nv) v[e] = __float_as_uint(-INFINITY);
-            }
-            if constexpr (MASKED)
-                if (valid) add_mask(p, tok, kb + hc * 64, nv, mscl, v);
-        };
-        int i = 0;
-        for_segments(p, c, [&](int k, const Seg &sg) {
-            const int b = sg.pair % p.nblk, kvh = sg.pair / p.nblk;
-            const int tok = (2 * b + rank) * p.tb + tok_in;
-            const bool valid = row_ok && tok < p.n_new;
-            const int64_t lim = !valid ? -1 : p.mask ? p.n_past + p.n_new - 1 : p.n_past + tok;
-            const float mscl = p.mask ? __fdiv_rn(1.0f, p.scale) : 0.0f;
-            const int i0 = i, i1 = i + (sg.t1 - sg.t0);
-            float mX = -INFINITY, lX = 0.0f;   // this set's share of the row sum, relative to mX
-            for (; i < i1; i++) {
-                if ((i & 1) != set) continue;
-                const int bf = i % NBUF;
-                if (!mbar_wait_ab(&s_full[bf], (i / NBUF) & 1, p.limit_ns, flags)) {
-                    give_up(p, flags, 1u);
-                    return false;
-                }
-                tc_fence_after();
-                const uint32_t tS = trow + bf * 128;
-                const int64_t kb = (int64_t)(sg.t0 + (i - i0)) * 128;   // the tile's first key
-                const int nvis = (int)max((int64_t)0, min((int64_t)128, lim - kb + 1));
-                uint32_t v[64];
-                float mx = -INFINITY;
-#pragma unroll 1
-                for (int hc = 0; hc < 2; hc++) {   // pass 1: the tile's row maximum
-                    load_s(tS, hc, kb, nvis, tok, valid, mscl, v);
-                    float m4[4];
-#pragma unroll
-                    for (int a = 0; a < 4; a++) m4[a] = fmaxf(__uint_as_float(v[a]), __uint_as_float(v[4 + a]));
-#pragma unroll
-                    for (int e = 8; e < 64; e += 8)
-#pragma unroll
-                        for (int a = 0; a < 4; a++)
-                            m4[a] = max3(m4[a], __uint_as_float(v[e + a]), __uint_as_float(v[e + 4 + a]));
-                    mx = max3(mx, fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-                }
-                // the running max after the previous tile (the other set's), raised lazily
-                float mprev = -INFINITY;
-                if (i > i0) {
-                    unsigned long long hv;
-                    if (!poll(hand + row, (unsigned)i, hv)) {
-                        give_up(p, flags, 1u);
-                        return false;
-                    }
-                    mprev = __uint_as_float((unsigned)hv);
-                }
-                float m = mprev;
-                const float xm = mx * cs;
-                if (xm > m + kLazy) m = xm;
-                if (i + 1 < i1) hand[row] = ((unsigned long long)(i + 1) << 32) | __float_as_uint(m);
-                if (m != mX) {   // this set's share follows the max
-                    lX = mX == -INFINITY ? 0.0f : lX * ex2_approx(mX - m);
-                    mX = m;
-                }
-                const bool resc = i > i0 && m != mprev && mprev != -INFINITY;   // O holds earlier tiles at mprev
-                const float f = resc ? ex2_approx(mprev - m) : 1.0f;
-                const float nm = m == -INFINITY ? 0.0f : -m;
-                const uint64_t nm2 = pk2(nm, nm);
-                uint64_t s2[2] = {0ull, 0ull};
-#pragma unroll 1
-                for (int hc = 0; hc < 2; hc++) {   // pass 2: P = F16(2^(s*cs - m)) over S's first 64 columns
-                    load_s(tS, hc, kb, nvis, tok, valid, mscl, v);
-#pragma unroll
-                    for (int u = 0; u < 2; u++) {
-                        uint32_t pkd[16];
-#pragma unroll
-                        for (int e = 0; e < 16; e++) {
-                            const float2 xy = up2(fma2(pk2(__uint_as_float(v[u * 32 + 2 * e]),
-                                                           __uint_as_float(v[u * 32 + 2 * e + 1])), cs2, nm2));
-                            const float x0 = ex2_approx(xy.x), x1 = ex2_approx(xy.y);
-                            s2[e & 1] = add2(s2[e & 1], pk2(x0, x1));
-                            const __half2 h2 = __floats2half2_rn(x0, x1);
-                            pkd[e] = *reinterpret_cast<const uint32_t *>(&h2);
-                        }
-                        // keys 64 hc + 32 u .. +31 -> packed columns 32 hc + 16 u .. +15
-                        // (S columns this thread has already read)
-                        tmem_st16(tS + hc * 32 + u * 16, pkd);
-                    }
-                }
-                const float2 sa = up2(add2(s2[0], s2[1]));
-                lX += sa.x + sa.y;
-                if (i > i0 && __any_sync(0xffffffffu, resc)) {
-                    // the row of O, once the previous tile's P . V has completed
-                    if (!mbar_wait_ab(&o_ready[(i - 1) % NBUF], ((i - 1) / NBUF) & 1, p.limit_ns, flags)) {
-                        give_up(p, flags, 1u);
-                        return false;
-                    }
-                    tc_fence_after();
-                    const float fo = resc ? f : 1.0f;
-#pragma unroll 1
-                    for (int ch = 0; ch < D / 16; ch++) {
-                        uint32_t o[16];
-                        tmem_ld16(tO + ch * 16, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int e = 0; e < 16; e++) o[e] = __float_as_uint(__uint_as_float(o[e]) * fo);
-                        tmem_st16(tO + ch * 16, o);
-                    }
-                }
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_remote(pf_lead + (uint32_t)(bf * 8));
-            }
-            // the row sum over both sets (segment parity keeps a slot from
-            // being rewritten before the other set has read it)
-            const int sp = k & 1;
-            finl[(sp * 2 + set) * 128 + row] = lX;
-            __threadfence_block();
-            fin[(sp * 2 + set) * 128 + row] = ((unsigned long long)(k + 1) << 32) | __float_as_uint(mX);
-            unsigned long long ov;
-            if (!poll(fin + (sp * 2 + (set ^ 1)) * 128 + row, (unsigned)(k + 1), ov)) {
-                give_up(p, flags, 1u);
-                return false;
-            }
-            __threadfence_block();
-            const float mo = __uint_as_float((unsigned)ov), lo = finl[(sp * 2 + (set ^ 1)) * 128 + row];
-            const float m = fmaxf(mX, mo);   // the running max after the segment's last tile
-            const float lt = (mX == -INFINITY ? 0.0f : lX * ex2_approx(mX - m)) +
-                             (mo == -INFINITY ? 0.0f : lo * ex2_approx(mo - m));
-            if (!mbar_wait_ab(o_full, k & 1, p.limit_ns, flags)) {
-                give_up(p, flags, 1u);
-                return false;
-            }
-            tc_fence_after();
-            const bool whole = sg.t0 == 0 && sg.t1 == nt_of(p, b);
-            const int64_t slot = (((int64_t)c * p.kseg + k) * 2 + rank) * 128 + row;
-            float *dst = p.out + (int64_t)tok * p.out_stride + (int64_t)(p.out_head0 + kvh * p.r + hd) * p.dv;
-            float scl = 1.0f;
-            if (whole) {
-                scl = lt > 0.0f ? __fdiv_rn(1.0f, lt) : no_key_scale(p);
-            } else {
-                if (set == 0) reinterpret_cast<float2 *>(p.pstat)[slot] = make_float2(m, lt);
-                dst = p.pout + slot * D;
-            }
-            const uint64_t pol = policy_evict_last();
-#pragma unroll 1
-            for (int ch = 0; ch < 2; ch++) {   // this set's 64 dims of the row
-                uint32_t o[32];
-                tmem_ld32(tO + set * 64 + ch * 32, o);
-                tmem_wait_ld();
-                if (valid)
-#pragma unroll
-                    for (int q = 0; q < 8; q++) {
-                        const float4 val = make_float4(__uint_as_float(o[4 * q]) * scl, __uint_as_float(o[4 * q + 1]) * scl,
-                                                       __uint_as_float(o[4 * q + 2]) * scl,
-                                                       __uint_as_float(o[4 * q + 3]) * scl);
-                        float *d4 = dst + set * 64 + ch * 32 + 4 * q;
-                        if (whole) *reinterpret_cast<float4 *>(d4) = val;
-                        else st_v4_hint(d4, val, pol);
-                    }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_remote(oe_lead);
-            return true;
-        });
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0 && lane == 0 && rank == 0 && flags[0]) {
-        for (int j = issued_k > KS ? issued_k - KS : 0; j < issued_k; j++)
-            mbar_wait(&k_full[j % KS], (j / KS) & 1, p.limit_ns);
-        for (int j = issued_v > VS ? issued_v - VS : 0; j < issued_v; j++)
-            mbar_wait(&v_full[j % VS], (j / VS) & 1, p.limit_ns);
-        if (issued_q > 0) mbar_wait(q_full, (issued_q - 1) & 1, p.limit_ns);
-    }
-    __syncthreads();
-    cluster_sync_all();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc2(tmem, 512);
-    }
-}
-
-// ---------------------------------------------------------------------------
 // the fold of split pairs
 // ---------------------------------------------------------------------------
 // out = sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i over the pair's segments
@@ -1681,10 +1259,6 @@ cudaError_t prefill_pair_prepare(int *clusters)
                                          (int)PL2::bytes);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(prefill2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PL2::bytes);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(prefill3_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PL3::bytes);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(prefill3_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PL3::bytes);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2);
@@ -1696,15 +1270,9 @@ cudaError_t prefill_pair_prepare(int *clusters)
 cudaError_t launch_prefill_pair(const CUtensorMap &qmap, const CUtensorMap &kmap32, const CUtensorMap &vmap,
                                 const PrefillParams &p, cudaStream_t st)
 {
-    // (the kernels' cluster shape is compiled in: 2 x 1 x 1); p.nt selects the
-    // form: 4 tiles a pair (prefill2_kernel) or 2 (prefill3_kernel)
-    if (p.nt == 2) {
-        if (p.mask) prefill3_kernel<true><<<2 * p.n_cta, kPThreads, PL3::bytes, st>>>(qmap, kmap32, vmap, p);
-        else prefill3_kernel<false><<<2 * p.n_cta, kPThreads, PL3::bytes, st>>>(qmap, kmap32, vmap, p);
-    } else {
-        if (p.mask) prefill2_kernel<true><<<2 * p.n_cta, kPThreads, PL2::bytes, st>>>(qmap, kmap32, vmap, p);
-        else prefill2_kernel<false><<<2 * p.n_cta, kPThreads, PL2::bytes, st>>>(qmap, kmap32, vmap, p);
-    }
+    // (the kernel's cluster shape is compiled in: 2 x 1 x 1)
+    if (p.mask) prefill2_kernel<true><<<2 * p.n_cta, kPThreads, PL2::bytes, st>>>(qmap, kmap32, vmap, p);
+    else prefill2_kernel<false><<<2 * p.n_cta, kPThreads, PL2::bytes, st>>>(qmap, kmap32, vmap, p);
     return cudaGetLastError();
 }
 
