@@ -591,6 +591,10 @@ def run_ours(args, sp):
                          "peak": peak, "unit": "TFLOP/s" if prefill else "GB/s",
                          "frac": round(achieved / peak, 4) if achieved else None,
                          "peak_source": peak_kind + (" dense bf16/f16 burst" if prefill else " copy bandwidth"),
+                         # the chunk runs under the power cap for the whole timed region:
+                         # its fraction of the sustained GEMM figure beside the burst one
+                         **({"frac_of_sustained": round(achieved / measured_peak("bf16_tflops_sustained")[0], 4)
+                             if achieved else None} if prefill else {}),
                          ("algorithmic_flops_per_layer" if prefill else "algorithmic_bytes_per_launch"): int(algo[dom]),
                          "launch_us": round(dom_us, 3) if dom_us else None,
                          "launch_us_source": "timed region x device-time share / launches in the region",
