@@ -824,7 +824,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
             named_sync(1, kConsumers);
             // count the head in; the CTA that converts the last local head
             // collects the peers' heads
-            if (tid == 0) flags[3] = atomicAdd(p.xticket, 1u) == (unsigned)(p.hkv - 1);
+            // (a shard of one KV head: its converter is the collector, no ticket)
+            if (tid == 0) flags[3] = p.hkv == 1 || atomicAdd(p.xticket, 1u) == (unsigned)(p.hkv - 1);
             named_sync(1, kConsumers);
             if (flags[3]) {
                 KV_STAMP(tid == 0, 8);   // collector starts polling the peers' words
@@ -870,7 +871,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const __grid_c
                 }
                 if (named_sync_or(1, kConsumers, xlate) && tid == 0) atomicOr(p.err, 8u);
                 KV_STAMP(tid == 0, 9);   // collector done
-                if (tid == 0) *p.xticket = 0u;
+                if (tid == 0 && p.hkv > 1) *p.xticket = 0u;
             }
         }
     };

@@ -109,7 +109,8 @@ def _run_shards(world, name, n_past, n_new):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("name,n_past,n_new", [("llama3.1-8b-128k", 3000, 1), ("qwen3-8b-prefill", 2000, 40),
-                                               ("llama3.2-3b", 1500, 3)])
+                                               ("llama3.2-3b", 1500, 3),
+                                               ("qwen2-0.5b", 2048, 1)])   # one KV head a shard
 def test_two_gpu_shards_match_oracle(name, n_past, n_new):
     import torch
     if torch.cuda.device_count() < 2:
