@@ -371,3 +371,21 @@ def test_decode_cluster_shapes():
             assert c <= 148 and q <= 8 and ncl == 1
             if q > 1:                                     # one cluster a head, within the device's capacity
                 assert c == hkv * q and roomy[q] >= hkv and (n_kv + 255) // 256 >= q
+
+
+def test_phase_stamps_only_in_the_measurement_build():
+    """kv_debug_stamps is exported by every build; outside the phase-stamp
+    build (build.py --stamps) it reports KV_E_UNSUPPORTED without touching
+    its arguments."""
+    r, m = ctypes.c_int32(-5), ctypes.c_int32(-5)
+    rc = K.lib().kv_debug_stamps(None, None, ctypes.byref(r), ctypes.byref(m))
+    assert rc == K.KV_E_UNSUPPORTED
+    assert (r.value, m.value) == (-5, -5)
+    assert "KV_PHASE_STAMPS" in K.lib().kv_last_error().decode()
+
+
+def test_bench_shard_of_rejects_a_non_divisor():
+    import subprocess
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--shard-of", "3"],
+                       capture_output=True, text=True, timeout=120)
+    assert r.returncode != 0 and "does not divide" in (r.stdout + r.stderr)
