@@ -45,7 +45,7 @@ def case(i):
     return sp, n_past, n_new, n_ctx
 
 
-@pytest.mark.parametrize("i", range(40))
+@pytest.mark.parametrize("i", range(240))
 def test_random_shape_matches_oracle(i, cuda):
     import torch
     sp, n_past, n_new, n_ctx = case(i)
