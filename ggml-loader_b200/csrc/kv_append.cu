@@ -22,9 +22,13 @@
 #include <algorithm>
 
 #include "kv_internal.h"
+#include "kv_sm100.cuh"
 
 namespace kvb {
 namespace {
+
+using sm100::pdl_launch_dependents;
+using sm100::pdl_wait;
 
 constexpr int kRowsPerBlock = 32;
 
@@ -131,6 +135,10 @@ __global__ void __launch_bounds__(kRowsPerBlock *(D / 8)) append_kernel(const Ap
     int t, kind, h;
     const bool active = row_of(p, row0 + rloc, t, kind, h);
     const bool rotates = active && kind < 2;
+    // launched programmatically: the inputs and the cache rows only after the
+    // previous kernel in the stream has completed
+    pdl_wait();
+    pdl_launch_dependents();
 
     float x[8];
 #pragma unroll
@@ -316,6 +324,11 @@ __global__ void __launch_bounds__(256) append_kernel_warp(const AppendParams p)
             for (int q = 0; q < 2; q++) *reinterpret_cast<float4 *>(c + 2 * q) = __ldg(reinterpret_cast<const float4 *>(cs + i0 / 2) + q);
         }
     }
+    // launched programmatically: the RoPE entries above come from a table
+    // written once at kv_alloc; the inputs and the cache rows only after the
+    // previous kernel in the stream has completed
+    pdl_wait();
+    pdl_launch_dependents();
     float x[8];
 #pragma unroll
     for (int e = 0; e < 8; e++) x[e] = 0.0f;
@@ -400,6 +413,24 @@ __global__ void __launch_bounds__(256) append_kernel_warp(const AppendParams p)
     store8_f16(dst + i0, x);
 }
 
+// a launch that may start while the previous kernel in the stream finishes
+// (programmatic dependent launch; the kernels wait for it before they touch
+// memory that kernel may write)
+template <class K>
+cudaError_t launch_early(K kernel, dim3 grid, dim3 block, cudaStream_t st, const AppendParams &p)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
 template <int D>
 cudaError_t launch_append_d(bool vec, const AppendParams &p, cudaStream_t st)
 {
@@ -412,9 +443,8 @@ cudaError_t launch_append_d(bool vec, const AppendParams &p, cudaStream_t st)
         // rotation with the nGPT norm nowhere (dory rotates whole heads)
         if (p.n_rot == 0 || p.n_rot == D) {
             const int64_t wblocks = (rows * (D / 8) + 255) / 256;
-            if (vec) append_kernel_warp<D, true><<<(unsigned)wblocks, 256, 0, st>>>(p);
-            else append_kernel_warp<D, false><<<(unsigned)wblocks, 256, 0, st>>>(p);
-            return cudaGetLastError();
+            return vec ? launch_early(append_kernel_warp<D, true>, dim3((unsigned)wblocks), dim3(256), st, p)
+                       : launch_early(append_kernel_warp<D, false>, dim3((unsigned)wblocks), dim3(256), st, p);
         }
     }
     if constexpr (D == 256) {
@@ -422,9 +452,8 @@ cudaError_t launch_append_d(bool vec, const AppendParams &p, cudaStream_t st)
     } else {
     if (p.qk_norm == 2) return cudaErrorInvalidValue;   // the nGPT norm needs whole-head rotation
     const dim3 grid((unsigned)blocks), block(kRowsPerBlock * (D / 8));
-    if (vec) append_kernel<D, true><<<grid, block, 0, st>>>(p);
-    else append_kernel<D, false><<<grid, block, 0, st>>>(p);
-    return cudaGetLastError();
+    return vec ? launch_early(append_kernel<D, true>, grid, block, st, p)
+               : launch_early(append_kernel<D, false>, grid, block, st, p);
     }
 }
 

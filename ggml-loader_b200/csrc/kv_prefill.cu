@@ -322,6 +322,9 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_kernel(const __grid_cons
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tm_slot;
+    // launched programmatically: the set-up above overlapped the previous
+    // kernel (the append that wrote the Q tiles and the new K/V rows)
+    pdl_wait();
     pdl_launch_dependents();   // the fold may start its set-up (it waits for this grid)
 
     if (warp == 0) {
@@ -763,6 +766,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem = *tm_slot;
+    pdl_wait();   // (as prefill_kernel)
     pdl_launch_dependents();
 
     if (warp == 0) {
@@ -1196,13 +1200,35 @@ cudaError_t prep_pf()
     return e == cudaSuccess ? prep_pf_m<D, true>() : e;
 }
 
-template <int D, bool MASKED>
-void launch_pf_kernel(int which, const CUtensorMap &qmap, const CUtensorMap &kmap, const CUtensorMap &vmap,
-                      const PrefillParams &p, cudaStream_t st)
+// The attention kernels are launched programmatically: their set-up (barriers,
+// tensor memory, the cluster barrier) overlaps the previous kernel's tail, and
+// they wait for it (griddepcontrol.wait) before any memory access it may affect.
+template <class K>
+cudaError_t launch_attn_early(K kernel, int n_ctas, size_t smem, cudaStream_t st, const CUtensorMap &qmap,
+                              const CUtensorMap &kmap, const CUtensorMap &vmap, const PrefillParams &p)
 {
-    if (which == 0) prefill_kernel<D, kOnePass, MASKED><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p);
-    else if (which == 2) prefill_kernel<D, kStats, MASKED><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p);
-    else prefill_kernel<D, kExact, MASKED><<<p.n_cta, kPThreads, PL<D>::bytes, st>>>(qmap, kmap, vmap, p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)n_ctas);
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, qmap, kmap, vmap, p);
+}
+
+template <int D, bool MASKED>
+cudaError_t launch_pf_kernel(int which, const CUtensorMap &qmap, const CUtensorMap &kmap, const CUtensorMap &vmap,
+                             const PrefillParams &p, cudaStream_t st)
+{
+    if (which == 0)
+        return launch_attn_early(prefill_kernel<D, kOnePass, MASKED>, p.n_cta, PL<D>::bytes, st, qmap, kmap, vmap, p);
+    if (which == 2)
+        return launch_attn_early(prefill_kernel<D, kStats, MASKED>, p.n_cta, PL<D>::bytes, st, qmap, kmap, vmap, p);
+    return launch_attn_early(prefill_kernel<D, kExact, MASKED>, p.n_cta, PL<D>::bytes, st, qmap, kmap, vmap, p);
 }
 
 template <int D>
@@ -1213,9 +1239,8 @@ cudaError_t launch_pf(int which, const CUtensorMap &qmap, const CUtensorMap &kma
     case 0:
     case 2:
     case 4:
-        if (p.mask) launch_pf_kernel<D, true>(which, qmap, kmap, vmap, p, st);
-        else launch_pf_kernel<D, false>(which, qmap, kmap, vmap, p, st);
-        break;
+        return p.mask ? launch_pf_kernel<D, true>(which, qmap, kmap, vmap, p, st)
+                      : launch_pf_kernel<D, false>(which, qmap, kmap, vmap, p, st);
     case 3: prefill_stats_fold<<<p.hkv * p.nblk, 256, 0, st>>>(p); break;
     default: {
         // the fold may be scheduled once every attention CTA has started
@@ -1271,9 +1296,8 @@ cudaError_t launch_prefill_pair(const CUtensorMap &qmap, const CUtensorMap &kmap
                                 const PrefillParams &p, cudaStream_t st)
 {
     // (the kernel's cluster shape is compiled in: 2 x 1 x 1)
-    if (p.mask) prefill2_kernel<true><<<2 * p.n_cta, kPThreads, PL2::bytes, st>>>(qmap, kmap32, vmap, p);
-    else prefill2_kernel<false><<<2 * p.n_cta, kPThreads, PL2::bytes, st>>>(qmap, kmap32, vmap, p);
-    return cudaGetLastError();
+    return p.mask ? launch_attn_early(prefill2_kernel<true>, 2 * p.n_cta, PL2::bytes, st, qmap, kmap32, vmap, p)
+                  : launch_attn_early(prefill2_kernel<false>, 2 * p.n_cta, PL2::bytes, st, qmap, kmap32, vmap, p);
 }
 
 cudaError_t launch_prefill(int D, int which, const CUtensorMap &qmap, const CUtensorMap &kmap,
