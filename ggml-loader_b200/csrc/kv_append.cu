@@ -298,43 +298,30 @@ __device__ __forceinline__ float row_mean(const float (&x)[8], bool rotates, int
     return mean;
 }
 
-#ifndef KV_APPEND_WARP_BLOCKS
-#define KV_APPEND_WARP_BLOCKS 4   // resident blocks an SM the register budget allows
-#endif
 template <int D, bool VEC>
-__global__ void __launch_bounds__(256, KV_APPEND_WARP_BLOCKS) append_kernel_warp(const AppendParams p)
+__global__ void __launch_bounds__(256) append_kernel_warp(const AppendParams p)
 {
-    // Two rows a thread, the second a grid's worth of rows past the first, so
-    // the grid is one wave of resident threads and both rows' loads are in
-    // flight together; each row's arithmetic is the one-row form's.
     constexpr int G = D / 8;               // threads per row (16 or 8)
-    constexpr int RT = 2;                  // rows a thread
     const int lane = threadIdx.x & 31;
     const int tig = lane % G;
-    const int64_t row0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / G;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x / G;
+    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / G;
+    int t, kind, h;
+    const bool active = row_of(p, row, t, kind, h);
+    const bool rotates = active && kind < 2;
     const int half = p.n_rot >> 1, i0 = tig * 8;
     const bool neox = p.rope_mode == 2;
-    int t[RT], kind[RT], h[RT];
-    bool active[RT], rotates[RT];
-    float2 c[RT][8];
+
+    // RoPE entries first: they do not depend on the row's values
+    float2 c[8];
+    if (rotates && p.n_rot > 0) {
+        const float2 *cs = p.rope + (p.n_past + t) * (int64_t)half;
+        if (neox) {
+            const int j0 = i0 < half ? i0 : i0 - half;
 #pragma unroll
-    for (int rr = 0; rr < RT; rr++) {
-        active[rr] = row_of(p, row0 + rr * stride, t[rr], kind[rr], h[rr]);
-        rotates[rr] = active[rr] && kind[rr] < 2;
-        // RoPE entries first: they do not depend on the row's values
-        if (rotates[rr] && p.n_rot > 0) {
-            const float2 *cs = p.rope + (p.n_past + t[rr]) * (int64_t)half;
-            if (neox) {
-                const int j0 = i0 < half ? i0 : i0 - half;
+            for (int q = 0; q < 4; q++) *reinterpret_cast<float4 *>(c + 2 * q) = __ldg(reinterpret_cast<const float4 *>(cs + j0) + q);
+        } else {
 #pragma unroll
-                for (int q = 0; q < 4; q++)
-                    *reinterpret_cast<float4 *>(c[rr] + 2 * q) = __ldg(reinterpret_cast<const float4 *>(cs + j0) + q);
-            } else {
-#pragma unroll
-                for (int q = 0; q < 2; q++)
-                    *reinterpret_cast<float4 *>(c[rr] + 2 * q) = __ldg(reinterpret_cast<const float4 *>(cs + i0 / 2) + q);
-            }
+            for (int q = 0; q < 2; q++) *reinterpret_cast<float4 *>(c + 2 * q) = __ldg(reinterpret_cast<const float4 *>(cs + i0 / 2) + q);
         }
     }
     // launched programmatically: the RoPE entries above come from a table
@@ -342,99 +329,88 @@ __global__ void __launch_bounds__(256, KV_APPEND_WARP_BLOCKS) append_kernel_warp
     // previous kernel in the stream has completed
     pdl_wait();
     pdl_launch_dependents();
-    float x[RT][8];
-    const float *bias[RT];
+    float x[8];
 #pragma unroll
-    for (int rr = 0; rr < RT; rr++) {   // every row's loads out before any is used
+    for (int e = 0; e < 8; e++) x[e] = 0.0f;
+    if (active) {
+        const float *src, *bias;
+        if (kind == 0) {
+            src = p.q + (int64_t)t * p.q_stride + (int64_t)(p.hq0 + h) * D;
+            bias = p.q_bias ? p.q_bias + (int64_t)(p.hq0 + h) * D : nullptr;
+        } else if (kind == 1) {
+            src = p.k + (int64_t)t * p.k_stride + (int64_t)(p.hkv0 + h) * D;
+            bias = p.k_bias ? p.k_bias + (int64_t)(p.hkv0 + h) * D : nullptr;
+        } else {
+            src = p.v + (int64_t)t * p.v_stride + (int64_t)(p.hkv0 + h) * D;
+            bias = p.v_bias ? p.v_bias + (int64_t)(p.hkv0 + h) * D : nullptr;
+        }
+        load8(src + i0, VEC, x);
+        if (bias)   // ggml_add of the projection bias (model.cpp:1099-1102): one rounded add
 #pragma unroll
-        for (int e = 0; e < 8; e++) x[rr][e] = 0.0f;
-        bias[rr] = nullptr;
-        if (active[rr]) {
-            const float *src;
-            if (kind[rr] == 0) {
-                src = p.q + (int64_t)t[rr] * p.q_stride + (int64_t)(p.hq0 + h[rr]) * D;
-                bias[rr] = p.q_bias ? p.q_bias + (int64_t)(p.hq0 + h[rr]) * D : nullptr;
-            } else if (kind[rr] == 1) {
-                src = p.k + (int64_t)t[rr] * p.k_stride + (int64_t)(p.hkv0 + h[rr]) * D;
-                bias[rr] = p.k_bias ? p.k_bias + (int64_t)(p.hkv0 + h[rr]) * D : nullptr;
-            } else {
-                src = p.v + (int64_t)t[rr] * p.v_stride + (int64_t)(p.hkv0 + h[rr]) * D;
-                bias[rr] = p.v_bias ? p.v_bias + (int64_t)(p.hkv0 + h[rr]) * D : nullptr;
-            }
-            load8(src + i0, VEC, x[rr]);
+            for (int e = 0; e < 8; e++) x[e] = __fadd_rn(x[e], __ldg(bias + i0 + e));
+    }
+
+    // ---- QK-Norm (see append_kernel); warps of V rows only skip it --------------
+    if (p.qk_norm == 1 && __any_sync(0xffffffffu, rotates)) {
+        const float mean = row_mean<G, D>(x, rotates, lane);
+        if (rotates) {
+            const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+            float wv[8];
+            load8((kind == 0 ? p.q_norm_w : p.k_norm_w) + i0, VEC, wv);   // (VEC: gammas 16-byte aligned too)
+#pragma unroll
+            for (int e = 0; e < 8; e++) x[e] = __fmul_rn(__fmul_rn(x[e], sc), wv[e]);
         }
     }
+
+    // ---- RoPE ---------------------------------------------------------------
+    if (p.n_rot > 0) {
+        if (neox) {
+            // partner of element i is i +- D/2: the thread D/16 lanes away
+            float y[8];
 #pragma unroll
-    for (int rr = 0; rr < RT; rr++)
-        if (bias[rr])   // ggml_add of the projection bias (model.cpp:1099-1102): one rounded add
+            for (int e = 0; e < 8; e++) y[e] = __shfl_xor_sync(0xffffffffu, x[e], G / 2);
+            if (rotates) {
+                const bool lo = i0 < half;
 #pragma unroll
-            for (int e = 0; e < 8; e++) x[rr][e] = __fadd_rn(x[rr][e], __ldg(bias[rr] + i0 + e));
+                for (int e = 0; e < 8; e++)
+                    x[e] = lo ? __fsub_rn(__fmul_rn(x[e], c[e].x), __fmul_rn(y[e], c[e].y))
+                              : __fadd_rn(__fmul_rn(y[e], c[e].y), __fmul_rn(x[e], c[e].x));
+            }
+        } else if (rotates) {
 #pragma unroll
-    for (int rr = 0; rr < RT; rr++) {
-        // ---- QK-Norm (see append_kernel); warps of V rows only skip it ----------
-        if (p.qk_norm == 1 && __any_sync(0xffffffffu, rotates[rr])) {
-            const float mean = row_mean<G, D>(x[rr], rotates[rr], lane);
-            if (rotates[rr]) {
-                const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+            for (int e = 0; e < 8; e += 2) {
+                const float2 cc = c[e / 2];
+                const float a = x[e], b = x[e + 1];
+                x[e] = __fsub_rn(__fmul_rn(a, cc.x), __fmul_rn(b, cc.y));
+                x[e + 1] = __fadd_rn(__fmul_rn(a, cc.y), __fmul_rn(b, cc.x));
+            }
+        }
+    }
+
+    // ---- nGPT (dory, qk_norm 2; dory.c:577-580, 646-649): after RoPE,
+    // rms_norm(x, 1e-6/D) (ggml's arithmetic, as QK-Norm) times 1/sqrt(D), then
+    // Q times its per-head, per-channel scale (q_norm_w [n_head][D]); K unscaled
+    if (p.qk_norm == 2 && __any_sync(0xffffffffu, rotates)) {
+        const float mean = row_mean<G, D>(x, rotates, lane);
+        if (rotates) {
+            const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+#pragma unroll
+            for (int e = 0; e < 8; e++) x[e] = __fmul_rn(__fmul_rn(x[e], sc), p.post);
+            if (kind == 0) {
                 float wv[8];
-                load8((kind[rr] == 0 ? p.q_norm_w : p.k_norm_w) + i0, VEC, wv);   // (VEC: gammas 16-byte aligned too)
+                load8(p.q_norm_w + (int64_t)(p.hq0 + h) * D + i0, VEC, wv);
 #pragma unroll
-                for (int e = 0; e < 8; e++) x[rr][e] = __fmul_rn(__fmul_rn(x[rr][e], sc), wv[e]);
+                for (int e = 0; e < 8; e++) x[e] = __fmul_rn(x[e], wv[e]);
             }
-        }
-
-        // ---- RoPE -----------------------------------------------------------
-        if (p.n_rot > 0) {
-            if (neox) {
-                // partner of element i is i +- D/2: the thread D/16 lanes away
-                float y[8];
-#pragma unroll
-                for (int e = 0; e < 8; e++) y[e] = __shfl_xor_sync(0xffffffffu, x[rr][e], G / 2);
-                if (rotates[rr]) {
-                    const bool lo = i0 < half;
-#pragma unroll
-                    for (int e = 0; e < 8; e++)
-                        x[rr][e] = lo ? __fsub_rn(__fmul_rn(x[rr][e], c[rr][e].x), __fmul_rn(y[e], c[rr][e].y))
-                                      : __fadd_rn(__fmul_rn(y[e], c[rr][e].y), __fmul_rn(x[rr][e], c[rr][e].x));
-                }
-            } else if (rotates[rr]) {
-#pragma unroll
-                for (int e = 0; e < 8; e += 2) {
-                    const float2 cc = c[rr][e / 2];
-                    const float a = x[rr][e], b = x[rr][e + 1];
-                    x[rr][e] = __fsub_rn(__fmul_rn(a, cc.x), __fmul_rn(b, cc.y));
-                    x[rr][e + 1] = __fadd_rn(__fmul_rn(a, cc.y), __fmul_rn(b, cc.x));
-                }
-            }
-        }
-
-        // ---- nGPT (dory, qk_norm 2; dory.c:577-580, 646-649): after RoPE,
-        // rms_norm(x, 1e-6/D) (ggml's arithmetic, as QK-Norm) times 1/sqrt(D),
-        // then Q times its per-head, per-channel scale (q_norm_w [n_head][D]);
-        // K unscaled
-        if (p.qk_norm == 2 && __any_sync(0xffffffffu, rotates[rr])) {
-            const float mean = row_mean<G, D>(x[rr], rotates[rr], lane);
-            if (rotates[rr]) {
-                const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-#pragma unroll
-                for (int e = 0; e < 8; e++) x[rr][e] = __fmul_rn(__fmul_rn(x[rr][e], sc), p.post);
-                if (kind[rr] == 0) {
-                    float wv[8];
-                    load8(p.q_norm_w + (int64_t)(p.hq0 + h[rr]) * D + i0, VEC, wv);
-#pragma unroll
-                    for (int e = 0; e < 8; e++) x[rr][e] = __fmul_rn(x[rr][e], wv[e]);
-                }
-            }
-        }
-
-        if (active[rr]) {
-            __half *dst;
-            if (kind[rr] == 0) dst = p.qbuf + ((int64_t)t[rr] * p.hq_loc + h[rr]) * D;
-            else if (kind[rr] == 1) dst = p.kc + (cache_row(p, t[rr]) * p.hkv_loc + h[rr]) * D;
-            else dst = p.vc + (cache_row(p, t[rr]) * p.hkv_loc + h[rr]) * D;
-            store8_f16(dst + i0, x[rr]);
         }
     }
+
+    if (!active) return;
+    __half *dst;
+    if (kind == 0) dst = p.qbuf + ((int64_t)t * p.hq_loc + h) * D;
+    else if (kind == 1) dst = p.kc + (cache_row(p, t) * p.hkv_loc + h) * D;
+    else dst = p.vc + (cache_row(p, t) * p.hkv_loc + h) * D;
+    store8_f16(dst + i0, x);
 }
 
 // a launch that may start while the previous kernel in the stream finishes
@@ -466,8 +442,7 @@ cudaError_t launch_append_d(bool vec, const AppendParams &p, cudaStream_t st)
         // rotary takes append_kernel (head_dim <= 128), as does a partial
         // rotation with the nGPT norm nowhere (dory rotates whole heads)
         if (p.n_rot == 0 || p.n_rot == D) {
-            // two rows a thread (append_kernel_warp)
-            const int64_t wblocks = ((rows + 1) / 2 * (D / 8) + 255) / 256;
+            const int64_t wblocks = (rows * (D / 8) + 255) / 256;
             return vec ? launch_early(append_kernel_warp<D, true>, dim3((unsigned)wblocks), dim3(256), st, p)
                        : launch_early(append_kernel_warp<D, false>, dim3((unsigned)wblocks), dim3(256), st, p);
         }
