@@ -1059,9 +1059,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 // CTAs before its grid-dependency wait, so with a programmatic launch that
 // overlaps the attention kernel's tail.
 template <int D>
-// (four blocks an SM up to head_dim 128: the 1024 blocks of a 512-token
-// chunk in fewer waves; head_dim 256 would spill at that register budget)
-__global__ void __launch_bounds__(256, D <= 128 ? 4 : 1) prefill_out_fold(const PrefillParams p)
+__global__ void __launch_bounds__(256) prefill_out_fold(const PrefillParams p)
 {
     constexpr int F4 = D / 64;   // float4s of a thread
     const int bpp = 8 * p.nt;    // blocks of 16 rows a pair
